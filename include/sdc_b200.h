@@ -1,0 +1,236 @@
+/*
+ * sdc_b200 — C ABI of the B200 (sm_100a) ABFT GEMM hot path.
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA
+ * stream, enqueues its kernels on that stream and returns an SDC_* status.
+ * Nothing here synchronises the host or allocates device memory: buffers and
+ * scratch ("workspace") are owned by the caller, whose allocator orders their
+ * reuse on the stream. On a non-zero status, sdc_last_error() returns a
+ * thread-local message naming the violated contract.
+ *
+ * Each function names the reference operator it replaces (meiyou666/SDC,
+ * paths relative to that project). The torch extension in sdc_b200/csrc
+ * registers the reference's `sdc_cutlass::*` schemas on top of this ABI.
+ *
+ * Layout conventions (identical to the reference operators):
+ *   FP8 operands   a: e4m3 [M,K] row-major, b_rows: e4m3 [N,K] row-major.
+ *   NVFP4 operands a_packed: u8 [M,K/2], b_packed: u8 [N,K/2]; two e2m1 codes
+ *                  per byte, even K index in the low nibble; sfa/sfb: ue4m3
+ *                  block-16 scales in the 128x4 interleaved atom layout
+ *                  (see sdc_nvfp4_scale_offset).
+ *   Checksums      C = 2 channels for algorithm 0 (Classic), 1 for algorithm 1
+ *                  (Sum). weights: fp32 [C,M]. Partials: fp32 [C, Tm, Np] with
+ *                  Tm = ceil(M/128) and Np = ceil(N/64)*64 (FP8) or
+ *                  ceil(N/128)*128 (NVFP4).
+ */
+#ifndef SDC_B200_H
+#define SDC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* sdc_stream_t; /* == cudaStream_t */
+
+enum sdc_status {
+  SDC_OK = 0,
+  SDC_ERR_INVALID = 1,            /* argument contract violated (message in sdc_last_error) */
+  SDC_ERR_UNSUPPORTED_DEVICE = 2, /* current device is not sm_100 */
+  SDC_ERR_CUDA = 3,               /* a CUDA runtime/driver call failed */
+  SDC_ERR_WORKSPACE = 4,          /* workspace missing or too small */
+  SDC_ERR_UNKNOWN_ALGORITHM = 5   /* algorithm id is not a compiled policy */
+};
+
+/* Checksum partial layouts for the input-fused ABFT GEMMs. */
+enum sdc_reference_layout {
+  /* predicted/magnitude[c, t, col] = contribution of M-tile t (rows
+   * 128t..128t+127), exactly the reference operator's layout. */
+  SDC_LAYOUT_TILE = 0,
+  /* predicted/magnitude[c, t, col] = contribution of the K-blocks assigned to
+   * slot t, summed over ALL rows. The sum over t equals the TILE layout's sum
+   * over t; finalize is unchanged. Costs ~1/M of the GEMM instead of ~C/64. */
+  SDC_LAYOUT_KSLICE = 1
+};
+
+/* ---- library / device ------------------------------------------------- */
+
+const char* sdc_last_error(void);
+/* Returns SDC_OK when `device` is an sm_100 GPU this library was built for. */
+int sdc_device_check(int device);
+/* Reads and clears the device watchdog word of the current device: 0 when no
+ * kernel gave up a bounded wait since the last call, otherwise the code of the
+ * first wait that expired. Synchronises `stream`. */
+int sdc_read_device_error(sdc_stream_t stream, int32_t* code);
+
+/* ---- quantisation (src/cutlass_gemm/quantization.py:99-162) ------------ */
+
+/* Scratch bytes sdc_quantize_* needs for a [rows, cols] input. */
+size_t sdc_quantize_workspace_bytes(int64_t rows, int64_t cols);
+
+/* FP8 tensorwise quantize: replaces quantize(matrix, "fp8", global_scale)
+ * (src/cutlass_gemm/quantization.py:114-140). x is fp32 (dtype 0) or bf16
+ * (dtype 1) [rows, cols]. st = 448/amax(|x|) (1 when amax == 0) if use_amax,
+ * else global_scale. codes = e4m3_rn_satfinite(x*st); *multiplier = st. */
+int sdc_quantize_fp8(const void* x, int dtype, int64_t rows, int64_t cols,
+                     int use_amax, float global_scale, uint8_t* codes,
+                     float* multiplier, void* workspace, size_t workspace_bytes,
+                     sdc_stream_t stream);
+
+/* NVFP4 quantize: replaces quantize(matrix, "nvfp4", global_scale)
+ * (src/cutlass_gemm/quantization.py:141-162) fused with the scale scatter of
+ * _pack_scales (src/cutlass_gemm/backend.py:124-127). st = 2688/amax;
+ * per 16-block: s = e4m3(amax16 * (st * (1/6))); codes =
+ * e2m1_rn_satfinite(x * min(st/s, FLT_MAX)). Writes codes [rows, cols/2],
+ * natural scales [rows, cols/16] (nullable) and MMA-layout scales (nullable,
+ * sdc_nvfp4_scale_size(rows, cols) bytes, padding zeroed). */
+int sdc_quantize_nvfp4(const void* x, int dtype, int64_t rows, int64_t cols,
+                       int use_amax, float global_scale, uint8_t* codes,
+                       uint8_t* scales, uint8_t* scales_mma, float* multiplier,
+                       void* workspace, size_t workspace_bytes,
+                       sdc_stream_t stream);
+
+/* ---- NVFP4 scale-factor layout (src/cutlass_gemm/csrc/gemm/nvfp4.cu:122-147)
+ * Byte offset of natural scale (row, block) in the 128x4 atom layout, and the
+ * layout's byte size for a [rows, k] operand. Host functions. */
+int64_t sdc_nvfp4_scale_offset(int64_t row, int64_t block, int64_t k);
+int64_t sdc_nvfp4_scale_size(int64_t rows, int64_t k);
+/* Replaces sdc_cutlass_nvfp4_scale_layout: fills indices[rows*(k/16)]. */
+int sdc_nvfp4_scale_layout(int64_t rows, int64_t k, int64_t* indices);
+/* Device scatter of natural scales into the atom layout (zero padding);
+ * replaces _pack_scales (src/cutlass_gemm/backend.py:124-127). */
+int sdc_nvfp4_pack_scales(const uint8_t* scales, int64_t rows, int64_t k,
+                          uint8_t* packed, sdc_stream_t stream);
+
+/* ---- GEMMs -------------------------------------------------------------- */
+
+/* Replaces sdc_cutlass_fp8_mm (src/cutlass_gemm/csrc/gemm/fp8.cu:96-139):
+ * d = alpha * a . b_rows^T, fp32 column-major [M,N] (element (r,c) at
+ * d[c*M + r]). alpha: device fp32 scalar. K % 16 == 0. */
+int sdc_fp8_gemm(const uint8_t* a, const uint8_t* b_rows, int64_t m, int64_t n,
+                 int64_t k, const float* alpha, float* d, sdc_stream_t stream);
+
+/* Replaces sdc_cutlass_nvfp4_mm (src/cutlass_gemm/csrc/gemm/nvfp4.cu:150-200):
+ * d = alpha * sum_k (a*sfa)(b*sfb), bf16 row-major [M,N]. K % 32 == 0. */
+int sdc_nvfp4_gemm(const uint8_t* a_packed, const uint8_t* b_packed,
+                   const uint8_t* sfa, const uint8_t* sfb, int64_t m, int64_t n,
+                   int64_t k, const float* alpha, uint16_t* d,
+                   sdc_stream_t stream);
+
+/* ---- ABFT GEMMs --------------------------------------------------------
+ * Common arguments:
+ *   algorithm  0 = Classic (2 channels), 1 = Sum (1 channel); other values
+ *              return SDC_ERR_UNKNOWN_ALGORITHM.
+ *   weights    fp32 [C, M] row weights of the column checksums.
+ *   row,col,bit  accumulator fault: all -1, or 0<=row<M, 0<=col<N, 0<=bit<32.
+ *              The epilogue XORs bit `bit` of the post-alpha fp32 value at
+ *              (row, col) before the checksum and the output cast.
+ *   nonfinite  nullable int32[1]; zeroed, then set to 1 when a converted
+ *              in-bounds output element is not finite.
+ *   observed   fp32 [C,Tm,Np]: sum over the tile's rows of w_c[row]*value.
+ *   hit        int32[1]: 1 when the fault was applied.
+ * Input-fused variants also write predicted = alpha * w^T A B and
+ * magnitude = |alpha| * |w|^T |A| |B| partials in `reference_layout`.
+ */
+
+/* Workspace bytes of the input-fused ABFT GEMMs. */
+size_t sdc_abft_workspace_bytes(int algorithm, int64_t m, int64_t n, int64_t k,
+                                int reference_layout);
+
+/* Replaces sdc_cutlass_abft_fp8_mm (src/cutlass_gemm/csrc/abft/fp8/fp8_observe.cu:113-190). */
+int sdc_abft_fp8_gemm(const uint8_t* a, const uint8_t* b_rows, int64_t m,
+                      int64_t n, int64_t k, const float* alpha, int algorithm,
+                      const float* weights, int64_t row, int64_t col,
+                      int64_t bit, int32_t* nonfinite, float* d,
+                      float* observed, int32_t* hit, sdc_stream_t stream);
+
+/* Replaces sdc_cutlass_abft_fp8_reference_mm
+ * (src/cutlass_gemm/csrc/abft/fp8/fp8_reference.cu:123-216). */
+int sdc_abft_fp8_reference_gemm(
+    const uint8_t* a, const uint8_t* b_rows, int64_t m, int64_t n, int64_t k,
+    const float* alpha, int algorithm, const float* weights, int64_t row,
+    int64_t col, int64_t bit, int32_t* nonfinite, float* d, float* observed,
+    int32_t* hit, float* predicted, float* magnitude, int reference_layout,
+    void* workspace, size_t workspace_bytes, sdc_stream_t stream);
+
+/* Replaces sdc_cutlass_abft_nvfp4_mm (src/cutlass_gemm/csrc/abft/nvfp4/nvfp4_observe.cu:159-245). */
+int sdc_abft_nvfp4_gemm(const uint8_t* a_packed, const uint8_t* b_packed,
+                        const uint8_t* sfa, const uint8_t* sfb, int64_t m,
+                        int64_t n, int64_t k, const float* alpha,
+                        int algorithm, const float* weights, int64_t row,
+                        int64_t col, int64_t bit, int32_t* nonfinite,
+                        uint16_t* d, float* observed, int32_t* hit,
+                        sdc_stream_t stream);
+
+/* Replaces sdc_cutlass_abft_nvfp4_reference_mm
+ * (src/cutlass_gemm/csrc/abft/nvfp4/nvfp4_reference.cu:165-267). */
+int sdc_abft_nvfp4_reference_gemm(
+    const uint8_t* a_packed, const uint8_t* b_packed, const uint8_t* sfa,
+    const uint8_t* sfb, int64_t m, int64_t n, int64_t k, const float* alpha,
+    int algorithm, const float* weights, int64_t row, int64_t col, int64_t bit,
+    int32_t* nonfinite, uint16_t* d, float* observed, int32_t* hit,
+    float* predicted, float* magnitude, int reference_layout, void* workspace,
+    size_t workspace_bytes, sdc_stream_t stream);
+
+/* ---- finalize (src/cutlass_gemm/csrc/abft/common/finalize.cu:55-319) ------
+ * Sums the per-tile partials of each (channel, column) in ascending tile
+ * order with IEEE round-to-nearest adds, then applies the policy
+ *   res = obs - pred;  thr = override ? t : atol + (rtol * mag)  (no FMA)
+ *   nonfinite = !finite(obs, pred, mag, res, thr)
+ *   detected  = nonfinite || thr < 0 || |res| > thr
+ * observed/predicted/magnitude: fp32 [C, m_tiles, padded_n] each (padding
+ * columns are never read). reference: fp32 [2, C, n]; written when
+ * use_reference == 0, read (first-call evidence) otherwise. residual and
+ * threshold: fp32 [C, n], written when diagnostics != 0. thresholds: nullable
+ * fp32 override, [1] (scalar_threshold=1) or [C, n]. Status inputs: either
+ * tile_flags int32[flag_count] (bit0 hit, bit1 nonfinite; packed entry) or
+ * hit_in/nonfinite_in int32[1] (input-fused entry). Outputs: flags u8[5] =
+ * {detected, nonfinite, 0, 0, 0}, hit_out int32[1], location int64[2] = -1.
+ */
+size_t sdc_abft_finalize_workspace_bytes(int algorithm, int64_t n,
+                                         int64_t m_tiles);
+int sdc_abft_finalize(int algorithm, const float* observed,
+                      const float* predicted, const float* magnitude,
+                      int64_t m_tiles, int64_t padded_n, int64_t n,
+                      const int32_t* tile_flags, int64_t flag_count,
+                      const int32_t* hit_in, const int32_t* nonfinite_in,
+                      float atol, float rtol, float* reference,
+                      int use_reference, int diagnostics, float* residual,
+                      float* threshold, const float* thresholds,
+                      int scalar_threshold, uint8_t* flags, int32_t* hit_out,
+                      int64_t* location, void* workspace,
+                      size_t workspace_bytes, sdc_stream_t stream);
+
+/* ---- localisation and single-error correction (extension) ---------------
+ * Device restatement of the Classic ratio locator (src/abft/methods.py:
+ * 201-237 of the reference; no reference operator exists for it). Inputs are
+ * finalize's residual/threshold fp32 [2, n] and flags u8[5]; writes
+ * location int64[2] ((row, col) or (-1, -1)) and located u8[1]. Only
+ * meaningful for algorithm 0 (two channels: ones and row+1 weights). */
+int sdc_abft_locate(const float* residual, const float* threshold,
+                    const uint8_t* flags, int64_t m, int64_t n,
+                    int64_t* location, uint8_t* located, sdc_stream_t stream);
+
+/* Single-error correction: when *located != 0, recomputes output element
+ * location = (row, col) as alpha * sum_k a[row,k] * b[col,k] in fp32 on CUDA
+ * cores and overwrites it in d; sets corrected u8[1]. Replaces the
+ * reference's full-GEMM recompute for a located single error. */
+int sdc_abft_correct_fp8(const uint8_t* a, const uint8_t* b_rows, int64_t m,
+                         int64_t n, int64_t k, const float* alpha,
+                         const int64_t* location, const uint8_t* located,
+                         float* d_colmajor, uint8_t* corrected,
+                         sdc_stream_t stream);
+int sdc_abft_correct_nvfp4(const uint8_t* a_packed, const uint8_t* b_packed,
+                           const uint8_t* sfa, const uint8_t* sfb, int64_t m,
+                           int64_t n, int64_t k, const float* alpha,
+                           const int64_t* location, const uint8_t* located,
+                           uint16_t* d_rowmajor, uint8_t* corrected,
+                           sdc_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SDC_B200_H */

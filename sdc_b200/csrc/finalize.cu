@@ -1,0 +1,212 @@
+// ABFT checksum finalize: merge per-tile partials and decide.
+//
+// Semantics follow src/cutlass_gemm/csrc/abft/common/finalize.cu:55-153 and
+// policy.cuh:54-63 of the reference: each (channel, column) is reduced by one
+// thread in ascending tile order with round-to-nearest adds, the threshold is
+// a separate multiply then add (never an FMA), and only exact integer status
+// bits cross thread-block boundaries. Work is memory bound (3 partial planes
+// read once); the grid is one thread per (channel, column) so loads of
+// consecutive columns coalesce, and a second one-block kernel ORs the
+// per-block status words, so no float atomics or host syncs are involved.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace sdc {
+namespace {
+
+constexpr int kFinalizeThreads = 256;
+constexpr unsigned kDetected = 1u;
+constexpr unsigned kNonfinite = 2u;
+constexpr unsigned kHit = 4u;
+
+struct FinalizeParams {
+  const float* observed;
+  const float* predicted;
+  const float* magnitude;
+  int64_t m_tiles, padded_n, n;
+  const int32_t* tile_flags;
+  int64_t flag_count;
+  const int32_t* hit_in;
+  const int32_t* nonfinite_in;
+  float atol, rtol;
+  float* reference;
+  bool use_reference;
+  bool diagnostics;
+  float* residual;
+  float* threshold;
+  const float* thresholds;
+  bool scalar_threshold;
+  int32_t* block_states;
+};
+
+template <int C>
+__global__ void __launch_bounds__(kFinalizeThreads) finalize_columns(FinalizeParams p) {
+  unsigned state = 0;
+  const int channel = blockIdx.y;
+  const int64_t block = static_cast<int64_t>(blockIdx.y) * gridDim.x + blockIdx.x;
+  const int64_t col = static_cast<int64_t>(blockIdx.x) * kFinalizeThreads + threadIdx.x;
+
+  // Status inputs: each packed tile flag is read by exactly one thread of the grid.
+  if (p.tile_flags != nullptr) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * gridDim.y * kFinalizeThreads;
+    for (int64_t i = block * kFinalizeThreads + threadIdx.x; i < p.flag_count; i += stride) {
+      const int32_t t = p.tile_flags[i];
+      if (t & 1) state |= kHit;
+      if (t & 2) state |= kDetected | kNonfinite;
+    }
+  } else if (block == 0 && threadIdx.x == 0) {
+    if (*p.hit_in != 0) state |= kHit;
+    if (*p.nonfinite_in != 0) state |= kDetected | kNonfinite;
+  }
+
+  if (col < p.n) {
+    const int64_t base = static_cast<int64_t>(channel) * p.m_tiles * p.padded_n + col;
+    float observed = 0.f, predicted = 0.f, magnitude = 0.f;
+    if (p.use_reference) {
+      for (int64_t t = 0; t < p.m_tiles; ++t) {
+        observed = __fadd_rn(observed, p.observed[base + t * p.padded_n]);
+      }
+    } else {
+      for (int64_t t = 0; t < p.m_tiles; ++t) {
+        const int64_t off = base + t * p.padded_n;
+        observed = __fadd_rn(observed, p.observed[off]);
+        predicted = __fadd_rn(predicted, p.predicted[off]);
+        magnitude = __fadd_rn(magnitude, p.magnitude[off]);
+      }
+    }
+    const int64_t out = static_cast<int64_t>(channel) * p.n + col;
+    if (p.use_reference) {
+      predicted = p.reference[out];
+      magnitude = p.reference[static_cast<int64_t>(C) * p.n + out];
+    } else {
+      p.reference[out] = predicted;
+      p.reference[static_cast<int64_t>(C) * p.n + out] = magnitude;
+    }
+    const float residual = __fsub_rn(observed, predicted);
+    const float threshold =
+        p.thresholds != nullptr ? p.thresholds[p.scalar_threshold ? 0 : out]
+                                : __fadd_rn(p.atol, __fmul_rn(p.rtol, magnitude));
+    const bool nonfinite = !isfinite(observed) || !isfinite(predicted) || !isfinite(magnitude) ||
+                           !isfinite(residual) || !isfinite(threshold);
+    if (nonfinite) state |= kDetected | kNonfinite;
+    if (threshold < 0.f || fabsf(residual) > threshold) state |= kDetected;
+    if (p.diagnostics) {
+      p.residual[out] = residual;
+      p.threshold[out] = threshold;
+    }
+  }
+
+  // Deterministic OR across the block: warp shuffle, then shared memory.
+  for (int offset = 16; offset > 0; offset >>= 1) state |= __shfl_xor_sync(0xffffffffu, state, offset);
+  __shared__ unsigned warp_state[kFinalizeThreads / 32];
+  if ((threadIdx.x & 31) == 0) warp_state[threadIdx.x >> 5] = state;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned combined = 0;
+    for (int w = 0; w < kFinalizeThreads / 32; ++w) combined |= warp_state[w];
+    p.block_states[block] = static_cast<int32_t>(combined);
+  }
+}
+
+__global__ void __launch_bounds__(kFinalizeThreads)
+    finalize_flags(const int32_t* block_states, int64_t blocks, uint8_t* flags, int32_t* hit_out,
+                   int64_t* location) {
+  unsigned state = 0;
+  for (int64_t i = threadIdx.x; i < blocks; i += kFinalizeThreads) {
+    state |= static_cast<unsigned>(block_states[i]);
+  }
+  for (int offset = 16; offset > 0; offset >>= 1) state |= __shfl_xor_sync(0xffffffffu, state, offset);
+  __shared__ unsigned warp_state[kFinalizeThreads / 32];
+  if ((threadIdx.x & 31) == 0) warp_state[threadIdx.x >> 5] = state;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned combined = 0;
+    for (int w = 0; w < kFinalizeThreads / 32; ++w) combined |= warp_state[w];
+    flags[0] = (combined & kDetected) ? 1 : 0;
+    flags[1] = (combined & kNonfinite) ? 1 : 0;
+    flags[2] = 0;  // located: reported by sdc_abft_locate, not by the policy decision
+    flags[3] = 0;  // recovered: owned by the caller's retry transaction
+    flags[4] = 0;  // recheck_failed: owned by the caller's retry transaction
+    hit_out[0] = (combined & kHit) ? 1 : 0;
+    location[0] = -1;
+    location[1] = -1;
+  }
+}
+
+int64_t finalize_blocks(int channels, int64_t n) {
+  return static_cast<int64_t>(channels) * ceil_div(n, kFinalizeThreads);
+}
+
+}  // namespace
+}  // namespace sdc
+
+extern "C" {
+
+size_t sdc_abft_finalize_workspace_bytes(int algorithm, int64_t n, int64_t m_tiles) {
+  (void)m_tiles;
+  const int channels = sdc::policy_channels(algorithm);
+  if (channels == 0 || n <= 0) return 0;
+  return static_cast<size_t>(sdc::finalize_blocks(channels, n)) * sizeof(int32_t);
+}
+
+int sdc_abft_finalize(int algorithm, const float* observed, const float* predicted,
+                      const float* magnitude, int64_t m_tiles, int64_t padded_n, int64_t n,
+                      const int32_t* tile_flags, int64_t flag_count, const int32_t* hit_in,
+                      const int32_t* nonfinite_in, float atol, float rtol, float* reference,
+                      int use_reference, int diagnostics, float* residual, float* threshold,
+                      const float* thresholds, int scalar_threshold, uint8_t* flags,
+                      int32_t* hit_out, int64_t* location, void* workspace,
+                      size_t workspace_bytes, sdc_stream_t stream) {
+  using namespace sdc;
+  const int channels = policy_channels(algorithm);
+  if (channels == 0) return fail(SDC_ERR_UNKNOWN_ALGORITHM, "Unknown compiled ABFT algorithm ID");
+  SDC_REQUIRE(n > 0 && m_tiles > 0 && padded_n >= n, "ABFT finalize requires n > 0, m_tiles > 0, padded_n >= n");
+  SDC_REQUIRE(observed != nullptr && reference != nullptr && flags != nullptr &&
+                  hit_out != nullptr && location != nullptr,
+              "ABFT finalize pointers must not be null");
+  SDC_REQUIRE(use_reference || (predicted != nullptr && magnitude != nullptr),
+              "ABFT finalize needs predicted/magnitude partials without a reference");
+  SDC_REQUIRE(tile_flags != nullptr || (hit_in != nullptr && nonfinite_in != nullptr),
+              "ABFT finalize needs tile_flags or hit/nonfinite inputs");
+  SDC_REQUIRE(!diagnostics || (residual != nullptr && threshold != nullptr),
+              "ABFT finalize diagnostics need residual and threshold outputs");
+  const int64_t blocks = finalize_blocks(channels, n);
+  if (workspace == nullptr || workspace_bytes < static_cast<size_t>(blocks) * sizeof(int32_t)) {
+    return fail(SDC_ERR_WORKSPACE, "ABFT finalize workspace too small");
+  }
+  FinalizeParams p{};
+  p.observed = observed;
+  p.predicted = predicted;
+  p.magnitude = magnitude;
+  p.m_tiles = m_tiles;
+  p.padded_n = padded_n;
+  p.n = n;
+  p.tile_flags = tile_flags;
+  p.flag_count = flag_count;
+  p.hit_in = hit_in;
+  p.nonfinite_in = nonfinite_in;
+  p.atol = atol;
+  p.rtol = rtol;
+  p.reference = reference;
+  p.use_reference = use_reference != 0;
+  p.diagnostics = diagnostics != 0;
+  p.residual = residual;
+  p.threshold = threshold;
+  p.thresholds = thresholds;
+  p.scalar_threshold = scalar_threshold != 0;
+  p.block_states = static_cast<int32_t*>(workspace);
+  const dim3 grid(static_cast<unsigned>(ceil_div(n, kFinalizeThreads)), channels);
+  if (channels == 2) {
+    finalize_columns<2><<<grid, kFinalizeThreads, 0, stream>>>(p);
+  } else {
+    finalize_columns<1><<<grid, kFinalizeThreads, 0, stream>>>(p);
+  }
+  SDC_CUDA_CHECK(cudaGetLastError());
+  finalize_flags<<<1, kFinalizeThreads, 0, stream>>>(p.block_states, blocks, flags, hit_out,
+                                                       location);
+  SDC_CUDA_CHECK(cudaGetLastError());
+  return SDC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,56 @@
+// Internal interface of the tcgen05 GEMM kernels (FP8 e4m3 and NVFP4).
+#pragma once
+
+#include "common.cuh"
+
+namespace sdc {
+
+enum class Kind : int { kFp8 = 0, kNvf4 = 1 };
+
+struct GemmProblem {
+  Kind kind;
+  const uint8_t* a;    // [M, K] e4m3 or [M, K/2] packed e2m1
+  const uint8_t* b;    // [N, K] e4m3 or [N, K/2] packed e2m1
+  const uint8_t* sfa;  // NVFP4 scale atoms of A
+  const uint8_t* sfb;  // NVFP4 scale atoms of B
+  int64_t m, n, k;
+  const float* alpha;  // device scalar
+  // Epilogue
+  bool out_bf16_rowmajor;  // else fp32 column-major
+  void* d;
+  int channels;            // 0 = unprotected
+  const float* weights;    // [C, M]
+  int64_t fault_row, fault_col, fault_bit;
+  int32_t* nonfinite;      // nullable
+  float* observed;         // [C, Tm, Np]
+  int32_t* hit;
+  int64_t padded_n;
+};
+
+// Launches the GEMM (and its fused epilogue) on `stream`. Zeroes hit/nonfinite
+// first. Returns an SDC_* status.
+int launch_gemm(const GemmProblem& p, cudaStream_t stream);
+
+// Input-side checksum partials (predicted, magnitude), reference layouts.
+struct ReferenceProblem {
+  Kind kind;
+  const uint8_t* a;
+  const uint8_t* b;
+  const uint8_t* sfa;
+  const uint8_t* sfb;
+  int64_t m, n, k;
+  const float* alpha;
+  int channels;
+  const float* weights;
+  float* predicted;  // [C, Tm, Np]
+  float* magnitude;
+  int64_t padded_n;
+  int layout;        // sdc_reference_layout
+  void* workspace;
+  size_t workspace_bytes;
+};
+
+size_t reference_workspace_bytes(int channels, int64_t m, int64_t n, int64_t k, int layout);
+int launch_reference(const ReferenceProblem& p, cudaStream_t stream);
+
+}  // namespace sdc

@@ -1,0 +1,285 @@
+// Input-side ABFT checksums: predicted = alpha * w^T A B and
+// magnitude = |alpha| * |w|^T |A| |B| partials.
+//
+// TILE layout (reference parity). Restates the arithmetic of
+// src/cutlass_gemm/csrc/abft/fp8/fp8_reference.cuh:31-83 and
+// nvfp4/nvfp4_reference.cuh:31-84 of the reference: per 128-row M-tile,
+//   q_c[k]  = fma over rows (ascending) of w_c[row] * A[row, k]
+//   |q|_c[k] likewise with |w|, |A|
+//   r_c[n] = fma over k (ascending) of q_c[k] * B[n, k];  a_c[n] with |q|, |B|
+//   predicted = alpha * r, magnitude = |alpha| * a   (columns < padded N)
+// with the same fp32 operation order, so results match the reference's
+// mainloop bit for bit. Cost is ~C/32 of the GEMM on CUDA cores, so this
+// layout is the parity path, not the fast path.
+//
+// KSLICE layout (fast path). q is summed over all M-tiles (ascending tile
+// order) and K-block kb (128 K) contributes to slot kb % Tm:
+//   predicted[c, t, n] = alpha * sum_{kb % Tm == t} sum_{k in kb} q_c[k] B[n,k]
+// The per-column sum over slots equals the TILE layout's sum over tiles up to
+// fp32 rounding, so finalize is unchanged, at ~1/M of the GEMM's work.
+#include <algorithm>
+
+#include "gemm.cuh"
+
+namespace sdc {
+namespace {
+
+constexpr int kTileRows = 128;
+constexpr int kRefThreads = 128;
+constexpr int kTilesPerBlock = 8;
+constexpr int kChunkK = 64;
+constexpr int kSliceK = 128;
+
+__device__ __forceinline__ int64_t sf_off(int64_t row, int64_t block, int64_t k_atoms) {
+  return ((row >> 7) * k_atoms + (block >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4 +
+         (block & 3);
+}
+
+// Decoded operand value at (row, k): e4m3 byte, or e2m1 nibble times its ue4m3 scale.
+template <Kind KIND>
+__device__ __forceinline__ float operand_value(const uint8_t* x, const uint8_t* sf, int64_t row,
+                                               int64_t k, int64_t kdim) {
+  if constexpr (KIND == Kind::kFp8) {
+    return decode_e4m3(x[row * kdim + k]);
+  } else {
+    const uint32_t byte = x[row * (kdim / 2) + (k >> 1)];
+    const float code = decode_e2m1((k & 1) ? (byte >> 4) : (byte & 15u));
+    const float scale = decode_e4m3(sf[sf_off(row, k >> 4, (kdim + 63) / 64)]);
+    return code * scale;
+  }
+}
+
+// q[(c*2 + h) * Tm * K + t * K + k]: h = 0 signed projection, h = 1 magnitude.
+template <Kind KIND, int C>
+__global__ void __launch_bounds__(kRefThreads)
+    q_encode(const uint8_t* a, const uint8_t* sfa, int64_t m, int64_t k, const float* weights,
+             float* q, int64_t tiles_m) {
+  const int64_t kk = static_cast<int64_t>(blockIdx.x) * kRefThreads + threadIdx.x;
+  const int64_t t = blockIdx.y;
+  if (kk >= k) return;
+  float enc[C], mag[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) enc[c] = mag[c] = 0.f;
+  const int64_t rows = std::min<int64_t>(kTileRows, m - t * kTileRows);
+  for (int64_t r = 0; r < rows; ++r) {
+    const int64_t row = t * kTileRows + r;
+    const float v = operand_value<KIND>(a, sfa, row, kk, k);
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const float w = __ldg(weights + c * m + row);
+      enc[c] = fmaf(w, v, enc[c]);
+      mag[c] = fmaf(fabsf(w), fabsf(v), mag[c]);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    q[((c * 2 + 0) * tiles_m + t) * k + kk] = enc[c];
+    q[((c * 2 + 1) * tiles_m + t) * k + kk] = mag[c];
+  }
+}
+
+// Loads the B operand values of columns k0..k0+63 of `row` (k0 % 64 == 0).
+template <Kind KIND>
+__device__ __forceinline__ void load_b_chunk(const uint8_t* b, const uint8_t* sfb, int64_t row,
+                                             int64_t k0, int64_t kdim, int kc, float (&v)[kChunkK]) {
+  if (kc == kChunkK) {
+    if constexpr (KIND == Kind::kFp8) {
+      const uint4* p = reinterpret_cast<const uint4*>(b + row * kdim + k0);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 u = __ldg(p + i);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[16 * i + j] = decode_e4m3((w[j >> 2] >> (8 * (j & 3))) & 0xFFu);
+      }
+    } else {
+      const uint4* p = reinterpret_cast<const uint4*>(b + row * (kdim / 2) + k0 / 2);
+      const uint32_t sf_word =
+          *reinterpret_cast<const uint32_t*>(sfb + sf_off(row, k0 >> 4, (kdim + 63) / 64));
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const uint4 u = __ldg(p + i);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int kk = 32 * i + j;
+          const uint32_t byte = (w[j >> 3] >> (8 * ((j >> 1) & 3))) & 0xFFu;
+          const float code = decode_e2m1((j & 1) ? (byte >> 4) : (byte & 15u));
+          v[kk] = code * decode_e4m3((sf_word >> (8 * (kk >> 4))) & 0xFFu);
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kChunkK; ++j) v[j] = j < kc ? operand_value<KIND>(b, sfb, row, k0 + j, kdim) : 0.f;
+  }
+}
+
+template <Kind KIND, int C>
+__global__ void __launch_bounds__(kRefThreads)
+    propagate_tiles(const uint8_t* b, const uint8_t* sfb, int64_t n, int64_t k, const float* q,
+                    int64_t tiles_m, const float* alpha_ptr, float* pred, float* mag,
+                    int64_t padded_n) {
+  __shared__ float qs[kTilesPerBlock][C][2][kChunkK];
+  const int64_t col = static_cast<int64_t>(blockIdx.x) * kRefThreads + threadIdx.x;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kTilesPerBlock;
+  const int nt = static_cast<int>(std::min<int64_t>(kTilesPerBlock, tiles_m - t0));
+  float r[kTilesPerBlock][C], a[kTilesPerBlock][C];
+#pragma unroll
+  for (int t = 0; t < kTilesPerBlock; ++t) {
+#pragma unroll
+    for (int c = 0; c < C; ++c) r[t][c] = a[t][c] = 0.f;
+  }
+  for (int64_t k0 = 0; k0 < k; k0 += kChunkK) {
+    const int kc = static_cast<int>(std::min<int64_t>(kChunkK, k - k0));
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < kTilesPerBlock * C * 2 * kChunkK; idx += kRefThreads) {
+      const int kk = idx % kChunkK;
+      const int h = (idx / kChunkK) % 2;
+      const int c = (idx / (2 * kChunkK)) % C;
+      const int t = idx / (C * 2 * kChunkK);
+      qs[t][c][h][kk] = (t < nt && kk < kc) ? q[((c * 2 + h) * tiles_m + t0 + t) * k + k0 + kk] : 0.f;
+    }
+    __syncthreads();
+    if (col < n) {
+      float v[kChunkK];
+      load_b_chunk<KIND>(b, sfb, col, k0, k, kc, v);
+      for (int kk = 0; kk < kc; ++kk) {
+        const float value = v[kk];
+        const float av = fabsf(value);
+#pragma unroll
+        for (int t = 0; t < kTilesPerBlock; ++t) {
+          if (t < nt) {
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+              r[t][c] = fmaf(qs[t][c][0][kk], value, r[t][c]);
+              a[t][c] = fmaf(qs[t][c][1][kk], av, a[t][c]);
+            }
+          }
+        }
+      }
+    }
+  }
+  if (col < padded_n) {
+    const float alpha = *alpha_ptr;
+#pragma unroll
+    for (int t = 0; t < kTilesPerBlock; ++t) {
+      if (t < nt) {
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+          const int64_t off = (c * tiles_m + t0 + t) * padded_n + col;
+          pred[off] = alpha * r[t][c];
+          mag[off] = fabsf(alpha) * a[t][c];
+        }
+      }
+    }
+  }
+}
+
+// q_full[(c*2 + h) * K + k] = sum over tiles (ascending) of q[(c*2+h), t, k].
+__global__ void reduce_tiles(const float* q, int64_t planes, int64_t tiles_m, int64_t k, float* q_full) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= planes * k) return;
+  const int64_t plane = idx / k, kk = idx - plane * k;
+  float s = 0.f;
+  for (int64_t t = 0; t < tiles_m; ++t) s = __fadd_rn(s, q[(plane * tiles_m + t) * k + kk]);
+  q_full[idx] = s;
+}
+
+template <Kind KIND, int C>
+__global__ void __launch_bounds__(kRefThreads)
+    propagate_slots(const uint8_t* b, const uint8_t* sfb, int64_t n, int64_t k, const float* q_full,
+                    int64_t tiles_m, const float* alpha_ptr, float* pred, float* mag, int64_t padded_n) {
+  __shared__ float qs[C][2][kSliceK];
+  const int64_t col = static_cast<int64_t>(blockIdx.x) * kRefThreads + threadIdx.x;
+  const int64_t slot = blockIdx.y;
+  const int64_t k_blocks = (k + kSliceK - 1) / kSliceK;
+  float r[C], a[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) r[c] = a[c] = 0.f;
+  for (int64_t kb = slot; kb < k_blocks; kb += tiles_m) {
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < C * 2 * kSliceK; idx += kRefThreads) {
+      const int kk = idx % kSliceK;
+      const int plane = idx / kSliceK;
+      const int64_t kg = kb * kSliceK + kk;
+      (&qs[0][0][0])[idx] = kg < k ? q_full[plane * k + kg] : 0.f;
+    }
+    __syncthreads();
+    if (col < n) {
+      for (int half = 0; half < kSliceK / kChunkK; ++half) {
+        const int64_t k0 = kb * kSliceK + half * kChunkK;
+        if (k0 >= k) break;
+        const int kc = static_cast<int>(std::min<int64_t>(kChunkK, k - k0));
+        float v[kChunkK];
+        load_b_chunk<KIND>(b, sfb, col, k0, k, kc, v);
+        for (int kk = 0; kk < kc; ++kk) {
+#pragma unroll
+          for (int c = 0; c < C; ++c) {
+            r[c] = fmaf(qs[c][0][half * kChunkK + kk], v[kk], r[c]);
+            a[c] = fmaf(qs[c][1][half * kChunkK + kk], fabsf(v[kk]), a[c]);
+          }
+        }
+      }
+    }
+  }
+  if (col < padded_n) {
+    const float alpha = *alpha_ptr;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int64_t off = (c * tiles_m + slot) * padded_n + col;
+      pred[off] = alpha * r[c];
+      mag[off] = fabsf(alpha) * a[c];
+    }
+  }
+}
+
+template <Kind KIND, int C>
+int launch_ref_impl(const ReferenceProblem& p, cudaStream_t stream) {
+  const int64_t tiles_m = ceil_div(p.m, kTileRows);
+  float* q = static_cast<float*>(p.workspace);
+  q_encode<KIND, C><<<dim3(static_cast<unsigned>(ceil_div(p.k, kRefThreads)), static_cast<unsigned>(tiles_m)),
+                      kRefThreads, 0, stream>>>(p.a, p.sfa, p.m, p.k, p.weights, q, tiles_m);
+  SDC_CUDA_CHECK(cudaGetLastError());
+  const unsigned col_blocks = static_cast<unsigned>(ceil_div(p.padded_n, kRefThreads));
+  if (p.layout == SDC_LAYOUT_TILE) {
+    propagate_tiles<KIND, C><<<dim3(col_blocks, static_cast<unsigned>(ceil_div(tiles_m, kTilesPerBlock))),
+                               kRefThreads, 0, stream>>>(p.b, p.sfb, p.n, p.k, q, tiles_m, p.alpha,
+                                                         p.predicted, p.magnitude, p.padded_n);
+  } else {
+    float* q_full = q + C * 2 * tiles_m * p.k;
+    const int64_t total = C * 2 * p.k;
+    reduce_tiles<<<static_cast<unsigned>(ceil_div(total, 256)), 256, 0, stream>>>(q, C * 2, tiles_m, p.k, q_full);
+    SDC_CUDA_CHECK(cudaGetLastError());
+    propagate_slots<KIND, C><<<dim3(col_blocks, static_cast<unsigned>(tiles_m)), kRefThreads, 0, stream>>>(
+        p.b, p.sfb, p.n, p.k, q_full, tiles_m, p.alpha, p.predicted, p.magnitude, p.padded_n);
+  }
+  SDC_CUDA_CHECK(cudaGetLastError());
+  return SDC_OK;
+}
+
+}  // namespace
+
+size_t reference_workspace_bytes(int channels, int64_t m, int64_t n, int64_t k, int layout) {
+  (void)n;
+  const int64_t tiles_m = ceil_div(m, kTileRows);
+  int64_t floats = static_cast<int64_t>(channels) * 2 * tiles_m * k;
+  if (layout == SDC_LAYOUT_KSLICE) floats += static_cast<int64_t>(channels) * 2 * k;
+  return static_cast<size_t>(floats) * sizeof(float);
+}
+
+int launch_reference(const ReferenceProblem& p, cudaStream_t stream) {
+  if (p.layout != SDC_LAYOUT_TILE && p.layout != SDC_LAYOUT_KSLICE) {
+    return fail(SDC_ERR_INVALID, "unknown ABFT reference layout");
+  }
+  const size_t need = reference_workspace_bytes(p.channels, p.m, p.n, p.k, p.layout);
+  if (p.workspace == nullptr || p.workspace_bytes < need) {
+    return fail(SDC_ERR_WORKSPACE, "ABFT reference workspace too small");
+  }
+  if (p.kind == Kind::kFp8) {
+    return p.channels == 2 ? launch_ref_impl<Kind::kFp8, 2>(p, stream) : launch_ref_impl<Kind::kFp8, 1>(p, stream);
+  }
+  return p.channels == 2 ? launch_ref_impl<Kind::kNvf4, 2>(p, stream) : launch_ref_impl<Kind::kNvf4, 1>(p, stream);
+}
+
+}  // namespace sdc

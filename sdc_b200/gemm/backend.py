@@ -1,0 +1,58 @@
+"""Unprotected GEMM entry and NVFP4 scale-layout helpers.
+
+Mirrors src/cutlass_gemm/backend.py of the reference: ``require_device``,
+``_scale_layout``, ``_pack_scales`` and ``gemm(a, b, precision, scaling,
+global_scale)`` with the same precision/scaling pairs and output contracts
+(FP8: fp32 column-major; NVFP4: bf16 row-major). The FP32/BF16 legacy
+precisions of the reference are outside this path and raise.
+"""
+from __future__ import annotations
+
+from functools import lru_cache
+
+import torch
+
+from .. import ops
+from .. import require_device as _require
+
+SCALING = {"fp32": "none", "bf16": "none", "fp8": "tensorwise", "nvfp4": "block16"}
+
+
+def require_device(device):
+    _require(device)
+
+
+@lru_cache(maxsize=128)
+def _scale_layout(m, n, k, device):
+    """Natural-scale -> atom-layout indices (CPU op), moved to ``device``."""
+    ia, ib, size_a, size_b = ops.nvfp4_scale_layout(m, n, k)
+    return ia.to(device), ib.to(device), size_a, size_b
+
+
+def _pack_scales(scales, indices, size):
+    storage = torch.zeros(size, device=scales.device, dtype=torch.uint8)
+    storage.scatter_(0, indices.flatten(), scales.view(torch.uint8).flatten())
+    return storage
+
+
+def mm(a, b):
+    raise NotImplementedError("FP32/BF16 legacy GEMMs are not part of the sdc_b200 FP8/NVFP4 path")
+
+
+def gemm(a, b, precision, scaling, global_scale="amax"):
+    """A @ B through the quantised sm_100a kernel selected by precision."""
+    if precision not in SCALING or scaling != SCALING[precision]:
+        raise ValueError(f"GEMM precision and scaling do not match: {precision}/{scaling}")
+    if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[0] or a.device != b.device:
+        raise ValueError("GEMM inputs must be two matching matrices on one device")
+    if precision in {"fp32", "bf16"}:
+        return mm(a, b)
+    require_device(a.device)
+    from .quantization import quantize
+
+    qa = quantize(a.contiguous(), precision, global_scale)
+    qb = quantize(b.T.contiguous(), precision, global_scale)
+    alpha = (qa.multiplier * qb.multiplier).reciprocal()
+    if precision == "fp8":
+        return ops.fp8_mm(qa.codes.view(torch.float8_e4m3fn), qb.codes.view(torch.float8_e4m3fn), alpha)
+    return ops.nvfp4_mm(qa.codes, qb.codes, qa.scales_mma, qb.scales_mma, a.shape[1], alpha)
