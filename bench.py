@@ -1,0 +1,404 @@
+#!/usr/bin/env python
+"""Benchmark of the ABFT-protected FP8 / NVFP4 GEMM path on B200.
+
+Metric: ABFT NVFP4/FP8 GEMM TFLOPS, % overhead vs the
+unprotected kernel, detection recall. One step = one protected GEMM on
+operands already quantised and resident in HBM: the input-fused ABFT GEMM
+(tcgen05 mainloop, fused observed-checksum epilogue, input-side prediction in
+the K-slice layout) followed by the device finalize that merges partials and
+decides. Throughput counts only the useful 2*M*N*K flops.
+
+Headline workload (config[1]): FP8 e4m3, M=N=K=8192, tensorwise scales (the
+reference's FP8 semantics; block-scaled FP8 is not built yet), fp32 output.
+The NVFP4 workload of config[2] (M=N=K=16384, e2m1 + ue4m3/16 + fp32 global
+scale, bf16 out) is measured in the same run and reported under "nvfp4".
+
+Multi-GPU (python -m torch.distributed.run ... bench.py --gpus N): each rank
+protects its own M-shard (8192 rows x N=K=8192, weak scaling: the job's M is
+8192*N) and the ranks all-reduce (MAX) their detection status words over
+NCCL after every step, the path's only exchange. Time is the max over ranks.
+
+--impl reference times the reference's own CPU/torch ABFT path (restated in
+oracle/cpu_path.py, bit-identical to it) on this host's cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "ABFT NVFP4/FP8 GEMM TFLOPS, % overhead vs unprotected, detection recall"
+UNIT = "TFLOPS"
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return data["bf16_tflops"], data["hbm_gbs"], "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self):
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        sm_max = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        loaded = [s for s in sm if s > 0.5 * sm_max] or sm
+        reasons = set()
+        for r in rows:
+            for name, flag in (("hw_slowdown", r[5]), ("hw_thermal_slowdown", r[6]),
+                               ("sw_thermal_slowdown", r[7]), ("sw_power_cap", r[8])):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": sm_max, "reasons": sorted(reasons),
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+def make_operands(precision, m, n, k, device, seed):
+    """Seeded N(0,1) bf16 A [m,k] and B_rows [n,k] (synthetic, BASELINE shapes) quantised once."""
+    from sdc_b200.gemm.quantization import quantize
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    a = torch.randn(m, k, device=device, generator=g, dtype=torch.bfloat16)
+    b = torch.randn(n, k, device=device, generator=g, dtype=torch.bfloat16)
+    qa, qb = quantize(a, precision), quantize(b, precision)
+    alpha = (qa.multiplier * qb.multiplier).reciprocal()
+    if precision == "fp8":
+        args = (qa.codes.view(torch.float8_e4m3fn), qb.codes.view(torch.float8_e4m3fn), alpha)
+    else:
+        args = (qa.codes, qb.codes, qa.scales_mma, qb.scales_mma, k, alpha)
+    del a, b
+    return args
+
+
+class Protected:
+    """One protected GEMM step on resident operands (the hot path)."""
+
+    def __init__(self, precision, m, n, k, device, seed, layout=1, atol=1e-3, rtol=1e-4):
+        self.ops = torch.ops.sdc_cutlass
+        self.precision, self.m, self.n, self.k = precision, m, n, k
+        self.args = make_operands(precision, m, n, k, device, seed)
+        self.weights = torch.stack((torch.ones(m, device=device),
+                                    torch.arange(1, m + 1, device=device, dtype=torch.float32)))
+        self.nonfinite = torch.zeros(1, dtype=torch.int32, device=device)
+        self.layout, self.atol, self.rtol = layout, atol, rtol
+        self.fused = self.ops.abft_fp8_reference_mm if precision == "fp8" else self.ops.abft_nvfp4_reference_mm
+        self.observe = self.ops.abft_fp8_mm if precision == "fp8" else self.ops.abft_nvfp4_mm
+        self.plain = self.ops.fp8_mm if precision == "fp8" else self.ops.nvfp4_mm
+
+    def step(self, fault=(-1, -1, -1)):
+        out, obs, hit, pred, mag = self.fused(*self.args, self.weights, *fault, 0, self.nonfinite, self.layout)
+        packet = self.ops.abft_finalize_reference(obs, pred, mag, hit, self.nonfinite, self.n, self.atol,
+                                                  self.rtol, None, True)
+        return out, packet
+
+    def unprotected(self):
+        return self.plain(*self.args)
+
+    def gemm_only(self):
+        return self.observe(*self.args, self.weights, -1, -1, -1)
+
+
+# Kernels this library launches per protected step: projection of A, tile
+# reduce, the GEMM (prediction fused) + 2 finalize kernels.
+LAUNCHES_PER_STEP = 5
+
+
+def timed(fn, steps, warmup, stream):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) / 1e3
+
+
+def detection_campaign(prot, flips, seed):
+    """Seeded single-bit accumulator flips (bits 23-30 exponent, 20-22 high
+    mantissa) at uniform (row, col); recall over all flips and over flips
+    whose checksum perturbation exceeds the threshold."""
+    g = torch.Generator().manual_seed(seed)
+    clean_out, clean_packet = prot.step()
+    residual0 = clean_packet[1].clone()
+    threshold0 = clean_packet[2].clone()
+    detected = detectable = 0
+    by_class = {"exponent": [0, 0], "high_mantissa": [0, 0]}
+    for _ in range(flips):
+        row = int(torch.randint(0, prot.m, (1,), generator=g))
+        col = int(torch.randint(0, prot.n, (1,), generator=g))
+        bit = int(torch.randint(20, 31, (1,), generator=g))
+        _, packet = prot.step((row, col, bit))
+        flags = packet[3].tolist()
+        hit = bool(flags[0])
+        # Detectable: the flip's own checksum perturbation exceeds the clean threshold.
+        delta = (packet[1][:, col] - residual0[:, col]).abs()
+        can = bool((delta > threshold0[:, col]).any()) or bool(flags[1])
+        detected += hit
+        detectable += can
+        cls = "exponent" if bit >= 23 else "high_mantissa"
+        by_class[cls][0] += hit
+        by_class[cls][1] += 1
+    clean_runs = 8
+    false_positives = sum(bool(prot.step()[1][3][0]) for _ in range(clean_runs))
+    return {"flips": flips, "detected": detected, "detectable": detectable,
+            "recall_all": detected / max(flips, 1), "recall_detectable": min(detected, detectable) / max(detectable, 1),
+            "by_class": {k: {"detected": v[0], "flips": v[1]} for k, v in by_class.items()},
+            "clean_runs": clean_runs + 1, "false_positives": false_positives + int(bool(clean_packet[3][0]))}
+
+
+def e2e_step(precision, host_a, host_b, device, weights, nonfinite, atol, rtol):
+    """Public-API protected GEMM from pinned host bf16 buffers to host flags."""
+    from sdc_b200.gemm.quantization import quantize
+
+    ops = torch.ops.sdc_cutlass
+    a = host_a.to(device, non_blocking=True)
+    b = host_b.to(device, non_blocking=True)
+    qa, qb = quantize(a, precision), quantize(b, precision)
+    alpha = (qa.multiplier * qb.multiplier).reciprocal()
+    if precision == "fp8":
+        res = ops.abft_fp8_reference_mm(qa.codes.view(torch.float8_e4m3fn), qb.codes.view(torch.float8_e4m3fn),
+                                        alpha, weights, -1, -1, -1, 0, nonfinite, 1)
+    else:
+        res = ops.abft_nvfp4_reference_mm(qa.codes, qb.codes, qa.scales_mma, qb.scales_mma, a.shape[1], alpha,
+                                          weights, -1, -1, -1, 0, nonfinite, 1)
+    out, obs, hit, pred, mag = res
+    packet = ops.abft_finalize_reference(obs, pred, mag, hit, nonfinite, b.shape[0], atol, rtol, None, False)
+    return packet[3].to("cpu"), out
+
+
+def run_ours(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    import sdc_b200
+
+    sdc_b200.require_device(device)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    stream = torch.cuda.current_stream(device)
+    bf16_peak, hbm_peak, basis = measured_peaks()
+    results = {}
+    for precision, size, seed in (("fp8", 8192, 1), ("nvfp4", 16384, 2)):
+        if args.format not in ("both", precision):
+            continue
+        m = n = k = size
+        prot = Protected(precision, m, n, k, device, seed + 1000 * rank)
+        flops = 2.0 * m * n * k
+        status = torch.zeros(2, dtype=torch.int32, device=device)
+
+        def step():
+            _, packet = prot.step()
+            if dist is not None:
+                status[0] = packet[3][0].to(torch.int32)
+                status[1] = packet[4][0]
+                dist.all_reduce(status, op=dist.ReduceOp.MAX)
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        with ClockSampler(local) as clocks:
+            elapsed = timed(step, args.steps, 0, stream)
+        torch.cuda.synchronize()
+        if dist is not None:
+            t = torch.tensor([elapsed], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            elapsed = float(t.item())
+        t_unprot = timed(prot.unprotected, args.steps, 2, stream)
+        t_gemm = timed(prot.gemm_only, args.steps, 2, stream)
+        per_step = elapsed / args.steps
+        peak = bf16_peak * (2 if precision == "fp8" else 4)
+        entry = {
+            "workload": f"{precision} M=N=K={size}" + (" tensorwise" if precision == "fp8" else " block16"),
+            "tflops": world * flops / per_step / 1e12,
+            "ms_per_step": per_step * 1e3,
+            "unprotected_tflops": flops / (t_unprot / args.steps) / 1e12,
+            "overhead_pct": 100.0 * (per_step / (t_unprot / args.steps) - 1.0),
+            "roofline": {"bound": "tensor", "achieved": flops / (t_gemm / args.steps) / 1e12, "peak": peak,
+                         "unit": "TFLOP/s", "frac": flops / (t_gemm / args.steps) / 1e12 / peak,
+                         "traffic": None,
+                         "peak_basis": f"{2 if precision == 'fp8' else 4}x {basis} bf16 dense burst "
+                                       f"({bf16_peak} TFLOP/s); nominal dense {4500 if precision == 'fp8' else 9000}"},
+            "clocks": clocks.summary(),
+        }
+        if rank == 0 and not args.no_detection:
+            entry["detection"] = detection_campaign(prot, args.flips, seed)
+        if rank == 0 and not args.no_e2e:
+            host_a = torch.randn(m, k, dtype=torch.bfloat16).pin_memory()
+            host_b = torch.randn(n, k, dtype=torch.bfloat16).pin_memory()
+            w = prot.weights
+            for _ in range(2):
+                e2e_step(precision, host_a, host_b, device, w, prot.nonfinite, prot.atol, prot.rtol)
+            torch.cuda.synchronize()
+            e_steps = max(3, args.steps // 4)
+            t0 = time.perf_counter()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            for _ in range(e_steps):
+                flags, _ = e2e_step(precision, host_a, host_b, device, w, prot.nonfinite, prot.atol, prot.rtol)
+            end.record(stream)
+            end.synchronize()
+            e_time = start.elapsed_time(end) / 1e3 / e_steps
+            entry["e2e"] = {"value": flops / e_time / 1e12, "unit": UNIT,
+                            "h2d_bytes_per_step": host_a.numel() * 2 + host_b.numel() * 2,
+                            "d2h_bytes_per_step": 5, "host_wall_s_per_step": (time.perf_counter() - t0) / e_steps}
+        results[precision] = entry
+        del prot
+        torch.cuda.empty_cache()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    head = results.get("fp8") or results["nvfp4"]
+    line = {
+        "metric": METRIC, "value": head["tflops"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "e4m3" if "fp8" in results else "e2m1", "data": "synthetic",
+        "config": {"workload": head["workload"] + " ABFT (Classic, K-slice input reference) + finalize",
+                   "per_gpu": "M=N=K=8192" if "fp8" in results else "M=N=K=16384",
+                   "parallelism": f"M-shard x{world}, NCCL all-reduce of detection status",
+                   "l2": "working set (A+B codes, fp32 output) > 126 MB L2; no explicit flush"},
+        "overhead_pct": head["overhead_pct"], "unprotected_tflops": head["unprotected_tflops"],
+        "roofline": head["roofline"], "clocks": head["clocks"],
+        "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+        "e2e": head.get("e2e"), "detection": head.get("detection"),
+    }
+    if "nvfp4" in results and "fp8" in results:
+        line["nvfp4"] = results["nvfp4"]
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_sample_rows)
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(rows):
+    """The reference's CPU/torch ABFT path on a row sample of the FP8 workload."""
+    from oracle import cpu_path
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    k = n = 8192
+    a = torch.randn(rows, k, generator=g)
+    b = torch.randn(k, n, generator=g)
+    cpu_path.execute(a[:64], b[:, :64], block_k=256)  # warm the BLAS
+    t0 = time.perf_counter()
+    _, report, _ = cpu_path.execute(a, b, atol=1e-3, rtol=1e-4, block_k=256)
+    seconds = time.perf_counter() - t0
+    return {"value": 2.0 * rows * n * k / seconds / 1e12, "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"fp32 {rows}x{n}x{k} row sample of the 8192^3 workload, Classic, "
+                                      f"1 protected GEMM ({seconds:.2f} s)", "detected": report["detected"]}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import cpu_path
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    rows, k, n = args.cpu_sample_rows, 8192, 8192
+    g = torch.Generator().manual_seed(0)
+    a = torch.randn(rows, k, generator=g)
+    b = torch.randn(k, n, generator=g)
+    for _ in range(max(1, min(args.warmup, 2))):
+        cpu_path.execute(a, b, atol=1e-3, rtol=1e-4)
+    steps = max(1, min(args.steps, 5))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        cpu_path.execute(a, b, atol=1e-3, rtol=1e-4)
+    seconds = (time.perf_counter() - t0) / steps
+    value = 2.0 * rows * n * k / seconds / 1e12
+    sample = f"fp32 {rows}x{n}x{k} row sample of the FP8 8192^3 workload per step"
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": steps, "warmup": args.warmup, "ms_per_step": seconds * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "fp8 M=N=K=8192 tensorwise ABFT (Classic) + finalize",
+                   "reference_path": "abft.execute fp32 CPU path (reference_mm=torch.mm), restated in oracle/cpu_path.py"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--format", choices=["both", "fp8", "nvfp4"], default="both")
+    parser.add_argument("--flips", type=int, default=64)
+    parser.add_argument("--cpu-sample-rows", type=int, default=1024)
+    parser.add_argument("--no-detection", action="store_true")
+    parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -49,9 +49,11 @@ enum sdc_reference_layout {
   /* predicted/magnitude[c, t, col] = contribution of M-tile t (rows
    * 128t..128t+127), exactly the reference operator's layout. */
   SDC_LAYOUT_TILE = 0,
-  /* predicted/magnitude[c, t, col] = contribution of the K-blocks assigned to
-   * slot t, summed over ALL rows. The sum over t equals the TILE layout's sum
-   * over t; finalize is unchanged. Costs ~1/M of the GEMM instead of ~C/64. */
+  /* predicted/magnitude[c, t, col] = contribution of the 64-wide K slices s
+   * with s % Tm == t, summed over ALL rows. The sum over t equals the TILE
+   * layout's sum over t (up to fp32 rounding); finalize is unchanged. The
+   * propagation runs inside the GEMM on its shared-memory B tiles, so it
+   * costs one extra read of A instead of ~C/32 of the GEMM on CUDA cores. */
   SDC_LAYOUT_KSLICE = 1
 };
 

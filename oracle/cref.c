@@ -17,7 +17,7 @@
  *
  * The KSLICE entry restates the sdc_b200 fast layout (an extension with no
  * reference counterpart): q summed over tiles ascending, then per slot
- * t = kb % Tm over its 128-wide K blocks.
+ * t = s % Tm over its 64-wide K slices s (slices ascending, k ascending).
  */
 #include <math.h>
 #include <stdint.h>
@@ -109,7 +109,7 @@ int oracle_kslice_reference(int kind, const uint8_t* a, const uint8_t* sfa, cons
                             const uint8_t* sfb, int64_t m, int64_t n, int64_t k, const float* w,
                             int channels, float alpha, float* pred, float* mag, int64_t padded_n) {
   const int64_t tiles = (m + 127) / 128;
-  const int64_t kblocks = (k + 127) / 128;
+  const int64_t slices = (k + 63) / 64;
   float* q = (float*)malloc(sizeof(float) * channels * 2 * tiles * k);
   float* qf = (float*)malloc(sizeof(float) * channels * 2 * k);
   if (!q || !qf) return 1;
@@ -126,8 +126,8 @@ int oracle_kslice_reference(int kind, const uint8_t* a, const uint8_t* sfa, cons
       for (int64_t col = 0; col < padded_n; ++col) {
         float r = 0.f, s = 0.f;
         if (col < n) {
-          for (int64_t kb = slot; kb < kblocks; kb += tiles) {
-            for (int64_t kk = kb * 128; kk < kb * 128 + 128 && kk < k; ++kk) {
+          for (int64_t sl = slot; sl < slices; sl += tiles) {
+            for (int64_t kk = sl * 64; kk < sl * 64 + 64 && kk < k; ++kk) {
               const float v = value_at(kind, b, sfb, col, kk, k);
               r = fmaf(qf[(c * 2 + 0) * k + kk], v, r);
               s = fmaf(qf[(c * 2 + 1) * k + kk], fabsf(v), s);

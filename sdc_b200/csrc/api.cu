@@ -91,9 +91,8 @@ void set_abft(GemmProblem& g, int algorithm, const float* weights, int64_t row, 
   g.padded_n = ceil_div(g.n, tile_n) * tile_n;
 }
 
-int run_reference(const GemmProblem& g, float* predicted, float* magnitude, int layout,
-                  void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  SDC_REQUIRE(predicted != nullptr && magnitude != nullptr, "predicted/magnitude must not be null");
+ReferenceProblem reference_problem(const GemmProblem& g, float* predicted, float* magnitude, int layout,
+                                   void* workspace, size_t workspace_bytes) {
   ReferenceProblem r{};
   r.kind = g.kind;
   r.a = g.a;
@@ -112,7 +111,27 @@ int run_reference(const GemmProblem& g, float* predicted, float* magnitude, int 
   r.layout = layout;
   r.workspace = workspace;
   r.workspace_bytes = workspace_bytes;
-  return launch_reference(r, stream);
+  return r;
+}
+
+// Input-fused ABFT GEMM: TILE layout = GEMM, then the per-tile projection and
+// propagation on CUDA cores; K-SLICE layout = projection of A first, then the
+// GEMM with the propagation fused into its checksum warps.
+int run_input_fused(GemmProblem g, float* predicted, float* magnitude, int layout, void* workspace,
+                    size_t workspace_bytes, cudaStream_t stream) {
+  SDC_REQUIRE(predicted != nullptr && magnitude != nullptr, "predicted/magnitude must not be null");
+  const ReferenceProblem r = reference_problem(g, predicted, magnitude, layout, workspace, workspace_bytes);
+  int rc = launch_projection(r, stream);
+  if (rc != SDC_OK) return rc;
+  if (layout == SDC_LAYOUT_KSLICE) {
+    g.q_full = kslice_q_full(r);
+    g.predicted = predicted;
+    g.magnitude = magnitude;
+    return launch_gemm(g, stream);
+  }
+  rc = launch_gemm(g, stream);
+  if (rc != SDC_OK) return rc;
+  return launch_tile_propagate(r, stream);
 }
 
 }  // namespace
@@ -168,9 +187,7 @@ int sdc_abft_fp8_reference_gemm(const uint8_t* a, const uint8_t* b_rows, int64_t
   if (rc != SDC_OK) return rc;
   GemmProblem g = make_problem(Kind::kFp8, a, b_rows, nullptr, nullptr, m, n, k, alpha, false, d);
   set_abft(g, algorithm, weights, row, col, bit, nonfinite, observed, hit, 64);
-  rc = launch_gemm(g, stream);
-  if (rc != SDC_OK) return rc;
-  return run_reference(g, predicted, magnitude, reference_layout, workspace, workspace_bytes, stream);
+  return run_input_fused(g, predicted, magnitude, reference_layout, workspace, workspace_bytes, stream);
 }
 
 int sdc_abft_nvfp4_gemm(const uint8_t* a_packed, const uint8_t* b_packed, const uint8_t* sfa,
@@ -200,9 +217,7 @@ int sdc_abft_nvfp4_reference_gemm(const uint8_t* a_packed, const uint8_t* b_pack
   if (rc != SDC_OK) return rc;
   GemmProblem g = make_problem(Kind::kNvf4, a_packed, b_packed, sfa, sfb, m, n, k, alpha, true, d);
   set_abft(g, algorithm, weights, row, col, bit, nonfinite, observed, hit, 128);
-  rc = launch_gemm(g, stream);
-  if (rc != SDC_OK) return rc;
-  return run_reference(g, predicted, magnitude, reference_layout, workspace, workspace_bytes, stream);
+  return run_input_fused(g, predicted, magnitude, reference_layout, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

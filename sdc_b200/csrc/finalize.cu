@@ -64,10 +64,12 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_columns(FinalizePar
     const int64_t base = static_cast<int64_t>(channel) * p.m_tiles * p.padded_n + col;
     float observed = 0.f, predicted = 0.f, magnitude = 0.f;
     if (p.use_reference) {
+#pragma unroll 8
       for (int64_t t = 0; t < p.m_tiles; ++t) {
         observed = __fadd_rn(observed, p.observed[base + t * p.padded_n]);
       }
     } else {
+#pragma unroll 8
       for (int64_t t = 0; t < p.m_tiles; ++t) {
         const int64_t off = base + t * p.padded_n;
         observed = __fadd_rn(observed, p.observed[off]);

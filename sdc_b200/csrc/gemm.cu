@@ -1,21 +1,30 @@
-// tcgen05 GEMMs for sm_100a with the ABFT epilogue fused.
+// Persistent tcgen05 GEMMs for sm_100a with the ABFT checksums fused.
 //
-// One CTA computes a 128 x 256 output tile (one reference M-tile of 128 rows,
-// so each observed-checksum partial is produced by exactly one CTA):
-//   warp 0     TMA producer: 128-byte-swizzled K-major A/B stages (and, for
-//              NVFP4, the 512-byte scale-factor atoms) into a 4-stage ring.
-//   warp 1     allocates tensor memory; one thread issues tcgen05.mma
-//              (kind::f8f6f4 for e4m3, kind::mxf4nvf4.block16 for NVFP4 with
-//              scales copied to TMEM by tcgen05.cp) into a 128x256 fp32
-//              accumulator and releases stages with tcgen05.commit.
-//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time, alpha * acc,
-//              optional accumulator bit flip, column checksums
-//              sum_rows w_c[row] * v (butterfly transpose-reduce across lanes,
-//              fixed-order sum across the four row quarters), non-finite
-//              check of the converted output, and the output store.
+// One CTA per SM loops over 128 x 256 output tiles (one reference M-tile of
+// 128 rows per tile, so every observed-checksum partial comes from one CTA)
+// in a grouped raster order that keeps a band of A and B tiles resident in
+// L2. Warp roles:
+//   warp 0      TMA producer: 128-byte-swizzled K-major A/B stages (and the
+//               512-byte NVFP4 scale atoms) into a 4-stage ring.
+//   warp 1      allocates tensor memory; one thread issues tcgen05.mma
+//               (kind::f8f6f4 e4m3, or kind::mxf4nvf4.block16 with scales
+//               copied to TMEM by tcgen05.cp) into a 128x256 fp32
+//               accumulator. FP8 double-buffers the accumulator (2 x 256
+//               columns) so a tile's epilogue overlaps the next mainloop.
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, alpha * acc,
+//               optional accumulator bit flip, column checksums
+//               sum_rows w_c[row] * v (butterfly transpose-reduce across
+//               lanes, fixed-order sum across the four row quarters),
+//               non-finite check of the converted output, output store.
+//   warps 6-9   (K-slice layout only) input-side prediction from the B stage
+//               already in shared memory: for the 64-wide K slices assigned to
+//               this tile's slot (slice % Tm == tile row), fma chains of the
+//               full-M projection q_c[k] (precomputed, tile_reference.cu) with
+//               B[n, k] and |q|, |B|. The stage is released once the slice is
+//               copied to registers, so B is never read from HBM twice.
 // Epilogue semantics follow src/cutlass_gemm/csrc/abft/common/
 // sm120_epilogue.cuh:52-151 of the reference (inject after alpha, observe
-// before the output cast); every wait is bounded (common.cuh).
+// before the output cast). Every wait is bounded (common.cuh).
 #include <algorithm>
 
 #include "gemm.cuh"
@@ -27,11 +36,12 @@ constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBKBytes = 128;  // one 128-byte swizzle atom of K per stage
 constexpr int kStages = 4;
-constexpr int kThreads = 192;  // 6 warps
+constexpr int kSliceK = 64;    // K elements per input-checksum slice
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSfaCol = 256;  // NVFP4: 4 k-steps x 4 columns
 constexpr uint32_t kSfbCol = 272;  // NVFP4: 4 k-steps x 8 columns
 constexpr int kChunks = kBN / 32;
+constexpr int kGroupM = 16;        // M-tiles per raster group
 
 constexpr int kABytes = kBM * kBKBytes;
 constexpr int kBBytes = kBN * kBKBytes;
@@ -45,9 +55,11 @@ __host__ __device__ constexpr int stage_bytes(Kind k) {
 __host__ __device__ constexpr int smem_bytes(Kind k) {
   return 1024 + kStages * stage_bytes(k) + kRedFloats * 4 + 256;
 }
+__host__ __device__ constexpr int num_acc(Kind k) { return k == Kind::kFp8 ? 2 : 1; }
+__host__ __device__ constexpr int num_threads(bool chk) { return chk ? 320 : 192; }
 
 struct Params {
-  int32_t m, n, num_kb;
+  int32_t m, n, k, num_kb, tiles_m, tiles_n, num_tiles;
   const float* alpha;
   void* d;
   const float* weights;
@@ -55,9 +67,22 @@ struct Params {
   int32_t* nonfinite;
   float* observed;
   int32_t* hit;
-  int32_t padded_n, tiles_m;
+  int32_t padded_n;
+  const float* q_full;  // [K][C][2]: full-M projection (h=0) and magnitude (h=1)
+  float* predicted;
+  float* magnitude;
   int32_t* watchdog;
 };
+
+__device__ __forceinline__ void tile_coords(int t, const Params& p, int& mt, int& nt) {
+  const int group_tiles = kGroupM * p.tiles_n;
+  const int group = t / group_tiles;
+  const int first_m = group * kGroupM;
+  const int gm = min(kGroupM, p.tiles_m - first_m);
+  const int in_group = t - group * group_tiles;
+  mt = first_m + in_group % gm;
+  nt = in_group / gm;
+}
 
 // Lane j of the warp returns sum over the 32 lanes of x[j] (x is consumed).
 __device__ __forceinline__ float transpose_reduce32(float (&x)[32], int lane) {
@@ -77,33 +102,36 @@ __device__ __forceinline__ float transpose_reduce32(float (&x)[32], int lane) {
 // Scale-factor atom (32 rows x 16 bytes, contiguous) as a tcgen05.cp source.
 __device__ __forceinline__ uint64_t sf_desc(uint32_t addr) { return smem_desc(addr, 0, 128, 0); }
 
-template <Kind KIND, int C, bool BF16OUT>
-__global__ void __launch_bounds__(kThreads, 1)
+template <Kind KIND, int C, bool BF16OUT, bool CHK>
+__global__ void __launch_bounds__(num_threads(CHK), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ CUtensorMap tm_sfa,
                 const __grid_constant__ CUtensorMap tm_sfb, const Params p) {
   constexpr int kStageBytes = stage_bytes(KIND);
+  constexpr int kAcc = num_acc(KIND);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   float* red = reinterpret_cast<float*>(smem + kStages * kStageBytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(red + kRedFloats);
   uint64_t* empty = full + kStages;
-  uint64_t* accum = empty + kStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int nt = blockIdx.x, mt = blockIdx.y;
-  const int m0 = mt * kBM, n0 = nt * kBN;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(full + s, 1);
-      mbar_init(empty + s, 1);
+      mbar_init(empty + s, CHK ? 2 : 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, 4);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -127,22 +155,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      for (int kb = 0; kb < p.num_kb; ++kb) {
-        const int s = kb % kStages;
-        if (kb >= kStages &&
-            !mbar_wait(empty + s, ((kb / kStages) - 1) & 1, kWaitEmpty, abort_flag, p.watchdog)) {
-          break;
-        }
-        uint8_t* sa = smem + s * kStageBytes;
-        uint8_t* sb = sa + kABytes;
-        mbar_arrive_expect_tx(full + s, kStageBytes);
-        tma_load_2d(sa, &tm_a, full + s, kb * kBKBytes, m0);
-        tma_load_2d(sb, &tm_b, full + s, kb * kBKBytes, n0);
-        if constexpr (KIND == Kind::kNvf4) {
-          uint8_t* ssfa = sb + kBBytes;
-          uint8_t* ssfb = ssfa + kSfaBytes;
-          tma_load_4d(ssfa, &tm_sfa, full + s, 0, 0, kb * 4, mt);
-          tma_load_4d(ssfb, &tm_sfb, full + s, 0, 0, kb * 4, nt * 2);
+      uint32_t kbg = 0;
+      for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
+        int mt, nt;
+        tile_coords(t, p, mt, nt);
+        for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
+          const int s = kbg % kStages;
+          if (kbg >= kStages &&
+              !mbar_wait(empty + s, ((kbg / kStages) - 1) & 1, kWaitEmpty, abort_flag, p.watchdog)) {
+            break;
+          }
+          uint8_t* sa = smem + s * kStageBytes;
+          uint8_t* sb = sa + kABytes;
+          mbar_arrive_expect_tx(full + s, kStageBytes);
+          tma_load_2d(sa, &tm_a, full + s, kb * kBKBytes, mt * kBM);
+          tma_load_2d(sb, &tm_b, full + s, kb * kBKBytes, nt * kBN);
+          if constexpr (KIND == Kind::kNvf4) {
+            uint8_t* ssfa = sb + kBBytes;
+            uint8_t* ssfb = ssfa + kSfaBytes;
+            tma_load_4d(ssfa, &tm_sfa, full + s, 0, 0, kb * 4, mt);
+            tma_load_4d(ssfb, &tm_sfb, full + s, 0, 0, kb * 4, nt * 2);
+          }
         }
       }
     }
@@ -150,130 +183,275 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc = KIND == Kind::kFp8 ? idesc_e4m3(kBM, kBN) : idesc_nvf4(kBM, kBN);
-      for (int kb = 0; kb < p.num_kb; ++kb) {
-        const int s = kb % kStages;
-        if (!mbar_wait(full + s, (kb / kStages) & 1, kWaitFull, abort_flag, p.watchdog)) break;
-        tc_fence_after();
-        const uint32_t sa = smem_u32(smem + s * kStageBytes);
-        const uint32_t sb = sa + kABytes;
-        if constexpr (KIND == Kind::kNvf4) {
-          const uint32_t ssfa = sb + kBBytes;
-          const uint32_t ssfb = ssfa + kSfaBytes;
+      uint32_t kbg = 0;
+      int i = 0;
+      for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x, ++i) {
+        const int b = i % kAcc;
+        if (i >= kAcc) {
+          if (!mbar_wait(acc_empty + b, ((i / kAcc) - 1) & 1, kWaitAccumFree, abort_flag, p.watchdog)) break;
+          tc_fence_after();
+        }
+        const uint32_t d_tmem = tmem + b * kBN;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
+          const int s = kbg % kStages;
+          if (!mbar_wait(full + s, (kbg / kStages) & 1, kWaitFull, abort_flag, p.watchdog)) break;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * kStageBytes);
+          const uint32_t sb = sa + kABytes;
+          if constexpr (KIND == Kind::kNvf4) {
+            const uint32_t ssfa = sb + kBBytes;
+            const uint32_t ssfb = ssfa + kSfaBytes;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              tmem_cp_32x128b_x4(tmem + kSfaCol + 4 * j, sf_desc(ssfa + 512 * j));
+              tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j, sf_desc(ssfb + 512 * j));
+              tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j + 4, sf_desc(ssfb + 2048 + 512 * j));
+            }
+          }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            tmem_cp_32x128b_x4(tmem + kSfaCol + 4 * j, sf_desc(ssfa + 512 * j));
-            tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j, sf_desc(ssfb + 512 * j));
-            tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j + 4, sf_desc(ssfb + 2048 + 512 * j));
+            const uint64_t adesc = sw128_desc(sa + 32 * j);
+            const uint64_t bdesc = sw128_desc(sb + 32 * j);
+            const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
+            if constexpr (KIND == Kind::kFp8) {
+              mma_f8f6f4(d_tmem, adesc, bdesc, idesc, acc);
+            } else {
+              mma_nvf4(d_tmem, adesc, bdesc, idesc, tmem + kSfaCol + 4 * j, tmem + kSfbCol + 8 * j, acc);
+            }
           }
+          tc_commit(empty + s);
         }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint64_t adesc = sw128_desc(sa + 32 * j);
-          const uint64_t bdesc = sw128_desc(sb + 32 * j);
-          const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
-          if constexpr (KIND == Kind::kFp8) {
-            mma_f8f6f4(tmem, adesc, bdesc, idesc, acc);
-          } else {
-            mma_nvf4(tmem, adesc, bdesc, idesc, tmem + kSfaCol + 4 * j, tmem + kSfbCol + 8 * j, acc);
-          }
-        }
-        tc_commit(empty + s);
+        tc_commit(acc_full + b);
       }
-      tc_commit(accum);
     }
-  } else {
+  } else if (warp < 6) {
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = m0 + q * 32 + lane;
-    const bool row_ok = row < p.m;
-    float w[C > 0 ? C : 1];
+    const float alpha = *p.alpha;
+    int i = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++i) {
+      int mt, nt;
+      tile_coords(t, p, mt, nt);
+      const int m0 = mt * kBM, n0 = nt * kBN;
+      const int row = m0 + q * 32 + lane;
+      const bool row_ok = row < p.m;
+      float w[C > 0 ? C : 1];
 #pragma unroll
-    for (int c = 0; c < C; ++c) w[c] = row_ok ? p.weights[static_cast<int64_t>(c) * p.m + row] : 0.f;
-    const bool ready = mbar_wait(accum, 0, kWaitAccum, abort_flag, p.watchdog);
-    tc_fence_after();
-    if (ready && *abort_flag == 0) {
-      const float alpha = *p.alpha;
-      bool nonfinite = false;
+      for (int c = 0; c < C; ++c) w[c] = row_ok ? p.weights[static_cast<int64_t>(c) * p.m + row] : 0.f;
+      const int b = i % kAcc;
+      const bool ready = mbar_wait(acc_full + b, (i / kAcc) & 1, kWaitAccum, abort_flag, p.watchdog);
+      const bool live = !named_barrier_or(1, 128, !ready || *abort_flag != 0);
+      tc_fence_after();
+      if (live) {
+        bool nonfinite = false;
 #pragma unroll 1
-      for (int chunk = 0; chunk < kChunks; ++chunk) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + chunk * 32, r);
-        tmem_ld_wait();
-        const int c0 = n0 + chunk * 32;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(alpha, __uint_as_float(r[j]));
-        if (C > 0 && p.fbit >= 0 && row == p.frow && p.fcol >= c0 && p.fcol < c0 + 32) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (c0 + j == p.fcol) v[j] = __uint_as_float(__float_as_uint(v[j]) ^ (1u << p.fbit));
+        for (int chunk = 0; chunk < kChunks; ++chunk) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + b * kBN + chunk * 32, r);
+          tmem_ld_wait();
+          if (chunk == kChunks - 1) {
+            // All of this warp's accumulator columns are in registers: hand
+            // the buffer back to the MMA warp before the remaining math.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + b);
           }
-          *p.hit = 1;
-        }
-        if (C > 0 && p.nonfinite != nullptr && row_ok) {
+          const int c0 = n0 + chunk * 32;
+          float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float out = BF16OUT ? bf16_bits_to_float(float_to_bf16_bits(v[j])) : v[j];
-            if (c0 + j < p.n && !isfinite(out)) nonfinite = true;
-          }
-        }
-        if constexpr (C > 0) {
-#pragma unroll
-          for (int c = 0; c < C; ++c) {
-            float x[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) x[j] = w[c] * v[j];
-            red[((chunk * 4 + q) * C + c) * 32 + lane] = transpose_reduce32(x, lane);
-          }
-        }
-        if (row_ok) {
-          if constexpr (BF16OUT) {
-            uint16_t* d = static_cast<uint16_t*>(p.d) + static_cast<int64_t>(row) * p.n;
-            if (c0 + 32 <= p.n && (p.n & 7) == 0) {
-              uint32_t packed[16];
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                packed[j] = static_cast<uint32_t>(float_to_bf16_bits(v[2 * j])) |
-                            (static_cast<uint32_t>(float_to_bf16_bits(v[2 * j + 1])) << 16);
-              }
-              uint4* dst = reinterpret_cast<uint4*>(d + c0);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                if (c0 + j < p.n) d[c0 + j] = float_to_bf16_bits(v[j]);
-              }
-            }
-          } else {
-            float* d = static_cast<float*>(p.d);
+          for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(alpha, __uint_as_float(r[j]));
+          if (C > 0 && p.fbit >= 0 && row == p.frow && p.fcol >= c0 && p.fcol < c0 + 32) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              if (c0 + j < p.n) d[static_cast<int64_t>(c0 + j) * p.m + row] = v[j];
+              if (c0 + j == p.fcol) v[j] = __uint_as_float(__float_as_uint(v[j]) ^ (1u << p.fbit));
+            }
+            *p.hit = 1;
+          }
+          if (C > 0 && p.nonfinite != nullptr && row_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float out = BF16OUT ? bf16_bits_to_float(float_to_bf16_bits(v[j])) : v[j];
+              if (c0 + j < p.n && !isfinite(out)) nonfinite = true;
+            }
+          }
+          if constexpr (C > 0) {
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+              float x[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) x[j] = w[c] * v[j];
+              red[((chunk * 4 + q) * C + c) * 32 + lane] = transpose_reduce32(x, lane);
+            }
+          }
+          if (row_ok) {
+            if constexpr (BF16OUT) {
+              uint16_t* d = static_cast<uint16_t*>(p.d) + static_cast<int64_t>(row) * p.n;
+              if (c0 + 32 <= p.n && (p.n & 7) == 0) {
+                uint32_t packed[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  packed[j] = static_cast<uint32_t>(float_to_bf16_bits(v[2 * j])) |
+                              (static_cast<uint32_t>(float_to_bf16_bits(v[2 * j + 1])) << 16);
+                }
+                uint4* dst = reinterpret_cast<uint4*>(d + c0);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  if (c0 + j < p.n) d[c0 + j] = float_to_bf16_bits(v[j]);
+                }
+              }
+            } else {
+              float* d = static_cast<float*>(p.d);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (c0 + j < p.n) d[static_cast<int64_t>(c0 + j) * p.m + row] = v[j];
+              }
+            }
+          }
+        }
+        if (nonfinite) atomicExch(p.nonfinite, 1);
+      }
+      if constexpr (C > 0) {
+        named_barrier(1, 128);
+        if (live) {
+          const int e = threadIdx.x - 64;
+          for (int idx = e; idx < kChunks * C * 32; idx += 128) {
+            const int chunk = idx / (C * 32);
+            const int rem = idx - chunk * C * 32;
+            const int c = rem >> 5;
+            const int col = rem & 31;
+            float sum = 0.f;
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) sum += red[((chunk * 4 + qq) * C + c) * 32 + col];
+            const int gcol = n0 + chunk * 32 + col;
+            if (gcol < p.padded_n) {
+              p.observed[(static_cast<int64_t>(c) * p.tiles_m + mt) * p.padded_n + gcol] = sum;
+            }
+          }
+        }
+        named_barrier(1, 128);
+      }
+      if (!live) break;
+    }
+  } else if constexpr (CHK) {
+    // ---------------- input-side prediction (warps 6..9) ----------------
+    constexpr int kSlicesPerKb = KIND == Kind::kFp8 ? 2 : 4;
+    const int ct = threadIdx.x - 192;  // 0..127: rows ct and ct + 128 of the B tile
+    const float alpha = *p.alpha;
+    uint32_t kbg = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      int mt, nt;
+      tile_coords(t, p, mt, nt);
+      float acc[2][C][2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c = 0; c < C; ++c) acc[h][c][0] = acc[h][c][1] = 0.f;
+      bool live = true;
+      for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
+        const int s = kbg % kStages;
+        const bool ok = mbar_wait(full + s, (kbg / kStages) & 1, kWaitFull, abort_flag, p.watchdog);
+        uint32_t mask = 0;
+#pragma unroll
+        for (int j = 0; j < kSlicesPerKb; ++j) {
+          const int sl = kb * kSlicesPerKb + j;
+          if (sl * kSliceK < p.k && sl % p.tiles_m == mt) mask |= 1u << j;
+        }
+        uint4 raw[2][8];
+        uint32_t sfw[2][4];
+        if (mask && ok) {
+          const uint8_t* sb = smem + s * kStageBytes + kABytes;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int r = ct + 128 * h;
+            const uint8_t* row_base = sb + r * kBKBytes;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              raw[h][j] = *reinterpret_cast<const uint4*>(row_base + ((j ^ (r & 7)) << 4));
+            }
+            if constexpr (KIND == Kind::kNvf4) {
+              const uint8_t* ssfb = sb + kBBytes + kSfaBytes;
+              const int rr = r & 127;
+#pragma unroll
+              for (int g = 0; g < 4; ++g) {
+                sfw[h][g] = *reinterpret_cast<const uint32_t*>(ssfb + (r >> 7) * 2048 + g * 512 + (rr & 31) * 16 +
+                                                               ((rr >> 5) & 3) * 4);
+              }
+            }
+          }
+        }
+        // Uniform decision: every checksum thread has copied its rows (or the
+        // wait failed somewhere); only then is the stage handed back.
+        if (named_barrier_or(2, 128, !ok || *abort_flag != 0)) {
+          live = false;
+          break;
+        }
+        if (ct == 0) mbar_arrive(empty + s);
+        if (!mask) continue;
+#pragma unroll
+        for (int j = 0; j < kSlicesPerKb; ++j) {
+          if (!(mask & (1u << j))) continue;
+          const int k0 = (kb * kSlicesPerKb + j) * kSliceK;
+          constexpr int kChunksPerSlice = KIND == Kind::kFp8 ? 4 : 2;  // 16-byte chunks
+          constexpr int kElemsPerChunk = KIND == Kind::kFp8 ? 16 : 32;
+#pragma unroll
+          for (int ch = 0; ch < kChunksPerSlice; ++ch) {
+#pragma unroll
+            for (int e = 0; e < kElemsPerChunk; ++e) {
+              const int kg = k0 + ch * kElemsPerChunk + e;
+              float qv[C][2];
+              if (kg < p.k) {
+                const float* qk = p.q_full + static_cast<int64_t>(kg) * C * 2;
+                if constexpr (C == 2) {
+                  const float4 f = __ldg(reinterpret_cast<const float4*>(qk));
+                  qv[0][0] = f.x; qv[0][1] = f.y; qv[1][0] = f.z; qv[1][1] = f.w;
+                } else {
+                  const float2 f = __ldg(reinterpret_cast<const float2*>(qk));
+                  qv[0][0] = f.x; qv[0][1] = f.y;
+                }
+              } else {
+#pragma unroll
+                for (int c = 0; c < C; ++c) qv[c][0] = qv[c][1] = 0.f;
+              }
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint4 chunk = raw[h][j * kChunksPerSlice + ch];
+                float value;
+                if constexpr (KIND == Kind::kFp8) {
+                  const uint32_t word = e < 4 ? chunk.x : e < 8 ? chunk.y : e < 12 ? chunk.z : chunk.w;
+                  value = decode_e4m3((word >> (8 * (e & 3))) & 0xFFu);
+                } else {
+                  const uint32_t word = e < 8 ? chunk.x : e < 16 ? chunk.y : e < 24 ? chunk.z : chunk.w;
+                  const uint32_t nib = (word >> (4 * (e & 7))) & 0xFu;
+                  const int blk = (ch * kElemsPerChunk + e) >> 4;  // 16-element block within the slice
+                  value = decode_e2m1(nib) * decode_e4m3((sfw[h][j] >> (8 * blk)) & 0xFFu);
+                }
+                const float av = fabsf(value);
+#pragma unroll
+                for (int c = 0; c < C; ++c) {
+                  acc[h][c][0] = fmaf(qv[c][0], value, acc[h][c][0]);
+                  acc[h][c][1] = fmaf(qv[c][1], av, acc[h][c][1]);
+                }
+              }
             }
           }
         }
       }
-      if (nonfinite) atomicExch(p.nonfinite, 1);
-    }
-    tc_fence_before();
-    if constexpr (C > 0) {
-      named_barrier(1, 128);
-      if (ready && *abort_flag == 0) {
-        const int e = threadIdx.x - 64;
-        for (int idx = e; idx < kChunks * C * 32; idx += 128) {
-          const int chunk = idx / (C * 32);
-          const int rem = idx - chunk * C * 32;
-          const int c = rem >> 5;
-          const int col = rem & 31;
-          float sum = 0.f;
+      if (!live) break;
 #pragma unroll
-          for (int qq = 0; qq < 4; ++qq) sum += red[((chunk * 4 + qq) * C + c) * 32 + col];
-          const int gcol = n0 + chunk * 32 + col;
-          if (gcol < p.padded_n) {
-            p.observed[(static_cast<int64_t>(c) * p.tiles_m + mt) * p.padded_n + gcol] = sum;
+      for (int h = 0; h < 2; ++h) {
+        const int col = nt * kBN + ct + 128 * h;
+        if (col < p.padded_n) {
+          const bool in = col < p.n;
+#pragma unroll
+          for (int c = 0; c < C; ++c) {
+            const int64_t off = (static_cast<int64_t>(c) * p.tiles_m + mt) * p.padded_n + col;
+            p.predicted[off] = alpha * (in ? acc[h][c][0] : 0.f);
+            p.magnitude[off] = fabsf(alpha) * (in ? acc[h][c][1] : 0.f);
           }
         }
       }
@@ -288,7 +466,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <Kind KIND, int C, bool BF16OUT>
+int sm_count() {
+  static int cached[64] = {};
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return 148;
+  if (cached[device] == 0) {
+    int count = 0;
+    if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 148;
+    cached[device] = count;
+  }
+  return cached[device];
+}
+
+template <Kind KIND, int C, bool BF16OUT, bool CHK>
 int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   const int64_t k_bytes = KIND == Kind::kFp8 ? g.k : g.k / 2;
   CUtensorMap ta{}, tb{}, tsa{}, tsb{};
@@ -333,7 +523,11 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   Params p{};
   p.m = static_cast<int32_t>(g.m);
   p.n = static_cast<int32_t>(g.n);
+  p.k = static_cast<int32_t>(g.k);
   p.num_kb = static_cast<int32_t>(ceil_div(k_bytes, kBKBytes));
+  p.tiles_m = static_cast<int32_t>(ceil_div(g.m, kBM));
+  p.tiles_n = static_cast<int32_t>(ceil_div(g.n, kBN));
+  p.num_tiles = p.tiles_m * p.tiles_n;
   p.alpha = g.alpha;
   p.d = g.d;
   p.weights = g.weights;
@@ -344,16 +538,38 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   p.observed = g.observed;
   p.hit = g.hit;
   p.padded_n = static_cast<int32_t>(g.padded_n);
-  p.tiles_m = static_cast<int32_t>(ceil_div(g.m, kBM));
+  p.q_full = g.q_full;
+  p.predicted = g.predicted;
+  p.magnitude = g.magnitude;
   p.watchdog = watchdog_ptr();
   if (p.watchdog == nullptr) return fail(SDC_ERR_CUDA, "watchdog symbol unavailable");
-  auto kernel = gemm_kernel<KIND, C, BF16OUT>;
+  auto kernel = gemm_kernel<KIND, C, BF16OUT, CHK>;
   constexpr int smem = smem_bytes(KIND);
-  SDC_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  const dim3 grid(static_cast<unsigned>(ceil_div(g.n, kBN)), static_cast<unsigned>(ceil_div(g.m, kBM)));
-  kernel<<<grid, kThreads, smem, stream>>>(ta, tb, tsa, tsb, p);
+  static bool configured[64] = {};
+  int device = 0;
+  SDC_CUDA_CHECK(cudaGetDevice(&device));
+  if (device < 0 || device >= 64 || !configured[device]) {
+    SDC_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    if (device >= 0 && device < 64) configured[device] = true;
+  }
+  const int grid = std::min(p.num_tiles, sm_count());
+  kernel<<<grid, num_threads(CHK), smem, stream>>>(ta, tb, tsa, tsb, p);
   SDC_CUDA_CHECK(cudaGetLastError());
   return SDC_OK;
+}
+
+template <Kind KIND, int C>
+int dispatch_out(const GemmProblem& g, cudaStream_t stream) {
+  const bool chk = g.q_full != nullptr;
+  if constexpr (C == 0) {
+    return g.out_bf16_rowmajor ? launch_impl<KIND, 0, true, false>(g, stream)
+                               : launch_impl<KIND, 0, false, false>(g, stream);
+  } else {
+    if (g.out_bf16_rowmajor) {
+      return chk ? launch_impl<KIND, C, true, true>(g, stream) : launch_impl<KIND, C, true, false>(g, stream);
+    }
+    return chk ? launch_impl<KIND, C, false, true>(g, stream) : launch_impl<KIND, C, false, false>(g, stream);
+  }
 }
 
 }  // namespace
@@ -365,18 +581,14 @@ int launch_gemm(const GemmProblem& g, cudaStream_t stream) {
     SDC_CUDA_CHECK(cudaMemsetAsync(g.hit, 0, sizeof(int32_t), stream));
     if (g.nonfinite != nullptr) SDC_CUDA_CHECK(cudaMemsetAsync(g.nonfinite, 0, sizeof(int32_t), stream));
   }
-  const bool bf16 = g.out_bf16_rowmajor;
-#define SDC_DISPATCH(KIND, C)                                                   \
-  return bf16 ? launch_impl<KIND, C, true>(g, stream) : launch_impl<KIND, C, false>(g, stream)
   if (g.kind == Kind::kFp8) {
-    if (g.channels == 0) SDC_DISPATCH(Kind::kFp8, 0);
-    if (g.channels == 1) SDC_DISPATCH(Kind::kFp8, 1);
-    SDC_DISPATCH(Kind::kFp8, 2);
+    if (g.channels == 0) return dispatch_out<Kind::kFp8, 0>(g, stream);
+    if (g.channels == 1) return dispatch_out<Kind::kFp8, 1>(g, stream);
+    return dispatch_out<Kind::kFp8, 2>(g, stream);
   }
-  if (g.channels == 0) SDC_DISPATCH(Kind::kNvf4, 0);
-  if (g.channels == 1) SDC_DISPATCH(Kind::kNvf4, 1);
-  SDC_DISPATCH(Kind::kNvf4, 2);
-#undef SDC_DISPATCH
+  if (g.channels == 0) return dispatch_out<Kind::kNvf4, 0>(g, stream);
+  if (g.channels == 1) return dispatch_out<Kind::kNvf4, 1>(g, stream);
+  return dispatch_out<Kind::kNvf4, 2>(g, stream);
 }
 
 }  // namespace sdc

@@ -25,6 +25,10 @@ struct GemmProblem {
   float* observed;         // [C, Tm, Np]
   int32_t* hit;
   int64_t padded_n;
+  // K-slice input prediction fused into the GEMM (all null: not fused).
+  const float* q_full;     // [K][C][2], from launch_projection
+  float* predicted;        // [C, Tm, Np]
+  float* magnitude;
 };
 
 // Launches the GEMM (and its fused epilogue) on `stream`. Zeroes hit/nonfinite
@@ -51,6 +55,13 @@ struct ReferenceProblem {
 };
 
 size_t reference_workspace_bytes(int channels, int64_t m, int64_t n, int64_t k, int layout);
-int launch_reference(const ReferenceProblem& p, cudaStream_t stream);
+// Per-tile projections q[c][h][t][k] of A (and, for the K-slice layout, their
+// ascending-tile sum q_full[k][c][h] at the end of the workspace). Must run
+// before the GEMM when the prediction is fused into it.
+int launch_projection(const ReferenceProblem& p, cudaStream_t stream);
+// TILE layout: per-tile propagation against B on CUDA cores (after projection).
+int launch_tile_propagate(const ReferenceProblem& p, cudaStream_t stream);
+// Device pointer of q_full inside the workspace of a K-slice problem.
+const float* kslice_q_full(const ReferenceProblem& p);
 
 }  // namespace sdc

@@ -1,6 +1,7 @@
 // Host-side status plumbing, device checks and TMA descriptor encoding.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 #include <string>
@@ -42,9 +43,18 @@ int cuda_fail(cudaError_t error, const char* what) {
 }
 
 int check_current_device() {
+  // Cached per device: cudaGetDeviceProperties costs milliseconds, which
+  // would dominate every launch; the attribute query is cheap.
+  constexpr int kMaxDevices = 64;
+  static std::atomic<int> verified[kMaxDevices] = {};
   int device = 0;
   SDC_CUDA_CHECK(cudaGetDevice(&device));
-  return sdc_device_check(device);
+  if (device >= 0 && device < kMaxDevices && verified[device].load(std::memory_order_relaxed) == 1) {
+    return SDC_OK;
+  }
+  int rc = sdc_device_check(device);
+  if (rc == SDC_OK && device >= 0 && device < kMaxDevices) verified[device].store(1, std::memory_order_relaxed);
+  return rc;
 }
 
 namespace {
@@ -94,13 +104,14 @@ extern "C" {
 const char* sdc_last_error(void) { return sdc::t_last_error.c_str(); }
 
 int sdc_device_check(int device) {
-  cudaDeviceProp prop{};
-  cudaError_t e = cudaGetDeviceProperties(&prop, device);
-  if (e != cudaSuccess) return sdc::cuda_fail(e, "cudaGetDeviceProperties");
-  if (prop.major != 10 || prop.minor != 0) {
+  int major = 0, minor = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+  if (e != cudaSuccess) return sdc::cuda_fail(e, "cudaDeviceGetAttribute");
+  if (major != 10 || minor != 0) {
     return sdc::fail(SDC_ERR_UNSUPPORTED_DEVICE,
                      "sdc_b200 kernels are built for sm_100a (B200); device is sm_" +
-                         std::to_string(prop.major) + std::to_string(prop.minor));
+                         std::to_string(major) + std::to_string(minor));
   }
   return SDC_OK;
 }

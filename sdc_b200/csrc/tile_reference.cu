@@ -13,10 +13,13 @@
 // layout is the parity path, not the fast path.
 //
 // KSLICE layout (fast path). q is summed over all M-tiles (ascending tile
-// order) and K-block kb (128 K) contributes to slot kb % Tm:
-//   predicted[c, t, n] = alpha * sum_{kb % Tm == t} sum_{k in kb} q_c[k] B[n,k]
-// The per-column sum over slots equals the TILE layout's sum over tiles up to
-// fp32 rounding, so finalize is unchanged, at ~1/M of the GEMM's work.
+// order) and the 64-wide K slice s contributes to slot s % Tm:
+//   predicted[c, t, n] = alpha * sum_{s % Tm == t} sum_{k in s} q_c[k] B[n,k]
+// (fma chain over slices, then k, ascending). The propagation runs inside the
+// GEMM (gemm.cu, checksum warps) on the B tiles already in shared memory;
+// this file only produces q. The per-column sum over slots equals the TILE
+// layout's sum over tiles up to fp32 rounding, so finalize is unchanged, at
+// ~1/M of the GEMM's work.
 #include <algorithm>
 
 #include "gemm.cuh"
@@ -28,7 +31,6 @@ constexpr int kTileRows = 128;
 constexpr int kRefThreads = 128;
 constexpr int kTilesPerBlock = 8;
 constexpr int kChunkK = 64;
-constexpr int kSliceK = 128;
 
 __device__ __forceinline__ int64_t sf_off(int64_t row, int64_t block, int64_t k_atoms) {
   return ((row >> 7) * k_atoms + (block >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4 +
@@ -50,31 +52,54 @@ __device__ __forceinline__ float operand_value(const uint8_t* x, const uint8_t* 
 }
 
 // q[(c*2 + h) * Tm * K + t * K + k]: h = 0 signed projection, h = 1 magnitude.
+// Each thread owns 8 consecutive k of one tile and walks the tile's rows in
+// ascending order (the reference's fma order), so a warp reads 256 contiguous
+// bytes (FP8) or 128 bytes (NVFP4) of each row.
 template <Kind KIND, int C>
 __global__ void __launch_bounds__(kRefThreads)
     q_encode(const uint8_t* a, const uint8_t* sfa, int64_t m, int64_t k, const float* weights,
              float* q, int64_t tiles_m) {
-  const int64_t kk = static_cast<int64_t>(blockIdx.x) * kRefThreads + threadIdx.x;
+  const int64_t k0 = (static_cast<int64_t>(blockIdx.x) * kRefThreads + threadIdx.x) * 8;
   const int64_t t = blockIdx.y;
-  if (kk >= k) return;
-  float enc[C], mag[C];
+  if (k0 >= k) return;
+  float enc[C][8], mag[C][8];
 #pragma unroll
-  for (int c = 0; c < C; ++c) enc[c] = mag[c] = 0.f;
+  for (int c = 0; c < C; ++c)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) enc[c][e] = mag[c][e] = 0.f;
   const int64_t rows = std::min<int64_t>(kTileRows, m - t * kTileRows);
+  const int64_t k_atoms = (k + 63) / 64;
   for (int64_t r = 0; r < rows; ++r) {
     const int64_t row = t * kTileRows + r;
-    const float v = operand_value<KIND>(a, sfa, row, kk, k);
+    float v[8];
+    if constexpr (KIND == Kind::kFp8) {
+      const uint2 u = __ldg(reinterpret_cast<const uint2*>(a + row * k + k0));
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = decode_e4m3(((e < 4 ? u.x : u.y) >> (8 * (e & 3))) & 0xFFu);
+    } else {
+      const uint32_t u = __ldg(reinterpret_cast<const uint32_t*>(a + row * (k / 2) + k0 / 2));
+      const float scale = decode_e4m3(sfa[sf_off(row, k0 >> 4, k_atoms)]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = decode_e2m1((u >> (4 * e)) & 15u) * scale;
+    }
 #pragma unroll
     for (int c = 0; c < C; ++c) {
       const float w = __ldg(weights + c * m + row);
-      enc[c] = fmaf(w, v, enc[c]);
-      mag[c] = fmaf(fabsf(w), fabsf(v), mag[c]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        enc[c][e] = fmaf(w, v[e], enc[c][e]);
+        mag[c][e] = fmaf(fabsf(w), fabsf(v[e]), mag[c][e]);
+      }
     }
   }
 #pragma unroll
   for (int c = 0; c < C; ++c) {
-    q[((c * 2 + 0) * tiles_m + t) * k + kk] = enc[c];
-    q[((c * 2 + 1) * tiles_m + t) * k + kk] = mag[c];
+    float4* pe = reinterpret_cast<float4*>(q + ((c * 2 + 0) * tiles_m + t) * k + k0);
+    float4* pm = reinterpret_cast<float4*>(q + ((c * 2 + 1) * tiles_m + t) * k + k0);
+    pe[0] = make_float4(enc[c][0], enc[c][1], enc[c][2], enc[c][3]);
+    pe[1] = make_float4(enc[c][4], enc[c][5], enc[c][6], enc[c][7]);
+    pm[0] = make_float4(mag[c][0], mag[c][1], mag[c][2], mag[c][3]);
+    pm[1] = make_float4(mag[c][4], mag[c][5], mag[c][6], mag[c][7]);
   }
 }
 
@@ -144,7 +169,9 @@ __global__ void __launch_bounds__(kRefThreads)
     if (col < n) {
       float v[kChunkK];
       load_b_chunk<KIND>(b, sfb, col, k0, k, kc, v);
-      for (int kk = 0; kk < kc; ++kk) {
+#pragma unroll
+      for (int kk = 0; kk < kChunkK; ++kk) {
+        if (kk >= kc) break;
         const float value = v[kk];
         const float av = fabsf(value);
 #pragma unroll
@@ -176,99 +203,55 @@ __global__ void __launch_bounds__(kRefThreads)
   }
 }
 
-// q_full[(c*2 + h) * K + k] = sum over tiles (ascending) of q[(c*2+h), t, k].
-__global__ void reduce_tiles(const float* q, int64_t planes, int64_t tiles_m, int64_t k, float* q_full) {
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= planes * k) return;
-  const int64_t plane = idx / k, kk = idx - plane * k;
-  float s = 0.f;
-  for (int64_t t = 0; t < tiles_m; ++t) s = __fadd_rn(s, q[(plane * tiles_m + t) * k + kk]);
-  q_full[idx] = s;
-}
-
-template <Kind KIND, int C>
-__global__ void __launch_bounds__(kRefThreads)
-    propagate_slots(const uint8_t* b, const uint8_t* sfb, int64_t n, int64_t k, const float* q_full,
-                    int64_t tiles_m, const float* alpha_ptr, float* pred, float* mag, int64_t padded_n) {
-  __shared__ float qs[C][2][kSliceK];
-  const int64_t col = static_cast<int64_t>(blockIdx.x) * kRefThreads + threadIdx.x;
-  const int64_t slot = blockIdx.y;
-  const int64_t k_blocks = (k + kSliceK - 1) / kSliceK;
-  float r[C], a[C];
+// q_full[(k * C + c) * 2 + h] = sum over tiles (ascending) of q[(c*2+h), t, k].
+template <int C>
+__global__ void reduce_tiles(const float* q, int64_t tiles_m, int64_t k, float* q_full) {
+  const int64_t kk = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (kk >= k) return;
+  float s[C * 2];
 #pragma unroll
-  for (int c = 0; c < C; ++c) r[c] = a[c] = 0.f;
-  for (int64_t kb = slot; kb < k_blocks; kb += tiles_m) {
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < C * 2 * kSliceK; idx += kRefThreads) {
-      const int kk = idx % kSliceK;
-      const int plane = idx / kSliceK;
-      const int64_t kg = kb * kSliceK + kk;
-      (&qs[0][0][0])[idx] = kg < k ? q_full[plane * k + kg] : 0.f;
-    }
-    __syncthreads();
-    if (col < n) {
-      for (int half = 0; half < kSliceK / kChunkK; ++half) {
-        const int64_t k0 = kb * kSliceK + half * kChunkK;
-        if (k0 >= k) break;
-        const int kc = static_cast<int>(std::min<int64_t>(kChunkK, k - k0));
-        float v[kChunkK];
-        load_b_chunk<KIND>(b, sfb, col, k0, k, kc, v);
-        for (int kk = 0; kk < kc; ++kk) {
-#pragma unroll
-          for (int c = 0; c < C; ++c) {
-            r[c] = fmaf(qs[c][0][half * kChunkK + kk], v[kk], r[c]);
-            a[c] = fmaf(qs[c][1][half * kChunkK + kk], fabsf(v[kk]), a[c]);
-          }
-        }
-      }
-    }
+  for (int plane = 0; plane < C * 2; ++plane) {
+    float acc = 0.f;
+    for (int64_t t = 0; t < tiles_m; ++t) acc = __fadd_rn(acc, q[(plane * tiles_m + t) * k + kk]);
+    s[plane] = acc;
   }
-  if (col < padded_n) {
-    const float alpha = *alpha_ptr;
-#pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const int64_t off = (c * tiles_m + slot) * padded_n + col;
-      pred[off] = alpha * r[c];
-      mag[off] = fabsf(alpha) * a[c];
-    }
+  if constexpr (C == 2) {
+    reinterpret_cast<float4*>(q_full)[kk] = make_float4(s[0], s[1], s[2], s[3]);
+  } else {
+    reinterpret_cast<float2*>(q_full)[kk] = make_float2(s[0], s[1]);
   }
 }
 
+int64_t q_floats(int channels, int64_t m, int64_t k) { return static_cast<int64_t>(channels) * 2 * ceil_div(m, kTileRows) * k; }
+
 template <Kind KIND, int C>
-int launch_ref_impl(const ReferenceProblem& p, cudaStream_t stream) {
+int projection_impl(const ReferenceProblem& p, cudaStream_t stream) {
   const int64_t tiles_m = ceil_div(p.m, kTileRows);
   float* q = static_cast<float*>(p.workspace);
-  q_encode<KIND, C><<<dim3(static_cast<unsigned>(ceil_div(p.k, kRefThreads)), static_cast<unsigned>(tiles_m)),
+  q_encode<KIND, C><<<dim3(static_cast<unsigned>(ceil_div(p.k, kRefThreads * 8)), static_cast<unsigned>(tiles_m)),
                       kRefThreads, 0, stream>>>(p.a, p.sfa, p.m, p.k, p.weights, q, tiles_m);
   SDC_CUDA_CHECK(cudaGetLastError());
-  const unsigned col_blocks = static_cast<unsigned>(ceil_div(p.padded_n, kRefThreads));
-  if (p.layout == SDC_LAYOUT_TILE) {
-    propagate_tiles<KIND, C><<<dim3(col_blocks, static_cast<unsigned>(ceil_div(tiles_m, kTilesPerBlock))),
-                               kRefThreads, 0, stream>>>(p.b, p.sfb, p.n, p.k, q, tiles_m, p.alpha,
-                                                         p.predicted, p.magnitude, p.padded_n);
-  } else {
-    float* q_full = q + C * 2 * tiles_m * p.k;
-    const int64_t total = C * 2 * p.k;
-    reduce_tiles<<<static_cast<unsigned>(ceil_div(total, 256)), 256, 0, stream>>>(q, C * 2, tiles_m, p.k, q_full);
+  if (p.layout == SDC_LAYOUT_KSLICE) {
+    float* q_full = q + q_floats(C, p.m, p.k);
+    reduce_tiles<C><<<static_cast<unsigned>(ceil_div(p.k, 256)), 256, 0, stream>>>(q, tiles_m, p.k, q_full);
     SDC_CUDA_CHECK(cudaGetLastError());
-    propagate_slots<KIND, C><<<dim3(col_blocks, static_cast<unsigned>(tiles_m)), kRefThreads, 0, stream>>>(
-        p.b, p.sfb, p.n, p.k, q_full, tiles_m, p.alpha, p.predicted, p.magnitude, p.padded_n);
   }
+  return SDC_OK;
+}
+
+template <Kind KIND, int C>
+int tile_propagate_impl(const ReferenceProblem& p, cudaStream_t stream) {
+  const int64_t tiles_m = ceil_div(p.m, kTileRows);
+  const float* q = static_cast<const float*>(p.workspace);
+  const unsigned col_blocks = static_cast<unsigned>(ceil_div(p.padded_n, kRefThreads));
+  propagate_tiles<KIND, C><<<dim3(col_blocks, static_cast<unsigned>(ceil_div(tiles_m, kTilesPerBlock))),
+                             kRefThreads, 0, stream>>>(p.b, p.sfb, p.n, p.k, q, tiles_m, p.alpha, p.predicted,
+                                                       p.magnitude, p.padded_n);
   SDC_CUDA_CHECK(cudaGetLastError());
   return SDC_OK;
 }
 
-}  // namespace
-
-size_t reference_workspace_bytes(int channels, int64_t m, int64_t n, int64_t k, int layout) {
-  (void)n;
-  const int64_t tiles_m = ceil_div(m, kTileRows);
-  int64_t floats = static_cast<int64_t>(channels) * 2 * tiles_m * k;
-  if (layout == SDC_LAYOUT_KSLICE) floats += static_cast<int64_t>(channels) * 2 * k;
-  return static_cast<size_t>(floats) * sizeof(float);
-}
-
-int launch_reference(const ReferenceProblem& p, cudaStream_t stream) {
+int check_problem(const ReferenceProblem& p) {
   if (p.layout != SDC_LAYOUT_TILE && p.layout != SDC_LAYOUT_KSLICE) {
     return fail(SDC_ERR_INVALID, "unknown ABFT reference layout");
   }
@@ -276,10 +259,43 @@ int launch_reference(const ReferenceProblem& p, cudaStream_t stream) {
   if (p.workspace == nullptr || p.workspace_bytes < need) {
     return fail(SDC_ERR_WORKSPACE, "ABFT reference workspace too small");
   }
-  if (p.kind == Kind::kFp8) {
-    return p.channels == 2 ? launch_ref_impl<Kind::kFp8, 2>(p, stream) : launch_ref_impl<Kind::kFp8, 1>(p, stream);
+  if (reinterpret_cast<uintptr_t>(p.workspace) % 16 != 0) {
+    return fail(SDC_ERR_WORKSPACE, "ABFT reference workspace must be 16-byte aligned");
   }
-  return p.channels == 2 ? launch_ref_impl<Kind::kNvf4, 2>(p, stream) : launch_ref_impl<Kind::kNvf4, 1>(p, stream);
+  return SDC_OK;
+}
+
+}  // namespace
+
+size_t reference_workspace_bytes(int channels, int64_t m, int64_t n, int64_t k, int layout) {
+  (void)n;
+  int64_t floats = q_floats(channels, m, k);
+  if (layout == SDC_LAYOUT_KSLICE) floats += static_cast<int64_t>(channels) * 2 * k;
+  return static_cast<size_t>(floats) * sizeof(float);
+}
+
+const float* kslice_q_full(const ReferenceProblem& p) {
+  return static_cast<const float*>(p.workspace) + q_floats(p.channels, p.m, p.k);
+}
+
+int launch_projection(const ReferenceProblem& p, cudaStream_t stream) {
+  int rc = check_problem(p);
+  if (rc != SDC_OK) return rc;
+  if (p.kind == Kind::kFp8) {
+    return p.channels == 2 ? projection_impl<Kind::kFp8, 2>(p, stream) : projection_impl<Kind::kFp8, 1>(p, stream);
+  }
+  return p.channels == 2 ? projection_impl<Kind::kNvf4, 2>(p, stream) : projection_impl<Kind::kNvf4, 1>(p, stream);
+}
+
+int launch_tile_propagate(const ReferenceProblem& p, cudaStream_t stream) {
+  int rc = check_problem(p);
+  if (rc != SDC_OK) return rc;
+  if (p.kind == Kind::kFp8) {
+    return p.channels == 2 ? tile_propagate_impl<Kind::kFp8, 2>(p, stream)
+                           : tile_propagate_impl<Kind::kFp8, 1>(p, stream);
+  }
+  return p.channels == 2 ? tile_propagate_impl<Kind::kNvf4, 2>(p, stream)
+                         : tile_propagate_impl<Kind::kNvf4, 1>(p, stream);
 }
 
 }  // namespace sdc
