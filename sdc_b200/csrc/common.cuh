@@ -353,6 +353,39 @@ __device__ __forceinline__ uint32_t cvt_e2m1x8(const float (&v)[8]) {
   return out;
 }
 
+// Exact widening decodes through the hardware conversions (e4m3 and e2m1
+// values are all representable in fp16): element 0 in .x.
+__device__ __forceinline__ float2 e4m3x2_to_float2(uint32_t two_bytes) {
+  uint32_t h2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(static_cast<uint16_t>(two_bytes)));
+  float2 out;
+  asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "cvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
+      : "=f"(out.x), "=f"(out.y)
+      : "r"(h2));
+  return out;
+}
+
+// Eight e2m1 codes of a 32-bit word (low nibble first) to fp32.
+__device__ __forceinline__ void e2m1x8_to_float(uint32_t word, float (&v)[8]) {
+  uint32_t h[4];
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(word));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+        "cvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
+        : "=f"(v[2 * i]), "=f"(v[2 * i + 1])
+        : "r"(h[i]));
+  }
+}
+
 __device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
   return __uint_as_float(static_cast<uint32_t>(b) << 16);
 }

@@ -15,7 +15,7 @@
 namespace sdc {
 namespace {
 
-constexpr int kFinalizeThreads = 256;
+constexpr int kFinalizeThreads = 64;  // small blocks: one thread per (channel, column)
 constexpr unsigned kDetected = 1u;
 constexpr unsigned kNonfinite = 2u;
 constexpr unsigned kHit = 4u;
@@ -63,18 +63,25 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_columns(FinalizePar
   if (col < p.n) {
     const int64_t base = static_cast<int64_t>(channel) * p.m_tiles * p.padded_n + col;
     float observed = 0.f, predicted = 0.f, magnitude = 0.f;
-    if (p.use_reference) {
-#pragma unroll 8
-      for (int64_t t = 0; t < p.m_tiles; ++t) {
-        observed = __fadd_rn(observed, p.observed[base + t * p.padded_n]);
+    // Loads of 8 tiles are issued before their (ordered) adds.
+    constexpr int kBatch = 8;
+    for (int64_t t0 = 0; t0 < p.m_tiles; t0 += kBatch) {
+      float o[kBatch], pr[kBatch], mg[kBatch];
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        const bool in = t0 + i < p.m_tiles;
+        const int64_t off = base + (t0 + i) * p.padded_n;
+        o[i] = in ? __ldg(p.observed + off) : 0.f;
+        pr[i] = (in && !p.use_reference) ? __ldg(p.predicted + off) : 0.f;
+        mg[i] = (in && !p.use_reference) ? __ldg(p.magnitude + off) : 0.f;
       }
-    } else {
-#pragma unroll 8
-      for (int64_t t = 0; t < p.m_tiles; ++t) {
-        const int64_t off = base + t * p.padded_n;
-        observed = __fadd_rn(observed, p.observed[off]);
-        predicted = __fadd_rn(predicted, p.predicted[off]);
-        magnitude = __fadd_rn(magnitude, p.magnitude[off]);
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        if (t0 + i < p.m_tiles) {
+          observed = __fadd_rn(observed, o[i]);
+          predicted = __fadd_rn(predicted, pr[i]);
+          magnitude = __fadd_rn(magnitude, mg[i]);
+        }
       }
     }
     const int64_t out = static_cast<int64_t>(channel) * p.n + col;

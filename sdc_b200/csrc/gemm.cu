@@ -16,12 +16,13 @@
 //               sum_rows w_c[row] * v (butterfly transpose-reduce across
 //               lanes, fixed-order sum across the four row quarters),
 //               non-finite check of the converted output, output store.
-//   warps 6-9   (K-slice layout only) input-side prediction from the B stage
-//               already in shared memory: for the 64-wide K slices assigned to
-//               this tile's slot (slice % Tm == tile row), fma chains of the
-//               full-M projection q_c[k] (precomputed, tile_reference.cu) with
-//               B[n, k] and |q|, |B|. The stage is released once the slice is
-//               copied to registers, so B is never read from HBM twice.
+//   warps 6-9   (K-slice layout only) input-side prediction, independent of
+//               the MMA pipeline: for the 64-wide K slices assigned to this
+//               tile's slot (slice % Tm == tile row), fma chains of the full-M
+//               projection q_c[k] (precomputed, tile_reference.cu) with
+//               B[n, k] and |q|, |B|. The slices are read from global memory,
+//               where the tile's column block is L2-hot; in total this is one
+//               extra L2 pass over B.
 // Epilogue semantics follow src/cutlass_gemm/csrc/abft/common/
 // sm120_epilogue.cuh:52-151 of the reference (inject after alpha, observe
 // before the output cast). Every wait is bounded (common.cuh).
@@ -69,6 +70,8 @@ struct Params {
   int32_t* hit;
   int32_t padded_n;
   const float* q_full;  // [K][C][2]: full-M projection (h=0) and magnitude (h=1)
+  const uint8_t* b;     // B operand rows (prediction warps read them directly)
+  const uint8_t* sfb;
   float* predicted;
   float* magnitude;
   int32_t* watchdog;
@@ -126,7 +129,7 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(full + s, 1);
-      mbar_init(empty + s, CHK ? 2 : 1);
+      mbar_init(empty + s, 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full + b, 1);
@@ -156,13 +159,15 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       uint32_t kbg = 0;
-      for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
+      bool stop = false;
+      for (int t = blockIdx.x; t < p.num_tiles && !stop; t += gridDim.x) {
         int mt, nt;
         tile_coords(t, p, mt, nt);
         for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
           const int s = kbg % kStages;
           if (kbg >= kStages &&
               !mbar_wait(empty + s, ((kbg / kStages) - 1) & 1, kWaitEmpty, abort_flag, p.watchdog)) {
+            stop = true;
             break;
           }
           uint8_t* sa = smem + s * kStageBytes;
@@ -339,11 +344,16 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
     }
   } else if constexpr (CHK) {
     // ---------------- input-side prediction (warps 6..9) ----------------
-    constexpr int kSlicesPerKb = KIND == Kind::kFp8 ? 2 : 4;
+    // Independent of the MMA pipeline: for each of this CTA's tiles, the
+    // slices s = mt, mt + Tm, ... (ascending) of the tile's 256 B rows are
+    // read from global memory (hot in L2: the same column block is streaming
+    // through this SM) and folded into fma chains with q_full.
     const int ct = threadIdx.x - 192;  // 0..127: rows ct and ct + 128 of the B tile
     const float alpha = *p.alpha;
-    uint32_t kbg = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+    const int num_slices = (p.k + kSliceK - 1) / kSliceK;
+    const int64_t row_bytes = KIND == Kind::kFp8 ? p.k : p.k / 2;
+    const int64_t k_atoms = (p.k + 63) / 64;
+    for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
       int mt, nt;
       tile_coords(t, p, mt, nt);
       float acc[2][C][2];
@@ -351,97 +361,75 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int c = 0; c < C; ++c) acc[h][c][0] = acc[h][c][1] = 0.f;
-      bool live = true;
-      for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
-        const int s = kbg % kStages;
-        const bool ok = mbar_wait(full + s, (kbg / kStages) & 1, kWaitFull, abort_flag, p.watchdog);
-        uint32_t mask = 0;
+      for (int sl = mt; sl < num_slices; sl += p.tiles_m) {
+        const int k0 = sl * kSliceK;
+        constexpr int kChunksPerSlice = KIND == Kind::kFp8 ? 4 : 2;  // 16-byte chunks per row
+        uint4 raw[2][kChunksPerSlice];
+        uint32_t sfw[2];
 #pragma unroll
-        for (int j = 0; j < kSlicesPerKb; ++j) {
-          const int sl = kb * kSlicesPerKb + j;
-          if (sl * kSliceK < p.k && sl % p.tiles_m == mt) mask |= 1u << j;
-        }
-        uint4 raw[2][8];
-        uint32_t sfw[2][4];
-        if (mask && ok) {
-          const uint8_t* sb = smem + s * kStageBytes + kABytes;
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int r = ct + 128 * h;
-            const uint8_t* row_base = sb + r * kBKBytes;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              raw[h][j] = *reinterpret_cast<const uint4*>(row_base + ((j ^ (r & 7)) << 4));
-            }
-            if constexpr (KIND == Kind::kNvf4) {
-              const uint8_t* ssfb = sb + kBBytes + kSfaBytes;
-              const int rr = r & 127;
-#pragma unroll
-              for (int g = 0; g < 4; ++g) {
-                sfw[h][g] = *reinterpret_cast<const uint32_t*>(ssfb + (r >> 7) * 2048 + g * 512 + (rr & 31) * 16 +
-                                                               ((rr >> 5) & 3) * 4);
-              }
-            }
-          }
-        }
-        // Uniform decision: every checksum thread has copied its rows (or the
-        // wait failed somewhere); only then is the stage handed back.
-        if (named_barrier_or(2, 128, !ok || *abort_flag != 0)) {
-          live = false;
-          break;
-        }
-        if (ct == 0) mbar_arrive(empty + s);
-        if (!mask) continue;
-#pragma unroll
-        for (int j = 0; j < kSlicesPerKb; ++j) {
-          if (!(mask & (1u << j))) continue;
-          const int k0 = (kb * kSlicesPerKb + j) * kSliceK;
-          constexpr int kChunksPerSlice = KIND == Kind::kFp8 ? 4 : 2;  // 16-byte chunks
-          constexpr int kElemsPerChunk = KIND == Kind::kFp8 ? 16 : 32;
+        for (int h = 0; h < 2; ++h) {
+          const int64_t r = static_cast<int64_t>(nt) * kBN + ct + 128 * h;
+          const bool row_in = r < p.n;
+          const uint8_t* src = p.b + r * row_bytes + (KIND == Kind::kFp8 ? k0 : k0 / 2);
 #pragma unroll
           for (int ch = 0; ch < kChunksPerSlice; ++ch) {
+            const int byte = (KIND == Kind::kFp8 ? k0 : k0 / 2) + ch * 16;
+            raw[h][ch] = (row_in && byte < row_bytes) ? __ldg(reinterpret_cast<const uint4*>(src) + ch)
+                                                       : make_uint4(0, 0, 0, 0);
+          }
+          if constexpr (KIND == Kind::kNvf4) {
+            const int64_t off = ((r >> 7) * k_atoms + (k0 >> 6)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4;
+            sfw[h] = row_in ? __ldg(reinterpret_cast<const uint32_t*>(p.sfb + off)) : 0u;
+          }
+        }
+        // q_full is zero-padded to a multiple of 64 K, so loads need no guard;
+        // 8 elements of q are loaded ahead of their fma chains.
 #pragma unroll
-            for (int e = 0; e < kElemsPerChunk; ++e) {
-              const int kg = k0 + ch * kElemsPerChunk + e;
-              float qv[C][2];
-              if (kg < p.k) {
-                const float* qk = p.q_full + static_cast<int64_t>(kg) * C * 2;
-                if constexpr (C == 2) {
-                  const float4 f = __ldg(reinterpret_cast<const float4*>(qk));
-                  qv[0][0] = f.x; qv[0][1] = f.y; qv[1][0] = f.z; qv[1][1] = f.w;
-                } else {
-                  const float2 f = __ldg(reinterpret_cast<const float2*>(qk));
-                  qv[0][0] = f.x; qv[0][1] = f.y;
-                }
-              } else {
+        for (int e0 = 0; e0 < kSliceK; e0 += 8) {
+          float qv[8][C][2];
 #pragma unroll
-                for (int c = 0; c < C; ++c) qv[c][0] = qv[c][1] = 0.f;
-              }
+          for (int e = 0; e < 8; ++e) {
+            const float* qk = p.q_full + static_cast<int64_t>(k0 + e0 + e) * C * 2;
+            if constexpr (C == 2) {
+              const float4 f = __ldg(reinterpret_cast<const float4*>(qk));
+              qv[e][0][0] = f.x; qv[e][0][1] = f.y; qv[e][1][0] = f.z; qv[e][1][1] = f.w;
+            } else {
+              const float2 f = __ldg(reinterpret_cast<const float2*>(qk));
+              qv[e][0][0] = f.x; qv[e][0][1] = f.y;
+            }
+          }
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const uint4 chunk = raw[h][j * kChunksPerSlice + ch];
-                float value;
-                if constexpr (KIND == Kind::kFp8) {
-                  const uint32_t word = e < 4 ? chunk.x : e < 8 ? chunk.y : e < 12 ? chunk.z : chunk.w;
-                  value = decode_e4m3((word >> (8 * (e & 3))) & 0xFFu);
-                } else {
-                  const uint32_t word = e < 8 ? chunk.x : e < 16 ? chunk.y : e < 24 ? chunk.z : chunk.w;
-                  const uint32_t nib = (word >> (4 * (e & 7))) & 0xFu;
-                  const int blk = (ch * kElemsPerChunk + e) >> 4;  // 16-element block within the slice
-                  value = decode_e2m1(nib) * decode_e4m3((sfw[h][j] >> (8 * blk)) & 0xFFu);
-                }
-                const float av = fabsf(value);
+          for (int h = 0; h < 2; ++h) {
+            float value[8];
+            if constexpr (KIND == Kind::kFp8) {
+              const uint4 chunk = raw[h][e0 >> 4];
+              const uint32_t w0 = (e0 & 8) ? chunk.z : chunk.x;
+              const uint32_t w1 = (e0 & 8) ? chunk.w : chunk.y;
+              const float2 v01 = e4m3x2_to_float2(w0 & 0xFFFFu), v23 = e4m3x2_to_float2(w0 >> 16);
+              const float2 v45 = e4m3x2_to_float2(w1 & 0xFFFFu), v67 = e4m3x2_to_float2(w1 >> 16);
+              value[0] = v01.x; value[1] = v01.y; value[2] = v23.x; value[3] = v23.y;
+              value[4] = v45.x; value[5] = v45.y; value[6] = v67.x; value[7] = v67.y;
+            } else {
+              const uint4 chunk = raw[h][e0 >> 5];
+              const int wi = (e0 >> 3) & 3;
+              const uint32_t word = wi == 0 ? chunk.x : wi == 1 ? chunk.y : wi == 2 ? chunk.z : chunk.w;
+              e2m1x8_to_float(word, value);
+              const float scale = decode_e4m3((sfw[h] >> (8 * (e0 >> 4))) & 0xFFu);
 #pragma unroll
-                for (int c = 0; c < C; ++c) {
-                  acc[h][c][0] = fmaf(qv[c][0], value, acc[h][c][0]);
-                  acc[h][c][1] = fmaf(qv[c][1], av, acc[h][c][1]);
-                }
+              for (int e = 0; e < 8; ++e) value[e] *= scale;
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float av = fabsf(value[e]);
+#pragma unroll
+              for (int c = 0; c < C; ++c) {
+                acc[h][c][0] = fmaf(qv[e][c][0], value[e], acc[h][c][0]);
+                acc[h][c][1] = fmaf(qv[e][c][1], av, acc[h][c][1]);
               }
             }
           }
         }
       }
-      if (!live) break;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int col = nt * kBN + ct + 128 * h;
@@ -539,6 +527,8 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   p.hit = g.hit;
   p.padded_n = static_cast<int32_t>(g.padded_n);
   p.q_full = g.q_full;
+  p.b = g.b;
+  p.sfb = g.sfb;
   p.predicted = g.predicted;
   p.magnitude = g.magnitude;
   p.watchdog = watchdog_ptr();

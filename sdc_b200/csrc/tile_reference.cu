@@ -53,8 +53,9 @@ __device__ __forceinline__ float operand_value(const uint8_t* x, const uint8_t* 
 
 // q[(c*2 + h) * Tm * K + t * K + k]: h = 0 signed projection, h = 1 magnitude.
 // Each thread owns 8 consecutive k of one tile and walks the tile's rows in
-// ascending order (the reference's fma order), so a warp reads 256 contiguous
-// bytes (FP8) or 128 bytes (NVFP4) of each row.
+// ascending order (the reference's fma order); loads of 8 rows are issued
+// ahead of their fma chains so enough bytes are in flight to stream A at
+// HBM speed. A warp reads 256 contiguous bytes (FP8) or 128 (NVFP4) per row.
 template <Kind KIND, int C>
 __global__ void __launch_bounds__(kRefThreads)
     q_encode(const uint8_t* a, const uint8_t* sfa, int64_t m, int64_t k, const float* weights,
@@ -69,26 +70,47 @@ __global__ void __launch_bounds__(kRefThreads)
     for (int e = 0; e < 8; ++e) enc[c][e] = mag[c][e] = 0.f;
   const int64_t rows = std::min<int64_t>(kTileRows, m - t * kTileRows);
   const int64_t k_atoms = (k + 63) / 64;
-  for (int64_t r = 0; r < rows; ++r) {
-    const int64_t row = t * kTileRows + r;
-    float v[8];
-    if constexpr (KIND == Kind::kFp8) {
-      const uint2 u = __ldg(reinterpret_cast<const uint2*>(a + row * k + k0));
+  constexpr int kBatch = 8;
+  for (int64_t r0 = 0; r0 < rows; r0 += kBatch) {
+    uint2 u8[kBatch];
+    uint32_t u4[kBatch];
+    uint32_t sfb[kBatch];
+    float w[kBatch][C];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = decode_e4m3(((e < 4 ? u.x : u.y) >> (8 * (e & 3))) & 0xFFu);
-    } else {
-      const uint32_t u = __ldg(reinterpret_cast<const uint32_t*>(a + row * (k / 2) + k0 / 2));
-      const float scale = decode_e4m3(sfa[sf_off(row, k0 >> 4, k_atoms)]);
+    for (int i = 0; i < kBatch; ++i) {
+      const int64_t row = t * kTileRows + r0 + i;
+      const bool in = r0 + i < rows;
+      if constexpr (KIND == Kind::kFp8) {
+        u8[i] = in ? __ldg(reinterpret_cast<const uint2*>(a + row * k + k0)) : make_uint2(0, 0);
+      } else {
+        u4[i] = in ? __ldg(reinterpret_cast<const uint32_t*>(a + row * (k / 2) + k0 / 2)) : 0u;
+        sfb[i] = in ? sfa[sf_off(row, k0 >> 4, k_atoms)] : 0u;
+      }
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = decode_e2m1((u >> (4 * e)) & 15u) * scale;
+      for (int c = 0; c < C; ++c) w[i][c] = in ? __ldg(weights + c * m + row) : 0.f;
     }
 #pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const float w = __ldg(weights + c * m + row);
+    for (int i = 0; i < kBatch; ++i) {
+      if (r0 + i >= rows) break;
+      float v[8];
+      if constexpr (KIND == Kind::kFp8) {
+        const float2 v01 = e4m3x2_to_float2(u8[i].x & 0xFFFFu), v23 = e4m3x2_to_float2(u8[i].x >> 16);
+        const float2 v45 = e4m3x2_to_float2(u8[i].y & 0xFFFFu), v67 = e4m3x2_to_float2(u8[i].y >> 16);
+        v[0] = v01.x; v[1] = v01.y; v[2] = v23.x; v[3] = v23.y;
+        v[4] = v45.x; v[5] = v45.y; v[6] = v67.x; v[7] = v67.y;
+      } else {
+        const float scale = decode_e4m3(sfb[i]);
+        e2m1x8_to_float(u4[i], v);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        enc[c][e] = fmaf(w, v[e], enc[c][e]);
-        mag[c][e] = fmaf(fabsf(w), fabsf(v[e]), mag[c][e]);
+        for (int e = 0; e < 8; ++e) v[e] *= scale;
+      }
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          enc[c][e] = fmaf(w[i][c], v[e], enc[c][e]);
+          mag[c][e] = fmaf(fabsf(w[i][c]), fabsf(v[e]), mag[c][e]);
+        }
       }
     }
   }
@@ -204,22 +226,22 @@ __global__ void __launch_bounds__(kRefThreads)
 }
 
 // q_full[(k * C + c) * 2 + h] = sum over tiles (ascending) of q[(c*2+h), t, k].
+// q_full[(k * C + c) * 2 + h] = sum over tiles (ascending) of q[(c*2+h), t, k];
+// one thread per (plane, k) so the sequential per-entry sums run in parallel.
+// Entries k <= kk < K rounded up to 64 are zero (the GEMM reads whole slices).
 template <int C>
 __global__ void reduce_tiles(const float* q, int64_t tiles_m, int64_t k, float* q_full) {
-  const int64_t kk = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (kk >= k) return;
-  float s[C * 2];
-#pragma unroll
-  for (int plane = 0; plane < C * 2; ++plane) {
-    float acc = 0.f;
-    for (int64_t t = 0; t < tiles_m; ++t) acc = __fadd_rn(acc, q[(plane * tiles_m + t) * k + kk]);
-    s[plane] = acc;
+  const int64_t k_pad = ((k + 63) / 64) * 64;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= C * 2 * k_pad) return;
+  const int64_t plane = idx / k_pad, kk = idx - plane * k_pad;
+  float acc = 0.f;
+  if (kk < k) {
+    const float* src = q + plane * tiles_m * k + kk;
+#pragma unroll 8
+    for (int64_t t = 0; t < tiles_m; ++t) acc = __fadd_rn(acc, src[t * k]);
   }
-  if constexpr (C == 2) {
-    reinterpret_cast<float4*>(q_full)[kk] = make_float4(s[0], s[1], s[2], s[3]);
-  } else {
-    reinterpret_cast<float2*>(q_full)[kk] = make_float2(s[0], s[1]);
-  }
+  q_full[kk * C * 2 + plane] = acc;
 }
 
 int64_t q_floats(int channels, int64_t m, int64_t k) { return static_cast<int64_t>(channels) * 2 * ceil_div(m, kTileRows) * k; }
@@ -233,7 +255,8 @@ int projection_impl(const ReferenceProblem& p, cudaStream_t stream) {
   SDC_CUDA_CHECK(cudaGetLastError());
   if (p.layout == SDC_LAYOUT_KSLICE) {
     float* q_full = q + q_floats(C, p.m, p.k);
-    reduce_tiles<C><<<static_cast<unsigned>(ceil_div(p.k, 256)), 256, 0, stream>>>(q, tiles_m, p.k, q_full);
+    reduce_tiles<C><<<static_cast<unsigned>(ceil_div(C * 2 * ceil_div(p.k, 64) * 64, 256)), 256, 0, stream>>>(
+        q, tiles_m, p.k, q_full);
     SDC_CUDA_CHECK(cudaGetLastError());
   }
   return SDC_OK;
@@ -270,7 +293,7 @@ int check_problem(const ReferenceProblem& p) {
 size_t reference_workspace_bytes(int channels, int64_t m, int64_t n, int64_t k, int layout) {
   (void)n;
   int64_t floats = q_floats(channels, m, k);
-  if (layout == SDC_LAYOUT_KSLICE) floats += static_cast<int64_t>(channels) * 2 * k;
+  if (layout == SDC_LAYOUT_KSLICE) floats += static_cast<int64_t>(channels) * 2 * ceil_div(k, 64) * 64;
   return static_cast<size_t>(floats) * sizeof(float);
 }
 

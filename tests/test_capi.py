@@ -51,7 +51,7 @@ def test_argument_contracts_are_checked_before_launch():
     rc = lib.sdc_abft_finalize(7, fake, fake, fake, 1, 16, 16, None, 0, fake, fake, 0.0, 0.0, fake, 0, 0, None,
                                None, None, 0, fake, fake, fake, fake, 64, None)
     assert rc == capi.SDC_ERR_UNKNOWN_ALGORITHM
-    assert lib.sdc_abft_finalize_workspace_bytes(0, 300, 4) == 2 * 2 * 4
+    assert lib.sdc_abft_finalize_workspace_bytes(0, 300, 4) == 2 * ((300 + 63) // 64) * 4
     assert lib.sdc_abft_workspace_bytes(0, 256, 64, 128, 0) == 2 * 2 * 2 * 128 * 4
 
 

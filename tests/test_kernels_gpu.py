@@ -415,6 +415,32 @@ def test_input_reference_bit_exact_vs_oracle(precision, shape, layout):
 
 
 @pytest.mark.parametrize("precision", ["fp8", "nvfp4"])
+@pytest.mark.parametrize("shape,layout", [((2560, 4352, 2048), 1), ((2560, 4352, 512), 0), ((640, 33024, 1024), 1)])
+def test_persistent_multi_tile_per_cta_bit_exact(precision, shape, layout):
+    # More tiles than SMs: every CTA walks several tiles, the accumulator
+    # buffers rotate and the prediction warps skip across many pipeline phases.
+    m, n, k = shape
+    qa, qb, alpha = _varying_case(precision, m, n, k)
+    base, _, reference, _ = _ops(precision)
+    args = _args(precision, qa, qb, alpha, k)
+    weights = _dyadic_weights(m)
+    out, obs, hit, pred, mag = reference(*args, weights, -1, -1, -1, 0, None, layout)
+    assert torch.equal(out, base(*args))
+    a, sfa, b, sfb = _oracle_inputs(precision, qa, qb)
+    epred, emag = native.input_reference(precision, a, sfa, b, sfb, m, n, k, _np(weights), _np(alpha),
+                                         pred.shape[-1], "tile" if layout == 0 else "kslice")
+    assert np.array_equal(_np(pred), epred)
+    assert np.array_equal(_np(mag), emag)
+    tol = 2e-5 * _np(mag).sum(axis=1) + 1e-3
+    assert np.all(np.abs(_np(obs).sum(axis=1) - _np(pred).sum(axis=1)) <= tol)
+    from sdc_b200 import capi
+    import ctypes
+    code = ctypes.c_int32(-1)
+    capi.check(capi.lib().sdc_read_device_error(torch.cuda.current_stream().cuda_stream, ctypes.byref(code)))
+    assert code.value == 0, f"a bounded wait expired (watchdog code {code.value})"
+
+
+@pytest.mark.parametrize("precision", ["fp8", "nvfp4"])
 def test_epilogue_fault_changes_only_observation(precision):
     m, n, k = 136, 144, 288
     qa, qb, alpha = _varying_case(precision, m, n, k)
