@@ -386,6 +386,19 @@ __device__ __forceinline__ void e2m1x8_to_float(uint32_t word, float (&v)[8]) {
   }
 }
 
+// Two independent IEEE fp32 fused multiply-adds in one sm_100 instruction
+// (bit-identical to two fmaf calls): returns {fma(a.x,b.x,c.x), fma(a.y,b.y,c.y)}.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
 __device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
   return __uint_as_float(static_cast<uint32_t>(b) << 16);
 }

@@ -63,11 +63,11 @@ __global__ void __launch_bounds__(kRefThreads)
   const int64_t k0 = (static_cast<int64_t>(blockIdx.x) * kRefThreads + threadIdx.x) * 8;
   const int64_t t = blockIdx.y;
   if (k0 >= k) return;
-  float enc[C][8], mag[C][8];
+  // acc[e] = {enc_c0, enc_c1} and {mag_c0, mag_c1} pairs for packed f32x2 fmas
+  // (C == 1 keeps the second lane at zero weight).
+  float2 enc[8], mag[8];
 #pragma unroll
-  for (int c = 0; c < C; ++c)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) enc[c][e] = mag[c][e] = 0.f;
+  for (int e = 0; e < 8; ++e) enc[e] = mag[e] = make_float2(0.f, 0.f);
   const int64_t rows = std::min<int64_t>(kTileRows, m - t * kTileRows);
   const int64_t k_atoms = (k + 63) / 64;
   constexpr int kBatch = 8;
@@ -104,13 +104,13 @@ __global__ void __launch_bounds__(kRefThreads)
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] *= scale;
       }
+      const float2 wv = make_float2(w[i][0], C == 2 ? w[i][C - 1] : 0.f);
+      const float2 wa = make_float2(fabsf(wv.x), fabsf(wv.y));
 #pragma unroll
-      for (int c = 0; c < C; ++c) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          enc[c][e] = fmaf(w[i][c], v[e], enc[c][e]);
-          mag[c][e] = fmaf(fabsf(w[i][c]), fabsf(v[e]), mag[c][e]);
-        }
+      for (int e = 0; e < 8; ++e) {
+        enc[e] = fma2(wv, make_float2(v[e], v[e]), enc[e]);
+        const float av = fabsf(v[e]);
+        mag[e] = fma2(wa, make_float2(av, av), mag[e]);
       }
     }
   }
@@ -118,10 +118,16 @@ __global__ void __launch_bounds__(kRefThreads)
   for (int c = 0; c < C; ++c) {
     float4* pe = reinterpret_cast<float4*>(q + ((c * 2 + 0) * tiles_m + t) * k + k0);
     float4* pm = reinterpret_cast<float4*>(q + ((c * 2 + 1) * tiles_m + t) * k + k0);
-    pe[0] = make_float4(enc[c][0], enc[c][1], enc[c][2], enc[c][3]);
-    pe[1] = make_float4(enc[c][4], enc[c][5], enc[c][6], enc[c][7]);
-    pm[0] = make_float4(mag[c][0], mag[c][1], mag[c][2], mag[c][3]);
-    pm[1] = make_float4(mag[c][4], mag[c][5], mag[c][6], mag[c][7]);
+    float e8[8], m8[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      e8[e] = c == 0 ? enc[e].x : enc[e].y;
+      m8[e] = c == 0 ? mag[e].x : mag[e].y;
+    }
+    pe[0] = make_float4(e8[0], e8[1], e8[2], e8[3]);
+    pe[1] = make_float4(e8[4], e8[5], e8[6], e8[7]);
+    pm[0] = make_float4(m8[0], m8[1], m8[2], m8[3]);
+    pm[1] = make_float4(m8[4], m8[5], m8[6], m8[7]);
   }
 }
 
@@ -238,8 +244,17 @@ __global__ void reduce_tiles(const float* q, int64_t tiles_m, int64_t k, float* 
   float acc = 0.f;
   if (kk < k) {
     const float* src = q + plane * tiles_m * k + kk;
-#pragma unroll 8
-    for (int64_t t = 0; t < tiles_m; ++t) acc = __fadd_rn(acc, src[t * k]);
+    // 32 loads in flight ahead of their ordered adds.
+    constexpr int kBatch = 32;
+    for (int64_t t0 = 0; t0 < tiles_m; t0 += kBatch) {
+      float v[kBatch];
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) v[i] = t0 + i < tiles_m ? __ldg(src + (t0 + i) * k) : 0.f;
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        if (t0 + i < tiles_m) acc = __fadd_rn(acc, v[i]);
+      }
+    }
   }
   q_full[kk * C * 2 + plane] = acc;
 }
