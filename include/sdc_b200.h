@@ -205,6 +205,31 @@ int sdc_abft_finalize(int algorithm, const float* observed,
                       int64_t* location, void* workspace,
                       size_t workspace_bytes, sdc_stream_t stream);
 
+/* Allocation-free variant of sdc_abft_finalize (no counterpart in the
+ * reference). For hosts that cannot allocate device memory when they run the
+ * check, e.g. a plain C/FFI caller with no device allocator of its own: the
+ * per-block scratch comes from a fixed 64 KiB device array inside this
+ * library (allocated once per GPU that loads it, kept until process exit).
+ * Same arguments and results as sdc_abft_finalize minus the workspace.
+ * Limit: channels * ceil(n / 64) <= 16384 (n <= 524288 for Classic); larger
+ * n returns SDC_ERR_INVALID without launching. The first call on a device
+ * looks the array's address up with that device current; make that first
+ * call before any stream capture. Every call shares the one array, so calls
+ * that may overlap on the GPU (different streams, concurrent hosts) race:
+ * serialise them. The entry point itself allocates nothing. */
+int sdc_abft_finalize_noalloc(int algorithm, const float* observed,
+                              const float* predicted, const float* magnitude,
+                              int64_t m_tiles, int64_t padded_n, int64_t n,
+                              const int32_t* tile_flags, int64_t flag_count,
+                              const int32_t* hit_in,
+                              const int32_t* nonfinite_in, float atol,
+                              float rtol, float* reference, int use_reference,
+                              int diagnostics, float* residual,
+                              float* threshold, const float* thresholds,
+                              int scalar_threshold, uint8_t* flags,
+                              int32_t* hit_out, int64_t* location,
+                              sdc_stream_t stream);
+
 /* ---- localisation and single-error correction (extension) ---------------
  * Device restatement of the Classic ratio locator (src/abft/methods.py:
  * 201-237 of the reference; no reference operator exists for it). Inputs are

@@ -9,6 +9,7 @@
 // consecutive columns coalesce, and a second one-block kernel ORs the
 // per-block status words, so no float atomics or host syncs are involved.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -216,6 +217,71 @@ int sdc_abft_finalize(int algorithm, const float* observed, const float* predict
                                                        location);
   SDC_CUDA_CHECK(cudaGetLastError());
   return SDC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free finalize. Some hosts that bind this ABI have no device
+// allocator they may call at this point (a plain C or FFI host driving the
+// check from a monitoring hook, or code that must not grow device memory
+// between steps), so they cannot hand finalize its per-block scratch. This
+// variant takes the scratch from a fixed, file-scope device array instead.
+// ---------------------------------------------------------------------------
+namespace sdc {
+namespace {
+
+// 16384 int32 status words (64 KiB per GPU that loads the library, held until
+// the process exits): channels * ceil(n / 64) <= 16384, i.e. n <= 524288 for
+// the two-channel Classic policy.
+constexpr int64_t kNoAllocMaxBlocks = 16384;
+static __device__ __align__(256) int32_t g_finalize_noalloc_scratch[kNoAllocMaxBlocks];
+
+// In host code the array's name is only a host-side stand-in, so its device
+// address is looked up once per device (with that device current) and cached.
+int noalloc_scratch(int32_t** out) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex lock;
+  static int32_t* cached[kMaxDevices] = {};
+  int device = 0;
+  SDC_CUDA_CHECK(cudaGetDevice(&device));
+  if (device < 0 || device >= kMaxDevices) return fail(SDC_ERR_INVALID, "device index out of range");
+  std::lock_guard<std::mutex> guard(lock);
+  if (cached[device] == nullptr) {
+    void* ptr = nullptr;
+    SDC_CUDA_CHECK(cudaGetSymbolAddress(&ptr, g_finalize_noalloc_scratch));
+    cached[device] = static_cast<int32_t*>(ptr);
+  }
+  *out = cached[device];
+  return SDC_OK;
+}
+
+}  // namespace
+}  // namespace sdc
+
+int sdc_abft_finalize_noalloc(int algorithm, const float* observed, const float* predicted,
+                              const float* magnitude, int64_t m_tiles, int64_t padded_n, int64_t n,
+                              const int32_t* tile_flags, int64_t flag_count, const int32_t* hit_in,
+                              const int32_t* nonfinite_in, float atol, float rtol, float* reference,
+                              int use_reference, int diagnostics, float* residual, float* threshold,
+                              const float* thresholds, int scalar_threshold, uint8_t* flags,
+                              int32_t* hit_out, int64_t* location, sdc_stream_t stream) {
+  using namespace sdc;
+  const int channels = policy_channels(algorithm);
+  if (channels == 0) return fail(SDC_ERR_UNKNOWN_ALGORITHM, "Unknown compiled ABFT algorithm ID");
+  if (n <= 0 || finalize_blocks(channels, n) > kNoAllocMaxBlocks) {
+    return fail(SDC_ERR_INVALID,
+                "sdc_abft_finalize_noalloc supports channels * ceil(n/64) <= 16384 status words "
+                "(n <= 524288 for Classic); use sdc_abft_finalize with a caller workspace");
+  }
+  int32_t* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != SDC_OK) return rc;
+  // The status words are written by every block before they are read, so the
+  // shared array needs no clearing between calls.
+  return sdc_abft_finalize(algorithm, observed, predicted, magnitude, m_tiles, padded_n, n, tile_flags,
+                           flag_count, hit_in, nonfinite_in, atol, rtol, reference, use_reference,
+                           diagnostics, residual, threshold, thresholds, scalar_threshold, flags, hit_out,
+                           location, scratch, static_cast<size_t>(kNoAllocMaxBlocks) * sizeof(int32_t),
+                           stream);
 }
 
 }  // extern "C"
