@@ -1,0 +1,137 @@
+"""Prepared GEMM operands: quantise once, run native kernels, decode K blocks.
+
+Mirrors src/abft/operands.py of the reference (``PreparedGemm``): the same
+fields, ``prepare`` (FP8/NVFP4 through this library's quantizer, B transposed
+to K-major rows), ``raw_native`` / ``collected_native`` /
+``collected_reference_native`` op routing, the CPU-capable ``decode_block``
+and ``injected`` input-code bit flips (NVFP4 nibble rule). FP32/BF16 operands
+are kept for the separate reference mode and CPU tests; their native GEMMs
+are outside this path.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, replace
+from typing import Any
+
+import torch
+
+SCALING = {"fp32": "none", "bf16": "none", "fp8": "tensorwise", "nvfp4": "block16"}
+INPUT_REFERENCE_PRECISIONS = frozenset({"fp8", "nvfp4"})
+LAYOUTS = {"tile": 0, "kslice": 1}
+_E2M1 = (0., .5, 1., 1.5, 2., 3., 4., 6., -0., -.5, -1., -1.5, -2., -3., -4., -6.)
+
+
+def _ops():
+    from .. import ops
+    return ops
+
+
+@dataclass
+class PreparedGemm:
+    a: torch.Tensor
+    b: torch.Tensor
+    precision: str
+    m: int
+    n: int
+    k: int
+    qa: Any = None
+    qb: Any = None
+    alpha: Any = None
+    sfa: Any = None
+    sfb: Any = None
+
+    @classmethod
+    def prepare(cls, a, b, precision, scaling, global_scale="amax"):
+        if precision not in SCALING or scaling != SCALING[precision]:
+            raise ValueError("Incompatible precision/scaling")
+        if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[0] or a.device != b.device:
+            raise ValueError("GEMM requires compatible matrices on one device")
+        m, k = a.shape
+        n = b.shape[1]
+        if min(m, n, k) <= 0:
+            raise ValueError("Empty GEMM is not supported")
+        if precision in {"fp32", "bf16"}:
+            dtype = torch.float32 if precision == "fp32" else torch.bfloat16
+            return cls(a.to(dtype), b.to(dtype), precision, m, n, k)
+        from .. import require_device
+        from ..gemm.quantization import quantize
+
+        require_device(a.device)
+        qa = quantize(a.contiguous(), precision, global_scale)
+        qb = quantize(b.T.contiguous(), precision, global_scale)
+        alpha = (qa.multiplier * qb.multiplier).reciprocal()
+        prepared = cls(qa.codes, qb.codes, precision, m, n, k, qa, qb, alpha)
+        if precision == "nvfp4":
+            prepared.sfa, prepared.sfb = qa.scales_mma, qb.scales_mma
+        return prepared
+
+    def _native_args(self):
+        if self.precision == "fp8":
+            return (self.a.view(torch.float8_e4m3fn), self.b.view(torch.float8_e4m3fn), self.alpha)
+        if self.precision == "nvfp4":
+            return (self.a, self.b, self.sfa, self.sfb, self.k, self.alpha)
+        raise NotImplementedError(f"native {self.precision} GEMMs are outside the FP8/NVFP4 path")
+
+    def raw_native(self):
+        ops = _ops()
+        gemm = ops.fp8_mm if self.precision == "fp8" else ops.nvfp4_mm
+        return gemm(*self._native_args())
+
+    def collected_native(self, weights, fault=(-1, -1, -1), *, algorithm=0, nonfinite=None):
+        """Output, observed partials and hit (epilogue checksums only)."""
+        ops = _ops()
+        op = ops.abft_fp8_mm if self.precision == "fp8" else ops.abft_nvfp4_mm
+        return op(*self._native_args(), weights, *fault, algorithm, nonfinite)
+
+    def collected_reference_native(self, weights, fault=(-1, -1, -1), *, algorithm=0, nonfinite=None,
+                                   layout="tile"):
+        """Output, observed, hit, predicted and magnitude partials."""
+        if self.precision not in INPUT_REFERENCE_PRECISIONS:
+            raise NotImplementedError(f"input_fused reference is not implemented for {self.precision}")
+        ops = _ops()
+        op = ops.abft_fp8_reference_mm if self.precision == "fp8" else ops.abft_nvfp4_reference_mm
+        return op(*self._native_args(), weights, *fault, algorithm, nonfinite, LAYOUTS[layout])
+
+    def decode_block(self, start, end):
+        """Decoded fp32 A[:, start:end] and B[start:end, :] (works on the CPU)."""
+        if not 0 <= start < end <= self.k:
+            raise ValueError("Invalid K block")
+        if self.precision == "nvfp4" and (start % 16 or end % 16):
+            raise ValueError("NVFP4 reference blocks must align to block16 scales")
+        if self.precision in {"fp32", "bf16"}:
+            return self.a[:, start:end].float(), self.b[start:end, :].float()
+
+        def decode(codes, q):
+            if self.precision == "fp8":
+                return codes[:, start:end].view(torch.float8_e4m3fn).float() / q.multiplier
+            packed = codes[:, start // 2:end // 2]
+            nibbles = torch.stack((packed & 15, packed >> 4), dim=-1).reshape(codes.shape[0], end - start).long()
+            values = torch.tensor(_E2M1, device=codes.device)[nibbles]
+            scales = q.scales[:, start // 16:end // 16].view(torch.float8_e4m3fn).float()
+            blocks = values.reshape(values.shape[0], -1, 16) * scales.unsqueeze(-1)
+            return blocks.reshape_as(values) / q.multiplier
+
+        return decode(self.a, self.qa), decode(self.b, self.qb).T
+
+    def injected(self, config):
+        """Copy of the operands with one input-code bit flipped (the clean
+        buffers are untouched). Logical B coordinates map to the B rows."""
+        if config.location not in {"a", "b"}:
+            raise ValueError("Prepared input injection requires location a or b")
+        rows, cols = (self.m, self.k) if config.location == "a" else (self.k, self.n)
+        width = {"fp32": 32, "bf16": 16, "fp8": 8, "nvfp4": 4}[self.precision]
+        if config.row >= rows or config.col >= cols or config.bit >= width:
+            raise ValueError("Input fault coordinate/bit outside actual representation")
+        target = (self.a if config.location == "a" else self.b).clone()
+        row, col = config.row, config.col
+        if config.location == "b" and self.precision in {"fp8", "nvfp4"}:
+            row, col = col, row
+        if self.precision == "nvfp4":
+            target[row, col // 2] ^= 1 << (config.bit + 4 * (col % 2))
+        else:
+            dtype = {32: torch.int32, 16: torch.int16, 8: torch.uint8}[width]
+            mask = 1 << config.bit
+            if width > 8 and config.bit == width - 1:
+                mask = -(1 << config.bit)
+            target.view(dtype)[row, col] ^= mask
+        return replace(self, **{config.location: target})

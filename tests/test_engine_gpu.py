@@ -1,0 +1,138 @@
+"""GPU tests of the ABFT engine mirror on the native sm_100a path.
+
+``execute(..., implementation="native")`` must give the unprotected GEMM's
+output bit for bit when clean, detect an accumulator fault, locate it with
+``locate=True`` and repair it (``recovery="recompute"``: bit-exact clean
+output; ``"correct"``: the located element recomputed). The Python
+``reference`` implementation fed by the same native collectors must reach the
+same decisions.
+"""
+import pytest
+import torch
+
+import sdc_b200
+from sdc_b200.abft import execute, execute_prepared
+from sdc_b200.abft.engine import AbftError
+from sdc_b200.abft.methods import get_method
+from sdc_b200.abft.operands import PreparedGemm
+from sdc_b200.gemm import backend
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+SCALING = {"fp8": "tensorwise", "nvfp4": "block16"}
+
+
+def _operands(m, n, k, seed=5):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return torch.randn(m, k, device=DEV, generator=g), torch.randn(k, n, device=DEV, generator=g)
+
+
+def _cfg(**changes):
+    return {"method": "classic", "implementation": "native", "reference_mode": "input_fused",
+            "on_error": "report", "atol": 1e-3, "rtol": 1e-4, "diagnostics": True, **changes}
+
+
+def _clear_exponent_bit(value):
+    bits = torch.tensor([value], dtype=torch.float32).view(torch.int32).item()
+    return next(b for b in range(25, 30) if not bits & (1 << b))
+
+
+@pytest.mark.parametrize("precision", ["fp8", "nvfp4"])
+@pytest.mark.parametrize("layout", ["tile", "kslice"])
+def test_native_clean_output_is_the_unprotected_gemm(precision, layout):
+    a, b = _operands(384, 520, 512)
+    plain = backend.gemm(a, b, precision, SCALING[precision])
+    output, report = execute(a, b, precision, SCALING[precision], abft_config=_cfg(reference_layout=layout))
+    assert torch.equal(output, plain)
+    assert not report.detected and not report.nonfinite
+    assert report.execution_path == "input_fused_native"
+    record = report.to_record()
+    assert record["context"]["reference_layout"] == layout and record["fault_hit"] == [0]
+
+
+@pytest.mark.parametrize("precision", ["fp8", "nvfp4"])
+@pytest.mark.parametrize("recovery", ["recompute", "correct"])
+def test_native_fault_detected_located_and_repaired(precision, recovery):
+    m, n, k = 520, 384, 512
+    a, b = _operands(m, n, k, seed=9)
+    prepared = PreparedGemm.prepare(a, b, precision, SCALING[precision])
+    clean = prepared.raw_native()
+    row, col = 389, 201
+    bit = _clear_exponent_bit(clean[row, col].float().item())
+    fault = {"location": "accumulator", "row": row, "col": col, "bit": bit}
+    output, report = execute_prepared(prepared, _cfg(locate=True, recovery=recovery, reference_layout="kslice"),
+                                      fault)
+    assert report.detected and report.fault_hit.item() == 1
+    assert report.located and report.location.tolist() == [row, col]
+    assert report.recovered and not report.recheck_failed
+    if recovery == "recompute":
+        assert torch.equal(output, clean)
+        assert report.context["recovery_action"] == "full_recompute"
+    else:
+        assert report.context["recovery_action"] == "located_element_recomputed"
+        torch.testing.assert_close(output.float(), clean.float(), rtol=1e-2, atol=1e-3)
+
+
+@pytest.mark.parametrize("precision", ["fp8", "nvfp4"])
+def test_native_unrecovered_fault_raises(precision):
+    a, b = _operands(256, 256, 256, seed=3)
+    prepared = PreparedGemm.prepare(a, b, precision, SCALING[precision])
+    clean = prepared.raw_native()
+    bit = _clear_exponent_bit(clean[17, 33].float().item())
+    with pytest.raises(AbftError) as error:
+        execute_prepared(prepared, _cfg(on_error="raise"),
+                         {"location": "accumulator", "row": 17, "col": 33, "bit": bit})
+    assert error.value.report.detected and not error.value.report.recovered
+
+
+@pytest.mark.parametrize("precision", ["fp8", "nvfp4"])
+def test_native_sum_policy_detects_without_location(precision):
+    a, b = _operands(256, 320, 256, seed=4)
+    prepared = PreparedGemm.prepare(a, b, precision, SCALING[precision])
+    bit = _clear_exponent_bit(prepared.raw_native()[5, 6].float().item())
+    _, report = execute_prepared(prepared, _cfg(method="sum", locate=True),
+                                 {"location": "accumulator", "row": 5, "col": 6, "bit": bit})
+    assert report.detected and not report.located and report.location.tolist() == [-1, -1]
+    assert report.context["compiled_policy"]["id"] == 1
+
+
+@pytest.mark.parametrize("precision", ["fp8", "nvfp4"])
+def test_python_reference_implementation_agrees_with_native(precision):
+    a, b = _operands(264, 272, 288, seed=11)
+    prepared = PreparedGemm.prepare(a, b, precision, SCALING[precision])
+    bit = _clear_exponent_bit(prepared.raw_native()[100, 200].float().item())
+    fault = {"location": "accumulator", "row": 100, "col": 200, "bit": bit}
+    for layout in ("tile", "kslice"):
+        native_out, native = execute_prepared(prepared, _cfg(locate=True, reference_layout=layout), fault)
+        python_out, python = execute_prepared(prepared, _cfg(implementation="reference", reference_layout=layout),
+                                              fault)
+        assert torch.equal(native_out, python_out)
+        assert bool(native.detected) == bool(python.detected) is True
+        assert native.location.tolist() == python.location.tolist() == [100, 200]
+        # Totals are summed in a different order (serial vs torch.sum): equal
+        # up to rounding, far below the detection threshold, off the faulty column.
+        clean_cols = torch.arange(prepared.n, device=DEV) != 200
+        diff = (native.residual - python.residual).abs()[:, clean_cols]
+        assert (diff <= native.threshold[:, clean_cols]).all()
+
+
+def test_native_weights_are_cached_per_stream():
+    from sdc_b200.abft import native
+
+    a, b = _operands(128, 128, 128)
+    prepared = PreparedGemm.prepare(a, b, "fp8", "tensorwise")
+    execute_prepared(prepared, _cfg())
+    key = (0, torch.device(DEV).index or 0, 128)
+    first = native._weights[key][0]
+    execute_prepared(prepared, _cfg())
+    assert native._weights[key][0] is first
+    assert torch.equal(first, get_method("classic").projection_weights(prepared))
+
+
+def test_timing_events_are_reported():
+    a, b = _operands(256, 256, 256)
+    _, report = execute(a, b, "fp8", "tensorwise", abft_config=_cfg(timing=True, locate=True))
+    timing = report.to_record()["timing_ms"]
+    assert {"reference", "execute", "finalize", "locate"} <= set(timing)
+    assert all(value >= 0 for value in timing.values())
+    assert sdc_b200.LIB_PATH.exists()
