@@ -235,7 +235,7 @@ def run_ours(args):
     stream = torch.cuda.current_stream(device)
     bf16_peak, hbm_peak, basis = measured_peaks()
     results = {}
-    for precision, size, seed in (("fp8", 8192, 1), ("nvfp4", 16384, 2)):
+    for precision, size, seed in (("fp8", args.size or 8192, 1), ("nvfp4", args.size or 16384, 2)):
         if args.format not in ("both", precision):
             continue
         m = n = k = size
@@ -314,7 +314,7 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "e4m3" if "fp8" in results else "e2m1", "data": "synthetic",
         "config": {"workload": head["workload"] + " ABFT (Classic, K-slice input reference) + finalize",
-                   "per_gpu": "M=N=K=8192" if "fp8" in results else "M=N=K=16384",
+                   "per_gpu": head["workload"].split(" ")[1],
                    "parallelism": f"M-shard x{world}, NCCL all-reduce of detection status",
                    "l2": "working set (A+B codes, fp32 output) > 126 MB L2; no explicit flush"},
         "overhead_pct": head["overhead_pct"], "unprotected_tflops": head["unprotected_tflops"],
@@ -391,6 +391,8 @@ def main():
     parser.add_argument("--no-detection", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--size", type=int, default=0,
+                        help="override M=N=K of both workloads (profiling captures; not a bench line)")
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
