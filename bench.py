@@ -101,13 +101,15 @@ class ClockSampler:
                 "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
 
 
-def make_operands(precision, m, n, k, device, seed):
+def make_operands(precision, m, n, k, device, seed, b_std=1.0):
     """Seeded N(0,1) bf16 A [m,k] and B_rows [n,k] (synthetic, BASELINE shapes) quantised once."""
     from sdc_b200.gemm.quantization import quantize
 
     g = torch.Generator(device=device).manual_seed(seed)
     a = torch.randn(m, k, device=device, generator=g, dtype=torch.bfloat16)
     b = torch.randn(n, k, device=device, generator=g, dtype=torch.bfloat16)
+    if b_std != 1.0:
+        b = b * b_std
     qa, qb = quantize(a, precision), quantize(b, precision)
     alpha = (qa.multiplier * qb.multiplier).reciprocal()
     if precision == "fp8":
@@ -121,10 +123,10 @@ def make_operands(precision, m, n, k, device, seed):
 class Protected:
     """One protected GEMM step on resident operands (the hot path)."""
 
-    def __init__(self, precision, m, n, k, device, seed, layout=1, atol=1e-3, rtol=1e-4):
+    def __init__(self, precision, m, n, k, device, seed, layout=1, atol=1e-3, rtol=1e-4, b_std=1.0):
         self.ops = torch.ops.sdc_cutlass
         self.precision, self.m, self.n, self.k = precision, m, n, k
-        self.args = make_operands(precision, m, n, k, device, seed)
+        self.args = make_operands(precision, m, n, k, device, seed, b_std)
         self.weights = torch.stack((torch.ones(m, device=device),
                                     torch.arange(1, m + 1, device=device, dtype=torch.float32)))
         self.nonfinite = torch.zeros(1, dtype=torch.int32, device=device)
@@ -195,6 +197,48 @@ def detection_campaign(prot, flips, seed):
             "recall_all": detected / max(flips, 1), "recall_detectable": min(detected, detectable) / max(detectable, 1),
             "by_class": {k: {"detected": v[0], "flips": v[1]} for k, v in by_class.items()},
             "clean_runs": clean_runs + 1, "false_positives": false_positives + int(bool(clean_packet[3][0]))}
+
+
+# Qwen2.5-7B linear layers at T = 16384 tokens: (name, M, N, K).
+QWEN_SHAPES = (("qkv", 16384, 4608, 3584), ("o", 16384, 3584, 3584), ("gate_up", 16384, 37888, 3584),
+               ("down", 16384, 3584, 18944))
+
+
+def qwen_sweep(args, device, stream, rank, world, dist):
+    """Protected vs unprotected GEMM on the Qwen linear shapes, rows of the
+    activations sharded over the ranks (the shape's M split into 128-aligned
+    blocks); time = max over ranks. gate and up share K and the activation,
+    so they run as one N = 2*18944 GEMM."""
+    from sdc_b200.abft.distributed import shard_rows
+
+    out = {}
+    for precision in ("fp8", "nvfp4"):
+        if args.format not in ("both", precision):
+            continue
+        rows = {}
+        total_flops = total_prot = total_plain = 0.0
+        for name, m, n, k in QWEN_SHAPES:
+            start, stop = shard_rows(m, world, rank)
+            prot = Protected(precision, stop - start, n, k, device, 7 + rank, b_std=0.02)
+            t = torch.tensor([timed(prot.step, args.sweep_steps, 3, stream),
+                              timed(prot.unprotected, args.sweep_steps, 3, stream)], device=device)
+            if dist is not None:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t_prot, t_plain = (float(v) / args.sweep_steps for v in t.tolist())
+            flops = 2.0 * m * n * k
+            rows[name] = {"m": m, "n": n, "k": k, "tflops": flops / t_prot / 1e12,
+                          "unprotected_tflops": flops / t_plain / 1e12,
+                          "overhead_pct": 100.0 * (t_prot / t_plain - 1.0)}
+            total_flops += flops
+            total_prot += t_prot
+            total_plain += t_plain
+            del prot
+        torch.cuda.empty_cache()
+        out[precision] = {"layers": rows, "tflops": total_flops / total_prot / 1e12,
+                          "overhead_pct": 100.0 * (total_prot / total_plain - 1.0)}
+    out["config"] = (f"T=16384 tokens, activations N(0,1), weights N(0,0.02), bf16 before quantisation; "
+                     f"M sharded over {world} rank(s); {args.sweep_steps} timed steps per shape")
+    return out
 
 
 def e2e_step(precision, host_a, host_b, device, weights, nonfinite, atol, rtol):
@@ -303,6 +347,7 @@ def run_ours(args):
         results[precision] = entry
         del prot
         torch.cuda.empty_cache()
+    sweep = None if args.no_sweep else qwen_sweep(args, device, stream, rank, world, dist)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -324,6 +369,8 @@ def run_ours(args):
     }
     if "nvfp4" in results and "fp8" in results:
         line["nvfp4"] = results["nvfp4"]
+    if sweep is not None:
+        line["qwen2.5_7b_linears"] = sweep
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_sample_rows)
     print(json.dumps(line), flush=True)
@@ -391,6 +438,8 @@ def main():
     parser.add_argument("--no-detection", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-sweep", action="store_true", help="skip the Qwen2.5-7B linear-shape sweep")
+    parser.add_argument("--sweep-steps", type=int, default=5)
     parser.add_argument("--size", type=int, default=0,
                         help="override M=N=K of both workloads (profiling captures; not a bench line)")
     args = parser.parse_args()

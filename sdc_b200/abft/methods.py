@@ -184,7 +184,8 @@ class Classic(AbftMethod):
 
     def prepare(self, operands, config, mm=None):
         if mm is None:
-            raise ValueError("the separate reference mode needs an fp32 matmul (reference_mm)")
+            from ..gemm import backend
+            mm = backend.mm
         weights = self.projection_weights(operands)
         expected = torch.zeros((self.channels, operands.n), device=operands.a.device, dtype=torch.float32)
         magnitude = torch.zeros_like(expected)

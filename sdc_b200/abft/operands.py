@@ -73,6 +73,9 @@ class PreparedGemm:
         raise NotImplementedError(f"native {self.precision} GEMMs are outside the FP8/NVFP4 path")
 
     def raw_native(self):
+        if self.precision in {"fp32", "bf16"}:
+            from ..gemm import backend
+            return backend.mm(self.a, self.b)
         ops = _ops()
         gemm = ops.fp8_mm if self.precision == "fp8" else ops.nvfp4_mm
         return gemm(*self._native_args())
@@ -80,6 +83,10 @@ class PreparedGemm:
     def collected_native(self, weights, fault=(-1, -1, -1), *, algorithm=0, nonfinite=None):
         """Output, observed partials and hit (epilogue checksums only)."""
         ops = _ops()
+        if self.precision in {"fp32", "bf16"}:
+            from .. import require_device
+            require_device(self.a.device)
+            return ops.abft_mm(self.a, self.b, weights, *fault, algorithm, nonfinite)
         op = ops.abft_fp8_mm if self.precision == "fp8" else ops.abft_nvfp4_mm
         return op(*self._native_args(), weights, *fault, algorithm, nonfinite)
 

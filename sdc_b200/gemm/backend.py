@@ -36,6 +36,9 @@ def _pack_scales(scales, indices, size):
 
 
 def mm(a, b):
+    """The reference's FP32/BF16 GEMM entry: device-checked, then rejected
+    (those kernels are outside the FP8/NVFP4 path)."""
+    require_device(a.device)
     raise NotImplementedError("FP32/BF16 legacy GEMMs are not part of the sdc_b200 FP8/NVFP4 path")
 
 
@@ -46,7 +49,8 @@ def gemm(a, b, precision, scaling, global_scale="amax"):
     if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[0] or a.device != b.device:
         raise ValueError("GEMM inputs must be two matching matrices on one device")
     if precision in {"fp32", "bf16"}:
-        return mm(a, b)
+        dtype = torch.float32 if precision == "fp32" else torch.bfloat16
+        return mm(a.to(dtype), b.to(dtype))
     require_device(a.device)
     from .quantization import quantize
 
