@@ -110,15 +110,36 @@ int oracle_kslice_reference(int kind, const uint8_t* a, const uint8_t* sfa, cons
                             int channels, float alpha, float* pred, float* mag, int64_t padded_n) {
   const int64_t tiles = (m + 127) / 128;
   const int64_t slices = (k + 63) / 64;
-  float* q = (float*)malloc(sizeof(float) * channels * 2 * tiles * k);
   float* qf = (float*)malloc(sizeof(float) * channels * 2 * k);
-  if (!q || !qf) return 1;
-  encode_tiles(kind, a, sfa, m, k, w, channels, q);
-  for (int p = 0; p < channels * 2; ++p) {
+  if (!qf) return 1;
+  /* q over all rows in the K-slice kernel's order: 8 row bands of
+   * rb = ceil(m / 8) rows; in a band, 8 row lanes l each run an fma chain
+   * over rows band_start + l, + 8, ... (ascending); band = ((p_0 + p_1) + ...)
+   * + p_7 and q = ((band_0 + band_1) + ...) + band_7. */
+  const int64_t rb = (m + 7) / 8;
+  for (int c = 0; c < channels; ++c) {
     for (int64_t kk = 0; kk < k; ++kk) {
-      float s = 0.f;
-      for (int64_t t = 0; t < tiles; ++t) s = s + q[(p * tiles + t) * k + kk];
-      qf[p * k + kk] = s;
+      float q[2] = {0.f, 0.f};
+      for (int b = 0; b < 8; ++b) {
+        const int64_t begin = b * rb < m ? b * rb : m;
+        const int64_t end = begin + rb < m ? begin + rb : m;
+        float band[2] = {0.f, 0.f};
+        for (int l = 0; l < 8; ++l) {
+          float e = 0.f, g = 0.f;
+          for (int64_t row = begin + l; row < end; row += 8) {
+            const float v = value_at(kind, a, sfa, row, kk, k);
+            const float wv = w[c * m + row];
+            e = fmaf(wv, v, e);
+            g = fmaf(fabsf(wv), fabsf(v), g);
+          }
+          band[0] = l == 0 ? e : band[0] + e;
+          band[1] = l == 0 ? g : band[1] + g;
+        }
+        q[0] = b == 0 ? band[0] : q[0] + band[0];
+        q[1] = b == 0 ? band[1] : q[1] + band[1];
+      }
+      qf[(c * 2 + 0) * k + kk] = q[0];
+      qf[(c * 2 + 1) * k + kk] = q[1];
     }
   }
   for (int c = 0; c < channels; ++c) {
@@ -139,7 +160,6 @@ int oracle_kslice_reference(int kind, const uint8_t* a, const uint8_t* sfa, cons
       }
     }
   }
-  free(q);
   free(qf);
   return 0;
 }

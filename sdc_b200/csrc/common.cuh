@@ -20,6 +20,8 @@ int fail(int status, const std::string& message);
 int cuda_fail(cudaError_t error, const char* what);
 // Returns SDC_OK when the current device is sm_100.
 int check_current_device();
+// Streaming multiprocessors of the current device (cached per device).
+int sm_count();
 // Encodes a tiled TMA descriptor through the driver entry point (no -lcuda).
 int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType type, int rank,
                       void* base, const uint64_t* dims,
@@ -59,6 +61,7 @@ enum WatchdogCode : int32_t {
   kWaitAccum = 3,     // epilogue waiting for the accumulator
   kWaitAccumFree = 4, // MMA waiting for the epilogue to drain TMEM
   kWaitOther = 5,
+  kWaitProjection = 6, // K-slice projection waiting for its A rows
 };
 
 // 2 seconds of globaltimer nanoseconds; a healthy wait ends in microseconds.

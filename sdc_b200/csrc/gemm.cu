@@ -349,6 +349,9 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
     // read from global memory (hot in L2: the same column block is streaming
     // through this SM) and folded into fma chains with q_full.
     const int ct = threadIdx.x - 192;  // 0..127: rows ct and ct + 128 of the B tile
+    // q_full comes from the projection kernel this GEMM may overlap
+    // (programmatic dependent launch): wait for it to complete here only.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const float alpha = *p.alpha;
     const int num_slices = (p.k + kSliceK - 1) / kSliceK;
     const int64_t row_bytes = KIND == Kind::kFp8 ? p.k : p.k / 2;
@@ -454,18 +457,6 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
   }
 }
 
-int sm_count() {
-  static int cached[64] = {};
-  int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return 148;
-  if (cached[device] == 0) {
-    int count = 0;
-    if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 148;
-    cached[device] = count;
-  }
-  return cached[device];
-}
-
 template <Kind KIND, int C, bool BF16OUT, bool CHK>
 int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   const int64_t k_bytes = KIND == Kind::kFp8 ? g.k : g.k / 2;
@@ -543,8 +534,17 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
     if (device >= 0 && device < 64) configured[device] = true;
   }
   const int grid = std::min(p.num_tiles, sm_count());
-  kernel<<<grid, num_threads(CHK), smem, stream>>>(ta, tb, tsa, tsb, p);
-  SDC_CUDA_CHECK(cudaGetLastError());
+  cudaLaunchConfig_t config{};
+  config.gridDim = dim3(static_cast<unsigned>(grid));
+  config.blockDim = dim3(num_threads(CHK));
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attribute[1];
+  attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attribute[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attribute;
+  config.numAttrs = (CHK && g.dependent_launch) ? 1 : 0;
+  SDC_CUDA_CHECK(cudaLaunchKernelEx(&config, kernel, ta, tb, tsa, tsb, p));
   return SDC_OK;
 }
 
@@ -567,7 +567,7 @@ int dispatch_out(const GemmProblem& g, cudaStream_t stream) {
 int launch_gemm(const GemmProblem& g, cudaStream_t stream) {
   int rc = check_current_device();
   if (rc != SDC_OK) return rc;
-  if (g.channels > 0) {
+  if (g.channels > 0 && !g.flags_zeroed) {
     SDC_CUDA_CHECK(cudaMemsetAsync(g.hit, 0, sizeof(int32_t), stream));
     if (g.nonfinite != nullptr) SDC_CUDA_CHECK(cudaMemsetAsync(g.nonfinite, 0, sizeof(int32_t), stream));
   }

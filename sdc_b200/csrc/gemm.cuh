@@ -29,10 +29,15 @@ struct GemmProblem {
   const float* q_full;     // [K][C][2], from launch_projection
   float* predicted;        // [C, Tm, Np]
   float* magnitude;
+  // hit/nonfinite were already zeroed earlier on the stream.
+  bool flags_zeroed;
+  // Launch as a programmatic dependent of the kernel just before it on the
+  // stream (the K-slice projection): only the prediction warps wait for it.
+  bool dependent_launch;
 };
 
 // Launches the GEMM (and its fused epilogue) on `stream`. Zeroes hit/nonfinite
-// first. Returns an SDC_* status.
+// first unless flags_zeroed. Returns an SDC_* status.
 int launch_gemm(const GemmProblem& p, cudaStream_t stream);
 
 // Input-side checksum partials (predicted, magnitude), reference layouts.

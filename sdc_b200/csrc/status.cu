@@ -57,6 +57,21 @@ int check_current_device() {
   return rc;
 }
 
+int sm_count() {
+  constexpr int kMaxDevices = 64;
+  static std::atomic<int> cached[kMaxDevices] = {};
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return 148;
+  int count = cached[device].load(std::memory_order_relaxed);
+  if (count == 0) {
+    if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || count <= 0) {
+      return 148;
+    }
+    cached[device].store(count, std::memory_order_relaxed);
+  }
+  return count;
+}
+
 namespace {
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;

@@ -48,13 +48,15 @@ def _worker(rank, world, port, precision, results):
         out, report = execute_sharded(a[start:stop], b, precision, scaling, cfg)
         same = bool(torch.equal(out, full[start:stop]))
         clean = report.to_record()
-        row, col = 600, 77
-        bits = full[row, col].float().view(torch.int32).item()
-        bit = next(b for b in range(25, 30) if not bits & (1 << b))
+        # First element at or after (600, 77) with 4 <= |v| < 256: flipping
+        # exponent bit 27 scales it by 2^16 (large, finite, locatable).
+        flat = full.float().reshape(-1)[600 * n + 77:]
+        index = 600 * n + 77 + int(((flat.abs() >= 4) & (flat.abs() < 256)).nonzero()[0, 0])
+        row, col, bit = index // n, index % n, 27
         _, faulty = execute_sharded(a[start:stop], b, precision, scaling, cfg,
                                     {"location": "accumulator", "row": row, "col": col, "bit": bit})
         results[rank] = {"same": same, "clean_detected": clean["detected"], "record": faulty.to_record(),
-                         "rows": (start, stop)}
+                         "rows": (start, stop), "fault": [row, col]}
     except Exception:
         results[rank] = {"error": traceback.format_exc()}
     finally:
@@ -78,4 +80,4 @@ def test_sharded_native_rows_bit_exact_and_verdict_global(precision):
         assert "error" not in r, r.get("error")
         assert r["same"] and r["clean_detected"] is False
         rec = r["record"]
-        assert rec["detected"] is True and rec["located"] is True and rec["location"] == [600, 77]
+        assert rec["detected"] is True and rec["located"] is True and rec["location"] == r["fault"]

@@ -32,9 +32,16 @@ def _cfg(**changes):
             "on_error": "report", "atol": 1e-3, "rtol": 1e-4, "diagnostics": True, **changes}
 
 
-def _clear_exponent_bit(value):
-    bits = torch.tensor([value], dtype=torch.float32).view(torch.int32).item()
-    return next(b for b in range(25, 30) if not bits & (1 << b))
+def _fault_near(clean, row, col):
+    """The first output element at or after (row, col) (row-major order)
+    with 4 <= |v| < 256, and exponent bit 27: those values have exponent bits
+    26..29 clear, so the flip scales the element by 2^16 and the checksum
+    change is large, finite and locatable."""
+    values = clean.float().reshape(-1)
+    start = row * clean.shape[1] + col
+    ok = (values[start:].abs() >= 4) & (values[start:].abs() < 256)
+    index = start + int(ok.nonzero()[0, 0])
+    return index // clean.shape[1], index % clean.shape[1], 27
 
 
 @pytest.mark.parametrize("precision", ["fp8", "nvfp4"])
@@ -57,8 +64,7 @@ def test_native_fault_detected_located_and_repaired(precision, recovery):
     a, b = _operands(m, n, k, seed=9)
     prepared = PreparedGemm.prepare(a, b, precision, SCALING[precision])
     clean = prepared.raw_native()
-    row, col = 389, 201
-    bit = _clear_exponent_bit(clean[row, col].float().item())
+    row, col, bit = _fault_near(clean, 389, 201)
     fault = {"location": "accumulator", "row": row, "col": col, "bit": bit}
     output, report = execute_prepared(prepared, _cfg(locate=True, recovery=recovery, reference_layout="kslice"),
                                       fault)
@@ -77,11 +83,10 @@ def test_native_fault_detected_located_and_repaired(precision, recovery):
 def test_native_unrecovered_fault_raises(precision):
     a, b = _operands(256, 256, 256, seed=3)
     prepared = PreparedGemm.prepare(a, b, precision, SCALING[precision])
-    clean = prepared.raw_native()
-    bit = _clear_exponent_bit(clean[17, 33].float().item())
+    row, col, bit = _fault_near(prepared.raw_native(), 17, 33)
     with pytest.raises(AbftError) as error:
         execute_prepared(prepared, _cfg(on_error="raise"),
-                         {"location": "accumulator", "row": 17, "col": 33, "bit": bit})
+                         {"location": "accumulator", "row": row, "col": col, "bit": bit})
     assert error.value.report.detected and not error.value.report.recovered
 
 
@@ -89,9 +94,9 @@ def test_native_unrecovered_fault_raises(precision):
 def test_native_sum_policy_detects_without_location(precision):
     a, b = _operands(256, 320, 256, seed=4)
     prepared = PreparedGemm.prepare(a, b, precision, SCALING[precision])
-    bit = _clear_exponent_bit(prepared.raw_native()[5, 6].float().item())
+    row, col, bit = _fault_near(prepared.raw_native(), 5, 6)
     _, report = execute_prepared(prepared, _cfg(method="sum", locate=True),
-                                 {"location": "accumulator", "row": 5, "col": 6, "bit": bit})
+                                 {"location": "accumulator", "row": row, "col": col, "bit": bit})
     assert report.detected and not report.located and report.location.tolist() == [-1, -1]
     assert report.context["compiled_policy"]["id"] == 1
 
@@ -100,18 +105,18 @@ def test_native_sum_policy_detects_without_location(precision):
 def test_python_reference_implementation_agrees_with_native(precision):
     a, b = _operands(264, 272, 288, seed=11)
     prepared = PreparedGemm.prepare(a, b, precision, SCALING[precision])
-    bit = _clear_exponent_bit(prepared.raw_native()[100, 200].float().item())
-    fault = {"location": "accumulator", "row": 100, "col": 200, "bit": bit}
+    row, col, bit = _fault_near(prepared.raw_native(), 100, 200)
+    fault = {"location": "accumulator", "row": row, "col": col, "bit": bit}
     for layout in ("tile", "kslice"):
         native_out, native = execute_prepared(prepared, _cfg(locate=True, reference_layout=layout), fault)
         python_out, python = execute_prepared(prepared, _cfg(implementation="reference", reference_layout=layout),
                                               fault)
         assert torch.equal(native_out, python_out)
         assert bool(native.detected) == bool(python.detected) is True
-        assert native.location.tolist() == python.location.tolist() == [100, 200]
+        assert native.location.tolist() == python.location.tolist() == [row, col]
         # Totals are summed in a different order (serial vs torch.sum): equal
         # up to rounding, far below the detection threshold, off the faulty column.
-        clean_cols = torch.arange(prepared.n, device=DEV) != 200
+        clean_cols = torch.arange(prepared.n, device=DEV) != col
         diff = (native.residual - python.residual).abs()[:, clean_cols]
         assert (diff <= native.threshold[:, clean_cols]).all()
 
