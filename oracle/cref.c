@@ -112,18 +112,18 @@ int oracle_kslice_reference(int kind, const uint8_t* a, const uint8_t* sfa, cons
   const int64_t slices = (k + 63) / 64;
   float* qf = (float*)malloc(sizeof(float) * channels * 2 * k);
   if (!qf) return 1;
-  /* q over all rows in the K-slice kernel's order: 8 row bands of
-   * rb = ceil(m / 8) rows; in a band, 8 row lanes l each run an fma chain
-   * over rows band_start + l, + 8, ... (ascending); band = ((p_0 + p_1) + ...)
-   * + p_7 and q = ((band_0 + band_1) + ...) + band_7. */
-  const int64_t rb = (m + 7) / 8;
+  /* q over all rows in the GEMM prediction warps' order: bands of 512 rows;
+   * in a band, 8 row lanes l each run an fma chain over rows
+   * band_start + l, + 8, ... (ascending), combined as
+   * ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)); q = ((band_0 + band_1)
+   * + ...) + band_last. */
+  const int64_t bands = (m + 511) / 512;
   for (int c = 0; c < channels; ++c) {
     for (int64_t kk = 0; kk < k; ++kk) {
       float q[2] = {0.f, 0.f};
-      for (int b = 0; b < 8; ++b) {
-        const int64_t begin = b * rb < m ? b * rb : m;
-        const int64_t end = begin + rb < m ? begin + rb : m;
-        float band[2] = {0.f, 0.f};
+      for (int64_t b = 0; b < bands; ++b) {
+        const int64_t begin = b * 512, end = begin + 512 < m ? begin + 512 : m;
+        float lanes[2][8];
         for (int l = 0; l < 8; ++l) {
           float e = 0.f, g = 0.f;
           for (int64_t row = begin + l; row < end; row += 8) {
@@ -132,11 +132,14 @@ int oracle_kslice_reference(int kind, const uint8_t* a, const uint8_t* sfa, cons
             e = fmaf(wv, v, e);
             g = fmaf(fabsf(wv), fabsf(v), g);
           }
-          band[0] = l == 0 ? e : band[0] + e;
-          band[1] = l == 0 ? g : band[1] + g;
+          lanes[0][l] = e;
+          lanes[1][l] = g;
         }
-        q[0] = b == 0 ? band[0] : q[0] + band[0];
-        q[1] = b == 0 ? band[1] : q[1] + band[1];
+        for (int h = 0; h < 2; ++h) {
+          const float* p = lanes[h];
+          const float band = ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
+          q[h] = b == 0 ? band : q[h] + band;
+        }
       }
       qf[(c * 2 + 0) * k + kk] = q[0];
       qf[(c * 2 + 1) * k + kk] = q[1];

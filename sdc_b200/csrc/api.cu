@@ -122,19 +122,15 @@ int run_input_fused(GemmProblem g, float* predicted, float* magnitude, int layou
   SDC_REQUIRE(predicted != nullptr && magnitude != nullptr, "predicted/magnitude must not be null");
   const ReferenceProblem r = reference_problem(g, predicted, magnitude, layout, workspace, workspace_bytes);
   if (layout == SDC_LAYOUT_KSLICE) {
-    // Flags are zeroed before the projection so that the GEMM can follow it
-    // directly as a programmatic dependent launch.
-    int rc = check_current_device();
+    // Projection and prediction both run inside the GEMM's prediction warps.
+    int rc = check_problem(r);
     if (rc != SDC_OK) return rc;
-    SDC_CUDA_CHECK(cudaMemsetAsync(g.hit, 0, sizeof(int32_t), stream));
-    if (g.nonfinite != nullptr) SDC_CUDA_CHECK(cudaMemsetAsync(g.nonfinite, 0, sizeof(int32_t), stream));
-    rc = launch_projection(r, stream);
-    if (rc != SDC_OK) return rc;
-    g.q_full = kslice_q_full(r);
+    const KsliceScratch scratch = kslice_scratch(r);
+    g.q_full = scratch.q_full;
+    g.q_part = scratch.q_part;
+    g.grid_sync = scratch.grid_sync;
     g.predicted = predicted;
     g.magnitude = magnitude;
-    g.flags_zeroed = true;
-    g.dependent_launch = true;
     return launch_gemm(g, stream);
   }
   int rc = launch_projection(r, stream);

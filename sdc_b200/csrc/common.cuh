@@ -62,6 +62,7 @@ enum WatchdogCode : int32_t {
   kWaitAccumFree = 4, // MMA waiting for the epilogue to drain TMEM
   kWaitOther = 5,
   kWaitProjection = 6, // K-slice projection waiting for its A rows
+  kWaitGrid = 7,       // prediction warps waiting at the grid-wide barrier
 };
 
 // 2 seconds of globaltimer nanoseconds; a healthy wait ends in microseconds.

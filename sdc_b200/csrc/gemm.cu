@@ -17,12 +17,19 @@
 //               lanes, fixed-order sum across the four row quarters),
 //               non-finite check of the converted output, output store.
 //   warps 6-9   (K-slice layout only) input-side prediction, independent of
-//               the MMA pipeline: for the 64-wide K slices assigned to this
-//               tile's slot (slice % Tm == tile row), fma chains of the full-M
-//               projection q_c[k] (precomputed, tile_reference.cu) with
-//               B[n, k] and |q|, |B|. The slices are read from global memory,
-//               where the tile's column block is L2-hot; in total this is one
-//               extra L2 pass over B.
+//               the MMA pipeline, in three phases separated by grid-wide
+//               barriers (the launch is cooperative, so every CTA is
+//               resident; each wait is bounded):
+//                 1. projection partials of A: each warp takes (64-wide K
+//                    chunk, 512-row band) items and writes
+//                    part[band][k][c][h] = sum over the band's rows of
+//                    w_c[row] * A[row, k] (h = 0) and |w_c| |A| (h = 1);
+//                 2. q_full[k][c][h] = sum over bands (ascending);
+//                 3. for the 64-wide K slices assigned to each of this CTA's
+//                    tiles (slice % Tm == tile row), fma chains of q_full
+//                    with B[n, k] and |q|, |B| (B rows read from L2).
+//               In total one extra pass over A and one over B, overlapped
+//               with the tensor-core mainloop.
 // Epilogue semantics follow src/cutlass_gemm/csrc/abft/common/
 // sm120_epilogue.cuh:52-151 of the reference (inject after alpha, observe
 // before the output cast). Every wait is bounded (common.cuh).
@@ -69,8 +76,13 @@ struct Params {
   float* observed;
   int32_t* hit;
   int32_t padded_n;
-  const float* q_full;  // [K][C][2]: full-M projection (h=0) and magnitude (h=1)
-  const uint8_t* b;     // B operand rows (prediction warps read them directly)
+  float* q_full;        // [K_pad][C][2]: full-M projection (h=0) and magnitude (h=1)
+  float* q_part;        // [bands][K_pad][C][2]: per-band partials
+  uint32_t* grid_sync;  // arrival counter of the prediction warpgroups (zeroed per launch)
+  int32_t q_bands;
+  const uint8_t* a;     // A operand rows (projection) and B rows (prediction),
+  const uint8_t* sfa;   // read directly by the prediction warps
+  const uint8_t* b;
   const uint8_t* sfb;
   float* predicted;
   float* magnitude;
@@ -100,6 +112,39 @@ __device__ __forceinline__ float transpose_reduce32(float (&x)[32], int lane) {
     }
   }
   return x[0];
+}
+
+constexpr int kBandRows = 512;  // rows per projection band (K-slice layout)
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid-wide barrier of the prediction warpgroups (thread ct == 0 of each CTA
+// arrives; all 128 threads leave together). Bounded: on timeout the CTA's
+// abort flag and the watchdog are set. Returns false when aborted.
+__device__ __forceinline__ bool prediction_grid_barrier(uint32_t* counter, uint32_t target, int ct,
+                                                        volatile int32_t* abort_flag, int32_t* watchdog) {
+  named_barrier(2, 128);
+  if (ct == 0) {
+    __threadfence();
+    atomicAdd(counter, 1u);
+    const uint64_t start = global_ns();
+    while (ld_acquire_u32(counter) < target) {
+      if (*abort_flag) break;
+      if (global_ns() - start > kWaitLimitNs) {
+        atomicCAS(watchdog, 0, kWaitGrid);
+        *abort_flag = kWaitGrid;
+        break;
+      }
+      __nanosleep(256);
+    }
+    __threadfence();
+  }
+  named_barrier(2, 128);
+  return *abort_flag == 0;
 }
 
 // Scale-factor atom (32 rows x 16 bytes, contiguous) as a tcgen05.cp source.
@@ -349,13 +394,117 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
     // read from global memory (hot in L2: the same column block is streaming
     // through this SM) and folded into fma chains with q_full.
     const int ct = threadIdx.x - 192;  // 0..127: rows ct and ct + 128 of the B tile
-    // q_full comes from the projection kernel this GEMM may overlap
-    // (programmatic dependent launch): wait for it to complete here only.
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     const float alpha = *p.alpha;
     const int num_slices = (p.k + kSliceK - 1) / kSliceK;
     const int64_t row_bytes = KIND == Kind::kFp8 ? p.k : p.k / 2;
     const int64_t k_atoms = (p.k + 63) / 64;
+    const int64_t k_pad = static_cast<int64_t>(num_slices) * kSliceK;
+    // ---- phase 1: per-band projection partials. Lane = 4 * l + g: k-group g
+    // (16 consecutive k), row lane l (rows band_start + l, + 8, ... ascending);
+    // the 8 row lanes combine as ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)).
+    {
+      const int g = lane & 3, l = lane >> 2;
+      const int64_t items = static_cast<int64_t>(num_slices) * p.q_bands;
+      for (int64_t item = static_cast<int64_t>(blockIdx.x) * 4 + (warp - 6); item < items && !*abort_flag;
+           item += static_cast<int64_t>(gridDim.x) * 4) {
+        const int64_t chunk = item % num_slices, band = item / num_slices;
+        const int64_t k0 = chunk * kSliceK + g * 16;
+        // K % 16 == 0 (FP8) / % 32 == 0 (NVFP4): a group of 16 is all in or all out.
+        const bool k_in = k0 < p.k;
+        const int64_t row_end = min(static_cast<int64_t>(p.m), (band + 1) * kBandRows);
+        float2 enc[16], mg[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) enc[e] = mg[e] = make_float2(0.f, 0.f);
+        constexpr int kBatch = 4;
+        for (int64_t r0 = band * kBandRows + l; r0 < row_end; r0 += 8 * kBatch) {
+          uint4 raw[kBatch];
+          uint32_t sfv[kBatch];
+          float w[kBatch][C];
+#pragma unroll
+          for (int i = 0; i < kBatch; ++i) {
+            const int64_t row = r0 + 8 * i;
+            const bool row_in = row < row_end;
+            const bool in = row_in && k_in;
+            if constexpr (KIND == Kind::kFp8) {
+              raw[i] = in ? __ldg(reinterpret_cast<const uint4*>(p.a + row * row_bytes + k0)) : make_uint4(0, 0, 0, 0);
+            } else {
+              const uint2 u = in ? __ldg(reinterpret_cast<const uint2*>(p.a + row * row_bytes + k0 / 2))
+                                 : make_uint2(0, 0);
+              raw[i] = make_uint4(u.x, u.y, 0, 0);
+              const int64_t off = ((row >> 7) * k_atoms + (k0 >> 6)) * 512 + (row & 31) * 16 +
+                                  ((row >> 5) & 3) * 4 + ((k0 >> 4) & 3);
+              sfv[i] = in ? __ldg(p.sfa + off) : 0u;
+            }
+#pragma unroll
+            for (int c = 0; c < C; ++c) w[i][c] = row_in ? __ldg(p.weights + static_cast<int64_t>(c) * p.m + row) : 0.f;
+          }
+#pragma unroll
+          for (int i = 0; i < kBatch; ++i) {
+            if (r0 + 8 * i >= row_end) break;
+            float v[16];
+            if constexpr (KIND == Kind::kFp8) {
+              const uint32_t words[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 lo = e4m3x2_to_float2(words[j] & 0xFFFFu), hi = e4m3x2_to_float2(words[j] >> 16);
+                v[4 * j] = lo.x; v[4 * j + 1] = lo.y; v[4 * j + 2] = hi.x; v[4 * j + 3] = hi.y;
+              }
+            } else {
+              float lo8[8], hi8[8];
+              e2m1x8_to_float(raw[i].x, lo8);
+              e2m1x8_to_float(raw[i].y, hi8);
+              const float scale = decode_e4m3(sfv[i]);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                v[e] = lo8[e] * scale;
+                v[8 + e] = hi8[e] * scale;
+              }
+            }
+            const float2 wv = make_float2(w[i][0], C == 2 ? w[i][C - 1] : 0.f);
+            const float2 wa = make_float2(fabsf(wv.x), fabsf(wv.y));
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              enc[e] = fma2(wv, make_float2(v[e], v[e]), enc[e]);
+              const float av = fabsf(v[e]);
+              mg[e] = fma2(wa, make_float2(av, av), mg[e]);
+            }
+          }
+        }
+#pragma unroll
+        for (int offset = 4; offset <= 16; offset <<= 1) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            enc[e].x += __shfl_xor_sync(0xffffffffu, enc[e].x, offset);
+            enc[e].y += __shfl_xor_sync(0xffffffffu, enc[e].y, offset);
+            mg[e].x += __shfl_xor_sync(0xffffffffu, mg[e].x, offset);
+            mg[e].y += __shfl_xor_sync(0xffffffffu, mg[e].y, offset);
+          }
+        }
+        if (l == 0) {
+          float* dst = p.q_part + (band * k_pad + chunk * kSliceK + g * 16) * C * 2;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            if constexpr (C == 2) {
+              reinterpret_cast<float4*>(dst)[e] = make_float4(enc[e].x, mg[e].x, enc[e].y, mg[e].y);
+            } else {
+              reinterpret_cast<float2*>(dst)[e] = make_float2(enc[e].x, mg[e].x);
+            }
+          }
+        }
+      }
+    }
+    // ---- phase 2: q_full = sum over bands (ascending) ----
+    if (prediction_grid_barrier(p.grid_sync, gridDim.x, ct, abort_flag, p.watchdog)) {
+      const int64_t entries = k_pad * C * 2;
+      for (int64_t e = static_cast<int64_t>(blockIdx.x) * 128 + ct; e < entries;
+           e += static_cast<int64_t>(gridDim.x) * 128) {
+        float acc = __ldcg(p.q_part + e);
+        for (int b = 1; b < p.q_bands; ++b) acc += __ldcg(p.q_part + b * entries + e);
+        p.q_full[e] = acc;
+      }
+    }
+    prediction_grid_barrier(p.grid_sync, 2 * gridDim.x, ct, abort_flag, p.watchdog);
+    // ---- phase 3: predictions of this CTA's tiles ----
     for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
       int mt, nt;
       tile_coords(t, p, mt, nt);
@@ -393,11 +542,12 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const float* qk = p.q_full + static_cast<int64_t>(k0 + e0 + e) * C * 2;
+            // q_full was written by other CTAs during this launch: read through L2.
             if constexpr (C == 2) {
-              const float4 f = __ldg(reinterpret_cast<const float4*>(qk));
+              const float4 f = __ldcg(reinterpret_cast<const float4*>(qk));
               qv[e][0][0] = f.x; qv[e][0][1] = f.y; qv[e][1][0] = f.z; qv[e][1][1] = f.w;
             } else {
-              const float2 f = __ldg(reinterpret_cast<const float2*>(qk));
+              const float2 f = __ldcg(reinterpret_cast<const float2*>(qk));
               qv[e][0][0] = f.x; qv[e][0][1] = f.y;
             }
           }
@@ -518,6 +668,11 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   p.hit = g.hit;
   p.padded_n = static_cast<int32_t>(g.padded_n);
   p.q_full = g.q_full;
+  p.q_part = g.q_part;
+  p.grid_sync = g.grid_sync;
+  p.q_bands = static_cast<int32_t>(ceil_div(g.m, kBandRows));
+  p.a = g.a;
+  p.sfa = g.sfa;
   p.b = g.b;
   p.sfb = g.sfb;
   p.predicted = g.predicted;
@@ -539,11 +694,12 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   config.blockDim = dim3(num_threads(CHK));
   config.dynamicSmemBytes = smem;
   config.stream = stream;
+  // The prediction warps synchronise across CTAs: every CTA must be resident.
   cudaLaunchAttribute attribute[1];
-  attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attribute[0].val.programmaticStreamSerializationAllowed = 1;
+  attribute[0].id = cudaLaunchAttributeCooperative;
+  attribute[0].val.cooperative = 1;
   config.attrs = attribute;
-  config.numAttrs = (CHK && g.dependent_launch) ? 1 : 0;
+  config.numAttrs = CHK ? 1 : 0;
   SDC_CUDA_CHECK(cudaLaunchKernelEx(&config, kernel, ta, tb, tsa, tsb, p));
   return SDC_OK;
 }
@@ -567,9 +723,10 @@ int dispatch_out(const GemmProblem& g, cudaStream_t stream) {
 int launch_gemm(const GemmProblem& g, cudaStream_t stream) {
   int rc = check_current_device();
   if (rc != SDC_OK) return rc;
-  if (g.channels > 0 && !g.flags_zeroed) {
+  if (g.channels > 0) {
     SDC_CUDA_CHECK(cudaMemsetAsync(g.hit, 0, sizeof(int32_t), stream));
     if (g.nonfinite != nullptr) SDC_CUDA_CHECK(cudaMemsetAsync(g.nonfinite, 0, sizeof(int32_t), stream));
+    if (g.grid_sync != nullptr) SDC_CUDA_CHECK(cudaMemsetAsync(g.grid_sync, 0, sizeof(uint32_t), stream));
   }
   if (g.kind == Kind::kFp8) {
     if (g.channels == 0) return dispatch_out<Kind::kFp8, 0>(g, stream);

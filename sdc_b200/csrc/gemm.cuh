@@ -26,14 +26,13 @@ struct GemmProblem {
   int32_t* hit;
   int64_t padded_n;
   // K-slice input prediction fused into the GEMM (all null: not fused).
-  const float* q_full;     // [K][C][2], from launch_projection
+  // Scratch from kslice_scratch(): q_full [K_pad][C][2], per-band partials
+  // and the grid-barrier counter (zeroed by launch_gemm).
+  float* q_full;
+  float* q_part;
+  uint32_t* grid_sync;
   float* predicted;        // [C, Tm, Np]
   float* magnitude;
-  // hit/nonfinite were already zeroed earlier on the stream.
-  bool flags_zeroed;
-  // Launch as a programmatic dependent of the kernel just before it on the
-  // stream (the K-slice projection): only the prediction warps wait for it.
-  bool dependent_launch;
 };
 
 // Launches the GEMM (and its fused epilogue) on `stream`. Zeroes hit/nonfinite
@@ -60,13 +59,18 @@ struct ReferenceProblem {
 };
 
 size_t reference_workspace_bytes(int channels, int64_t m, int64_t n, int64_t k, int layout);
-// Per-tile projections q[c][h][t][k] of A (and, for the K-slice layout, their
-// ascending-tile sum q_full[k][c][h] at the end of the workspace). Must run
-// before the GEMM when the prediction is fused into it.
+// Checks the layout id and the workspace size/alignment of `p`.
+int check_problem(const ReferenceProblem& p);
+// TILE layout: per-tile projections q[c][h][t][k] of A (before the GEMM) and
+// their propagation against B on CUDA cores (after it).
 int launch_projection(const ReferenceProblem& p, cudaStream_t stream);
-// TILE layout: per-tile propagation against B on CUDA cores (after projection).
 int launch_tile_propagate(const ReferenceProblem& p, cudaStream_t stream);
-// Device pointer of q_full inside the workspace of a K-slice problem.
-const float* kslice_q_full(const ReferenceProblem& p);
+// K-slice layout: the GEMM's scratch inside the workspace.
+struct KsliceScratch {
+  uint32_t* grid_sync;  // 256 bytes, zeroed by launch_gemm
+  float* q_full;        // [K_pad][C][2]
+  float* q_part;        // [ceil(M / 512)][K_pad][C][2]
+};
+KsliceScratch kslice_scratch(const ReferenceProblem& p);
 
 }  // namespace sdc

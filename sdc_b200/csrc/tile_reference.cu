@@ -15,17 +15,11 @@
 // KSLICE layout (fast path). q is the projection over ALL rows, and the
 // 64-wide K slice s contributes to slot s % Tm:
 //   predicted[c, t, n] = alpha * sum_{s % Tm == t} sum_{k in s} q_c[k] B[n,k]
-// (fma chain over slices, then k, ascending). The propagation runs inside the
-// GEMM (gemm.cu, prediction warps); this file only produces q, in one kernel
-// (q_kslice) that the GEMM overlaps through programmatic dependent launch:
-// the GEMM's mainloop starts while q is still being computed and only its
-// prediction warps wait for it. Summation order of q (fixed, so results are
-// deterministic): for each k, 16 row lanes l each run an fma chain over rows
-// l, l + 16, l + 32, ... (ascending), then the lanes are added pairwise
-// (l + 8, then + 4, + 2, + 1). The per-column sum over slots equals the TILE
-// layout's sum over tiles up to fp32 rounding, so finalize is unchanged.
+// Both q and the propagation run inside the GEMM (gemm.cu, prediction
+// warps); this file only sizes and lays out their scratch. The per-column
+// sum over slots equals the TILE layout's sum over tiles up to fp32
+// rounding, so finalize is unchanged.
 #include <algorithm>
-#include <atomic>
 
 #include "gemm.cuh"
 
@@ -136,202 +130,6 @@ __global__ void __launch_bounds__(kRefThreads)
   }
 }
 
-// q_full[(k * C + c) * 2 + h] over all M rows (h = 0 projection, 1 magnitude),
-// zero for K <= k < K rounded up to 64. A cluster of kQBands CTAs owns one
-// 256-wide K chunk; CTA b of the cluster owns row band b (rows
-// [b * rb, (b + 1) * rb), rb = ceil(M / kQBands)), streamed through shared
-// memory by TMA in 128-row segments (double-buffered; 256 contiguous bytes
-// of each FP8 row, 128 of each NVFP4 row). Thread t owns k-group t % 32
-// (8 consecutive k) and row lane l = t / 32 (its warp), an fma chain over
-// rows band_start + l, + 8, + 16, ... (ascending). Fixed combine order:
-//   band:  B = ((p_0 + p_1) + p_2) + ... + p_7     (over the row lanes)
-//   q:     ((B_0 + B_1) + B_2) + ... + B_7         (CTA 0 reads the bands'
-//                                                   partials through
-//                                                   distributed shared memory)
-constexpr int kQThreads = 256;
-constexpr int kQLanes = kQThreads / 32;  // row lanes = warps
-constexpr int kQChunkK = 256;
-constexpr int kQBands = 8;     // cluster size
-constexpr int kQSegRows = 64;  // rows per TMA segment
-constexpr int kQStages = 4;    // segments in flight per CTA
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ float4 ld_cluster_f32x4(const float* local, uint32_t rank) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(remote)
-               : "memory");
-  return v;
-}
-
-template <Kind KIND>
-struct QShared {
-  static constexpr int kRowBytes = KIND == Kind::kFp8 ? kQChunkK : kQChunkK / 2;
-  static constexpr int kSegBytes = kQSegRows * kRowBytes;
-  static constexpr int kPartFloats = kQLanes * kQChunkK * 4;  // [row lane][k * 4 + c * 2 + h]
-  // The row-lane partials reuse the segment ring once all rows are consumed.
-  static constexpr int kRingBytes =
-      kQStages * kSegBytes > kPartFloats * 4 ? kQStages * kSegBytes : kPartFloats * 4;
-  uint8_t ring[kRingBytes];
-  uint64_t bar[kQStages];
-  int32_t abort_flag;
-  __device__ uint8_t* seg(int s) { return ring + (s % kQStages) * kSegBytes; }
-  __device__ float* part(int lane) { return reinterpret_cast<float*>(ring) + lane * kQChunkK * 4; }
-};
-
-template <Kind KIND, int C>
-__global__ void __cluster_dims__(kQBands, 1, 1) __launch_bounds__(kQThreads)
-    q_kslice(const __grid_constant__ CUtensorMap tm_a, const uint8_t* sfa, int64_t m, int64_t k,
-             const float* weights, float* q_full, int32_t* watchdog) {
-  // Let the dependent GEMM launch as SMs free up: it needs q only in its
-  // prediction warps, which wait for this grid to complete.
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  using Shared = QShared<KIND>;
-  extern __shared__ __align__(128) uint8_t q_smem_raw[];
-  Shared& sh = *reinterpret_cast<Shared*>(q_smem_raw);
-  const int t = threadIdx.x;
-  const int g = t % 32;
-  const int lane_row = t / 32;
-  const uint32_t band = cluster_rank();
-  const int64_t chunk = blockIdx.x / kQBands;
-  const int64_t rb = (m + kQBands - 1) / kQBands;
-  const int64_t row_begin = band * rb < m ? band * rb : m;
-  const int64_t row_end = row_begin + rb < m ? row_begin + rb : m;
-  const int segments = static_cast<int>((row_end - row_begin + kQSegRows - 1) / kQSegRows);
-  const int64_t k_atoms = (k + 63) / 64;
-  const int64_t kg = chunk * kQChunkK + g * 8;  // first k of this thread's group
-  if (t == 0) {
-    for (int i = 0; i < kQStages; ++i) mbar_init(&sh.bar[i], 1);
-    sh.abort_flag = 0;
-    fence_barrier_init();
-  }
-  __syncthreads();
-  auto issue = [&](int s) {
-    mbar_arrive_expect_tx(&sh.bar[s % kQStages], Shared::kSegBytes);
-    tma_load_2d(sh.seg(s), &tm_a, &sh.bar[s % kQStages], static_cast<int32_t>(chunk * Shared::kRowBytes),
-                static_cast<int32_t>(row_begin + static_cast<int64_t>(s) * kQSegRows));
-  };
-  int issued = segments < kQStages ? segments : kQStages, consumed = 0;
-  if (t == 0) {
-    for (int s = 0; s < issued; ++s) issue(s);
-  }
-  float2 enc[8], mag[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) enc[e] = mag[e] = make_float2(0.f, 0.f);
-  for (int s = 0; s < segments; ++s) {
-    const bool ok = mbar_wait(&sh.bar[s % kQStages], (s / kQStages) & 1, kWaitProjection, &sh.abort_flag,
-                              watchdog);
-    if (__syncthreads_or(!ok)) break;
-    ++consumed;
-    const uint8_t* buf = sh.seg(s);
-    const int64_t seg_row0 = row_begin + static_cast<int64_t>(s) * kQSegRows + lane_row;
-    // All of this segment's per-row weights (and NVFP4 block scales) are
-    // requested up front, so their latency is paid once per segment.
-    constexpr int kRows = kQSegRows / kQLanes;
-    float w[kRows][C];
-    uint32_t sfv[KIND == Kind::kFp8 ? 1 : kRows];
-#pragma unroll
-    for (int i = 0; i < kRows; ++i) {
-      const int64_t row = seg_row0 + i * kQLanes;
-      const bool in = row < row_end;
-#pragma unroll
-      for (int c = 0; c < C; ++c) w[i][c] = in ? __ldg(weights + c * m + row) : 0.f;
-      if constexpr (KIND == Kind::kNvf4) sfv[i] = in && kg < k ? __ldg(sfa + sf_off(row, kg >> 4, k_atoms)) : 0u;
-    }
-#pragma unroll
-    for (int i = 0; i < kRows; ++i) {
-      const int r = lane_row + i * kQLanes;
-      if (seg_row0 + i * kQLanes >= row_end) break;
-      float v[8];
-      if constexpr (KIND == Kind::kFp8) {
-        const uint2 u = *reinterpret_cast<const uint2*>(buf + r * Shared::kRowBytes + g * 8);
-        const float2 v01 = e4m3x2_to_float2(u.x & 0xFFFFu), v23 = e4m3x2_to_float2(u.x >> 16);
-        const float2 v45 = e4m3x2_to_float2(u.y & 0xFFFFu), v67 = e4m3x2_to_float2(u.y >> 16);
-        v[0] = v01.x; v[1] = v01.y; v[2] = v23.x; v[3] = v23.y;
-        v[4] = v45.x; v[5] = v45.y; v[6] = v67.x; v[7] = v67.y;
-      } else {
-        const uint32_t u = *reinterpret_cast<const uint32_t*>(buf + r * Shared::kRowBytes + g * 4);
-        const float scale = decode_e4m3(sfv[i]);
-        e2m1x8_to_float(u, v);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] *= scale;
-      }
-      const float2 wv = make_float2(w[i][0], C == 2 ? w[i][C - 1] : 0.f);
-      const float2 wa = make_float2(fabsf(wv.x), fabsf(wv.y));
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        enc[e] = fma2(wv, make_float2(v[e], v[e]), enc[e]);
-        const float av = fabsf(v[e]);
-        mag[e] = fma2(wa, make_float2(av, av), mag[e]);
-      }
-    }
-    // Every thread is done with this buffer: refill it kQStages segments ahead.
-    __syncthreads();
-    if (issued < segments) {
-      if (t == 0) issue(issued);
-      ++issued;
-    }
-  }
-  if (issued > consumed && t == 0) {
-    // Aborted with loads in flight: give them a bounded chance to land
-    // before this CTA's shared memory is reused or goes away.
-    int32_t drain = 0;
-    for (int s = consumed; s < issued; ++s) {
-      mbar_wait(&sh.bar[s % kQStages], (s / kQStages) & 1, kWaitProjection, &drain, watchdog);
-    }
-  }
-  __syncthreads();
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    *reinterpret_cast<float4*>(sh.part(lane_row) + (g * 8 + e) * 4) =
-        make_float4(enc[e].x, mag[e].x, enc[e].y, mag[e].y);
-  }
-  __syncthreads();
-  // Band partial over the row lanes, in place in part(0); thread t owns
-  // entries 4t .. 4t + 3.
-  {
-    float4 acc = *reinterpret_cast<const float4*>(sh.part(0) + 4 * t);
-#pragma unroll
-    for (int l = 1; l < kQLanes; ++l) {
-      const float4 x = *reinterpret_cast<const float4*>(sh.part(l) + 4 * t);
-      acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
-    }
-    *reinterpret_cast<float4*>(sh.part(0) + 4 * t) = acc;
-  }
-  cluster_sync_all();
-  if (band == 0) {
-    float4 acc = *reinterpret_cast<const float4*>(sh.part(0) + 4 * t);
-    for (uint32_t b = 1; b < kQBands; ++b) {
-      const float4 x = ld_cluster_f32x4(sh.part(0) + 4 * t, b);
-      acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
-    }
-    // Entry 4t + j is (k = t, c = j / 2, h = j % 2) of this chunk.
-    const int64_t kk = chunk * kQChunkK + t;
-    if (kk < (k + 63) / 64 * 64) {
-      if constexpr (C == 2) {
-        *reinterpret_cast<float4*>(q_full + kk * 4) = acc;
-      } else {
-        *reinterpret_cast<float2*>(q_full + kk * 2) = make_float2(acc.x, acc.y);
-      }
-    }
-  }
-  // No CTA leaves while CTA 0 may still read its shared memory.
-  cluster_sync_all();
-}
-
-template <Kind KIND>
-constexpr int q_smem_bytes() { return static_cast<int>(sizeof(QShared<KIND>)) + 128; }
-
 // Loads the B operand values of columns k0..k0+63 of `row` (k0 % 64 == 0).
 template <Kind KIND>
 __device__ __forceinline__ void load_b_chunk(const uint8_t* b, const uint8_t* sfb, int64_t row,
@@ -437,35 +235,6 @@ int64_t q_floats(int channels, int64_t m, int64_t k) { return static_cast<int64_
 template <Kind KIND, int C>
 int projection_impl(const ReferenceProblem& p, cudaStream_t stream) {
   float* q = static_cast<float*>(p.workspace);
-  if (p.layout == SDC_LAYOUT_KSLICE) {
-    // Keep SMs configured for the GEMM's shared memory (a carveout change
-    // would make the GEMM CTAs that follow wait for the SM to drain).
-    static std::atomic<int> configured[64] = {};
-    int device = 0;
-    SDC_CUDA_CHECK(cudaGetDevice(&device));
-    constexpr int smem = q_smem_bytes<KIND>();
-    if (device < 0 || device >= 64 || configured[device].load(std::memory_order_relaxed) == 0) {
-      SDC_CUDA_CHECK(cudaFuncSetAttribute(q_kslice<KIND, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      SDC_CUDA_CHECK(cudaFuncSetAttribute(q_kslice<KIND, C>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                          cudaSharedmemCarveoutMaxShared));
-      if (device >= 0 && device < 64) configured[device].store(1, std::memory_order_relaxed);
-    }
-    CUtensorMap tm{};
-    const int64_t row_bytes = KIND == Kind::kFp8 ? p.k : p.k / 2;
-    const uint64_t dims[2] = {static_cast<uint64_t>(row_bytes), static_cast<uint64_t>(p.m)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(row_bytes)};
-    const uint32_t box[2] = {static_cast<uint32_t>(QShared<KIND>::kRowBytes), static_cast<uint32_t>(kQSegRows)};
-    int rc = encode_tensor_map(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(p.a), dims, strides,
-                               box, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc != SDC_OK) return rc;
-    int32_t* watchdog = watchdog_ptr();
-    if (watchdog == nullptr) return fail(SDC_ERR_CUDA, "watchdog symbol unavailable");
-    const int64_t grid = ceil_div(p.k, kQChunkK) * kQBands;
-    q_kslice<KIND, C><<<static_cast<unsigned>(grid), kQThreads, smem, stream>>>(tm, p.sfa, p.m, p.k, p.weights,
-                                                                                 q, watchdog);
-    SDC_CUDA_CHECK(cudaGetLastError());
-    return SDC_OK;
-  }
   const int64_t tiles_m = ceil_div(p.m, kTileRows);
   q_encode<KIND, C><<<dim3(static_cast<unsigned>(ceil_div(p.k, kRefThreads * 8)), static_cast<unsigned>(tiles_m)),
                       kRefThreads, 0, stream>>>(p.a, p.sfa, p.m, p.k, p.weights, q, tiles_m);
@@ -485,6 +254,30 @@ int tile_propagate_impl(const ReferenceProblem& p, cudaStream_t stream) {
   return SDC_OK;
 }
 
+
+}  // namespace
+
+namespace {
+constexpr int64_t kSyncBytes = 256;
+constexpr int64_t kBandRows = 512;  // rows per projection band (gemm.cu)
+int64_t kslice_q_floats(int channels, int64_t k) { return static_cast<int64_t>(channels) * 2 * ceil_div(k, 64) * 64; }
+}  // namespace
+
+size_t reference_workspace_bytes(int channels, int64_t m, int64_t n, int64_t k, int layout) {
+  (void)n;
+  if (layout == SDC_LAYOUT_KSLICE) {
+    const int64_t floats = kslice_q_floats(channels, k) * (1 + ceil_div(m, kBandRows));
+    return static_cast<size_t>(kSyncBytes + floats * static_cast<int64_t>(sizeof(float)));
+  }
+  return static_cast<size_t>(q_floats(channels, m, k)) * sizeof(float);
+}
+
+KsliceScratch kslice_scratch(const ReferenceProblem& p) {
+  uint8_t* base = static_cast<uint8_t*>(p.workspace);
+  float* q_full = reinterpret_cast<float*>(base + kSyncBytes);
+  return {reinterpret_cast<uint32_t*>(base), q_full, q_full + kslice_q_floats(p.channels, p.k)};
+}
+
 int check_problem(const ReferenceProblem& p) {
   if (p.layout != SDC_LAYOUT_TILE && p.layout != SDC_LAYOUT_KSLICE) {
     return fail(SDC_ERR_INVALID, "unknown ABFT reference layout");
@@ -499,16 +292,6 @@ int check_problem(const ReferenceProblem& p) {
   return SDC_OK;
 }
 
-}  // namespace
-
-size_t reference_workspace_bytes(int channels, int64_t m, int64_t n, int64_t k, int layout) {
-  (void)n;
-  const int64_t floats = layout == SDC_LAYOUT_KSLICE ? static_cast<int64_t>(channels) * 2 * ceil_div(k, 64) * 64
-                                                     : q_floats(channels, m, k);
-  return static_cast<size_t>(floats) * sizeof(float);
-}
-
-const float* kslice_q_full(const ReferenceProblem& p) { return static_cast<const float*>(p.workspace); }
 
 int launch_projection(const ReferenceProblem& p, cudaStream_t stream) {
   int rc = check_problem(p);
