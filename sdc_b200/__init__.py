@@ -1,10 +1,12 @@
 """sdc_b200 — B200-native (sm_100a) ABFT FP8/NVFP4 GEMM path of meiyou666/SDC.
 
-Importing the package loads the native libraries built in-tree by
-``sdc_b200._build``: ``libsdc_b200.so`` (kernels + C ABI, include/sdc_b200.h)
-and ``_sdc_ops.so`` (the ``torch.ops.sdc_cutlass`` operator library with the
-reference's schemas). There is no CPU or pure-PyTorch fallback: if the
-libraries are missing, import fails with the build command to run.
+The native libraries built in-tree by ``sdc_b200._build`` are loaded on first
+use of ``sdc_b200.ops`` or ``require_device`` (the ``gemm`` and ``abft``
+modules use them at import): ``libsdc_b200.so`` (kernels + C ABI,
+include/sdc_b200.h) and ``_sdc_ops.so`` (the ``torch.ops.sdc_cutlass``
+operator library with the reference's schemas). There is no CPU or
+pure-PyTorch fallback: if the libraries are missing, that first use raises
+with the build command to run.
 
 Subpackages mirror the reference's Python API for this path:
   sdc_b200.gemm   <- src/cutlass_gemm (quantize, dequantize, backend.gemm)
@@ -49,5 +51,11 @@ def require_device(device) -> None:
     load()
 
 
-load()
-ops = torch.ops.sdc_cutlass
+def __getattr__(name):
+    # ``sdc_b200.ops`` loads the libraries on first use (and raises with the
+    # build command if they are missing); importing the package alone does
+    # not, so ``python -m sdc_b200._build`` works on a fresh checkout.
+    if name == "ops":
+        load()
+        return torch.ops.sdc_cutlass
+    raise AttributeError(f"module 'sdc_b200' has no attribute {name!r}")

@@ -64,8 +64,9 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_columns(FinalizePar
   if (col < p.n) {
     const int64_t base = static_cast<int64_t>(channel) * p.m_tiles * p.padded_n + col;
     float observed = 0.f, predicted = 0.f, magnitude = 0.f;
-    // Loads of 16 tiles are issued before their (ordered) adds.
-    constexpr int kBatch = 16;
+    // Loads of 32 tiles (three planes) are issued before their ordered adds,
+    // so a column costs ceil(Tm / 32) memory latencies.
+    constexpr int kBatch = 32;
     for (int64_t t0 = 0; t0 < p.m_tiles; t0 += kBatch) {
       float o[kBatch], pr[kBatch], mg[kBatch];
 #pragma unroll

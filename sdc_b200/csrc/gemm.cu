@@ -57,17 +57,28 @@ constexpr int kSfaBytes = 4 * 512;
 constexpr int kSfbBytes = 2 * 4 * 512;
 constexpr int kRedFloats = kChunks * 4 * 2 * 32;
 
-__host__ __device__ constexpr int stage_bytes(Kind k) {
-  return kABytes + kBBytes + (k == Kind::kNvf4 ? kSfaBytes + kSfbBytes : 0);
+// CTA pairs (FP8): each CTA stages its 128 rows of A and 128 of the tile's
+// 256 B rows; one cta_group::2 MMA covers the 256 x 256 pair tile.
+constexpr int kPairStages = 6;
+__host__ __device__ constexpr int stage_bytes(Kind k, bool pair = false) {
+  return pair ? kABytes + kBBytes / 2 : kABytes + kBBytes + (k == Kind::kNvf4 ? kSfaBytes + kSfbBytes : 0);
 }
-__host__ __device__ constexpr int smem_bytes(Kind k) {
-  return 1024 + kStages * stage_bytes(k) + kRedFloats * 4 + 256;
+__host__ __device__ constexpr int num_stages(bool pair) { return pair ? kPairStages : kStages; }
+__host__ __device__ constexpr int smem_bytes(Kind k, bool pair = false) {
+  return 1024 + num_stages(pair) * stage_bytes(k, pair) + kRedFloats * 4 + 256;
 }
 __host__ __device__ constexpr int num_acc(Kind k) { return k == Kind::kFp8 ? 2 : 1; }
-__host__ __device__ constexpr int num_threads(bool chk) { return chk ? 320 : 192; }
+// Warps 0 (TMA) and 1 (MMA) run on SM sub-partitions 0 and 1 (warp % 4);
+// every other warp there steals their issue slots. The prediction warps
+// therefore sit on sub-partitions 2 and 3 only: warps 6, 7, 10, 11 (warps 8
+// and 9 exit at once).
+__host__ __device__ constexpr int num_threads(bool chk) { return chk ? 384 : 192; }
+__device__ __forceinline__ bool is_prediction_warp(int warp) { return warp == 6 || warp == 7 || warp >= 10; }
+__device__ __forceinline__ int prediction_index(int warp) { return warp < 8 ? warp - 6 : warp - 8; }
 
 struct Params {
   int32_t m, n, k, num_kb, tiles_m, tiles_n, num_tiles;
+  int32_t num_work;  // tiles, or 256-row pair tiles when CTAs are paired
   const float* alpha;
   void* d;
   const float* weights;
@@ -89,14 +100,28 @@ struct Params {
   int32_t* watchdog;
 };
 
-__device__ __forceinline__ void tile_coords(int t, const Params& p, int& mt, int& nt) {
-  const int group_tiles = kGroupM * p.tiles_n;
+__device__ __forceinline__ void raster(int t, int rows, int group_rows, int tiles_n, int& r, int& nt) {
+  const int group_tiles = group_rows * tiles_n;
   const int group = t / group_tiles;
-  const int first_m = group * kGroupM;
-  const int gm = min(kGroupM, p.tiles_m - first_m);
+  const int first = group * group_rows;
+  const int gm = min(group_rows, rows - first);
   const int in_group = t - group * group_tiles;
-  mt = first_m + in_group % gm;
+  r = first + in_group % gm;
   nt = in_group / gm;
+}
+
+// Work item -> this CTA's (M-tile, N-tile). With CTA pairs an item is a
+// 256-row pair tile and the CTA of rank r owns its 128-row half r (which may
+// lie beyond M when M % 256 <= 128).
+template <bool PAIR>
+__device__ __forceinline__ void work_coords(int w, const Params& p, uint32_t rank, int& mt, int& nt) {
+  if constexpr (PAIR) {
+    int mt2;
+    raster(w, (p.tiles_m + 1) / 2, kGroupM / 2, p.tiles_n, mt2, nt);
+    mt = 2 * mt2 + static_cast<int>(rank);
+  } else {
+    raster(w, p.tiles_m, kGroupM, p.tiles_n, mt, nt);
+  }
 }
 
 // Lane j of the warp returns sum over the 32 lanes of x[j] (x is consumed).
@@ -150,35 +175,43 @@ __device__ __forceinline__ bool prediction_grid_barrier(uint32_t* counter, uint3
 // Scale-factor atom (32 rows x 16 bytes, contiguous) as a tcgen05.cp source.
 __device__ __forceinline__ uint64_t sf_desc(uint32_t addr) { return smem_desc(addr, 0, 128, 0); }
 
-template <Kind KIND, int C, bool BF16OUT, bool CHK>
+template <Kind KIND, int C, bool BF16OUT, bool CHK, bool PAIR>
 __global__ void __launch_bounds__(num_threads(CHK), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ CUtensorMap tm_sfa,
                 const __grid_constant__ CUtensorMap tm_sfb, const Params p) {
-  constexpr int kStageBytes = stage_bytes(KIND);
+  static_assert(!PAIR || KIND == Kind::kFp8, "CTA pairs are built for FP8 only");
+  constexpr int kS = num_stages(PAIR);
+  constexpr int kStageBytes = stage_bytes(KIND, PAIR);
   constexpr int kAcc = num_acc(KIND);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  float* red = reinterpret_cast<float*>(smem + kStages * kStageBytes);
+  float* red = reinterpret_cast<float*>(smem + kS * kStageBytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(red + kRedFloats);
-  uint64_t* empty = full + kStages;
-  uint64_t* acc_full = empty + kStages;
+  uint64_t* empty = full + kS;
+  uint64_t* acc_full = empty + kS;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // CTA pairs: rank 0 (the leader) issues the MMAs for both CTAs; its
+  // barriers count both CTAs' loads and epilogues.
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int work_first = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int work_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kS; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full + b, 1);
-      mbar_init(acc_empty + b, 4);
+      mbar_init(acc_empty + b, PAIR ? 8 : 4);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -192,11 +225,18 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // Both CTAs' barriers must be initialised before either touches the other's.
+  if constexpr (PAIR) cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -205,18 +245,26 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
     if (lane == 0) {
       uint32_t kbg = 0;
       bool stop = false;
-      for (int t = blockIdx.x; t < p.num_tiles && !stop; t += gridDim.x) {
+      for (int t = work_first; t < p.num_work && !stop; t += work_step) {
         int mt, nt;
-        tile_coords(t, p, mt, nt);
+        work_coords<PAIR>(t, p, rank, mt, nt);
         for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
-          const int s = kbg % kStages;
-          if (kbg >= kStages &&
-              !mbar_wait(empty + s, ((kbg / kStages) - 1) & 1, kWaitEmpty, abort_flag, p.watchdog)) {
+          const int s = kbg % kS;
+          if (kbg >= kS &&
+              !mbar_wait(empty + s, ((kbg / kS) - 1) & 1, kWaitEmpty, abort_flag, p.watchdog)) {
             stop = true;
             break;
           }
           uint8_t* sa = smem + s * kStageBytes;
           uint8_t* sb = sa + kABytes;
+          if constexpr (PAIR) {
+            // Both halves complete on the leader's barrier, which expects both.
+            const uint32_t bar = mapa_shared(full + s, 0);
+            if (leader) mbar_arrive_expect_tx(full + s, 2 * kStageBytes);
+            tma_load_2d_pair(sa, &tm_a, bar, kb * kBKBytes, mt * kBM);
+            tma_load_2d_pair(sb, &tm_b, bar, kb * kBKBytes, nt * kBN + static_cast<int>(rank) * (kBN / 2));
+            continue;
+          }
           mbar_arrive_expect_tx(full + s, kStageBytes);
           tma_load_2d(sa, &tm_a, full + s, kb * kBKBytes, mt * kBM);
           tma_load_2d(sb, &tm_b, full + s, kb * kBKBytes, nt * kBN);
@@ -231,11 +279,11 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      constexpr uint32_t idesc = KIND == Kind::kFp8 ? idesc_e4m3(kBM, kBN) : idesc_nvf4(kBM, kBN);
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = KIND == Kind::kFp8 ? idesc_e4m3(PAIR ? 2 * kBM : kBM, kBN) : idesc_nvf4(kBM, kBN);
       uint32_t kbg = 0;
       int i = 0;
-      for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x, ++i) {
+      for (int t = work_first; t < p.num_work && !*abort_flag; t += work_step, ++i) {
         const int b = i % kAcc;
         if (i >= kAcc) {
           if (!mbar_wait(acc_empty + b, ((i / kAcc) - 1) & 1, kWaitAccumFree, abort_flag, p.watchdog)) break;
@@ -243,8 +291,8 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
         }
         const uint32_t d_tmem = tmem + b * kBN;
         for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
-          const int s = kbg % kStages;
-          if (!mbar_wait(full + s, (kbg / kStages) & 1, kWaitFull, abort_flag, p.watchdog)) break;
+          const int s = kbg % kS;
+          if (!mbar_wait(full + s, (kbg / kS) & 1, kWaitFull, abort_flag, p.watchdog)) break;
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * kStageBytes);
           const uint32_t sb = sa + kABytes;
@@ -263,15 +311,26 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
             const uint64_t adesc = sw128_desc(sa + 32 * j);
             const uint64_t bdesc = sw128_desc(sb + 32 * j);
             const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
-            if constexpr (KIND == Kind::kFp8) {
+            if constexpr (PAIR) {
+              mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, acc);
+            } else if constexpr (KIND == Kind::kFp8) {
               mma_f8f6f4(d_tmem, adesc, bdesc, idesc, acc);
             } else {
               mma_nvf4(d_tmem, adesc, bdesc, idesc, tmem + kSfaCol + 4 * j, tmem + kSfbCol + 8 * j, acc);
             }
           }
-          tc_commit(empty + s);
+          // Frees the stage in both CTAs (pairs) once these MMAs have read it.
+          if constexpr (PAIR) {
+            tc_commit_pair(empty + s, 0x3);
+          } else {
+            tc_commit(empty + s);
+          }
         }
-        tc_commit(acc_full + b);
+        if constexpr (PAIR) {
+          tc_commit_pair(acc_full + b, 0x3);
+        } else {
+          tc_commit(acc_full + b);
+        }
       }
     }
   } else if (warp < 6) {
@@ -279,9 +338,9 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const float alpha = *p.alpha;
     int i = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++i) {
+    for (int t = work_first; t < p.num_work; t += work_step, ++i) {
       int mt, nt;
-      tile_coords(t, p, mt, nt);
+      work_coords<PAIR>(t, p, rank, mt, nt);
       const int m0 = mt * kBM, n0 = nt * kBN;
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < p.m;
@@ -304,7 +363,13 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
             // the buffer back to the MMA warp before the remaining math.
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty + b);
+            if (lane == 0) {
+              if constexpr (PAIR) {
+                mbar_arrive_cluster(mapa_shared(acc_empty + b, 0));  // the leader's MMA waits on both CTAs
+              } else {
+                mbar_arrive(acc_empty + b);
+              }
+            }
           }
           const int c0 = n0 + chunk * 32;
           float v[32];
@@ -378,7 +443,7 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
 #pragma unroll
             for (int qq = 0; qq < 4; ++qq) sum += red[((chunk * 4 + qq) * C + c) * 32 + col];
             const int gcol = n0 + chunk * 32 + col;
-            if (gcol < p.padded_n) {
+            if (gcol < p.padded_n && mt < p.tiles_m) {
               p.observed[(static_cast<int64_t>(c) * p.tiles_m + mt) * p.padded_n + gcol] = sum;
             }
           }
@@ -388,211 +453,217 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
       if (!live) break;
     }
   } else if constexpr (CHK) {
-    // ---------------- input-side prediction (warps 6..9) ----------------
-    // Independent of the MMA pipeline: for each of this CTA's tiles, the
-    // slices s = mt, mt + Tm, ... (ascending) of the tile's 256 B rows are
-    // read from global memory (hot in L2: the same column block is streaming
-    // through this SM) and folded into fma chains with q_full.
-    const int ct = threadIdx.x - 192;  // 0..127: rows ct and ct + 128 of the B tile
-    const float alpha = *p.alpha;
-    const int num_slices = (p.k + kSliceK - 1) / kSliceK;
-    const int64_t row_bytes = KIND == Kind::kFp8 ? p.k : p.k / 2;
-    const int64_t k_atoms = (p.k + 63) / 64;
-    const int64_t k_pad = static_cast<int64_t>(num_slices) * kSliceK;
-    // ---- phase 1: per-band projection partials. Lane = 4 * l + g: k-group g
-    // (16 consecutive k), row lane l (rows band_start + l, + 8, ... ascending);
-    // the 8 row lanes combine as ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)).
-    {
-      const int g = lane & 3, l = lane >> 2;
-      const int64_t items = static_cast<int64_t>(num_slices) * p.q_bands;
-      for (int64_t item = static_cast<int64_t>(blockIdx.x) * 4 + (warp - 6); item < items && !*abort_flag;
-           item += static_cast<int64_t>(gridDim.x) * 4) {
-        const int64_t chunk = item % num_slices, band = item / num_slices;
-        const int64_t k0 = chunk * kSliceK + g * 16;
-        // K % 16 == 0 (FP8) / % 32 == 0 (NVFP4): a group of 16 is all in or all out.
-        const bool k_in = k0 < p.k;
-        const int64_t row_end = min(static_cast<int64_t>(p.m), (band + 1) * kBandRows);
-        float2 enc[16], mg[16];
+    if (is_prediction_warp(warp)) {
+      // ---------------- input-side prediction (warps 6..9) ----------------
+      // Independent of the MMA pipeline: for each of this CTA's tiles, the
+      // slices s = mt, mt + Tm, ... (ascending) of the tile's 256 B rows are
+      // read from global memory (hot in L2: the same column block is streaming
+      // through this SM) and folded into fma chains with q_full.
+      const int ct = prediction_index(warp) * 32 + lane;  // 0..127: rows ct and ct + 128 of the B tile
+      const float alpha = *p.alpha;
+      const int num_slices = (p.k + kSliceK - 1) / kSliceK;
+      const int64_t row_bytes = KIND == Kind::kFp8 ? p.k : p.k / 2;
+      const int64_t k_atoms = (p.k + 63) / 64;
+      const int64_t k_pad = static_cast<int64_t>(num_slices) * kSliceK;
+      // ---- phase 1: per-band projection partials. Lane = 4 * l + g: k-group g
+      // (16 consecutive k), row lane l (rows band_start + l, + 8, ... ascending);
+      // the 8 row lanes combine as ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)).
+      {
+        const int g = lane & 3, l = lane >> 2;
+        const int64_t items = static_cast<int64_t>(num_slices) * p.q_bands;
+        for (int64_t item = static_cast<int64_t>(blockIdx.x) * 4 + prediction_index(warp); item < items && !*abort_flag;
+             item += static_cast<int64_t>(gridDim.x) * 4) {
+          const int64_t chunk = item % num_slices, band = item / num_slices;
+          const int64_t k0 = chunk * kSliceK + g * 16;
+          // K % 16 == 0 (FP8) / % 32 == 0 (NVFP4): a group of 16 is all in or all out.
+          const bool k_in = k0 < p.k;
+          const int64_t row_end = min(static_cast<int64_t>(p.m), (band + 1) * kBandRows);
+          float2 enc[16], mg[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) enc[e] = mg[e] = make_float2(0.f, 0.f);
-        constexpr int kBatch = 4;
-        for (int64_t r0 = band * kBandRows + l; r0 < row_end; r0 += 8 * kBatch) {
-          uint4 raw[kBatch];
-          uint32_t sfv[kBatch];
-          float w[kBatch][C];
+          for (int e = 0; e < 16; ++e) enc[e] = mg[e] = make_float2(0.f, 0.f);
+          constexpr int kBatch = 4;
+          for (int64_t r0 = band * kBandRows + l; r0 < row_end; r0 += 8 * kBatch) {
+            uint4 raw[kBatch];
+            uint32_t sfv[kBatch];
+            float w[kBatch][C];
 #pragma unroll
-          for (int i = 0; i < kBatch; ++i) {
-            const int64_t row = r0 + 8 * i;
-            const bool row_in = row < row_end;
-            const bool in = row_in && k_in;
-            if constexpr (KIND == Kind::kFp8) {
-              raw[i] = in ? __ldg(reinterpret_cast<const uint4*>(p.a + row * row_bytes + k0)) : make_uint4(0, 0, 0, 0);
-            } else {
-              const uint2 u = in ? __ldg(reinterpret_cast<const uint2*>(p.a + row * row_bytes + k0 / 2))
-                                 : make_uint2(0, 0);
-              raw[i] = make_uint4(u.x, u.y, 0, 0);
-              const int64_t off = ((row >> 7) * k_atoms + (k0 >> 6)) * 512 + (row & 31) * 16 +
-                                  ((row >> 5) & 3) * 4 + ((k0 >> 4) & 3);
-              sfv[i] = in ? __ldg(p.sfa + off) : 0u;
-            }
-#pragma unroll
-            for (int c = 0; c < C; ++c) w[i][c] = row_in ? __ldg(p.weights + static_cast<int64_t>(c) * p.m + row) : 0.f;
-          }
-#pragma unroll
-          for (int i = 0; i < kBatch; ++i) {
-            if (r0 + 8 * i >= row_end) break;
-            float v[16];
-            if constexpr (KIND == Kind::kFp8) {
-              const uint32_t words[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float2 lo = e4m3x2_to_float2(words[j] & 0xFFFFu), hi = e4m3x2_to_float2(words[j] >> 16);
-                v[4 * j] = lo.x; v[4 * j + 1] = lo.y; v[4 * j + 2] = hi.x; v[4 * j + 3] = hi.y;
+            for (int i = 0; i < kBatch; ++i) {
+              const int64_t row = r0 + 8 * i;
+              const bool row_in = row < row_end;
+              const bool in = row_in && k_in;
+              if constexpr (KIND == Kind::kFp8) {
+                raw[i] = in ? __ldg(reinterpret_cast<const uint4*>(p.a + row * row_bytes + k0))
+                            : make_uint4(0, 0, 0, 0);
+              } else {
+                const uint2 u = in ? __ldg(reinterpret_cast<const uint2*>(p.a + row * row_bytes + k0 / 2))
+                                   : make_uint2(0, 0);
+                raw[i] = make_uint4(u.x, u.y, 0, 0);
+                const int64_t off = ((row >> 7) * k_atoms + (k0 >> 6)) * 512 + (row & 31) * 16 +
+                                    ((row >> 5) & 3) * 4 + ((k0 >> 4) & 3);
+                sfv[i] = in ? __ldg(p.sfa + off) : 0u;
               }
-            } else {
-              float lo8[8], hi8[8];
-              e2m1x8_to_float(raw[i].x, lo8);
-              e2m1x8_to_float(raw[i].y, hi8);
-              const float scale = decode_e4m3(sfv[i]);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                v[e] = lo8[e] * scale;
-                v[8 + e] = hi8[e] * scale;
-              }
-            }
-            const float2 wv = make_float2(w[i][0], C == 2 ? w[i][C - 1] : 0.f);
-            const float2 wa = make_float2(fabsf(wv.x), fabsf(wv.y));
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              enc[e] = fma2(wv, make_float2(v[e], v[e]), enc[e]);
-              const float av = fabsf(v[e]);
-              mg[e] = fma2(wa, make_float2(av, av), mg[e]);
-            }
-          }
-        }
-#pragma unroll
-        for (int offset = 4; offset <= 16; offset <<= 1) {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            enc[e].x += __shfl_xor_sync(0xffffffffu, enc[e].x, offset);
-            enc[e].y += __shfl_xor_sync(0xffffffffu, enc[e].y, offset);
-            mg[e].x += __shfl_xor_sync(0xffffffffu, mg[e].x, offset);
-            mg[e].y += __shfl_xor_sync(0xffffffffu, mg[e].y, offset);
-          }
-        }
-        if (l == 0) {
-          float* dst = p.q_part + (band * k_pad + chunk * kSliceK + g * 16) * C * 2;
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            if constexpr (C == 2) {
-              reinterpret_cast<float4*>(dst)[e] = make_float4(enc[e].x, mg[e].x, enc[e].y, mg[e].y);
-            } else {
-              reinterpret_cast<float2*>(dst)[e] = make_float2(enc[e].x, mg[e].x);
-            }
-          }
-        }
-      }
-    }
-    // ---- phase 2: q_full = sum over bands (ascending) ----
-    if (prediction_grid_barrier(p.grid_sync, gridDim.x, ct, abort_flag, p.watchdog)) {
-      const int64_t entries = k_pad * C * 2;
-      for (int64_t e = static_cast<int64_t>(blockIdx.x) * 128 + ct; e < entries;
-           e += static_cast<int64_t>(gridDim.x) * 128) {
-        float acc = __ldcg(p.q_part + e);
-        for (int b = 1; b < p.q_bands; ++b) acc += __ldcg(p.q_part + b * entries + e);
-        p.q_full[e] = acc;
-      }
-    }
-    prediction_grid_barrier(p.grid_sync, 2 * gridDim.x, ct, abort_flag, p.watchdog);
-    // ---- phase 3: predictions of this CTA's tiles ----
-    for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
-      int mt, nt;
-      tile_coords(t, p, mt, nt);
-      float acc[2][C][2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int c = 0; c < C; ++c) acc[h][c][0] = acc[h][c][1] = 0.f;
-      for (int sl = mt; sl < num_slices; sl += p.tiles_m) {
-        const int k0 = sl * kSliceK;
-        constexpr int kChunksPerSlice = KIND == Kind::kFp8 ? 4 : 2;  // 16-byte chunks per row
-        uint4 raw[2][kChunksPerSlice];
-        uint32_t sfw[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int64_t r = static_cast<int64_t>(nt) * kBN + ct + 128 * h;
-          const bool row_in = r < p.n;
-          const uint8_t* src = p.b + r * row_bytes + (KIND == Kind::kFp8 ? k0 : k0 / 2);
-#pragma unroll
-          for (int ch = 0; ch < kChunksPerSlice; ++ch) {
-            const int byte = (KIND == Kind::kFp8 ? k0 : k0 / 2) + ch * 16;
-            raw[h][ch] = (row_in && byte < row_bytes) ? __ldg(reinterpret_cast<const uint4*>(src) + ch)
-                                                       : make_uint4(0, 0, 0, 0);
-          }
-          if constexpr (KIND == Kind::kNvf4) {
-            const int64_t off = ((r >> 7) * k_atoms + (k0 >> 6)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4;
-            sfw[h] = row_in ? __ldg(reinterpret_cast<const uint32_t*>(p.sfb + off)) : 0u;
-          }
-        }
-        // q_full is zero-padded to a multiple of 64 K, so loads need no guard;
-        // 8 elements of q are loaded ahead of their fma chains.
-#pragma unroll
-        for (int e0 = 0; e0 < kSliceK; e0 += 8) {
-          float qv[8][C][2];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float* qk = p.q_full + static_cast<int64_t>(k0 + e0 + e) * C * 2;
-            // q_full was written by other CTAs during this launch: read through L2.
-            if constexpr (C == 2) {
-              const float4 f = __ldcg(reinterpret_cast<const float4*>(qk));
-              qv[e][0][0] = f.x; qv[e][0][1] = f.y; qv[e][1][0] = f.z; qv[e][1][1] = f.w;
-            } else {
-              const float2 f = __ldcg(reinterpret_cast<const float2*>(qk));
-              qv[e][0][0] = f.x; qv[e][0][1] = f.y;
-            }
-          }
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float value[8];
-            if constexpr (KIND == Kind::kFp8) {
-              const uint4 chunk = raw[h][e0 >> 4];
-              const uint32_t w0 = (e0 & 8) ? chunk.z : chunk.x;
-              const uint32_t w1 = (e0 & 8) ? chunk.w : chunk.y;
-              const float2 v01 = e4m3x2_to_float2(w0 & 0xFFFFu), v23 = e4m3x2_to_float2(w0 >> 16);
-              const float2 v45 = e4m3x2_to_float2(w1 & 0xFFFFu), v67 = e4m3x2_to_float2(w1 >> 16);
-              value[0] = v01.x; value[1] = v01.y; value[2] = v23.x; value[3] = v23.y;
-              value[4] = v45.x; value[5] = v45.y; value[6] = v67.x; value[7] = v67.y;
-            } else {
-              const uint4 chunk = raw[h][e0 >> 5];
-              const int wi = (e0 >> 3) & 3;
-              const uint32_t word = wi == 0 ? chunk.x : wi == 1 ? chunk.y : wi == 2 ? chunk.z : chunk.w;
-              e2m1x8_to_float(word, value);
-              const float scale = decode_e4m3((sfw[h] >> (8 * (e0 >> 4))) & 0xFFu);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) value[e] *= scale;
-            }
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float av = fabsf(value[e]);
 #pragma unroll
               for (int c = 0; c < C; ++c) {
-                acc[h][c][0] = fmaf(qv[e][c][0], value[e], acc[h][c][0]);
-                acc[h][c][1] = fmaf(qv[e][c][1], av, acc[h][c][1]);
+                w[i][c] = row_in ? __ldg(p.weights + static_cast<int64_t>(c) * p.m + row) : 0.f;
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < kBatch; ++i) {
+              if (r0 + 8 * i >= row_end) break;
+              float v[16];
+              if constexpr (KIND == Kind::kFp8) {
+                const uint32_t words[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const float2 lo = e4m3x2_to_float2(words[j] & 0xFFFFu), hi = e4m3x2_to_float2(words[j] >> 16);
+                  v[4 * j] = lo.x; v[4 * j + 1] = lo.y; v[4 * j + 2] = hi.x; v[4 * j + 3] = hi.y;
+                }
+              } else {
+                float lo8[8], hi8[8];
+                e2m1x8_to_float(raw[i].x, lo8);
+                e2m1x8_to_float(raw[i].y, hi8);
+                const float scale = decode_e4m3(sfv[i]);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  v[e] = lo8[e] * scale;
+                  v[8 + e] = hi8[e] * scale;
+                }
+              }
+              const float2 wv = make_float2(w[i][0], C == 2 ? w[i][C - 1] : 0.f);
+              const float2 wa = make_float2(fabsf(wv.x), fabsf(wv.y));
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                enc[e] = fma2(wv, make_float2(v[e], v[e]), enc[e]);
+                const float av = fabsf(v[e]);
+                mg[e] = fma2(wa, make_float2(av, av), mg[e]);
+              }
+            }
+          }
+#pragma unroll
+          for (int offset = 4; offset <= 16; offset <<= 1) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              enc[e].x += __shfl_xor_sync(0xffffffffu, enc[e].x, offset);
+              enc[e].y += __shfl_xor_sync(0xffffffffu, enc[e].y, offset);
+              mg[e].x += __shfl_xor_sync(0xffffffffu, mg[e].x, offset);
+              mg[e].y += __shfl_xor_sync(0xffffffffu, mg[e].y, offset);
+            }
+          }
+          if (l == 0) {
+            float* dst = p.q_part + (band * k_pad + chunk * kSliceK + g * 16) * C * 2;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              if constexpr (C == 2) {
+                reinterpret_cast<float4*>(dst)[e] = make_float4(enc[e].x, mg[e].x, enc[e].y, mg[e].y);
+              } else {
+                reinterpret_cast<float2*>(dst)[e] = make_float2(enc[e].x, mg[e].x);
               }
             }
           }
         }
       }
+      // ---- phase 2: q_full = sum over bands (ascending) ----
+      if (prediction_grid_barrier(p.grid_sync, gridDim.x, ct, abort_flag, p.watchdog)) {
+        const int64_t entries = k_pad * C * 2;
+        for (int64_t e = static_cast<int64_t>(blockIdx.x) * 128 + ct; e < entries;
+             e += static_cast<int64_t>(gridDim.x) * 128) {
+          float acc = __ldcg(p.q_part + e);
+          for (int b = 1; b < p.q_bands; ++b) acc += __ldcg(p.q_part + b * entries + e);
+          p.q_full[e] = acc;
+        }
+      }
+      prediction_grid_barrier(p.grid_sync, 2 * gridDim.x, ct, abort_flag, p.watchdog);
+      // ---- phase 3: predictions of this CTA's tiles ----
+      for (int t = work_first; t < p.num_work && !*abort_flag; t += work_step) {
+        int mt, nt;
+        work_coords<PAIR>(t, p, rank, mt, nt);
+        if (mt >= p.tiles_m) continue;
+        float acc[2][C][2];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int col = nt * kBN + ct + 128 * h;
-        if (col < p.padded_n) {
-          const bool in = col < p.n;
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
-          for (int c = 0; c < C; ++c) {
-            const int64_t off = (static_cast<int64_t>(c) * p.tiles_m + mt) * p.padded_n + col;
-            p.predicted[off] = alpha * (in ? acc[h][c][0] : 0.f);
-            p.magnitude[off] = fabsf(alpha) * (in ? acc[h][c][1] : 0.f);
+          for (int c = 0; c < C; ++c) acc[h][c][0] = acc[h][c][1] = 0.f;
+        for (int sl = mt; sl < num_slices; sl += p.tiles_m) {
+          const int k0 = sl * kSliceK;
+          constexpr int kChunksPerSlice = KIND == Kind::kFp8 ? 4 : 2;  // 16-byte chunks per row
+          uint4 raw[2][kChunksPerSlice];
+          uint32_t sfw[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int64_t r = static_cast<int64_t>(nt) * kBN + ct + 128 * h;
+            const bool row_in = r < p.n;
+            const uint8_t* src = p.b + r * row_bytes + (KIND == Kind::kFp8 ? k0 : k0 / 2);
+#pragma unroll
+            for (int ch = 0; ch < kChunksPerSlice; ++ch) {
+              const int byte = (KIND == Kind::kFp8 ? k0 : k0 / 2) + ch * 16;
+              raw[h][ch] = (row_in && byte < row_bytes) ? __ldg(reinterpret_cast<const uint4*>(src) + ch)
+                                                         : make_uint4(0, 0, 0, 0);
+            }
+            if constexpr (KIND == Kind::kNvf4) {
+              const int64_t off = ((r >> 7) * k_atoms + (k0 >> 6)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4;
+              sfw[h] = row_in ? __ldg(reinterpret_cast<const uint32_t*>(p.sfb + off)) : 0u;
+            }
+          }
+          // q_full is zero-padded to a multiple of 64 K, so loads need no guard;
+          // 8 elements of q are loaded ahead of their fma chains.
+#pragma unroll
+          for (int e0 = 0; e0 < kSliceK; e0 += 8) {
+            float qv[8][C][2];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float* qk = p.q_full + static_cast<int64_t>(k0 + e0 + e) * C * 2;
+              // q_full was written by other CTAs during this launch: read through L2.
+              if constexpr (C == 2) {
+                const float4 f = __ldcg(reinterpret_cast<const float4*>(qk));
+                qv[e][0][0] = f.x; qv[e][0][1] = f.y; qv[e][1][0] = f.z; qv[e][1][1] = f.w;
+              } else {
+                const float2 f = __ldcg(reinterpret_cast<const float2*>(qk));
+                qv[e][0][0] = f.x; qv[e][0][1] = f.y;
+              }
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              float value[8];
+              if constexpr (KIND == Kind::kFp8) {
+                const uint4 chunk = raw[h][e0 >> 4];
+                const uint32_t w0 = (e0 & 8) ? chunk.z : chunk.x;
+                const uint32_t w1 = (e0 & 8) ? chunk.w : chunk.y;
+                const float2 v01 = e4m3x2_to_float2(w0 & 0xFFFFu), v23 = e4m3x2_to_float2(w0 >> 16);
+                const float2 v45 = e4m3x2_to_float2(w1 & 0xFFFFu), v67 = e4m3x2_to_float2(w1 >> 16);
+                value[0] = v01.x; value[1] = v01.y; value[2] = v23.x; value[3] = v23.y;
+                value[4] = v45.x; value[5] = v45.y; value[6] = v67.x; value[7] = v67.y;
+              } else {
+                const uint4 chunk = raw[h][e0 >> 5];
+                const int wi = (e0 >> 3) & 3;
+                const uint32_t word = wi == 0 ? chunk.x : wi == 1 ? chunk.y : wi == 2 ? chunk.z : chunk.w;
+                e2m1x8_to_float(word, value);
+                const float scale = decode_e4m3((sfw[h] >> (8 * (e0 >> 4))) & 0xFFu);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) value[e] *= scale;
+              }
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float av = fabsf(value[e]);
+#pragma unroll
+                for (int c = 0; c < C; ++c) {
+                  acc[h][c][0] = fmaf(qv[e][c][0], value[e], acc[h][c][0]);
+                  acc[h][c][1] = fmaf(qv[e][c][1], av, acc[h][c][1]);
+                }
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int col = nt * kBN + ct + 128 * h;
+          if (col < p.padded_n) {
+            const bool in = col < p.n;
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+              const int64_t off = (static_cast<int64_t>(c) * p.tiles_m + mt) * p.padded_n + col;
+              p.predicted[off] = alpha * (in ? acc[h][c][0] : 0.f);
+              p.magnitude[off] = fabsf(alpha) * (in ? acc[h][c][1] : 0.f);
+            }
           }
         }
       }
@@ -600,14 +671,20 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
   }
 
   __syncthreads();
+  // No CTA of a pair leaves while the other may still signal its barriers.
+  if constexpr (PAIR) cluster_sync();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    if constexpr (PAIR) {
+      tmem_dealloc_pair(tmem, kTmemCols);
+    } else {
+      tmem_dealloc(tmem, kTmemCols);
+    }
   }
 }
 
-template <Kind KIND, int C, bool BF16OUT, bool CHK>
+template <Kind KIND, int C, bool BF16OUT, bool CHK, bool PAIR>
 int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   const int64_t k_bytes = KIND == Kind::kFp8 ? g.k : g.k / 2;
   CUtensorMap ta{}, tb{}, tsa{}, tsb{};
@@ -622,7 +699,7 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(k_bytes), static_cast<uint64_t>(g.n)};
     const uint64_t strides[1] = {static_cast<uint64_t>(k_bytes)};
-    const uint32_t box[2] = {kBKBytes, kBN};
+    const uint32_t box[2] = {kBKBytes, PAIR ? kBN / 2 : kBN};  // pairs: each CTA stages half the tile's B rows
     int rc = encode_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(g.b), dims,
                                strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != SDC_OK) return rc;
@@ -657,6 +734,7 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   p.tiles_m = static_cast<int32_t>(ceil_div(g.m, kBM));
   p.tiles_n = static_cast<int32_t>(ceil_div(g.n, kBN));
   p.num_tiles = p.tiles_m * p.tiles_n;
+  p.num_work = PAIR ? static_cast<int32_t>(ceil_div(p.tiles_m, 2)) * p.tiles_n : p.num_tiles;
   p.alpha = g.alpha;
   p.d = g.d;
   p.weights = g.weights;
@@ -679,42 +757,75 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   p.magnitude = g.magnitude;
   p.watchdog = watchdog_ptr();
   if (p.watchdog == nullptr) return fail(SDC_ERR_CUDA, "watchdog symbol unavailable");
-  auto kernel = gemm_kernel<KIND, C, BF16OUT, CHK>;
-  constexpr int smem = smem_bytes(KIND);
-  static bool configured[64] = {};
-  int device = 0;
-  SDC_CUDA_CHECK(cudaGetDevice(&device));
-  if (device < 0 || device >= 64 || !configured[device]) {
-    SDC_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    if (device >= 0 && device < 64) configured[device] = true;
-  }
-  const int grid = std::min(p.num_tiles, sm_count());
+  auto kernel = gemm_kernel<KIND, C, BF16OUT, CHK, PAIR>;
+  constexpr int smem = smem_bytes(KIND, PAIR);
   cudaLaunchConfig_t config{};
-  config.gridDim = dim3(static_cast<unsigned>(grid));
   config.blockDim = dim3(num_threads(CHK));
   config.dynamicSmemBytes = smem;
   config.stream = stream;
-  // The prediction warps synchronise across CTAs: every CTA must be resident.
-  cudaLaunchAttribute attribute[1];
-  attribute[0].id = cudaLaunchAttributeCooperative;
-  attribute[0].val.cooperative = 1;
+  cudaLaunchAttribute attribute[2];
+  int attrs = 0;
+  if constexpr (PAIR) {
+    attribute[attrs].id = cudaLaunchAttributeClusterDimension;
+    attribute[attrs].val.clusterDim.x = 2;
+    attribute[attrs].val.clusterDim.y = 1;
+    attribute[attrs].val.clusterDim.z = 1;
+    ++attrs;
+  }
   config.attrs = attribute;
-  config.numAttrs = CHK ? 1 : 0;
+  config.numAttrs = attrs;
+  // Per device: the shared-memory opt-in and how many CTAs (pairs) fit at once.
+  static int resident[64] = {};
+  int device = 0;
+  SDC_CUDA_CHECK(cudaGetDevice(&device));
+  int fit = device >= 0 && device < 64 ? resident[device] : 0;
+  if (fit == 0) {
+    SDC_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    if constexpr (PAIR) {
+      config.gridDim = dim3(2);
+      SDC_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&fit, kernel, &config));
+    } else {
+      fit = sm_count();
+    }
+    if (fit <= 0) return fail(SDC_ERR_CUDA, "GEMM kernel does not fit on this device");
+    if (device >= 0 && device < 64) resident[device] = fit;
+  }
+  const int units = std::min(p.num_work, fit);  // persistent: at most one wave
+  config.gridDim = dim3(static_cast<unsigned>(PAIR ? 2 * units : units));
+  // The prediction warps synchronise across CTAs, so every CTA must be
+  // resident: the grid never exceeds one wave of the occupancy computed above,
+  // single CTAs additionally launch cooperatively (a guarantee that cluster
+  // launches cannot combine with under the profiler), and every wait at the
+  // grid barrier is bounded.
+  if constexpr (CHK && !PAIR) {
+    attribute[attrs].id = cudaLaunchAttributeCooperative;
+    attribute[attrs].val.cooperative = 1;
+    config.numAttrs = ++attrs;
+  }
   SDC_CUDA_CHECK(cudaLaunchKernelEx(&config, kernel, ta, tb, tsa, tsb, p));
   return SDC_OK;
+}
+
+template <Kind KIND, int C, bool BF16OUT, bool CHK>
+int dispatch_pair(const GemmProblem& g, cudaStream_t stream) {
+  // FP8 runs as CTA pairs (256-row tiles) whenever there are two M-tiles.
+  if constexpr (KIND == Kind::kFp8) {
+    if (g.m > kBM) return launch_impl<KIND, C, BF16OUT, CHK, true>(g, stream);
+  }
+  return launch_impl<KIND, C, BF16OUT, CHK, false>(g, stream);
 }
 
 template <Kind KIND, int C>
 int dispatch_out(const GemmProblem& g, cudaStream_t stream) {
   const bool chk = g.q_full != nullptr;
   if constexpr (C == 0) {
-    return g.out_bf16_rowmajor ? launch_impl<KIND, 0, true, false>(g, stream)
-                               : launch_impl<KIND, 0, false, false>(g, stream);
+    return g.out_bf16_rowmajor ? dispatch_pair<KIND, 0, true, false>(g, stream)
+                               : dispatch_pair<KIND, 0, false, false>(g, stream);
   } else {
     if (g.out_bf16_rowmajor) {
-      return chk ? launch_impl<KIND, C, true, true>(g, stream) : launch_impl<KIND, C, true, false>(g, stream);
+      return chk ? dispatch_pair<KIND, C, true, true>(g, stream) : dispatch_pair<KIND, C, true, false>(g, stream);
     }
-    return chk ? launch_impl<KIND, C, false, true>(g, stream) : launch_impl<KIND, C, false, false>(g, stream);
+    return chk ? dispatch_pair<KIND, C, false, true>(g, stream) : dispatch_pair<KIND, C, false, false>(g, stream);
   }
 }
 
