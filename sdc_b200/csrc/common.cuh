@@ -63,6 +63,7 @@ enum WatchdogCode : int32_t {
   kWaitOther = 5,
   kWaitProjection = 6, // K-slice projection waiting for its A rows
   kWaitGrid = 7,       // prediction warps waiting at the grid-wide barrier
+  kWaitPace = 8,       // prediction warps waiting for the epilogue's progress
 };
 
 // 2 seconds of globaltimer nanoseconds; a healthy wait ends in microseconds.

@@ -8,6 +8,8 @@
 // read once); the grid is one thread per (channel, column) so loads of
 // consecutive columns coalesce, and a second one-block kernel ORs the
 // per-block status words, so no float atomics or host syncs are involved.
+// The partials are staged through shared memory by all warps of a block so
+// that many loads are in flight, while the additions stay serial per column.
 #include <algorithm>
 #include <mutex>
 
@@ -16,7 +18,9 @@
 namespace sdc {
 namespace {
 
-constexpr int kFinalizeThreads = 64;  // small blocks: one thread per (channel, column)
+constexpr int kFinalizeThreads = 64;   // columns per block (and threads of the flags kernel)
+constexpr int kColumnThreads = 256;    // threads of a finalize_columns block
+constexpr int kTileChunk = 32;         // tiles staged in shared memory per round
 constexpr unsigned kDetected = 1u;
 constexpr unsigned kNonfinite = 2u;
 constexpr unsigned kHit = 4u;
@@ -41,17 +45,28 @@ struct FinalizeParams {
   int32_t* block_states;
 };
 
+// Block = 64 columns of one channel. All 8 warps stage the partials of 32
+// tiles at a time in shared memory (warp w stages column group w % 2 of the
+// tiles t with t % 4 == w / 2), so many loads are in flight; then warps 0 and
+// 1 add them, one thread per column, in ascending tile order.
 template <int C>
-__global__ void __launch_bounds__(kFinalizeThreads) finalize_columns(FinalizeParams p) {
+__global__ void __launch_bounds__(kColumnThreads) finalize_columns(FinalizeParams p) {
+  __shared__ float staged[3][kTileChunk][kFinalizeThreads];
+  __shared__ unsigned warp_state[kColumnThreads / 32];
   unsigned state = 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int group = warp & 1;                 // column group of 32
+  const int phase = warp >> 1;                // tiles t with t % 4 == phase
   const int channel = blockIdx.y;
   const int64_t block = static_cast<int64_t>(blockIdx.y) * gridDim.x + blockIdx.x;
-  const int64_t col = static_cast<int64_t>(blockIdx.x) * kFinalizeThreads + threadIdx.x;
+  const int local = group * 32 + lane;        // column within the block
+  const int64_t col = static_cast<int64_t>(blockIdx.x) * kFinalizeThreads + local;
+  const bool col_in = col < p.n;
 
   // Status inputs: each packed tile flag is read by exactly one thread of the grid.
   if (p.tile_flags != nullptr) {
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * gridDim.y * kFinalizeThreads;
-    for (int64_t i = block * kFinalizeThreads + threadIdx.x; i < p.flag_count; i += stride) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * gridDim.y * kColumnThreads;
+    for (int64_t i = block * kColumnThreads + threadIdx.x; i < p.flag_count; i += stride) {
       const int32_t t = p.tile_flags[i];
       if (t & 1) state |= kHit;
       if (t & 2) state |= kDetected | kNonfinite;
@@ -61,31 +76,39 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_columns(FinalizePar
     if (*p.nonfinite_in != 0) state |= kDetected | kNonfinite;
   }
 
-  if (col < p.n) {
-    const int64_t base = static_cast<int64_t>(channel) * p.m_tiles * p.padded_n + col;
-    float observed = 0.f, predicted = 0.f, magnitude = 0.f;
-    // Loads of 32 tiles (three planes) are issued before their ordered adds,
-    // so a column costs ceil(Tm / 32) memory latencies.
-    constexpr int kBatch = 32;
-    for (int64_t t0 = 0; t0 < p.m_tiles; t0 += kBatch) {
-      float o[kBatch], pr[kBatch], mg[kBatch];
+  const int64_t base = static_cast<int64_t>(channel) * p.m_tiles * p.padded_n + col;
+  float observed = 0.f, predicted = 0.f, magnitude = 0.f;
+  for (int64_t t0 = 0; t0 < p.m_tiles; t0 += kTileChunk) {
+    // All 24 loads of this thread are issued before any lands in shared memory.
+    constexpr int kPerWarp = kTileChunk / 4;
+    float v[3][kPerWarp];
 #pragma unroll
-      for (int i = 0; i < kBatch; ++i) {
-        const bool in = t0 + i < p.m_tiles;
-        const int64_t off = base + (t0 + i) * p.padded_n;
-        o[i] = in ? __ldg(p.observed + off) : 0.f;
-        pr[i] = (in && !p.use_reference) ? __ldg(p.predicted + off) : 0.f;
-        mg[i] = (in && !p.use_reference) ? __ldg(p.magnitude + off) : 0.f;
-      }
+    for (int j = 0; j < kPerWarp; ++j) {
+      const int i = phase + 4 * j;
+      const bool in = col_in && t0 + i < p.m_tiles;
+      const int64_t off = base + (t0 + i) * p.padded_n;
+      v[0][j] = in ? __ldg(p.observed + off) : 0.f;
+      v[1][j] = (in && !p.use_reference) ? __ldg(p.predicted + off) : 0.f;
+      v[2][j] = (in && !p.use_reference) ? __ldg(p.magnitude + off) : 0.f;
+    }
 #pragma unroll
-      for (int i = 0; i < kBatch; ++i) {
-        if (t0 + i < p.m_tiles) {
-          observed = __fadd_rn(observed, o[i]);
-          predicted = __fadd_rn(predicted, pr[i]);
-          magnitude = __fadd_rn(magnitude, mg[i]);
-        }
+    for (int j = 0; j < kPerWarp; ++j) {
+#pragma unroll
+      for (int plane = 0; plane < 3; ++plane) staged[plane][phase + 4 * j][local] = v[plane][j];
+    }
+    __syncthreads();
+    if (warp < 2) {
+      const int64_t count = p.m_tiles - t0 < kTileChunk ? p.m_tiles - t0 : kTileChunk;
+      for (int i = 0; i < count; ++i) {
+        observed = __fadd_rn(observed, staged[0][i][local]);
+        predicted = __fadd_rn(predicted, staged[1][i][local]);
+        magnitude = __fadd_rn(magnitude, staged[2][i][local]);
       }
     }
+    __syncthreads();
+  }
+
+  if (warp < 2 && col_in) {
     const int64_t out = static_cast<int64_t>(channel) * p.n + col;
     if (p.use_reference) {
       predicted = p.reference[out];
@@ -110,12 +133,11 @@ __global__ void __launch_bounds__(kFinalizeThreads) finalize_columns(FinalizePar
 
   // Deterministic OR across the block: warp shuffle, then shared memory.
   for (int offset = 16; offset > 0; offset >>= 1) state |= __shfl_xor_sync(0xffffffffu, state, offset);
-  __shared__ unsigned warp_state[kFinalizeThreads / 32];
-  if ((threadIdx.x & 31) == 0) warp_state[threadIdx.x >> 5] = state;
+  if (lane == 0) warp_state[warp] = state;
   __syncthreads();
   if (threadIdx.x == 0) {
     unsigned combined = 0;
-    for (int w = 0; w < kFinalizeThreads / 32; ++w) combined |= warp_state[w];
+    for (int w = 0; w < kColumnThreads / 32; ++w) combined |= warp_state[w];
     p.block_states[block] = static_cast<int32_t>(combined);
   }
 }
@@ -209,9 +231,9 @@ int sdc_abft_finalize(int algorithm, const float* observed, const float* predict
   p.block_states = static_cast<int32_t*>(workspace);
   const dim3 grid(static_cast<unsigned>(ceil_div(n, kFinalizeThreads)), channels);
   if (channels == 2) {
-    finalize_columns<2><<<grid, kFinalizeThreads, 0, stream>>>(p);
+    finalize_columns<2><<<grid, kColumnThreads, 0, stream>>>(p);
   } else {
-    finalize_columns<1><<<grid, kFinalizeThreads, 0, stream>>>(p);
+    finalize_columns<1><<<grid, kColumnThreads, 0, stream>>>(p);
   }
   SDC_CUDA_CHECK(cudaGetLastError());
   finalize_flags<<<1, kFinalizeThreads, 0, stream>>>(p.block_states, blocks, flags, hit_out,

@@ -68,13 +68,9 @@ __host__ __device__ constexpr int smem_bytes(Kind k, bool pair = false) {
   return 1024 + num_stages(pair) * stage_bytes(k, pair) + kRedFloats * 4 + 256;
 }
 __host__ __device__ constexpr int num_acc(Kind k) { return k == Kind::kFp8 ? 2 : 1; }
-// Warps 0 (TMA) and 1 (MMA) run on SM sub-partitions 0 and 1 (warp % 4);
-// every other warp there steals their issue slots. The prediction warps
-// therefore sit on sub-partitions 2 and 3 only: warps 6, 7, 10, 11 (warps 8
-// and 9 exit at once).
-__host__ __device__ constexpr int num_threads(bool chk) { return chk ? 384 : 192; }
-__device__ __forceinline__ bool is_prediction_warp(int warp) { return warp == 6 || warp == 7 || warp >= 10; }
-__device__ __forceinline__ int prediction_index(int warp) { return warp < 8 ? warp - 6 : warp - 8; }
+__host__ __device__ constexpr int num_threads(bool chk) { return chk ? 320 : 192; }
+__device__ __forceinline__ bool is_prediction_warp(int warp) { return warp >= 6; }
+__device__ __forceinline__ int prediction_index(int warp) { return warp - 6; }
 
 struct Params {
   int32_t m, n, k, num_kb, tiles_m, tiles_n, num_tiles;
@@ -164,7 +160,9 @@ __device__ __forceinline__ bool prediction_grid_barrier(uint32_t* counter, uint3
         *abort_flag = kWaitGrid;
         break;
       }
-      __nanosleep(256);
+      // Sparse polling: every CTA polls the same word, and the wait is off the
+      // tensor cores' critical path.
+      __nanosleep(4000);
     }
     __threadfence();
   }
@@ -194,6 +192,8 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(tmem_slot + 1);
+  // Tiles whose epilogue has finished: paces the prediction warps.
+  volatile uint32_t* tiles_done = tmem_slot + 2;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -214,6 +214,7 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
       mbar_init(acc_empty + b, PAIR ? 8 : 4);
     }
     *abort_flag = 0;
+    *tiles_done = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -450,6 +451,7 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
         }
         named_barrier(1, 128);
       }
+      if (threadIdx.x == 64) *tiles_done = static_cast<uint32_t>(i + 1);
       if (!live) break;
     }
   } else if constexpr (CHK) {
@@ -465,14 +467,39 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
       const int64_t row_bytes = KIND == Kind::kFp8 ? p.k : p.k / 2;
       const int64_t k_atoms = (p.k + 63) / 64;
       const int64_t k_pad = static_cast<int64_t>(num_slices) * kSliceK;
+      // Pacing: this work is spread over the CTA's tiles (projection during
+      // the first half, prediction during the second) instead of running in
+      // bursts, which would take L2 bandwidth from the TMA loads feeding the
+      // tensor cores. A wait returns false once the CTA has aborted.
+      const uint32_t my_tiles =
+          work_first < p.num_work ? static_cast<uint32_t>((p.num_work - 1 - work_first) / work_step + 1) : 0u;
+      const uint32_t half = my_tiles / 2;
+      auto pace = [&](uint32_t target) -> bool {
+        if (*tiles_done >= target) return true;
+        const uint64_t start = global_ns();
+        while (*tiles_done < target) {
+          if (*abort_flag) return false;
+          if (global_ns() - start > kWaitLimitNs) {
+            atomicCAS(p.watchdog, 0, kWaitPace);
+            *abort_flag = kWaitPace;
+            return false;
+          }
+          __nanosleep(500);
+        }
+        return true;
+      };
       // ---- phase 1: per-band projection partials. Lane = 4 * l + g: k-group g
       // (16 consecutive k), row lane l (rows band_start + l, + 8, ... ascending);
       // the 8 row lanes combine as ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)).
       {
         const int g = lane & 3, l = lane >> 2;
         const int64_t items = static_cast<int64_t>(num_slices) * p.q_bands;
-        for (int64_t item = static_cast<int64_t>(blockIdx.x) * 4 + prediction_index(warp); item < items && !*abort_flag;
-             item += static_cast<int64_t>(gridDim.x) * 4) {
+        const int64_t first_item = static_cast<int64_t>(blockIdx.x) * 4 + prediction_index(warp);
+        const int64_t item_step = static_cast<int64_t>(gridDim.x) * 4;
+        const int64_t my_items = first_item < items ? (items - 1 - first_item) / item_step + 1 : 0;
+        int64_t j = 0;
+        for (int64_t item = first_item; item < items && !*abort_flag; item += item_step, ++j) {
+          if (!pace(static_cast<uint32_t>(j * half / my_items))) break;
           const int64_t chunk = item % num_slices, band = item / num_slices;
           const int64_t k0 = chunk * kSliceK + g * 16;
           // K % 16 == 0 (FP8) / % 32 == 0 (NVFP4): a group of 16 is all in or all out.
@@ -574,7 +601,10 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
       }
       prediction_grid_barrier(p.grid_sync, 2 * gridDim.x, ct, abort_flag, p.watchdog);
       // ---- phase 3: predictions of this CTA's tiles ----
-      for (int t = work_first; t < p.num_work && !*abort_flag; t += work_step) {
+      const uint32_t last = my_tiles > 0 ? my_tiles - 1 : 0u;
+      uint32_t jt = 0;
+      for (int t = work_first; t < p.num_work && !*abort_flag; t += work_step, ++jt) {
+        if (!pace(half + jt * (last > half ? last - half : 0u) / (my_tiles > 0 ? my_tiles : 1u))) break;
         int mt, nt;
         work_coords<PAIR>(t, p, rank, mt, nt);
         if (mt >= p.tiles_m) continue;
