@@ -304,6 +304,10 @@ def run_ours(args):
 
     sdc_b200.require_device(device)
     dist = None
+    # The result is the only line on stdout: libraries (NCCL prints its
+    # version) write to stderr instead while this run lasts.
+    result_fd = os.dup(1)
+    os.dup2(2, 1)
     if world > 1:
         import datetime
 
@@ -412,7 +416,8 @@ def run_ours(args):
         line["qwen2.5_7b_linears"] = sweep
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_sample_rows)
-    print(json.dumps(line), flush=True)
+    sys.stdout.flush()
+    os.write(result_fd, (json.dumps(line) + "\n").encode())
 
 
 def cpu_baseline(rows):

@@ -52,8 +52,9 @@ enum sdc_reference_layout {
   /* predicted/magnitude[c, t, col] = contribution of the 64-wide K slices s
    * with s % Tm == t, summed over ALL rows. The sum over t equals the TILE
    * layout's sum over t (up to fp32 rounding); finalize is unchanged. The
-   * propagation runs inside the GEMM on its shared-memory B tiles, so it
-   * costs one extra read of A instead of ~C/32 of the GEMM on CUDA cores. */
+   * projection w^T A and the propagation run inside the GEMM launch (one
+   * extra read of A and of B, overlapped with the tensor-core mainloop)
+   * instead of ~C/32 of the GEMM on CUDA cores. */
   SDC_LAYOUT_KSLICE = 1
 };
 
