@@ -46,26 +46,39 @@ constexpr int kBKBytes = 128;  // one 128-byte swizzle atom of K per stage
 constexpr int kStages = 4;
 constexpr int kSliceK = 64;    // K elements per input-checksum slice
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSfaCol = 256;  // NVFP4: 4 k-steps x 4 columns
-constexpr uint32_t kSfbCol = 272;  // NVFP4: 4 k-steps x 8 columns
-constexpr int kChunks = kBN / 32;
+// Tile width in output columns. NVFP4 keeps 256 as well: a 128-wide tile
+// would leave room for two accumulators next to the block scales, but the
+// extra operand traffic per MAC costs more (measured: 2.2 vs 3.1 PF/s
+// unprotected at 16384^3) than the exposed epilogue of one accumulator.
+__host__ __device__ constexpr int tile_n(Kind) { return kBN; }
+__host__ __device__ constexpr int chunks(Kind k) { return tile_n(k) / 32; }
+// NVFP4 block scales in TMEM after the accumulator(s): per 64-wide k-step,
+// 4 columns per 128 rows of A (the CTA's M-tile) and of B (the tile's rows).
+__host__ __device__ constexpr int sfb_groups(Kind k) { return tile_n(k) / 128; }
+constexpr uint32_t kSfaCol = 256;  // 4 k-steps x 4 columns
+constexpr uint32_t kSfbCol = 272;  // 4 k-steps x 4 columns x B row groups
+constexpr int kChunks = kBN / 32;  // the widest tile's 32-column chunks
 constexpr int kGroupM = 16;        // M-tiles per raster group
 
 constexpr int kABytes = kBM * kBKBytes;
-constexpr int kBBytes = kBN * kBKBytes;
 constexpr int kSfaBytes = 4 * 512;
-constexpr int kSfbBytes = 2 * 4 * 512;
+constexpr int kSfbBytes = 4 * 512 * (kBN / 128);  // per k-block: 4 k-steps x the tile's B row groups
 constexpr int kRedFloats = kChunks * 4 * 2 * 32;
 
-// CTA pairs (FP8): each CTA stages its 128 rows of A and 128 of the tile's
-// 256 B rows; one cta_group::2 MMA covers the 256 x 256 pair tile.
-constexpr int kPairStages = 6;
-__host__ __device__ constexpr int stage_bytes(Kind k, bool pair = false) {
-  return pair ? kABytes + kBBytes / 2 : kABytes + kBBytes + (k == Kind::kNvf4 ? kSfaBytes + kSfbBytes : 0);
+// CTA pairs: each CTA stages its 128 rows of A and 128 of the tile's 256 B
+// rows (NVFP4: plus its own A scales and all 256 rows' B scales); one
+// cta_group::2 MMA covers the 256 x 256 pair tile.
+__host__ __device__ constexpr int b_stage_bytes(Kind k, bool pair) {
+  return (pair ? tile_n(k) / 2 : tile_n(k)) * kBKBytes;
 }
-__host__ __device__ constexpr int num_stages(bool pair) { return pair ? kPairStages : kStages; }
+__host__ __device__ constexpr int stage_bytes(Kind k, bool pair = false) {
+  return kABytes + b_stage_bytes(k, pair) + (k == Kind::kNvf4 ? kSfaBytes + kSfbBytes : 0);
+}
+__host__ __device__ constexpr int num_stages(Kind k, bool pair) {
+  return pair ? (k == Kind::kFp8 ? 6 : 5) : kStages;
+}
 __host__ __device__ constexpr int smem_bytes(Kind k, bool pair = false) {
-  return 1024 + num_stages(pair) * stage_bytes(k, pair) + kRedFloats * 4 + 256;
+  return 1024 + num_stages(k, pair) * stage_bytes(k, pair) + kRedFloats * 4 + 256;
 }
 __host__ __device__ constexpr int num_acc(Kind k) { return k == Kind::kFp8 ? 2 : 1; }
 __host__ __device__ constexpr int num_threads(bool chk) { return chk ? 320 : 192; }
@@ -178,8 +191,10 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ CUtensorMap tm_sfa,
                 const __grid_constant__ CUtensorMap tm_sfb, const Params p) {
-  static_assert(!PAIR || KIND == Kind::kFp8, "CTA pairs are built for FP8 only");
-  constexpr int kS = num_stages(PAIR);
+  constexpr int kS = num_stages(KIND, PAIR);
+  constexpr int kBStage = b_stage_bytes(KIND, PAIR);
+  constexpr int kTN = tile_n(KIND);
+  constexpr int kTileChunks = chunks(KIND);
   constexpr int kStageBytes = stage_bytes(KIND, PAIR);
   constexpr int kAcc = num_acc(KIND);
   extern __shared__ uint8_t smem_raw[];
@@ -263,17 +278,25 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
             const uint32_t bar = mapa_shared(full + s, 0);
             if (leader) mbar_arrive_expect_tx(full + s, 2 * kStageBytes);
             tma_load_2d_pair(sa, &tm_a, bar, kb * kBKBytes, mt * kBM);
-            tma_load_2d_pair(sb, &tm_b, bar, kb * kBKBytes, nt * kBN + static_cast<int>(rank) * (kBN / 2));
+            tma_load_2d_pair(sb, &tm_b, bar, kb * kBKBytes, nt * kTN + static_cast<int>(rank) * (kTN / 2));
+            if constexpr (KIND == Kind::kNvf4) {
+              // Own A scales; the B scales of all the tile's rows (each CTA's
+              // accumulator spans every column of the tile).
+              uint8_t* ssfa = sb + kBStage;
+              uint8_t* ssfb = ssfa + kSfaBytes;
+              tma_load_4d_pair(ssfa, &tm_sfa, bar, 0, 0, kb * 4, mt);
+              tma_load_4d_pair(ssfb, &tm_sfb, bar, 0, 0, kb * 4, nt * sfb_groups(KIND));
+            }
             continue;
           }
           mbar_arrive_expect_tx(full + s, kStageBytes);
           tma_load_2d(sa, &tm_a, full + s, kb * kBKBytes, mt * kBM);
-          tma_load_2d(sb, &tm_b, full + s, kb * kBKBytes, nt * kBN);
+          tma_load_2d(sb, &tm_b, full + s, kb * kBKBytes, nt * kTN);
           if constexpr (KIND == Kind::kNvf4) {
-            uint8_t* ssfa = sb + kBBytes;
+            uint8_t* ssfa = sb + kBStage;
             uint8_t* ssfb = ssfa + kSfaBytes;
             tma_load_4d(ssfa, &tm_sfa, full + s, 0, 0, kb * 4, mt);
-            tma_load_4d(ssfb, &tm_sfb, full + s, 0, 0, kb * 4, nt * 2);
+            tma_load_4d(ssfb, &tm_sfb, full + s, 0, 0, kb * 4, nt * sfb_groups(KIND));
           }
         }
       }
@@ -281,7 +304,8 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc = KIND == Kind::kFp8 ? idesc_e4m3(PAIR ? 2 * kBM : kBM, kBN) : idesc_nvf4(kBM, kBN);
+      constexpr int kMmaM = PAIR ? 2 * kBM : kBM;
+      constexpr uint32_t idesc = KIND == Kind::kFp8 ? idesc_e4m3(kMmaM, kTN) : idesc_nvf4(kMmaM, kTN);
       uint32_t kbg = 0;
       int i = 0;
       for (int t = work_first; t < p.num_work && !*abort_flag; t += work_step, ++i) {
@@ -290,7 +314,7 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
           if (!mbar_wait(acc_empty + b, ((i / kAcc) - 1) & 1, kWaitAccumFree, abort_flag, p.watchdog)) break;
           tc_fence_after();
         }
-        const uint32_t d_tmem = tmem + b * kBN;
+        const uint32_t d_tmem = tmem + b * kTN;
         for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
           const int s = kbg % kS;
           if (!mbar_wait(full + s, (kbg / kS) & 1, kWaitFull, abort_flag, p.watchdog)) break;
@@ -298,13 +322,17 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
           const uint32_t sa = smem_u32(smem + s * kStageBytes);
           const uint32_t sb = sa + kABytes;
           if constexpr (KIND == Kind::kNvf4) {
-            const uint32_t ssfa = sb + kBBytes;
+            // Pairs: one copy moves each CTA's staged scales into its own TMEM.
+            const uint32_t ssfa = sb + kBStage;
             const uint32_t ssfb = ssfa + kSfaBytes;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              tmem_cp_32x128b_x4(tmem + kSfaCol + 4 * j, sf_desc(ssfa + 512 * j));
-              tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j, sf_desc(ssfb + 512 * j));
-              tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j + 4, sf_desc(ssfb + 2048 + 512 * j));
+              tmem_cp_32x128b_x4<PAIR>(tmem + kSfaCol + 4 * j, sf_desc(ssfa + 512 * j));
+#pragma unroll
+              for (int g = 0; g < sfb_groups(KIND); ++g) {
+                tmem_cp_32x128b_x4<PAIR>(tmem + kSfbCol + 4 * (sfb_groups(KIND) * j + g),
+                                         sf_desc(ssfb + 2048 * g + 512 * j));
+              }
             }
           }
 #pragma unroll
@@ -312,12 +340,15 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
             const uint64_t adesc = sw128_desc(sa + 32 * j);
             const uint64_t bdesc = sw128_desc(sb + 32 * j);
             const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
-            if constexpr (PAIR) {
-              mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, acc);
-            } else if constexpr (KIND == Kind::kFp8) {
-              mma_f8f6f4(d_tmem, adesc, bdesc, idesc, acc);
+            if constexpr (KIND == Kind::kFp8) {
+              if constexpr (PAIR) {
+                mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, acc);
+              } else {
+                mma_f8f6f4(d_tmem, adesc, bdesc, idesc, acc);
+              }
             } else {
-              mma_nvf4(d_tmem, adesc, bdesc, idesc, tmem + kSfaCol + 4 * j, tmem + kSfbCol + 8 * j, acc);
+              mma_nvf4<PAIR>(d_tmem, adesc, bdesc, idesc, tmem + kSfaCol + 4 * j,
+                             tmem + kSfbCol + 4 * sfb_groups(KIND) * j, acc);
             }
           }
           // Frees the stage in both CTAs (pairs) once these MMAs have read it.
@@ -342,7 +373,7 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
     for (int t = work_first; t < p.num_work; t += work_step, ++i) {
       int mt, nt;
       work_coords<PAIR>(t, p, rank, mt, nt);
-      const int m0 = mt * kBM, n0 = nt * kBN;
+      const int m0 = mt * kBM, n0 = nt * kTN;
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < p.m;
       float w[C > 0 ? C : 1];
@@ -355,11 +386,11 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
       if (live) {
         bool nonfinite = false;
 #pragma unroll 1
-        for (int chunk = 0; chunk < kChunks; ++chunk) {
+        for (int chunk = 0; chunk < kTileChunks; ++chunk) {
           uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + b * kBN + chunk * 32, r);
+          tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + b * kTN + chunk * 32, r);
           tmem_ld_wait();
-          if (chunk == kChunks - 1) {
+          if (chunk == kTileChunks - 1) {
             // All of this warp's accumulator columns are in registers: hand
             // the buffer back to the MMA warp before the remaining math.
             tc_fence_before();
@@ -435,7 +466,7 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
         named_barrier(1, 128);
         if (live) {
           const int e = threadIdx.x - 64;
-          for (int idx = e; idx < kChunks * C * 32; idx += 128) {
+          for (int idx = e; idx < kTileChunks * C * 32; idx += 128) {
             const int chunk = idx / (C * 32);
             const int rem = idx - chunk * C * 32;
             const int c = rem >> 5;
@@ -461,7 +492,9 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
       // slices s = mt, mt + Tm, ... (ascending) of the tile's 256 B rows are
       // read from global memory (hot in L2: the same column block is streaming
       // through this SM) and folded into fma chains with q_full.
-      const int ct = prediction_index(warp) * 32 + lane;  // 0..127: rows ct and ct + 128 of the B tile
+      // 0..127: the tile's B rows ct (and ct + 128 for 256-wide tiles).
+      const int ct = prediction_index(warp) * 32 + lane;
+      constexpr int kRowsPerThread = kTN / 128;
       const float alpha = *p.alpha;
       const int num_slices = (p.k + kSliceK - 1) / kSliceK;
       const int64_t row_bytes = KIND == Kind::kFp8 ? p.k : p.k / 2;
@@ -608,19 +641,19 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
         int mt, nt;
         work_coords<PAIR>(t, p, rank, mt, nt);
         if (mt >= p.tiles_m) continue;
-        float acc[2][C][2];
+        float acc[kRowsPerThread][C][2];
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+        for (int h = 0; h < kRowsPerThread; ++h)
 #pragma unroll
           for (int c = 0; c < C; ++c) acc[h][c][0] = acc[h][c][1] = 0.f;
         for (int sl = mt; sl < num_slices; sl += p.tiles_m) {
           const int k0 = sl * kSliceK;
           constexpr int kChunksPerSlice = KIND == Kind::kFp8 ? 4 : 2;  // 16-byte chunks per row
-          uint4 raw[2][kChunksPerSlice];
-          uint32_t sfw[2];
+          uint4 raw[kRowsPerThread][kChunksPerSlice];
+          uint32_t sfw[kRowsPerThread];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int64_t r = static_cast<int64_t>(nt) * kBN + ct + 128 * h;
+          for (int h = 0; h < kRowsPerThread; ++h) {
+            const int64_t r = static_cast<int64_t>(nt) * kTN + ct + 128 * h;
             const bool row_in = r < p.n;
             const uint8_t* src = p.b + r * row_bytes + (KIND == Kind::kFp8 ? k0 : k0 / 2);
 #pragma unroll
@@ -652,7 +685,7 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
               }
             }
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
+            for (int h = 0; h < kRowsPerThread; ++h) {
               float value[8];
               if constexpr (KIND == Kind::kFp8) {
                 const uint4 chunk = raw[h][e0 >> 4];
@@ -684,8 +717,8 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
           }
         }
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int col = nt * kBN + ct + 128 * h;
+        for (int h = 0; h < kRowsPerThread; ++h) {
+          const int col = nt * kTN + ct + 128 * h;
           if (col < p.padded_n) {
             const bool in = col < p.n;
 #pragma unroll
@@ -729,7 +762,8 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(k_bytes), static_cast<uint64_t>(g.n)};
     const uint64_t strides[1] = {static_cast<uint64_t>(k_bytes)};
-    const uint32_t box[2] = {kBKBytes, PAIR ? kBN / 2 : kBN};  // pairs: each CTA stages half the tile's B rows
+    // Pairs: each CTA stages half of the tile's B rows.
+    const uint32_t box[2] = {kBKBytes, static_cast<uint32_t>(PAIR ? tile_n(KIND) / 2 : tile_n(KIND))};
     int rc = encode_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(g.b), dims,
                                strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != SDC_OK) return rc;
@@ -747,7 +781,7 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
     {
       const uint64_t dims[4] = {16, 32, k_atoms, static_cast<uint64_t>(ceil_div(g.n, 128))};
       const uint64_t strides[3] = {16, 512, 512 * k_atoms};
-      const uint32_t box[4] = {16, 32, 4, 2};
+      const uint32_t box[4] = {16, 32, 4, static_cast<uint32_t>(tile_n(KIND) / 128)};  // the tile's B row groups
       int rc = encode_tensor_map(&tsb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t*>(g.sfb),
                                  dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
       if (rc != SDC_OK) return rc;
@@ -762,7 +796,7 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   p.k = static_cast<int32_t>(g.k);
   p.num_kb = static_cast<int32_t>(ceil_div(k_bytes, kBKBytes));
   p.tiles_m = static_cast<int32_t>(ceil_div(g.m, kBM));
-  p.tiles_n = static_cast<int32_t>(ceil_div(g.n, kBN));
+  p.tiles_n = static_cast<int32_t>(ceil_div(g.n, tile_n(KIND)));
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.num_work = PAIR ? static_cast<int32_t>(ceil_div(p.tiles_m, 2)) * p.tiles_n : p.num_tiles;
   p.alpha = g.alpha;
@@ -838,10 +872,8 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
 
 template <Kind KIND, int C, bool BF16OUT, bool CHK>
 int dispatch_pair(const GemmProblem& g, cudaStream_t stream) {
-  // FP8 runs as CTA pairs (256-row tiles) whenever there are two M-tiles.
-  if constexpr (KIND == Kind::kFp8) {
-    if (g.m > kBM) return launch_impl<KIND, C, BF16OUT, CHK, true>(g, stream);
-  }
+  // CTA pairs (256-row tiles) whenever there are two M-tiles.
+  if (g.m > kBM) return launch_impl<KIND, C, BF16OUT, CHK, true>(g, stream);
   return launch_impl<KIND, C, BF16OUT, CHK, false>(g, stream);
 }
 
