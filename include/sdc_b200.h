@@ -177,6 +177,44 @@ int sdc_abft_nvfp4_reference_gemm(
     float* predicted, float* magnitude, int reference_layout, void* workspace,
     size_t workspace_bytes, sdc_stream_t stream);
 
+/* ---- block-scaled FP8 (extension; the reference has no such operator) ----
+ * e4m3 codes with one fp32 dequantisation scale per 128-wide K block of
+ * `block_rows` rows: 1 x 128 for activations (A), 128 x 128 for weights (B,
+ * stored as rows [N, K]). d = amax(|x|) / 448 (1 when amax == 0),
+ * code = e4m3_rn_satfinite(x / d). cols (K) must be a multiple of 128.
+ * scales: float [ceil(rows / block_rows)][cols / 128]. */
+int sdc_quantize_fp8_block(const void* x, int dtype, int64_t rows,
+                           int64_t cols, int block_rows, uint8_t* codes,
+                           float* scales, sdc_stream_t stream);
+
+/* D (bf16 row-major [M,N]) = sum over 128-wide K blocks kb of
+ * scale_a[m][kb] * scale_b[n / 128][kb] * (A_kb . B_kb^T), each block
+ * accumulated in fp32 on the tensor cores and the scaled sum kept in fp32. */
+int sdc_fp8_block_gemm(const uint8_t* a, const uint8_t* b_rows,
+                       const float* scale_a, const float* scale_b, int64_t m,
+                       int64_t n, int64_t k, uint16_t* d, sdc_stream_t stream);
+
+/* Block-scaled FP8 with the ABFT epilogue (observed checksums of the fp32
+ * values before the bf16 cast; Np = ceil(N/128)*128), same fault and
+ * nonfinite semantics as sdc_abft_fp8_gemm. */
+int sdc_abft_fp8_block_gemm(const uint8_t* a, const uint8_t* b_rows,
+                            const float* scale_a, const float* scale_b,
+                            int64_t m, int64_t n, int64_t k, int algorithm,
+                            const float* weights, int64_t row, int64_t col,
+                            int64_t bit, int32_t* nonfinite, uint16_t* d,
+                            float* observed, int32_t* hit, sdc_stream_t stream);
+
+/* Block-scaled FP8 with the input-fused prediction in the K-slice layout
+ * (the only layout offered; the projection uses the dequantised operands
+ * code * scale). Workspace: sdc_abft_workspace_bytes(..., SDC_LAYOUT_KSLICE). */
+int sdc_abft_fp8_block_reference_gemm(
+    const uint8_t* a, const uint8_t* b_rows, const float* scale_a,
+    const float* scale_b, int64_t m, int64_t n, int64_t k, int algorithm,
+    const float* weights, int64_t row, int64_t col, int64_t bit,
+    int32_t* nonfinite, uint16_t* d, float* observed, int32_t* hit,
+    float* predicted, float* magnitude, void* workspace,
+    size_t workspace_bytes, sdc_stream_t stream);
+
 /* ---- finalize (src/cutlass_gemm/csrc/abft/common/finalize.cu:55-319) ------
  * Sums the per-tile partials of each (channel, column) in ascending tile
  * order with IEEE round-to-nearest adds, then applies the policy
@@ -256,6 +294,13 @@ int sdc_abft_correct_nvfp4(const uint8_t* a_packed, const uint8_t* b_packed,
                            const int64_t* location, const uint8_t* located,
                            uint16_t* d_rowmajor, uint8_t* corrected,
                            sdc_stream_t stream);
+/* Block-scaled FP8: sum_k (a * scale_a) * (b * scale_b), bf16 row-major d. */
+int sdc_abft_correct_fp8_block(const uint8_t* a, const uint8_t* b_rows,
+                               const float* scale_a, const float* scale_b,
+                               int64_t m, int64_t n, int64_t k,
+                               const int64_t* location, const uint8_t* located,
+                               uint16_t* d_rowmajor, uint8_t* corrected,
+                               sdc_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -15,6 +15,10 @@
  * C99 fmaf is correctly rounded, and this file is compiled with
  * -ffp-contract=off so every other operation is a single IEEE fp32 op.
  *
+ * kind 2 is block-scaled FP8 (an sdc_b200 extension; 1 x 128 A and
+ * 128 x 128 B fp32 scales): the operands are the dequantised values
+ * code * scale and alpha is 1.
+ *
  * The KSLICE entry restates the sdc_b200 fast layout (an extension with no
  * reference counterpart): q summed over tiles ascending, then per slot
  * t = s % Tm over its 64-wide K slices s (slices ascending, k ascending).
@@ -46,9 +50,17 @@ static int64_t sf_offset(int64_t row, int64_t block, int64_t k) {
   return ((row >> 7) * k_atoms + (block >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4 + (block & 3);
 }
 
-/* kind 0: e4m3 [rows, k]; kind 1: packed e2m1 [rows, k/2] with scale atoms. */
+/* kind 0: e4m3 [rows, k]; kind 1: packed e2m1 [rows, k/2] with scale atoms;
+ * kind 2 / 3: block-scaled e4m3 with fp32 scales [rows / r, k / 128] for
+ * r = 1 (kind 2, the A operand) / 128 (kind 3, B rows): code * scale, one
+ * fp32 rounding. */
 static float value_at(int kind, const uint8_t* x, const uint8_t* sf, int64_t row, int64_t kk, int64_t k) {
   if (kind == 0) return decode_e4m3(x[row * k + kk]);
+  if (kind >= 2) {
+    const float* scales = (const float*)sf;
+    const int64_t r = kind == 2 ? row : row / 128;
+    return decode_e4m3(x[row * k + kk]) * scales[r * (k / 128) + kk / 128];
+  }
   const uint8_t byte = x[row * (k / 2) + kk / 2];
   const float code = decode_e2m1((kk & 1) ? (byte >> 4) : (byte & 15));
   return code * decode_e4m3(sf[sf_offset(row, kk / 16, k)]);
@@ -91,7 +103,7 @@ int oracle_tile_reference(int kind, const uint8_t* a, const uint8_t* sfa, const 
         float r = 0.f, s = 0.f;
         if (col < n) {
           for (int64_t kk = 0; kk < k; ++kk) {
-            const float v = value_at(kind, b, sfb, col, kk, k);
+            const float v = value_at(kind == 2 ? 3 : kind, b, sfb, col, kk, k);
             r = fmaf(qe[kk], v, r);
             s = fmaf(qa[kk], fabsf(v), s);
           }
@@ -152,7 +164,7 @@ int oracle_kslice_reference(int kind, const uint8_t* a, const uint8_t* sfa, cons
         if (col < n) {
           for (int64_t sl = slot; sl < slices; sl += tiles) {
             for (int64_t kk = sl * 64; kk < sl * 64 + 64 && kk < k; ++kk) {
-              const float v = value_at(kind, b, sfb, col, kk, k);
+              const float v = value_at(kind == 2 ? 3 : kind, b, sfb, col, kk, k);
               r = fmaf(qf[(c * 2 + 0) * k + kk], v, r);
               s = fmaf(qf[(c * 2 + 1) * k + kk], fabsf(v), s);
             }
@@ -178,7 +190,7 @@ int oracle_gemm_f64(int kind, const uint8_t* a, const uint8_t* sfa, const uint8_
   for (int64_t row = 0; row < m; ++row)
     for (int64_t kk = 0; kk < k; ++kk) av[row * k + kk] = value_at(kind, a, sfa, row, kk, k);
   for (int64_t col = 0; col < n; ++col) {
-    for (int64_t kk = 0; kk < k; ++kk) bv[kk] = value_at(kind, b, sfb, col, kk, k);
+    for (int64_t kk = 0; kk < k; ++kk) bv[kk] = value_at(kind == 2 ? 3 : kind, b, sfb, col, kk, k);
     for (int64_t row = 0; row < m; ++row) {
       double s = 0.0;
       const float* ar = av + row * k;

@@ -47,7 +47,9 @@ def lib():
 def _u8(x):
     if x is None:
         return ctypes.POINTER(ctypes.c_uint8)()
-    x = np.ascontiguousarray(x, dtype=np.uint8)
+    x = np.ascontiguousarray(x)
+    # fp32 block scales travel as their bytes.
+    x = x.view(np.uint8) if x.dtype == np.float32 else x.astype(np.uint8, copy=False)
     return x.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), x
 
 
@@ -55,11 +57,15 @@ def _ptr(x):
     return _u8(x) if x is not None else (ctypes.POINTER(ctypes.c_uint8)(), None)
 
 
+KINDS = {"fp8": 0, "nvfp4": 1, "fp8_block": 2}
+
+
 def input_reference(kind, a, sfa, b, sfb, m, n, k, weights, alpha, padded_n, layout="tile"):
     """Predicted/magnitude partials [C, Tm, padded_n] (float32).
 
-    kind: "fp8" (a: uint8 e4m3 [m,k], b: [n,k]) or "nvfp4" (packed [rows,k/2]
-    plus scale atoms). layout "tile" is the reference's per-M-tile layout.
+    kind: "fp8" (a: uint8 e4m3 [m,k], b: [n,k]), "nvfp4" (packed [rows,k/2]
+    plus scale atoms) or "fp8_block" (e4m3 plus fp32 scales [m, k/128] and
+    [ceil(n/128), k/128]). layout "tile" is the reference's per-M-tile layout.
     """
     weights = np.ascontiguousarray(weights, dtype=np.float32)
     channels = weights.shape[0]
@@ -72,7 +78,7 @@ def input_reference(kind, a, sfa, b, sfb, m, n, k, weights, alpha, padded_n, lay
     psb, ksb = _ptr(sfb)
     fn = lib().oracle_tile_reference if layout == "tile" else lib().oracle_kslice_reference
     f32 = ctypes.POINTER(ctypes.c_float)
-    rc = fn(0 if kind == "fp8" else 1, pa, psa, pb, psb, m, n, k, weights.ctypes.data_as(f32), channels,
+    rc = fn(KINDS[kind], pa, psa, pb, psb, m, n, k, weights.ctypes.data_as(f32), channels,
             ctypes.c_float(np.float32(alpha)), pred.ctypes.data_as(f32), mag.ctypes.data_as(f32), padded_n)
     if rc:
         raise MemoryError("oracle allocation failed")
@@ -86,7 +92,7 @@ def gemm_f64(kind, a, sfa, b, sfb, m, n, k):
     pb, kb = _ptr(b)
     psa, ksa = _ptr(sfa)
     psb, ksb = _ptr(sfb)
-    rc = lib().oracle_gemm_f64(0 if kind == "fp8" else 1, pa, psa, pb, psb, m, n, k,
+    rc = lib().oracle_gemm_f64(KINDS[kind], pa, psa, pb, psb, m, n, k,
                                out.ctypes.data_as(ctypes.POINTER(ctypes.c_double)))
     if rc:
         raise MemoryError("oracle allocation failed")

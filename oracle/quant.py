@@ -56,6 +56,37 @@ def quantize_nvfp4(x, global_scale="amax"):
     return pack_e2m1(e2m1_encode(normalized)), scales, st
 
 
+def quantize_fp8_block(x, block_rows):
+    """Block-scaled FP8: one fp32 scale per (block_rows x 128) block.
+
+    The reference quantises FP8 tensorwise only; this restates the recipe
+    named by the benchmark configuration (1 x 128 activation blocks,
+    128 x 128 weight blocks): d = amax(|x_block|) / 448 in fp32 (1 when the
+    block is all zero), code = e4m3_rn_satfinite(x / d). Returns
+    (codes uint8 [R, C], scales float32 [ceil(R / block_rows), C / 128]).
+    """
+    x = np.asarray(x, np.float32)
+    rows, cols = x.shape
+    if cols % 128:
+        raise ValueError("nonempty input columns must be divisible by 128")
+    if block_rows not in (1, 128):
+        raise ValueError("block_rows must be 1 or 128")
+    row_blocks = -(-rows // block_rows)
+    padded = np.zeros((row_blocks * block_rows, cols), np.float32)
+    padded[:rows] = x
+    blocks = padded.reshape(row_blocks, block_rows, cols // 128, 128)
+    amax = np.abs(blocks).max(axis=(1, 3)).astype(np.float32)
+    scales = np.where(amax == 0, np.float32(1.0), amax / np.float32(448.0)).astype(np.float32)
+    expanded = np.repeat(np.repeat(scales, block_rows, axis=0)[:rows], 128, axis=1)
+    return e4m3_encode(x / expanded), scales
+
+
+def dequantize_fp8_block(codes, scales, block_rows):
+    rows, cols = np.asarray(codes).shape
+    expanded = np.repeat(np.repeat(np.asarray(scales, np.float32), block_rows, axis=0)[:rows], 128, axis=1)
+    return e4m3_decode(codes) * expanded
+
+
 def dequantize_fp8(codes, st):
     return e4m3_decode(codes) / np.float32(st)
 

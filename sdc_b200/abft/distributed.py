@@ -146,7 +146,7 @@ def execute_sharded(a_rows, b, precision, scaling, abft_config=None, fault_confi
 
     cfg, fault = parse_abft_config(abft_config), parse_fault_config(fault_config)
     offset, total = row_offsets(a_rows.shape[0], group)
-    if precision in _LIMIT and global_scale == "amax":
+    if precision in _LIMIT and global_scale == "amax" and scaling != "blockwise":
         scale_a = global_multiplier(a_rows, precision, group)
     else:
         scale_a = global_scale
@@ -157,7 +157,9 @@ def execute_sharded(a_rows, b, precision, scaling, abft_config=None, fault_confi
     report_cfg = cfg if cfg.method == "none" else parse_abft_config({**vars(cfg), "on_error": "report"})
     output, report = None, None
     if a_rows.shape[0] > 0:
-        if precision in _LIMIT:
+        if precision in _LIMIT and scaling != "blockwise":
+            # Block scales are per row (A) and per 128 x 128 block of B, so a
+            # row shard quantises exactly like the same rows of the whole A.
             prepared = _prepare_split(a_rows, b, precision, scaling, scale_a, global_scale)
         else:
             prepared = PreparedGemm.prepare(a_rows, b, precision, scaling, global_scale)

@@ -87,7 +87,7 @@ def _report_context(prepared, cfg, fault, context, selected, output, method=None
     channels = policy.channels if policy is not None else getattr(method, "channels", 2)
     native = cfg.implementation == "native"
     return {**context, "fault": asdict(fault), "fault_selected": selected,
-            "precision": prepared.precision, "scaling": SCALING[prepared.precision],
+            "precision": prepared.precision, "scaling": getattr(prepared, "scaling", SCALING[prepared.precision]),
             "reference_mode": cfg.reference_mode, "implementation": cfg.implementation,
             "threshold_scale": cfg.threshold_scale, "checksum_input_precision": "fp32",
             "reference_algorithm": "input_fused_fp32_projection" if fused else "separate_projection_arithmetic",
@@ -119,7 +119,7 @@ def _commit_method(method, state, tensors, context, prepared):
     metadata = {key: context[key] for key in ("layer", "role", "call_index", "execution_kind", "retry",
                                               "scale_profile") if key in context}
     metadata.update(precision=prepared.precision, device=str(prepared.a.device), m=prepared.m, n=prepared.n,
-                    k=prepared.k, scaling=SCALING[prepared.precision])
+                    k=prepared.k, scaling=getattr(prepared, "scaling", SCALING[prepared.precision]))
     method.commit(state, decisions, metadata)
 
 

@@ -152,7 +152,8 @@ def _execute_native(prepared, cfg, fault, context, *, method=None, policy=None, 
     if cfg.recovery in {"recompute", "correct"} and bool(tensors["detected"].item()):
         with phase("recover_recheck"):
             if cfg.recovery == "correct" and locate and bool(tensors["located"].item()):
-                correct = ops.abft_fp8_correct if prepared.precision == "fp8" else ops.abft_nvfp4_correct
+                correct = (ops.abft_fp8_block_correct if getattr(prepared, "blockwise", False) else
+                           ops.abft_fp8_correct if prepared.precision == "fp8" else ops.abft_nvfp4_correct)
                 corrected = correct(*prepared._native_args(), tensors["location"], tensors["located"], output)
                 tensors["recovered"] = corrected
                 tensors["recheck_failed"] = ~corrected

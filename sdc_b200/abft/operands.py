@@ -6,7 +6,9 @@ to K-major rows), ``raw_native`` / ``collected_native`` /
 ``collected_reference_native`` op routing, the CPU-capable ``decode_block``
 and ``injected`` input-code bit flips (NVFP4 nibble rule). FP32/BF16 operands
 are kept for the separate reference mode and CPU tests; their native GEMMs
-are outside this path.
+are outside this path. Extension: FP8 ``scaling="blockwise"`` (1 x 128 A and
+128 x 128 B fp32 block scales in ``sfa``/``sfb``, no alpha) routes to the
+block-scaled ops, whose input-fused prediction has the K-slice layout only.
 """
 from __future__ import annotations
 
@@ -16,6 +18,7 @@ from typing import Any
 import torch
 
 SCALING = {"fp32": "none", "bf16": "none", "fp8": "tensorwise", "nvfp4": "block16"}
+SCALINGS = {"fp32": {"none"}, "bf16": {"none"}, "fp8": {"tensorwise", "blockwise"}, "nvfp4": {"block16"}}
 INPUT_REFERENCE_PRECISIONS = frozenset({"fp8", "nvfp4"})
 LAYOUTS = {"tile": 0, "kslice": 1}
 _E2M1 = (0., .5, 1., 1.5, 2., 3., 4., 6., -0., -.5, -1., -1.5, -2., -3., -4., -6.)
@@ -39,10 +42,19 @@ class PreparedGemm:
     alpha: Any = None
     sfa: Any = None
     sfb: Any = None
+    scaling: str = ""
+
+    def __post_init__(self):
+        if not self.scaling:
+            self.scaling = SCALING[self.precision]
+
+    @property
+    def blockwise(self):
+        return self.scaling == "blockwise"
 
     @classmethod
     def prepare(cls, a, b, precision, scaling, global_scale="amax"):
-        if precision not in SCALING or scaling != SCALING[precision]:
+        if precision not in SCALINGS or scaling not in SCALINGS[precision]:
             raise ValueError("Incompatible precision/scaling")
         if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[0] or a.device != b.device:
             raise ValueError("GEMM requires compatible matrices on one device")
@@ -54,9 +66,12 @@ class PreparedGemm:
             dtype = torch.float32 if precision == "fp32" else torch.bfloat16
             return cls(a.to(dtype), b.to(dtype), precision, m, n, k)
         from .. import require_device
-        from ..gemm.quantization import quantize
+        from ..gemm.quantization import quantize, quantize_blockwise
 
         require_device(a.device)
+        if scaling == "blockwise":
+            qa, qb = quantize_blockwise(a.contiguous(), 1), quantize_blockwise(b.T.contiguous(), 128)
+            return cls(qa.codes, qb.codes, precision, m, n, k, qa, qb, None, qa.scales, qb.scales, scaling)
         qa = quantize(a.contiguous(), precision, global_scale)
         qb = quantize(b.T.contiguous(), precision, global_scale)
         alpha = (qa.multiplier * qb.multiplier).reciprocal()
@@ -66,6 +81,8 @@ class PreparedGemm:
         return prepared
 
     def _native_args(self):
+        if self.blockwise:
+            return (self.a.view(torch.float8_e4m3fn), self.b.view(torch.float8_e4m3fn), self.sfa, self.sfb)
         if self.precision == "fp8":
             return (self.a.view(torch.float8_e4m3fn), self.b.view(torch.float8_e4m3fn), self.alpha)
         if self.precision == "nvfp4":
@@ -77,7 +94,7 @@ class PreparedGemm:
             from ..gemm import backend
             return backend.mm(self.a, self.b)
         ops = _ops()
-        gemm = ops.fp8_mm if self.precision == "fp8" else ops.nvfp4_mm
+        gemm = ops.fp8_block_mm if self.blockwise else ops.fp8_mm if self.precision == "fp8" else ops.nvfp4_mm
         return gemm(*self._native_args())
 
     def collected_native(self, weights, fault=(-1, -1, -1), *, algorithm=0, nonfinite=None):
@@ -87,7 +104,8 @@ class PreparedGemm:
             from .. import require_device
             require_device(self.a.device)
             return ops.abft_mm(self.a, self.b, weights, *fault, algorithm, nonfinite)
-        op = ops.abft_fp8_mm if self.precision == "fp8" else ops.abft_nvfp4_mm
+        op = (ops.abft_fp8_block_mm if self.blockwise else ops.abft_fp8_mm if self.precision == "fp8"
+              else ops.abft_nvfp4_mm)
         return op(*self._native_args(), weights, *fault, algorithm, nonfinite)
 
     def collected_reference_native(self, weights, fault=(-1, -1, -1), *, algorithm=0, nonfinite=None,
@@ -96,6 +114,11 @@ class PreparedGemm:
         if self.precision not in INPUT_REFERENCE_PRECISIONS:
             raise NotImplementedError(f"input_fused reference is not implemented for {self.precision}")
         ops = _ops()
+        if self.blockwise:
+            if layout != "kslice":
+                raise NotImplementedError("block-scaled FP8 computes its input-fused prediction in the kslice "
+                                          "layout only")
+            return ops.abft_fp8_block_reference_mm(*self._native_args(), weights, *fault, algorithm, nonfinite)
         op = ops.abft_fp8_reference_mm if self.precision == "fp8" else ops.abft_nvfp4_reference_mm
         return op(*self._native_args(), weights, *fault, algorithm, nonfinite, LAYOUTS[layout])
 
@@ -109,6 +132,11 @@ class PreparedGemm:
             return self.a[:, start:end].float(), self.b[start:end, :].float()
 
         def decode(codes, q):
+            if self.blockwise:
+                scales = q.scales[:, start // 128:(end + 127) // 128].repeat_interleave(q.block_rows, 0)
+                scales = scales[:codes.shape[0]].repeat_interleave(128, 1)
+                offset = start - (start // 128) * 128
+                return codes[:, start:end].view(torch.float8_e4m3fn).float() * scales[:, offset:offset + end - start]
             if self.precision == "fp8":
                 return codes[:, start:end].view(torch.float8_e4m3fn).float() / q.multiplier
             packed = codes[:, start // 2:end // 2]

@@ -90,7 +90,8 @@ def _scope_key(scope):
     profile = scope["scale_profile"]
     if type(profile) is not dict or set(profile) != {"scaling", "global_scale", "input_dtypes"}:
         raise ValueError("ABFT scale profile metadata is invalid")
-    if profile["scaling"] != _SCALING[scope["precision"]]:
+    if profile["scaling"] != _SCALING[scope["precision"]] and (scope["precision"], profile["scaling"]) != (
+            "fp8", "blockwise"):
         raise ValueError("ABFT precision/scale profile mismatch")
     scale = profile["global_scale"]
     if scale != "amax" and (type(scale) not in (int, float) or not math.isfinite(scale) or scale <= 0):

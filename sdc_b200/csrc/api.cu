@@ -47,6 +47,19 @@ int check_nvfp4(const uint8_t* a, const uint8_t* b, const uint8_t* sfa, const ui
   return SDC_OK;
 }
 
+int check_fp8_block(const uint8_t* a, const uint8_t* b, const float* sa, const float* sb, int64_t m, int64_t n,
+                    int64_t k, const void* d) {
+  int rc = check_dims(m, n, k);
+  if (rc != SDC_OK) return rc;
+  SDC_REQUIRE(a != nullptr && b != nullptr && sa != nullptr && sb != nullptr && d != nullptr,
+              "block-scaled FP8 GEMM pointers must not be null");
+  SDC_REQUIRE(k % 128 == 0, "block-scaled FP8 K must be a multiple of 128 (one scale per 128-wide block)");
+  SDC_REQUIRE(reinterpret_cast<uintptr_t>(a) % 16 == 0 && reinterpret_cast<uintptr_t>(b) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(sa) % 4 == 0 && reinterpret_cast<uintptr_t>(sb) % 4 == 0,
+              "block-scaled FP8 operands must be 16-byte aligned and scales 4-byte aligned");
+  return SDC_OK;
+}
+
 int check_abft(int algorithm, const float* weights, int64_t m, int64_t n, int64_t row, int64_t col,
                int64_t bit, const float* observed, const int32_t* hit) {
   if (policy_channels(algorithm) == 0) return fail(SDC_ERR_UNKNOWN_ALGORITHM, "Unknown compiled ABFT algorithm ID");
@@ -224,6 +237,48 @@ int sdc_abft_nvfp4_reference_gemm(const uint8_t* a_packed, const uint8_t* b_pack
   GemmProblem g = make_problem(Kind::kNvf4, a_packed, b_packed, sfa, sfb, m, n, k, alpha, true, d);
   set_abft(g, algorithm, weights, row, col, bit, nonfinite, observed, hit, 128);
   return run_input_fused(g, predicted, magnitude, reference_layout, workspace, workspace_bytes, stream);
+}
+
+// ---- block-scaled FP8 (extension: no reference operator) ----
+
+int sdc_fp8_block_gemm(const uint8_t* a, const uint8_t* b_rows, const float* scale_a, const float* scale_b,
+                       int64_t m, int64_t n, int64_t k, uint16_t* d, sdc_stream_t stream) {
+  using namespace sdc;
+  int rc = check_fp8_block(a, b_rows, scale_a, scale_b, m, n, k, d);
+  if (rc != SDC_OK) return rc;
+  return launch_gemm(make_problem(Kind::kFp8Block, a, b_rows, reinterpret_cast<const uint8_t*>(scale_a),
+                                  reinterpret_cast<const uint8_t*>(scale_b), m, n, k, nullptr, true, d),
+                     stream);
+}
+
+int sdc_abft_fp8_block_gemm(const uint8_t* a, const uint8_t* b_rows, const float* scale_a,
+                            const float* scale_b, int64_t m, int64_t n, int64_t k, int algorithm,
+                            const float* weights, int64_t row, int64_t col, int64_t bit, int32_t* nonfinite,
+                            uint16_t* d, float* observed, int32_t* hit, sdc_stream_t stream) {
+  using namespace sdc;
+  int rc = check_fp8_block(a, b_rows, scale_a, scale_b, m, n, k, d);
+  if (rc == SDC_OK) rc = check_abft(algorithm, weights, m, n, row, col, bit, observed, hit);
+  if (rc != SDC_OK) return rc;
+  GemmProblem g = make_problem(Kind::kFp8Block, a, b_rows, reinterpret_cast<const uint8_t*>(scale_a),
+                               reinterpret_cast<const uint8_t*>(scale_b), m, n, k, nullptr, true, d);
+  set_abft(g, algorithm, weights, row, col, bit, nonfinite, observed, hit, 128);
+  return launch_gemm(g, stream);
+}
+
+int sdc_abft_fp8_block_reference_gemm(const uint8_t* a, const uint8_t* b_rows, const float* scale_a,
+                                      const float* scale_b, int64_t m, int64_t n, int64_t k, int algorithm,
+                                      const float* weights, int64_t row, int64_t col, int64_t bit,
+                                      int32_t* nonfinite, uint16_t* d, float* observed, int32_t* hit,
+                                      float* predicted, float* magnitude, void* workspace,
+                                      size_t workspace_bytes, sdc_stream_t stream) {
+  using namespace sdc;
+  int rc = check_fp8_block(a, b_rows, scale_a, scale_b, m, n, k, d);
+  if (rc == SDC_OK) rc = check_abft(algorithm, weights, m, n, row, col, bit, observed, hit);
+  if (rc != SDC_OK) return rc;
+  GemmProblem g = make_problem(Kind::kFp8Block, a, b_rows, reinterpret_cast<const uint8_t*>(scale_a),
+                               reinterpret_cast<const uint8_t*>(scale_b), m, n, k, nullptr, true, d);
+  set_abft(g, algorithm, weights, row, col, bit, nonfinite, observed, hit, 128);
+  return run_input_fused(g, predicted, magnitude, SDC_LAYOUT_KSLICE, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

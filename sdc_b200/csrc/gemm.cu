@@ -50,7 +50,7 @@ constexpr uint32_t kTmemCols = 512;
 // would leave room for two accumulators next to the block scales, but the
 // extra operand traffic per MAC costs more (measured: 2.2 vs 3.1 PF/s
 // unprotected at 16384^3) than the exposed epilogue of one accumulator.
-__host__ __device__ constexpr int tile_n(Kind) { return kBN; }
+__host__ __device__ constexpr int tile_n(Kind k) { return k == Kind::kFp8Block ? kBN / 2 : kBN; }
 __host__ __device__ constexpr int chunks(Kind k) { return tile_n(k) / 32; }
 // NVFP4 block scales in TMEM after the accumulator(s): per 64-wide k-step,
 // 4 columns per 128 rows of A (the CTA's M-tile) and of B (the tile's rows).
@@ -75,19 +75,26 @@ __host__ __device__ constexpr int stage_bytes(Kind k, bool pair = false) {
   return kABytes + b_stage_bytes(k, pair) + (k == Kind::kNvf4 ? kSfaBytes + kSfbBytes : 0);
 }
 __host__ __device__ constexpr int num_stages(Kind k, bool pair) {
-  return pair ? (k == Kind::kFp8 ? 6 : 5) : kStages;
+  return pair ? (k == Kind::kFp8 ? 6 : k == Kind::kFp8Block ? 8 : 5) : kStages;
 }
 __host__ __device__ constexpr int smem_bytes(Kind k, bool pair = false) {
   return 1024 + num_stages(k, pair) * stage_bytes(k, pair) + kRedFloats * 4 + 256;
 }
-__host__ __device__ constexpr int num_acc(Kind k) { return k == Kind::kFp8 ? 2 : 1; }
-__host__ __device__ constexpr int num_threads(bool chk) { return chk ? 320 : 192; }
-__device__ __forceinline__ bool is_prediction_warp(int warp) { return warp >= 6; }
+__host__ __device__ constexpr int num_acc(Kind k) { return k == Kind::kNvf4 ? 1 : 2; }
+// Warps: 0 TMA, 1 MMA, 2-5 epilogue, then 6-9 prediction (checked
+// K-slice launches) and 4 promotion warps (block-scaled FP8).
+__host__ __device__ constexpr int num_threads(bool chk, bool blk = false) {
+  return 192 + (chk ? 128 : 0) + (blk ? 128 : 0);
+}
+__device__ __forceinline__ bool is_prediction_warp(int warp) { return warp >= 6 && warp < 10; }
 __device__ __forceinline__ int prediction_index(int warp) { return warp - 6; }
 
 struct Params {
   int32_t m, n, k, num_kb, tiles_m, tiles_n, num_tiles;
   int32_t num_work;  // tiles, or 256-row pair tiles when CTAs are paired
+  const float* sa;   // block-scaled FP8: A scales [M][K/128], B scales [ceil(N/128)][K/128]
+  const float* sb;
+  int32_t k_blocks;
   const float* alpha;
   void* d;
   const float* weights;
@@ -187,7 +194,7 @@ __device__ __forceinline__ bool prediction_grid_barrier(uint32_t* counter, uint3
 __device__ __forceinline__ uint64_t sf_desc(uint32_t addr) { return smem_desc(addr, 0, 128, 0); }
 
 template <Kind KIND, int C, bool BF16OUT, bool CHK, bool PAIR>
-__global__ void __launch_bounds__(num_threads(CHK), 1)
+__global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ CUtensorMap tm_sfa,
                 const __grid_constant__ CUtensorMap tm_sfb, const Params p) {
@@ -197,6 +204,12 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
   constexpr int kTileChunks = chunks(KIND);
   constexpr int kStageBytes = stage_bytes(KIND, PAIR);
   constexpr int kAcc = num_acc(KIND);
+  // Block-scaled FP8: the MMA writes each 128-wide K block into one of two
+  // partial accumulators (TMEM columns 256..511); promotion warps add
+  // scale_a * scale_b * partial into the tile total (columns 0..255, two
+  // buffers), which the epilogue then reads like an ordinary accumulator.
+  constexpr bool BLK = KIND == Kind::kFp8Block;
+  constexpr uint32_t kPartialCol = 256;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -205,7 +218,9 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
   uint64_t* empty = full + kS;
   uint64_t* acc_full = empty + kS;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* part_full = acc_empty + 2;
+  uint64_t* part_empty = part_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(part_empty + 2);
   volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(tmem_slot + 1);
   // Tiles whose epilogue has finished: paces the prediction warps.
   volatile uint32_t* tiles_done = tmem_slot + 2;
@@ -225,8 +240,12 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
       mbar_init(empty + s, 1);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(acc_full + b, 1);
-      mbar_init(acc_empty + b, PAIR ? 8 : 4);
+      // Block-scaled: totals pass between this CTA's promotion and epilogue
+      // warps; otherwise the (leader's) MMA waits for both CTAs' epilogues.
+      mbar_init(acc_full + b, BLK ? 4 : 1);
+      mbar_init(acc_empty + b, (PAIR && !BLK) ? 8 : 4);
+      mbar_init(part_full + b, 1);
+      mbar_init(part_empty + b, PAIR ? 8 : 4);
     }
     *abort_flag = 0;
     *tiles_done = 0;
@@ -301,6 +320,98 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
         }
       }
     }
+  } else if (warp == 1 && BLK) {
+    // ---------------- MMA issuer, block-scaled: one partial per K block ----------------
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_e4m3(PAIR ? 2 * kBM : kBM, kTN);
+      uint32_t kbg = 0;
+      for (int t = work_first; t < p.num_work && !*abort_flag; t += work_step) {
+        for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
+          const int s = kbg % kS;
+          const uint32_t pb = kbg & 1u;
+          if (kbg >= 2) {
+            if (!mbar_wait(part_empty + pb, ((kbg >> 1) - 1) & 1, kWaitAccumFree, abort_flag, p.watchdog)) break;
+          }
+          if (!mbar_wait(full + s, (kbg / kS) & 1, kWaitFull, abort_flag, p.watchdog)) break;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * kStageBytes);
+          const uint32_t sb = sa + kABytes;
+          const uint32_t d_tmem = tmem + kPartialCol + pb * kTN;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t acc = j > 0 ? 1u : 0u;
+            if constexpr (PAIR) {
+              mma_f8f6f4_pair(d_tmem, sw128_desc(sa + 32 * j), sw128_desc(sb + 32 * j), idesc, acc);
+            } else {
+              mma_f8f6f4(d_tmem, sw128_desc(sa + 32 * j), sw128_desc(sb + 32 * j), idesc, acc);
+            }
+          }
+          if constexpr (PAIR) {
+            tc_commit_pair(empty + s, 0x3);
+            tc_commit_pair(part_full + pb, 0x3);
+          } else {
+            tc_commit(empty + s);
+            tc_commit(part_full + pb);
+          }
+        }
+      }
+    }
+  } else if (BLK && warp >= (CHK ? 10 : 6)) {
+    // ---------------- promotion (block-scaled): total += sa * sb * partial ----------------
+    const int q = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    uint32_t kbg = 0;
+    int i = 0;
+    for (int t = work_first; t < p.num_work && !*abort_flag; t += work_step, ++i) {
+      int mt, nt;
+      work_coords<PAIR>(t, p, rank, mt, nt);
+      const int row = mt * kBM + q * 32 + lane;
+      const float* sa_row = p.sa + static_cast<int64_t>(row < p.m ? row : 0) * p.k_blocks;
+      const float* sb_blk = p.sb + static_cast<int64_t>(nt) * p.k_blocks;  // 128-wide tile = one B block
+      const uint32_t tb = static_cast<uint32_t>(i & 1);
+      bool ok = true;
+      if (i >= 2) {
+        ok = mbar_wait(acc_empty + tb, ((i >> 1) - 1) & 1, kWaitAccumFree, abort_flag, p.watchdog);
+        tc_fence_after();
+      }
+      for (int kb = 0; kb < p.num_kb && ok; ++kb, ++kbg) {
+        const uint32_t pb = kbg & 1u;
+        const float scale = __fmul_rn(row < p.m ? __ldg(sa_row + kb) : 0.f, __ldg(sb_blk + kb));
+        if (!mbar_wait(part_full + pb, (kbg >> 1) & 1, kWaitAccum, abort_flag, p.watchdog)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int chunk = 0; chunk < kTileChunks; ++chunk) {
+          uint32_t part[32], total[32];
+          tmem_ld_32x32b_x32(tmem + lane_base + kPartialCol + pb * kTN + chunk * 32, part);
+          if (kb > 0) tmem_ld_32x32b_x32(tmem + lane_base + tb * kTN + chunk * 32, total);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float x = __uint_as_float(part[j]);
+            total[j] = __float_as_uint(kb > 0 ? fmaf(scale, x, __uint_as_float(total[j])) : __fmul_rn(scale, x));
+          }
+          tmem_st_32x32b_x32(tmem + lane_base + tb * kTN + chunk * 32, total);
+        }
+        tmem_st_wait();
+        // The partial is consumed: hand it back to the MMA warp.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (PAIR) {
+            mbar_arrive_cluster(mapa_shared(part_empty + pb, 0));
+          } else {
+            mbar_arrive(part_empty + pb);
+          }
+        }
+      }
+      if (!ok) break;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_full + tb);
+    }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0 && leader) {
@@ -368,7 +479,7 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
   } else if (warp < 6) {
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const float alpha = *p.alpha;
+    const float alpha = BLK ? 1.f : *p.alpha;  // block scales are applied by the promotion warps
     int i = 0;
     for (int t = work_first; t < p.num_work; t += work_step, ++i) {
       int mt, nt;
@@ -396,7 +507,7 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-              if constexpr (PAIR) {
+              if constexpr (PAIR && !BLK) {
                 mbar_arrive_cluster(mapa_shared(acc_empty + b, 0));  // the leader's MMA waits on both CTAs
               } else {
                 mbar_arrive(acc_empty + b);
@@ -495,9 +606,9 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
       // 0..127: the tile's B rows ct (and ct + 128 for 256-wide tiles).
       const int ct = prediction_index(warp) * 32 + lane;
       constexpr int kRowsPerThread = kTN / 128;
-      const float alpha = *p.alpha;
+      const float alpha = BLK ? 1.f : *p.alpha;
       const int num_slices = (p.k + kSliceK - 1) / kSliceK;
-      const int64_t row_bytes = KIND == Kind::kFp8 ? p.k : p.k / 2;
+      const int64_t row_bytes = is_e4m3(KIND) ? p.k : p.k / 2;
       const int64_t k_atoms = (p.k + 63) / 64;
       const int64_t k_pad = static_cast<int64_t>(num_slices) * kSliceK;
       // Pacing: this work is spread over the CTA's tiles (projection during
@@ -551,9 +662,11 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
               const int64_t row = r0 + 8 * i;
               const bool row_in = row < row_end;
               const bool in = row_in && k_in;
-              if constexpr (KIND == Kind::kFp8) {
+              if constexpr (is_e4m3(KIND)) {
                 raw[i] = in ? __ldg(reinterpret_cast<const uint4*>(p.a + row * row_bytes + k0))
                             : make_uint4(0, 0, 0, 0);
+                // Block-scaled: the row's scale of the 128-wide block holding these 16 k.
+                if constexpr (BLK) sfv[i] = in ? __float_as_uint(__ldg(p.sa + row * p.k_blocks + (k0 >> 7))) : 0u;
               } else {
                 const uint2 u = in ? __ldg(reinterpret_cast<const uint2*>(p.a + row * row_bytes + k0 / 2))
                                    : make_uint2(0, 0);
@@ -571,12 +684,17 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
             for (int i = 0; i < kBatch; ++i) {
               if (r0 + 8 * i >= row_end) break;
               float v[16];
-              if constexpr (KIND == Kind::kFp8) {
+              if constexpr (is_e4m3(KIND)) {
                 const uint32_t words[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                   const float2 lo = e4m3x2_to_float2(words[j] & 0xFFFFu), hi = e4m3x2_to_float2(words[j] >> 16);
                   v[4 * j] = lo.x; v[4 * j + 1] = lo.y; v[4 * j + 2] = hi.x; v[4 * j + 3] = hi.y;
+                }
+                if constexpr (BLK) {
+                  const float scale = __uint_as_float(sfv[i]);
+#pragma unroll
+                  for (int e = 0; e < 16; ++e) v[e] = __fmul_rn(v[e], scale);
                 }
               } else {
                 float lo8[8], hi8[8];
@@ -648,23 +766,26 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
           for (int c = 0; c < C; ++c) acc[h][c][0] = acc[h][c][1] = 0.f;
         for (int sl = mt; sl < num_slices; sl += p.tiles_m) {
           const int k0 = sl * kSliceK;
-          constexpr int kChunksPerSlice = KIND == Kind::kFp8 ? 4 : 2;  // 16-byte chunks per row
+          constexpr int kChunksPerSlice = is_e4m3(KIND) ? 4 : 2;  // 16-byte chunks per row
           uint4 raw[kRowsPerThread][kChunksPerSlice];
           uint32_t sfw[kRowsPerThread];
 #pragma unroll
           for (int h = 0; h < kRowsPerThread; ++h) {
             const int64_t r = static_cast<int64_t>(nt) * kTN + ct + 128 * h;
             const bool row_in = r < p.n;
-            const uint8_t* src = p.b + r * row_bytes + (KIND == Kind::kFp8 ? k0 : k0 / 2);
+            const uint8_t* src = p.b + r * row_bytes + (is_e4m3(KIND) ? k0 : k0 / 2);
 #pragma unroll
             for (int ch = 0; ch < kChunksPerSlice; ++ch) {
-              const int byte = (KIND == Kind::kFp8 ? k0 : k0 / 2) + ch * 16;
+              const int byte = (is_e4m3(KIND) ? k0 : k0 / 2) + ch * 16;
               raw[h][ch] = (row_in && byte < row_bytes) ? __ldg(reinterpret_cast<const uint4*>(src) + ch)
                                                          : make_uint4(0, 0, 0, 0);
             }
             if constexpr (KIND == Kind::kNvf4) {
               const int64_t off = ((r >> 7) * k_atoms + (k0 >> 6)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4;
               sfw[h] = row_in ? __ldg(reinterpret_cast<const uint32_t*>(p.sfb + off)) : 0u;
+            } else if constexpr (BLK) {
+              // The scale of this row's 128 x 128 block holding the slice.
+              sfw[h] = row_in ? __float_as_uint(__ldg(p.sb + (r >> 7) * p.k_blocks + (k0 >> 7))) : 0u;
             }
           }
           // q_full is zero-padded to a multiple of 64 K, so loads need no guard;
@@ -687,7 +808,7 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
 #pragma unroll
             for (int h = 0; h < kRowsPerThread; ++h) {
               float value[8];
-              if constexpr (KIND == Kind::kFp8) {
+              if constexpr (is_e4m3(KIND)) {
                 const uint4 chunk = raw[h][e0 >> 4];
                 const uint32_t w0 = (e0 & 8) ? chunk.z : chunk.x;
                 const uint32_t w1 = (e0 & 8) ? chunk.w : chunk.y;
@@ -695,6 +816,11 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
                 const float2 v45 = e4m3x2_to_float2(w1 & 0xFFFFu), v67 = e4m3x2_to_float2(w1 >> 16);
                 value[0] = v01.x; value[1] = v01.y; value[2] = v23.x; value[3] = v23.y;
                 value[4] = v45.x; value[5] = v45.y; value[6] = v67.x; value[7] = v67.y;
+                if constexpr (BLK) {
+                  const float scale = __uint_as_float(sfw[h]);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) value[e] = __fmul_rn(value[e], scale);
+                }
               } else {
                 const uint4 chunk = raw[h][e0 >> 5];
                 const int wi = (e0 >> 3) & 3;
@@ -749,7 +875,7 @@ __global__ void __launch_bounds__(num_threads(CHK), 1)
 
 template <Kind KIND, int C, bool BF16OUT, bool CHK, bool PAIR>
 int launch_impl(const GemmProblem& g, cudaStream_t stream) {
-  const int64_t k_bytes = KIND == Kind::kFp8 ? g.k : g.k / 2;
+  const int64_t k_bytes = is_e4m3(KIND) ? g.k : g.k / 2;
   CUtensorMap ta{}, tb{}, tsa{}, tsb{};
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(k_bytes), static_cast<uint64_t>(g.m)};
@@ -799,6 +925,11 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   p.tiles_n = static_cast<int32_t>(ceil_div(g.n, tile_n(KIND)));
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.num_work = PAIR ? static_cast<int32_t>(ceil_div(p.tiles_m, 2)) * p.tiles_n : p.num_tiles;
+  if constexpr (KIND == Kind::kFp8Block) {
+    p.sa = reinterpret_cast<const float*>(g.sfa);
+    p.sb = reinterpret_cast<const float*>(g.sfb);
+    p.k_blocks = static_cast<int32_t>(g.k / 128);
+  }
   p.alpha = g.alpha;
   p.d = g.d;
   p.weights = g.weights;
@@ -824,7 +955,7 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   auto kernel = gemm_kernel<KIND, C, BF16OUT, CHK, PAIR>;
   constexpr int smem = smem_bytes(KIND, PAIR);
   cudaLaunchConfig_t config{};
-  config.blockDim = dim3(num_threads(CHK));
+  config.blockDim = dim3(num_threads(CHK, KIND == Kind::kFp8Block));
   config.dynamicSmemBytes = smem;
   config.stream = stream;
   cudaLaunchAttribute attribute[2];
@@ -905,6 +1036,11 @@ int launch_gemm(const GemmProblem& g, cudaStream_t stream) {
     if (g.channels == 0) return dispatch_out<Kind::kFp8, 0>(g, stream);
     if (g.channels == 1) return dispatch_out<Kind::kFp8, 1>(g, stream);
     return dispatch_out<Kind::kFp8, 2>(g, stream);
+  }
+  if (g.kind == Kind::kFp8Block) {
+    if (g.channels == 0) return dispatch_out<Kind::kFp8Block, 0>(g, stream);
+    if (g.channels == 1) return dispatch_out<Kind::kFp8Block, 1>(g, stream);
+    return dispatch_out<Kind::kFp8Block, 2>(g, stream);
   }
   if (g.channels == 0) return dispatch_out<Kind::kNvf4, 0>(g, stream);
   if (g.channels == 1) return dispatch_out<Kind::kNvf4, 1>(g, stream);

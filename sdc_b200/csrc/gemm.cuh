@@ -5,7 +5,11 @@
 
 namespace sdc {
 
-enum class Kind : int { kFp8 = 0, kNvf4 = 1 };
+// kFp8Block: e4m3 codes with fp32 dequantisation scales per 1 x 128 block of
+// A (sfa: float [M][K/128]) and per 128 x 128 block of B rows (sfb: float
+// [ceil(N/128)][K/128]); bf16 row-major output.
+enum class Kind : int { kFp8 = 0, kNvf4 = 1, kFp8Block = 2 };
+__host__ __device__ constexpr bool is_e4m3(Kind k) { return k != Kind::kNvf4; }
 
 struct GemmProblem {
   Kind kind;

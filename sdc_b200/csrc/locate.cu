@@ -84,6 +84,11 @@ __global__ void __launch_bounds__(kLocThreads)
     if constexpr (KIND == Kind::kFp8) {
       av = decode_e4m3(a[row * k + kk]);
       bv = decode_e4m3(b[col * k + kk]);
+    } else if constexpr (KIND == Kind::kFp8Block) {
+      // fp32 scales [m, k/128] (A) and [ceil(n/128), k/128] (B rows).
+      const int64_t kb = k / 128;
+      av = __fmul_rn(decode_e4m3(a[row * k + kk]), reinterpret_cast<const float*>(sfa)[row * kb + (kk >> 7)]);
+      bv = __fmul_rn(decode_e4m3(b[col * k + kk]), reinterpret_cast<const float*>(sfb)[(col >> 7) * kb + (kk >> 7)]);
     } else {
       const int64_t k_atoms = (k + 63) / 64;
       const auto sf_off = [k_atoms](int64_t r, int64_t blk) {
@@ -103,7 +108,7 @@ __global__ void __launch_bounds__(kLocThreads)
     __syncthreads();
   }
   if (threadIdx.x == 0) {
-    const float v = __fmul_rn(*alpha, partial[0]);
+    const float v = alpha != nullptr ? __fmul_rn(*alpha, partial[0]) : partial[0];
     if constexpr (BF16OUT) {
       static_cast<uint16_t*>(d)[row * n + col] = float_to_bf16_bits(v);
     } else {
@@ -153,6 +158,21 @@ int sdc_abft_correct_nvfp4(const uint8_t* a_packed, const uint8_t* b_packed, con
   SDC_REQUIRE(m > 0 && n > 0 && k > 0 && k % 32 == 0, "correct needs positive dimensions, k % 32 == 0");
   correct_kernel<Kind::kNvf4, true><<<1, kLocThreads, 0, stream>>>(
       a_packed, b_packed, sfa, sfb, m, n, k, alpha, location, located, d_rowmajor, corrected);
+  SDC_CUDA_CHECK(cudaGetLastError());
+  return SDC_OK;
+}
+
+int sdc_abft_correct_fp8_block(const uint8_t* a, const uint8_t* b_rows, const float* scale_a,
+                               const float* scale_b, int64_t m, int64_t n, int64_t k, const int64_t* location,
+                               const uint8_t* located, uint16_t* d_rowmajor, uint8_t* corrected,
+                               sdc_stream_t stream) {
+  using namespace sdc;
+  SDC_REQUIRE(a && b_rows && scale_a && scale_b && location && located && d_rowmajor && corrected,
+              "correct pointers must not be null");
+  SDC_REQUIRE(m > 0 && n > 0 && k > 0 && k % 128 == 0, "correct needs positive dimensions, k % 128 == 0");
+  correct_kernel<Kind::kFp8Block, true><<<1, kLocThreads, 0, stream>>>(
+      a, b_rows, reinterpret_cast<const uint8_t*>(scale_a), reinterpret_cast<const uint8_t*>(scale_b), m, n, k,
+      nullptr, location, located, d_rowmajor, corrected);
   SDC_CUDA_CHECK(cudaGetLastError());
   return SDC_OK;
 }

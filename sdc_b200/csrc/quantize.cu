@@ -211,6 +211,68 @@ int grid_for(int64_t work) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(148 * 16, ceil_div(work, kQuantThreads))));
 }
 
+// ---- block-scaled FP8 (1 x 128 and 128 x 128 fp32 scales) ----------------
+// A 128-wide K block of `BR` rows shares one dequantisation scale
+// d = amax(|x|) / 448 (1 when amax == 0); codes = e4m3_rn_satfinite(x / d),
+// so x ~ code * d. BR = 1 (activations, one warp per block) or 128 (weights,
+// one CTA per block).
+template <int DT, int BR>
+__global__ void __launch_bounds__(kQuantThreads)
+    fp8_block_cast(const void* x, int64_t rows, int64_t cols, uint8_t* codes, float* scales) {
+  const int64_t kblocks = cols / 128;
+  if constexpr (BR == 1) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t blk = static_cast<int64_t>(blockIdx.x) * (kQuantThreads / 32) + warp;
+    if (blk >= rows * kblocks) return;
+    const int64_t r = blk / kblocks, kb = blk - r * kblocks;
+    const int64_t base = r * cols + kb * 128 + lane * 4;
+    float v[4];
+    uint32_t bits = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      v[e] = load_elem<DT>(x, base + e);
+      bits = max(bits, abs_bits(v[e]));
+    }
+    for (int o = 16; o > 0; o >>= 1) bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, o));
+    const float amax = __uint_as_float(bits);
+    const float d = amax == 0.f ? 1.f : __fdiv_rn(amax, 448.f);
+    const uint32_t lo = cvt_e4m3x2(__fdiv_rn(v[0], d), __fdiv_rn(v[1], d));
+    const uint32_t hi = cvt_e4m3x2(__fdiv_rn(v[2], d), __fdiv_rn(v[3], d));
+    *reinterpret_cast<uint32_t*>(codes + base) = lo | (hi << 16);
+    if (lane == 0) scales[r * kblocks + kb] = d;
+  } else {
+    __shared__ uint32_t warp_max[kQuantThreads / 32];
+    const int64_t rb = blockIdx.x / kblocks, kb = blockIdx.x - rb * kblocks;
+    const int64_t r = rb * 128 + (threadIdx.x >> 1);
+    const int64_t base = r * cols + kb * 128 + (threadIdx.x & 1) * 64;
+    const bool in = r < rows;
+    float v[64];
+    uint32_t bits = 0;
+#pragma unroll
+    for (int e = 0; e < 64; ++e) {
+      v[e] = in ? load_elem<DT>(x, base + e) : 0.f;
+      bits = max(bits, abs_bits(v[e]));
+    }
+    for (int o = 16; o > 0; o >>= 1) bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, o));
+    if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = bits;
+    __syncthreads();
+    bits = 0;
+#pragma unroll
+    for (int w = 0; w < kQuantThreads / 32; ++w) bits = max(bits, warp_max[w]);
+    const float amax = __uint_as_float(bits);
+    const float d = amax == 0.f ? 1.f : __fdiv_rn(amax, 448.f);
+    if (in) {
+#pragma unroll
+      for (int e = 0; e < 64; e += 4) {
+        const uint32_t lo = cvt_e4m3x2(__fdiv_rn(v[e], d), __fdiv_rn(v[e + 1], d));
+        const uint32_t hi = cvt_e4m3x2(__fdiv_rn(v[e + 2], d), __fdiv_rn(v[e + 3], d));
+        *reinterpret_cast<uint32_t*>(codes + base + e) = lo | (hi << 16);
+      }
+    }
+    if (threadIdx.x == 0) scales[rb * kblocks + kb] = d;
+  }
+}
+
 }  // namespace
 }  // namespace sdc
 
@@ -318,3 +380,25 @@ int sdc_quantize_nvfp4(const void* x, int dtype, int64_t rows, int64_t cols, int
 }
 
 }  // extern "C"
+
+extern "C" int sdc_quantize_fp8_block(const void* x, int dtype, int64_t rows, int64_t cols, int block_rows,
+                                      uint8_t* codes, float* scales, sdc_stream_t stream) {
+  using namespace sdc;
+  SDC_REQUIRE(dtype == 0 || dtype == 1, "quantize requires FP32 (0) or BF16 (1) input");
+  SDC_REQUIRE(rows > 0 && cols > 0 && cols % 128 == 0, "block-scaled FP8 needs rows > 0 and cols % 128 == 0");
+  SDC_REQUIRE(block_rows == 1 || block_rows == 128, "block-scaled FP8 blocks are 1 x 128 or 128 x 128");
+  SDC_REQUIRE(x != nullptr && codes != nullptr && scales != nullptr, "quantize pointers must not be null");
+  SDC_REQUIRE(reinterpret_cast<uintptr_t>(codes) % 4 == 0, "FP8 codes must be 4-byte aligned");
+  const int64_t kblocks = cols / 128;
+  if (block_rows == 1) {
+    const unsigned grid = static_cast<unsigned>(ceil_div(rows * kblocks, kQuantThreads / 32));
+    if (dtype == 0) fp8_block_cast<0, 1><<<grid, kQuantThreads, 0, stream>>>(x, rows, cols, codes, scales);
+    else fp8_block_cast<1, 1><<<grid, kQuantThreads, 0, stream>>>(x, rows, cols, codes, scales);
+  } else {
+    const unsigned grid = static_cast<unsigned>(ceil_div(rows, 128) * kblocks);
+    if (dtype == 0) fp8_block_cast<0, 128><<<grid, kQuantThreads, 0, stream>>>(x, rows, cols, codes, scales);
+    else fp8_block_cast<1, 128><<<grid, kQuantThreads, 0, stream>>>(x, rows, cols, codes, scales);
+  }
+  SDC_CUDA_CHECK(cudaGetLastError());
+  return SDC_OK;
+}

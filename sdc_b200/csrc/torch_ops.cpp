@@ -105,6 +105,32 @@ void check_projection(const Tensor& a, const Tensor& weights, int channels, int6
   }
 }
 
+// Block-scaled FP8 (an extension: the reference has no such operator): E4M3
+// codes, fp32 scales [M, K/128] for A and [ceil(N/128), K/128] for B_rows.
+void check_fp8_block_operands(const Tensor& a, const Tensor& b, const Tensor& scale_a, const Tensor& scale_b) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.device() == b.device(), "A and B must be on the same CUDA device");
+  TORCH_CHECK(a.layout() == at::kStrided && b.layout() == at::kStrided && a.dim() == 2 && b.dim() == 2 &&
+                  a.is_contiguous() && b.is_contiguous(),
+              "A and B_rows must be contiguous row-major matrices");
+  TORCH_CHECK(a.scalar_type() == at::ScalarType::Float8_e4m3fn && b.scalar_type() == at::ScalarType::Float8_e4m3fn,
+              "block-scaled FP8 GEMM requires E4M3FN operands");
+  TORCH_CHECK(a.size(1) == b.size(1), "A and B_rows K dimensions must match");
+  for (auto d : {a.size(0), b.size(0), a.size(1)}) {
+    TORCH_CHECK(d > 0 && d <= std::numeric_limits<int>::max() - 128,
+                "Matrix dimensions must be positive and allow int32 tile padding");
+  }
+  TORCH_CHECK(a.size(1) % 128 == 0, "block-scaled FP8 K must be a multiple of 128");
+  const int64_t kb = a.size(1) / 128;
+  for (const Tensor* t : {&scale_a, &scale_b}) {
+    TORCH_CHECK(t->is_cuda() && t->device() == a.device() && t->layout() == at::kStrided &&
+                    t->scalar_type() == at::kFloat && t->is_contiguous() && t->dim() == 2,
+                "block scales must be contiguous CUDA FP32 matrices on the operand device");
+  }
+  TORCH_CHECK(scale_a.size(0) == a.size(0) && scale_a.size(1) == kb, "scale_a must be [M, K/128]");
+  TORCH_CHECK(scale_b.size(0) == (b.size(0) + 127) / 128 && scale_b.size(1) == kb,
+              "scale_b must be [ceil(N/128), K/128]");
+}
+
 const uint8_t* u8(const Tensor& t) { return static_cast<const uint8_t*>(t.const_data_ptr()); }
 int32_t* opt_i32(OptTensor t) { return t.has_value() ? t->data_ptr<int32_t>() : nullptr; }
 
@@ -228,6 +254,66 @@ Out5 abft_nvfp4_reference_mm(const Tensor& a, const Tensor& b, const Tensor& sfa
       weights.const_data_ptr<float>(), row, col, bit, opt_i32(nonfinite), static_cast<uint16_t*>(out.data_ptr()),
       observed.data_ptr<float>(), hit.data_ptr<int32_t>(), predicted.data_ptr<float>(), magnitude.data_ptr<float>(),
       static_cast<int>(layout), ws.data_ptr(), ws_bytes, stream_of(a)));
+  return {out, observed, hit, predicted, magnitude};
+}
+
+Tensor fp8_block_mm(const Tensor& a, const Tensor& b, const Tensor& scale_a, const Tensor& scale_b) {
+  check_fp8_block_operands(a, b, scale_a, scale_b);
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int64_t m = a.size(0), n = b.size(0), k = a.size(1);
+  auto out = at::empty({m, n}, a.options().dtype(at::kBFloat16));
+  check_status(sdc_fp8_block_gemm(u8(a), u8(b), scale_a.const_data_ptr<float>(), scale_b.const_data_ptr<float>(), m,
+                                  n, k, static_cast<uint16_t*>(out.data_ptr()), stream_of(a)));
+  return out;
+}
+
+Out3 abft_fp8_block_mm(const Tensor& a, const Tensor& b, const Tensor& scale_a, const Tensor& scale_b,
+                       const Tensor& weights, int64_t row, int64_t col, int64_t bit, int64_t algorithm,
+                       OptTensor nonfinite) {
+  const int c = channels_of(algorithm);
+  check_fp8_block_operands(a, b, scale_a, scale_b);
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int64_t m = a.size(0), n = b.size(0), k = a.size(1);
+  if (nonfinite.has_value()) {
+    for (const Tensor* t : {&b, &scale_a, &scale_b}) at::assert_no_overlap(*nonfinite, *t);
+  }
+  check_projection(a, weights, c, m, n, row, col, bit, nonfinite);
+  const int64_t tm = (m + 127) / 128, np = ((n + 127) / 128) * 128;
+  auto out = at::empty({m, n}, a.options().dtype(at::kBFloat16));
+  auto observed = at::empty({c, tm, np}, a.options().dtype(at::kFloat));
+  auto hit = at::empty({1}, a.options().dtype(at::kInt));
+  check_status(sdc_abft_fp8_block_gemm(u8(a), u8(b), scale_a.const_data_ptr<float>(), scale_b.const_data_ptr<float>(),
+                                       m, n, k, static_cast<int>(algorithm), weights.const_data_ptr<float>(), row, col,
+                                       bit, opt_i32(nonfinite), static_cast<uint16_t*>(out.data_ptr()),
+                                       observed.data_ptr<float>(), hit.data_ptr<int32_t>(), stream_of(a)));
+  return {out, observed, hit};
+}
+
+Out5 abft_fp8_block_reference_mm(const Tensor& a, const Tensor& b, const Tensor& scale_a, const Tensor& scale_b,
+                                 const Tensor& weights, int64_t row, int64_t col, int64_t bit, int64_t algorithm,
+                                 OptTensor nonfinite) {
+  const int c = channels_of(algorithm);
+  check_fp8_block_operands(a, b, scale_a, scale_b);
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int64_t m = a.size(0), n = b.size(0), k = a.size(1);
+  if (nonfinite.has_value()) {
+    for (const Tensor* t : {&b, &scale_a, &scale_b}) at::assert_no_overlap(*nonfinite, *t);
+  }
+  check_projection(a, weights, c, m, n, row, col, bit, nonfinite);
+  const int64_t tm = (m + 127) / 128, np = ((n + 127) / 128) * 128;
+  auto out = at::empty({m, n}, a.options().dtype(at::kBFloat16));
+  auto observed = at::empty({c, tm, np}, a.options().dtype(at::kFloat));
+  auto predicted = at::empty_like(observed);
+  auto magnitude = at::empty_like(observed);
+  auto hit = at::empty({1}, a.options().dtype(at::kInt));
+  const size_t ws_bytes =
+      sdc_abft_workspace_bytes(static_cast<int>(algorithm), m, n, k, static_cast<int>(SDC_LAYOUT_KSLICE));
+  auto ws = workspace(a, ws_bytes);
+  check_status(sdc_abft_fp8_block_reference_gemm(
+      u8(a), u8(b), scale_a.const_data_ptr<float>(), scale_b.const_data_ptr<float>(), m, n, k,
+      static_cast<int>(algorithm), weights.const_data_ptr<float>(), row, col, bit, opt_i32(nonfinite),
+      static_cast<uint16_t*>(out.data_ptr()), observed.data_ptr<float>(), hit.data_ptr<int32_t>(),
+      predicted.data_ptr<float>(), magnitude.data_ptr<float>(), ws.data_ptr(), ws_bytes, stream_of(a)));
   return {out, observed, hit, predicted, magnitude};
 }
 
@@ -364,6 +450,21 @@ std::tuple<Tensor, Tensor> quantize_fp8(const Tensor& x, std::optional<double> g
   return {codes, st};
 }
 
+std::tuple<Tensor, Tensor> quantize_fp8_block(const Tensor& x, int64_t block_rows) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2, "quantize requires a two-dimensional CUDA tensor");
+  const int dt = dtype_code(x);
+  TORCH_CHECK(block_rows == 1 || block_rows == 128, "block_rows must be 1 (activations) or 128 (weights)");
+  TORCH_CHECK(x.size(0) > 0 && x.size(1) > 0 && x.size(1) % 128 == 0,
+              "nonempty input columns must be divisible by 128");
+  const c10::cuda::CUDAGuard guard(x.device());
+  Tensor xc = x.contiguous();
+  auto codes = at::empty(x.sizes(), x.options().dtype(at::kByte));
+  auto scales = at::empty({(x.size(0) + block_rows - 1) / block_rows, x.size(1) / 128}, x.options().dtype(at::kFloat));
+  check_status(sdc_quantize_fp8_block(xc.const_data_ptr(), dt, x.size(0), x.size(1), static_cast<int>(block_rows),
+                                      codes.data_ptr<uint8_t>(), scales.data_ptr<float>(), stream_of(x)));
+  return {codes, scales};
+}
+
 std::tuple<Tensor, Tensor, Tensor, Tensor> quantize_nvfp4(const Tensor& x, std::optional<double> global_scale) {
   TORCH_CHECK(x.is_cuda() && x.dim() == 2, "quantize requires a two-dimensional CUDA tensor");
   const int dt = dtype_code(x);
@@ -461,6 +562,23 @@ Tensor abft_nvfp4_correct(const Tensor& a, const Tensor& b, const Tensor& sfa, c
 }
 
 // Out-of-scope reference precisions (FP32/BF16 SM80 paths) keep their
+Tensor abft_fp8_block_correct(const Tensor& a, const Tensor& b, const Tensor& scale_a, const Tensor& scale_b,
+                              const Tensor& location, const Tensor& located, const Tensor& output) {
+  check_fp8_block_operands(a, b, scale_a, scale_b);
+  TORCH_CHECK(output.scalar_type() == at::kBFloat16 && output.is_contiguous() && output.size(0) == a.size(0) &&
+                  output.size(1) == b.size(0),
+              "abft_fp8_block_correct output must be the bf16 row-major GEMM output");
+  const c10::cuda::CUDAGuard guard(a.device());
+  auto corrected = at::empty({}, a.options().dtype(at::kBool));
+  check_status(sdc_abft_correct_fp8_block(u8(a), u8(b), scale_a.const_data_ptr<float>(),
+                                          scale_b.const_data_ptr<float>(), a.size(0), b.size(0), a.size(1),
+                                          location.const_data_ptr<int64_t>(),
+                                          static_cast<const uint8_t*>(located.const_data_ptr()),
+                                          static_cast<uint16_t*>(output.data_ptr()),
+                                          static_cast<uint8_t*>(corrected.data_ptr()), stream_of(a)));
+  return corrected;
+}
+
 // schemas so callers fail with a clear message instead of a missing op.
 [[noreturn]] void out_of_scope(const char* name) {
   TORCH_CHECK(false, "sdc_cutlass::", name,
@@ -496,6 +614,11 @@ TORCH_LIBRARY(sdc_cutlass, lib) {
   lib.def("abft_fp8_reference_mm(Tensor a, Tensor b_rows, Tensor alpha, Tensor weights, int row, int col, int bit, int algorithm=0, Tensor(a!)? nonfinite=None, int layout=0) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
   lib.def("abft_nvfp4_mm(Tensor a_packed, Tensor b_packed, Tensor sfa, Tensor sfb, int k, Tensor alpha, Tensor weights, int row, int col, int bit, int algorithm=0, Tensor(a!)? nonfinite=None) -> (Tensor, Tensor, Tensor)");
   lib.def("abft_nvfp4_reference_mm(Tensor a_packed, Tensor b_packed, Tensor sfa, Tensor sfb, int k, Tensor alpha, Tensor weights, int row, int col, int bit, int algorithm=0, Tensor(a!)? nonfinite=None, int layout=0) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
+  lib.def("fp8_block_mm(Tensor a, Tensor b_rows, Tensor scale_a, Tensor scale_b) -> Tensor");
+  lib.def("abft_fp8_block_mm(Tensor a, Tensor b_rows, Tensor scale_a, Tensor scale_b, Tensor weights, int row, int col, int bit, int algorithm=0, Tensor(a!)? nonfinite=None) -> (Tensor, Tensor, Tensor)");
+  lib.def("abft_fp8_block_reference_mm(Tensor a, Tensor b_rows, Tensor scale_a, Tensor scale_b, Tensor weights, int row, int col, int bit, int algorithm=0, Tensor(a!)? nonfinite=None) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
+  lib.def("quantize_fp8_block(Tensor x, int block_rows) -> (Tensor, Tensor)");
+  lib.def("abft_fp8_block_correct(Tensor a, Tensor b_rows, Tensor scale_a, Tensor scale_b, Tensor location, Tensor located, Tensor(a!) output) -> Tensor");
   lib.def("nvfp4_scale_layout(int m, int n, int k) -> (Tensor, Tensor, int, int)", &nvfp4_scale_layout);
   // sdc_b200 extensions.
   lib.def("quantize_fp8(Tensor x, float? global_scale=None) -> (Tensor, Tensor)");
@@ -522,6 +645,11 @@ TORCH_LIBRARY_IMPL(sdc_cutlass, CUDA, lib) {
   lib.impl("abft_finalize_reference", &abft_finalize_reference);
   lib.impl("quantize_fp8", &quantize_fp8);
   lib.impl("quantize_nvfp4", &quantize_nvfp4);
+  lib.impl("fp8_block_mm", &fp8_block_mm);
+  lib.impl("abft_fp8_block_mm", &abft_fp8_block_mm);
+  lib.impl("abft_fp8_block_reference_mm", &abft_fp8_block_reference_mm);
+  lib.impl("quantize_fp8_block", &quantize_fp8_block);
+  lib.impl("abft_fp8_block_correct", &abft_fp8_block_correct);
   lib.impl("nvfp4_pack_scales", &nvfp4_pack_scales);
   lib.impl("abft_locate", &abft_locate);
   lib.impl("abft_fp8_correct", &abft_fp8_correct);

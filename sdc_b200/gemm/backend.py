@@ -4,7 +4,9 @@ Mirrors src/cutlass_gemm/backend.py of the reference: ``require_device``,
 ``_scale_layout``, ``_pack_scales`` and ``gemm(a, b, precision, scaling,
 global_scale)`` with the same precision/scaling pairs and output contracts
 (FP8: fp32 column-major; NVFP4: bf16 row-major). The FP32/BF16 legacy
-precisions of the reference are outside this path and raise.
+precisions of the reference are outside this path and raise. Extension:
+FP8 with ``scaling="blockwise"`` (1 x 128 A / 128 x 128 B fp32 block scales,
+bf16 row-major output).
 """
 from __future__ import annotations
 
@@ -16,6 +18,7 @@ from .. import ops
 from .. import require_device as _require
 
 SCALING = {"fp32": "none", "bf16": "none", "fp8": "tensorwise", "nvfp4": "block16"}
+SCALINGS = {"fp32": {"none"}, "bf16": {"none"}, "fp8": {"tensorwise", "blockwise"}, "nvfp4": {"block16"}}
 
 
 def require_device(device):
@@ -44,7 +47,7 @@ def mm(a, b):
 
 def gemm(a, b, precision, scaling, global_scale="amax"):
     """A @ B through the quantised sm_100a kernel selected by precision."""
-    if precision not in SCALING or scaling != SCALING[precision]:
+    if precision not in SCALINGS or scaling not in SCALINGS[precision]:
         raise ValueError(f"GEMM precision and scaling do not match: {precision}/{scaling}")
     if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[0] or a.device != b.device:
         raise ValueError("GEMM inputs must be two matching matrices on one device")
@@ -52,8 +55,12 @@ def gemm(a, b, precision, scaling, global_scale="amax"):
         dtype = torch.float32 if precision == "fp32" else torch.bfloat16
         return mm(a.to(dtype), b.to(dtype))
     require_device(a.device)
-    from .quantization import quantize
+    from .quantization import quantize, quantize_blockwise
 
+    if scaling == "blockwise":
+        qa, qb = quantize_blockwise(a.contiguous(), 1), quantize_blockwise(b.T.contiguous(), 128)
+        return ops.fp8_block_mm(qa.codes.view(torch.float8_e4m3fn), qb.codes.view(torch.float8_e4m3fn),
+                                qa.scales, qb.scales)
     qa = quantize(a.contiguous(), precision, global_scale)
     qb = quantize(b.T.contiguous(), precision, global_scale)
     alpha = (qa.multiplier * qb.multiplier).reciprocal()

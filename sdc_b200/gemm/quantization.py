@@ -24,10 +24,12 @@ from .. import ops, require_device
 class QuantizedMatrix:
     """Codes reconstruct as ``decoded_codes * scales / multiplier``.
 
-    FP8 has no block scales. NVFP4 codes hold two E2M1 values per byte (even
-    column in the low nibble); ``scales`` holds E4M3 bytes in natural
-    ``[rows, columns // 16]`` order and ``scales_mma`` the same bytes in the
-    MMA scale-factor layout. ``multiplier`` is a 0-d CUDA float32 tensor.
+    Tensorwise FP8 has no block scales. NVFP4 codes hold two E2M1 values per
+    byte (even column in the low nibble); ``scales`` holds E4M3 bytes in
+    natural ``[rows, columns // 16]`` order and ``scales_mma`` the same bytes
+    in the MMA scale-factor layout. ``multiplier`` is a 0-d CUDA float32
+    tensor. Block-scaled FP8 (``block_rows`` 1 or 128) holds fp32 ``scales``
+    ``[ceil(rows / block_rows), columns // 128]`` and a multiplier of 1.
     """
 
     codes: torch.Tensor
@@ -36,6 +38,7 @@ class QuantizedMatrix:
     precision: str
     shape: tuple[int, int]
     scales_mma: torch.Tensor | None = None
+    block_rows: int | None = None
 
 
 def _fixed_scale(policy):
@@ -73,12 +76,37 @@ def quantize(matrix, precision, global_scale="amax"):
     return QuantizedMatrix(codes, scales, st, precision, (rows, columns), packed)
 
 
+@torch.no_grad()
+def quantize_blockwise(matrix, block_rows):
+    """Block-scaled FP8: one fp32 scale per (block_rows x 128) block,
+    d = amax / 448 (1 for an all-zero block), code = e4m3(x / d). Activations
+    use block_rows=1 (1 x 128), weights stored as rows [N, K] 128 (128 x 128).
+    The reference quantises FP8 tensorwise only; this is the block recipe of
+    the FP8 benchmark configuration."""
+    if matrix.device.type != "cuda" or matrix.ndim != 2:
+        raise ValueError("quantize requires a two-dimensional CUDA tensor")
+    if matrix.dtype not in {torch.float32, torch.bfloat16}:
+        raise ValueError("quantize requires FP32 or BF16 input")
+    if block_rows not in (1, 128):
+        raise ValueError("block_rows must be 1 or 128")
+    rows, columns = matrix.shape
+    if rows == 0 or columns == 0 or columns % 128:
+        raise ValueError("nonempty input columns must be divisible by 128")
+    require_device(matrix.device)
+    codes, scales = ops.quantize_fp8_block(matrix, block_rows)
+    one = torch.ones((), device=matrix.device, dtype=torch.float32)
+    return QuantizedMatrix(codes, scales, one, "fp8", (rows, columns), None, block_rows)
+
+
 _E2M1 = (0., .5, 1., 1.5, 2., 3., 4., 6., -0., -.5, -1., -1.5, -2., -3., -4., -6.)
 
 
 @torch.no_grad()
 def dequantize(matrix: QuantizedMatrix):
     """Decode to float32 (reference checks only; exact for these formats)."""
+    if matrix.precision == "fp8" and matrix.block_rows:
+        scales = matrix.scales.repeat_interleave(matrix.block_rows, 0)[:matrix.shape[0]]
+        return matrix.codes.view(torch.float8_e4m3fn).float() * scales.repeat_interleave(128, 1)
     if matrix.precision == "fp8":
         values = matrix.codes.view(torch.float8_e4m3fn).float()
     else:

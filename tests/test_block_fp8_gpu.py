@@ -1,0 +1,266 @@
+"""Block-scaled FP8 (1 x 128 A / 128 x 128 B fp32 scales, bf16 output) on sm_100a.
+
+The reference quantises FP8 tensorwise only; its FP8 benchmark configuration
+asks for this block recipe, so the oracle restates the recipe itself
+(``oracle.quant.quantize_fp8_block``, ``cref.c`` kind 2). Bars: codes and
+scales bit-exact; K-slice predicted/magnitude partials bit-exact against the
+C oracle; outputs on dyadic data bit-exact, random data within the fp32
+accumulation bound plus the bf16 half-ulp; the observed checksum within the
+reference tests' rtol 2e-5 / atol 2e-3 of float64; faults detected, located
+and corrected.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import sdc_b200  # noqa: F401  (registers torch.ops.sdc_cutlass)
+from oracle import abft as oabft
+from oracle import native, quant
+from sdc_b200 import capi
+from sdc_b200.abft import execute, execute_prepared
+from sdc_b200.abft.operands import PreparedGemm
+from sdc_b200.gemm import backend
+from sdc_b200.gemm.quantization import dequantize, quantize_blockwise
+
+pytestmark = pytest.mark.gpu
+ops = torch.ops.sdc_cutlass
+DEV = "cuda"
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+def _watchdog_clear():
+    code = ctypes.c_int32(-1)
+    capi.check(capi.lib().sdc_read_device_error(torch.cuda.current_stream().cuda_stream, ctypes.byref(code)))
+    assert code.value == 0, f"a bounded wait expired (watchdog code {code.value})"
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(1, 128), (7, 256), (200, 384), (1024, 4096)])
+@pytest.mark.parametrize("block_rows", [1, 128])
+def test_block_quantizer_bit_exact(dtype, shape, block_rows):
+    g = torch.Generator(device=DEV).manual_seed(shape[0] * 7 + shape[1] + block_rows)
+    x = (torch.randn(shape, device=DEV, generator=g) * 5).to(dtype)
+    x[0, :128] = 0  # an all-zero block keeps scale 1
+    q = quantize_blockwise(x, block_rows)
+    codes, scales = quant.quantize_fp8_block(_np(x.float()), block_rows)
+    assert np.array_equal(_np(q.codes), codes)
+    assert np.array_equal(_np(q.scales), scales)
+    assert q.multiplier.item() == 1.0 and q.block_rows == block_rows
+    assert np.array_equal(_np(dequantize(q)), quant.dequantize_fp8_block(codes, scales, block_rows))
+
+
+def _block_case(m, n, k, seed=5, dyadic=False):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    a = torch.randn(m, k, device=DEV, generator=g, dtype=torch.bfloat16)
+    b = torch.randn(n, k, device=DEV, generator=g, dtype=torch.bfloat16)
+    qa, qb = quantize_blockwise(a, 1), quantize_blockwise(b, 128)
+    if dyadic:
+        # Small integer codes and power-of-two scales: every partial and the
+        # scaled sum are exact in fp32, so the output is the bf16 rounding of
+        # the exact product.
+        ia = torch.randint(-4, 5, (m, k), device=DEV, generator=g).float()
+        ib = torch.randint(-4, 5, (n, k), device=DEV, generator=g).float()
+        sa = torch.pow(2.0, torch.randint(-3, 4, (m, k // 128), device=DEV, generator=g).float())
+        sb = torch.pow(2.0, torch.randint(-3, 4, ((n + 127) // 128, k // 128), device=DEV, generator=g).float())
+        return (ia.to(torch.float8_e4m3fn), ib.to(torch.float8_e4m3fn), sa.contiguous(), sb.contiguous())
+    return (qa.codes.view(torch.float8_e4m3fn), qb.codes.view(torch.float8_e4m3fn), qa.scales, qb.scales)
+
+
+def _oracle(args):
+    a, b, sa, sb = args
+    return _np(a.view(torch.uint8)), _np(sa), _np(b.view(torch.uint8)), _np(sb)
+
+
+@pytest.mark.parametrize("shape", [(128, 128, 128), (136, 144, 256), (300, 520, 1024), (1024, 1280, 2048)])
+def test_dyadic_output_bit_exact(shape):
+    m, n, k = shape
+    args = _block_case(m, n, k, dyadic=True)
+    out = ops.fp8_block_mm(*args)
+    assert out.dtype == torch.bfloat16 and out.shape == (m, n) and out.is_contiguous()
+    a, sa, b, sb = _oracle(args)
+    exact = native.gemm_f64("fp8_block", a, sa, b, sb, m, n, k)
+    expected = torch.from_numpy(exact.astype(np.float32)).to(torch.bfloat16)
+    assert torch.equal(out.cpu(), expected)
+
+
+@pytest.mark.parametrize("shape", [(1024, 768, 2048), (520, 384, 512), (8, 136, 8192)])
+def test_random_output_within_accumulation_bound(shape):
+    m, n, k = shape
+    args = _block_case(m, n, k, seed=3)
+    out = _np(ops.fp8_block_mm(*args).float()).astype(np.float64)
+    a, sa, b, sb = _oracle(args)
+    exact = native.gemm_f64("fp8_block", a, sa, b, sb, m, n, k)
+    bound = native.gemm_f64("fp8_block", a & 0x7F, sa, b & 0x7F, sb, m, n, k)
+    # fp32 accumulation over K (per-block partials, scaled fma sums), the
+    # dequantised-product rounding, and the bf16 output half-ulp.
+    limit = 2 * k * 2.0 ** -24 * bound + 2.0 ** -8 * np.abs(exact) + 1e-6
+    assert np.all(np.abs(out - exact) <= limit)
+
+
+@pytest.mark.parametrize("shape", [(136, 144, 128), (300, 200, 384), (2048, 2048, 512), (2560, 4352, 2048),
+                                   (640, 33024, 1024)])
+def test_kslice_prediction_bit_exact_vs_oracle(shape):
+    m, n, k = shape
+    args = _block_case(m, n, k, seed=11)
+    rows = torch.arange(m, device=DEV, dtype=torch.int64)
+    weights = torch.stack(((rows * 7 % 29 - 14).float() / 8, (rows * 11 % 37 - 18).float() / 16))
+    base = ops.fp8_block_mm(*args)
+    fused_out, fused_obs, fused_hit = ops.abft_fp8_block_mm(*args, weights, -1, -1, -1)
+    out, obs, hit, pred, mag = ops.abft_fp8_block_reference_mm(*args, weights, -1, -1, -1)
+    assert torch.equal(out, base) and torch.equal(fused_out, base) and torch.equal(obs, fused_obs)
+    assert hit.item() == fused_hit.item() == 0
+    assert obs.shape == pred.shape == (2, (m + 127) // 128, ((n + 127) // 128) * 128)
+    a, sa, b, sb = _oracle(args)
+    epred, emag = native.input_reference("fp8_block", a, sa, b, sb, m, n, k, _np(weights), 1.0, pred.shape[-1],
+                                         "kslice")
+    assert np.array_equal(_np(pred), epred)
+    assert np.array_equal(_np(mag), emag)
+    tol = 2e-5 * _np(mag).sum(axis=1) + 1e-3
+    assert np.all(np.abs(_np(obs).sum(axis=1) - _np(pred).sum(axis=1)) <= tol)
+    _watchdog_clear()
+
+
+def test_observed_checksum_of_fp32_values_before_the_cast():
+    m, n, k = 264, 272, 384
+    args = _block_case(m, n, k, dyadic=True)
+    weights = torch.randn(2, m, device=DEV)
+    _, obs, _ = ops.abft_fp8_block_mm(*args, weights, -1, -1, -1)
+    a, sa, b, sb = _oracle(args)
+    values = native.gemm_f64("fp8_block", a, sa, b, sb, m, n, k)  # exact, fp32-representable
+    w = _np(weights).astype(np.float64)
+    for t in range(obs.shape[1]):
+        rows = slice(128 * t, min(m, 128 * t + 128))
+        assert np.allclose(_np(obs[:, t, :n]), w[:, rows] @ values[rows], rtol=2e-5, atol=2e-3)
+    assert not _np(obs[:, :, n:]).any()
+
+
+@pytest.mark.parametrize("location", [(0, 0), (127, 127), (128, 128), (263, 271)])
+def test_bitflip_exact_position(location):
+    m, n, k = 264, 272, 256
+    args = _block_case(m, n, k, dyadic=True)
+    weights = torch.ones(2, m, device=DEV)
+    clean, cobs, _ = ops.abft_fp8_block_mm(*args, weights, -1, -1, -1)
+    row, col = location
+    out, obs, hit = ops.abft_fp8_block_mm(*args, weights, row, col, 31)
+    assert hit.item() == 1
+    expected = clean.clone()
+    expected[row, col] = -expected[row, col]
+    assert torch.equal(out, expected)
+    changed = (obs != cobs).nonzero().tolist()
+    assert all(t == row // 128 and c == col for _, t, c in changed) and changed
+
+
+def test_nonfinite_injection_is_flagged():
+    m, n, k = 136, 144, 128
+    # Unit operands: every output is 1.0 (biased exponent 127), and flipping
+    # bit 30 makes the exponent all ones.
+    a = torch.zeros(m, k, device=DEV)
+    b = torch.zeros(n, k, device=DEV)
+    a[:, 0] = 1
+    b[:, 0] = 1
+    ones = torch.ones(m, 1, device=DEV), torch.ones(2, 1, device=DEV)
+    args = (a.to(torch.float8_e4m3fn), b.to(torch.float8_e4m3fn), *ones)
+    assert torch.equal(ops.fp8_block_mm(*args).float(), torch.ones(m, n, device=DEV))
+    bit = 30
+    nonfinite = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out, obs, hit = ops.abft_fp8_block_mm(*args, torch.ones(2, m, device=DEV), 128, 128, bit, 0, nonfinite)
+    assert hit.item() == 1 and nonfinite.item() == 1
+    assert not torch.isfinite(out[128, 128].float())
+
+
+@pytest.mark.parametrize("bad", ["k", "scale_shape", "scale_dtype"])
+def test_invalid_block_operands_rejected(bad):
+    a, b, sa, sb = _block_case(136, 144, 256, dyadic=True)
+    if bad == "k":
+        a, b = a[:, :200].contiguous(), b[:, :200].contiguous()
+    elif bad == "scale_shape":
+        sb = sb[:, :1].contiguous()
+    else:
+        sa = sa.double()
+    with pytest.raises(RuntimeError, match="multiple of 128|scale"):
+        ops.fp8_block_mm(a, b, sa, sb)
+
+
+def _fault_near(clean, row, col):
+    values = clean.float().reshape(-1)
+    start = row * clean.shape[1] + col
+    ok = (values[start:].abs() >= 4) & (values[start:].abs() < 256)
+    index = start + int(ok.nonzero()[0, 0])
+    return index // clean.shape[1], index % clean.shape[1], 27
+
+
+def _cfg(**changes):
+    return {"method": "classic", "implementation": "native", "reference_mode": "input_fused",
+            "reference_layout": "kslice", "on_error": "report", "atol": 1e-3, "rtol": 1e-4, "diagnostics": True,
+            **changes}
+
+
+def test_engine_blockwise_clean_equals_unprotected():
+    g = torch.Generator(device=DEV).manual_seed(5)
+    a = torch.randn(384, 512, device=DEV, generator=g)
+    b = torch.randn(512, 520, device=DEV, generator=g)
+    plain = backend.gemm(a, b, "fp8", "blockwise")
+    output, report = execute(a, b, "fp8", "blockwise", abft_config=_cfg())
+    assert torch.equal(output, plain) and plain.dtype == torch.bfloat16
+    assert not report.detected and not report.nonfinite
+    assert report.to_record()["context"]["scaling"] == "blockwise"
+    with pytest.raises(NotImplementedError, match="kslice"):
+        execute(a, b, "fp8", "blockwise", abft_config=_cfg(reference_layout="tile"))
+
+
+@pytest.mark.parametrize("recovery", ["recompute", "correct"])
+def test_engine_blockwise_fault_detected_located_repaired(recovery):
+    m, n, k = 520, 384, 512
+    g = torch.Generator(device=DEV).manual_seed(9)
+    a = torch.randn(m, k, device=DEV, generator=g) * 4
+    b = torch.randn(k, n, device=DEV, generator=g)
+    prepared = PreparedGemm.prepare(a, b, "fp8", "blockwise")
+    clean = prepared.raw_native()
+    row, col, bit = _fault_near(clean, 389, 201)
+    fault = {"location": "accumulator", "row": row, "col": col, "bit": bit}
+    output, report = execute_prepared(prepared, _cfg(locate=True, recovery=recovery), fault)
+    assert report.detected and report.fault_hit.item() == 1
+    assert report.located and report.location.tolist() == [row, col]
+    assert report.recovered and not report.recheck_failed
+    if recovery == "recompute":
+        assert torch.equal(output, clean)
+    else:
+        torch.testing.assert_close(output.float(), clean.float(), rtol=1e-2, atol=1e-3)
+
+
+def test_python_reference_implementation_agrees_with_native_blockwise():
+    g = torch.Generator(device=DEV).manual_seed(11)
+    a = torch.randn(264, 384, device=DEV, generator=g)
+    b = torch.randn(384, 272, device=DEV, generator=g)
+    prepared = PreparedGemm.prepare(a, b, "fp8", "blockwise")
+    row, col, bit = _fault_near(prepared.raw_native(), 100, 200)
+    fault = {"location": "accumulator", "row": row, "col": col, "bit": bit}
+    native_out, nrep = execute_prepared(prepared, _cfg(locate=True), fault)
+    python_out, prep = execute_prepared(prepared, _cfg(implementation="reference"), fault)
+    assert torch.equal(native_out, python_out)
+    assert bool(nrep.detected) == bool(prep.detected) is True
+    assert nrep.location.tolist() == prep.location.tolist() == [row, col]
+
+
+def test_finalize_and_locate_on_block_scaled_evidence():
+    m, n, k = 520, 384, 512
+    args = _block_case(m, n, k, seed=9)
+    weights = torch.stack((torch.ones(m, device=DEV), torch.arange(1, m + 1, device=DEV, dtype=torch.float32)))
+    clean, *_ = ops.abft_fp8_block_reference_mm(*args, weights, -1, -1, -1)
+    row, col, bit = _fault_near(clean, 389, 201)
+    nonfinite = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out, obs, hit, pred, mag = ops.abft_fp8_block_reference_mm(*args, weights, row, col, bit, 0, nonfinite)
+    packet = ops.abft_finalize_reference(obs, pred, mag, hit, nonfinite, n, 1e-3, 1e-4, None, True)
+    assert packet[3][0].item() and not packet[3][1].item()
+    location, located = ops.abft_locate(packet[1], packet[2], packet[3], m)
+    ok, loc = oabft.locate(_np(packet[1]), _np(packet[2]), True, False, m)
+    assert located.item() == ok and location.tolist() == list(loc) == [row, col]
+    fixed = out.clone()
+    assert ops.abft_fp8_block_correct(*args, location, located, fixed).item()
+    torch.testing.assert_close(fixed.float(), clean.float(), rtol=1e-2, atol=1e-3)
+    _watchdog_clear()

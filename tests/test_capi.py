@@ -51,6 +51,13 @@ def test_argument_contracts_are_checked_before_launch():
     rc = lib.sdc_abft_finalize(7, fake, fake, fake, 1, 16, 16, None, 0, fake, fake, 0.0, 0.0, fake, 0, 0, None,
                                None, None, 0, fake, fake, fake, fake, 64, None)
     assert rc == capi.SDC_ERR_UNKNOWN_ALGORITHM
+    rc = lib.sdc_fp8_block_gemm(fake, fake, fake, fake, 136, 144, 192, fake, None)
+    assert rc == capi.SDC_ERR_INVALID and "multiple of 128" in capi.last_error()
+    rc = lib.sdc_abft_fp8_block_gemm(fake, fake, fake, fake, 136, 144, 256, 0, fake, 136, 0, 0, None, fake, fake,
+                                     fake, None)
+    assert rc == capi.SDC_ERR_INVALID and "fault" in capi.last_error()
+    rc = lib.sdc_quantize_fp8_block(fake, 0, 4, 128, 64, fake, fake, None)
+    assert rc == capi.SDC_ERR_INVALID and "1 x 128 or 128 x 128" in capi.last_error()
     assert lib.sdc_abft_finalize_workspace_bytes(0, 300, 4) == 2 * ((300 + 63) // 64) * 4
     assert lib.sdc_abft_workspace_bytes(0, 256, 64, 128, 0) == 2 * 2 * 2 * 128 * 4
 
@@ -66,6 +73,13 @@ REFERENCE_SCHEMAS = {
     "abft_nvfp4_mm": "abft_nvfp4_mm(Tensor a_packed, Tensor b_packed, Tensor sfa, Tensor sfb, int k, Tensor alpha, Tensor weights, int row, int col, int bit, int algorithm=0, Tensor(a!)? nonfinite=None) -> (Tensor, Tensor, Tensor)",
     "nvfp4_scale_layout": "nvfp4_scale_layout(int m, int n, int k) -> (Tensor, Tensor, int, int)",
 }
+# Block-scaled FP8 ops (no reference counterpart) follow the FP8 ops' argument
+# order with the fp32 block scales in place of alpha.
+BLOCK_SCALED = {
+    "fp8_block_mm": "fp8_block_mm(Tensor a, Tensor b_rows, Tensor scale_a, Tensor scale_b) -> Tensor",
+    "abft_fp8_block_mm": "abft_fp8_block_mm(Tensor a, Tensor b_rows, Tensor scale_a, Tensor scale_b, Tensor weights, int row, int col, int bit, int algorithm=0, Tensor(a!)? nonfinite=None) -> (Tensor, Tensor, Tensor)",
+    "quantize_fp8_block": "quantize_fp8_block(Tensor x, int block_rows) -> (Tensor, Tensor)",
+}
 # Input-fused ops keep the reference's arguments and add one trailing default.
 EXTENDED = {
     "abft_fp8_reference_mm": "abft_fp8_reference_mm(Tensor a, Tensor b_rows, Tensor alpha, Tensor weights, int row, int col, int bit, int algorithm=0, Tensor(a!)? nonfinite=None",
@@ -75,6 +89,8 @@ EXTENDED = {
 
 def test_torch_op_schemas_match_reference_bindings():
     for name, schema in REFERENCE_SCHEMAS.items():
+        assert str(getattr(torch.ops.sdc_cutlass, name).default._schema) == "sdc_cutlass::" + schema
+    for name, schema in BLOCK_SCALED.items():
         assert str(getattr(torch.ops.sdc_cutlass, name).default._schema) == "sdc_cutlass::" + schema
     for name, prefix in EXTENDED.items():
         schema = str(getattr(torch.ops.sdc_cutlass, name).default._schema)

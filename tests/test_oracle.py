@@ -286,3 +286,54 @@ def test_c_oracle_tile_reference_matches_float64(kind):
     kpred, kmag = native.input_reference(kind, a, sfa, b, sfb, m, n, k, w, 0.5, pn, "kslice")
     assert np.allclose(kpred.sum(axis=1), pred.sum(axis=1), rtol=1e-5, atol=1e-4 * mag.sum(axis=1).max())
     assert np.allclose(kmag.sum(axis=1), mag.sum(axis=1), rtol=1e-5)
+
+
+# --- block-scaled FP8 (1 x 128 activations, 128 x 128 weights) -----------------
+
+def test_fp8_block_quantizer_known_answers():
+    x = np.zeros((3, 256), np.float32)
+    x[0, :128] = np.linspace(-1, 1, 128, dtype=np.float32) * 896  # amax 896 -> d = 2
+    x[1, 130] = -3.0  # block (1, 1): d = 3 / 448
+    codes, scales = quant.quantize_fp8_block(x, 1)
+    assert scales.shape == (3, 2) and scales.dtype == np.float32
+    assert scales[0, 0] == 2.0 and scales[1, 1] == np.float32(3.0) / np.float32(448.0)
+    assert scales[0, 1] == scales[2, 0] == scales[2, 1] == 1.0  # all-zero blocks keep d = 1
+    assert codes[0, 0] == 0xFE and codes[0, 127] == 0x7E  # -/+448
+    assert codes[1, 130] == 0xFE and not codes[2].any()
+    dq = quant.dequantize_fp8_block(codes, scales, 1)
+    assert np.all(np.abs(dq - x) <= np.abs(x) * 2.0 ** -4 + 1e-30)
+
+
+def test_fp8_block_quantizer_weight_blocks_and_ragged_rows():
+    rng = np.random.default_rng(3)
+    x = rng.normal(size=(200, 384)).astype(np.float32)
+    codes, scales = quant.quantize_fp8_block(x, 128)
+    assert scales.shape == (2, 3)
+    for rb in range(2):
+        for kb in range(3):
+            block = x[128 * rb:128 * rb + 128, 128 * kb:128 * kb + 128]
+            assert scales[rb, kb] == np.float32(np.abs(block).max()) / np.float32(448.0)
+            d = scales[rb, kb]
+            assert np.array_equal(codes[128 * rb:128 * rb + 128, 128 * kb:128 * kb + 128],
+                                  formats.e4m3_encode(block / d))
+    # Every block's largest magnitude maps onto the top code 448 exactly.
+    assert (formats.e4m3_decode(codes) == 448).sum() + (formats.e4m3_decode(codes) == -448).sum() >= 6
+    with pytest.raises(ValueError):
+        quant.quantize_fp8_block(x[:, :100], 1)
+
+
+def test_c_oracle_block_scaled_matches_float64():
+    rng = np.random.default_rng(11)
+    m, n, k = 200, 160, 256
+    a, sa = quant.quantize_fp8_block(rng.normal(size=(m, k)).astype(np.float32), 1)
+    b, sb = quant.quantize_fp8_block(rng.normal(size=(n, k)).astype(np.float32), 128)
+    da, db = quant.dequantize_fp8_block(a, sa, 1), quant.dequantize_fp8_block(b, sb, 128)
+    out = native.gemm_f64("fp8_block", a, sa, b, sb, m, n, k)
+    assert np.allclose(out, da.astype(np.float64) @ db.T.astype(np.float64), rtol=1e-12, atol=1e-12)
+    w = rng.normal(size=(2, m)).astype(np.float32)
+    pred, mag = native.input_reference("fp8_block", a, sa, b, sb, m, n, k, w, 1.0, 256, "kslice")
+    exact = w.astype(np.float64) @ out
+    exact_mag = (np.abs(w).astype(np.float64) @ np.abs(da).astype(np.float64)) @ np.abs(db.T).astype(np.float64)
+    assert np.all(np.abs(pred.sum(axis=1)[:, :n] - exact) <= 1e-5 * exact_mag + 1e-6)
+    assert np.allclose(mag.sum(axis=1)[:, :n], exact_mag, rtol=1e-5)
+    assert not pred[:, :, n:].any()
