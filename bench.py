@@ -8,10 +8,11 @@ operands already quantised and resident in HBM: the input-fused ABFT GEMM
 the K-slice layout) followed by the device finalize that merges partials and
 decides. Throughput counts only the useful 2*M*N*K flops.
 
-Headline workload (config[1]): FP8 e4m3, M=N=K=8192, tensorwise scales (the
-reference's FP8 semantics; block-scaled FP8 is not built yet), fp32 output.
-The NVFP4 workload of config[2] (M=N=K=16384, e2m1 + ue4m3/16 + fp32 global
-scale, bf16 out) is measured in the same run and reported under "nvfp4".
+Headline workload (config[1]): FP8 e4m3, M=N=K=8192, 1 x 128 (A) and
+128 x 128 (B) fp32 block scales, fp32 accumulation, bf16 output. Measured in
+the same run: the NVFP4 workload of config[2] (M=N=K=16384, e2m1 + ue4m3/16 +
+fp32 global scale, bf16 out) under "nvfp4", and the reference's own FP8
+semantics (tensorwise scale, fp32 output) at 8192^3 under "fp8_tensorwise".
 
 Multi-GPU (python -m torch.distributed.run ... bench.py --gpus N): each rank
 protects its own M-shard (8192 rows x N=K=8192, weak scaling: the job's M is
@@ -101,15 +102,24 @@ class ClockSampler:
                 "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
 
 
+# Workload formats: (quantisation precision, bench key, description).
+FORMATS = {"fp8_block": ("fp8", "fp8 block-scaled 1x128 / 128x128, bf16 out"),
+           "fp8": ("fp8", "fp8 tensorwise, fp32 out"),
+           "nvfp4": ("nvfp4", "nvfp4 block16, bf16 out")}
+
+
 def make_operands(precision, m, n, k, device, seed, b_std=1.0):
     """Seeded N(0,1) bf16 A [m,k] and B_rows [n,k] (synthetic, BASELINE shapes) quantised once."""
-    from sdc_b200.gemm.quantization import quantize
+    from sdc_b200.gemm.quantization import quantize, quantize_blockwise
 
     g = torch.Generator(device=device).manual_seed(seed)
     a = torch.randn(m, k, device=device, generator=g, dtype=torch.bfloat16)
     b = torch.randn(n, k, device=device, generator=g, dtype=torch.bfloat16)
     if b_std != 1.0:
         b = b * b_std
+    if precision == "fp8_block":
+        qa, qb = quantize_blockwise(a, 1), quantize_blockwise(b, 128)
+        return (qa.codes.view(torch.float8_e4m3fn), qb.codes.view(torch.float8_e4m3fn), qa.scales, qb.scales)
     qa, qb = quantize(a, precision), quantize(b, precision)
     alpha = (qa.multiplier * qb.multiplier).reciprocal()
     if precision == "fp8":
@@ -130,13 +140,20 @@ class Protected:
         self.weights = torch.stack((torch.ones(m, device=device),
                                     torch.arange(1, m + 1, device=device, dtype=torch.float32)))
         self.nonfinite = torch.zeros(1, dtype=torch.int32, device=device)
-        self.layout, self.atol, self.rtol = layout, atol, rtol
-        self.fused = self.ops.abft_fp8_reference_mm if precision == "fp8" else self.ops.abft_nvfp4_reference_mm
-        self.observe = self.ops.abft_fp8_mm if precision == "fp8" else self.ops.abft_nvfp4_mm
-        self.plain = self.ops.fp8_mm if precision == "fp8" else self.ops.nvfp4_mm
+        self.atol, self.rtol = atol, rtol
+        ops = self.ops
+        if precision == "fp8_block":  # K-slice is the block-scaled op's only layout
+            self.fused, self.observe, self.plain = (ops.abft_fp8_block_reference_mm, ops.abft_fp8_block_mm,
+                                                    ops.fp8_block_mm)
+            self.layout_args = ()
+        else:
+            self.fused = ops.abft_fp8_reference_mm if precision == "fp8" else ops.abft_nvfp4_reference_mm
+            self.observe = ops.abft_fp8_mm if precision == "fp8" else ops.abft_nvfp4_mm
+            self.plain = ops.fp8_mm if precision == "fp8" else ops.nvfp4_mm
+            self.layout_args = (layout,)
 
     def step(self, fault=(-1, -1, -1)):
-        out, obs, hit, pred, mag = self.fused(*self.args, self.weights, *fault, 0, self.nonfinite, self.layout)
+        out, obs, hit, pred, mag = self.fused(*self.args, self.weights, *fault, 0, self.nonfinite, *self.layout_args)
         packet = self.ops.abft_finalize_reference(obs, pred, mag, hit, self.nonfinite, self.n, self.atol,
                                                   self.rtol, None, True)
         return out, packet
@@ -149,7 +166,7 @@ class Protected:
 
     def fused_only(self):
         """The step's dominant kernel alone: the protected GEMM without finalize."""
-        return self.fused(*self.args, self.weights, -1, -1, -1, 0, self.nonfinite, self.layout)
+        return self.fused(*self.args, self.weights, -1, -1, -1, 0, self.nonfinite, *self.layout_args)
 
 
 def paired_overhead(prot, steps, rounds=5):
@@ -181,9 +198,9 @@ def profiled_traffic(name):
     return total
 
 
-# Kernels this library launches per protected step: projection of A, tile
-# reduce, the GEMM (prediction fused) + 2 finalize kernels.
-LAUNCHES_PER_STEP = 5
+# Kernels this library launches per protected step: the GEMM (projection and
+# K-slice prediction fused into it) + finalize_columns + finalize_flags.
+LAUNCHES_PER_STEP = 3
 
 
 def timed(fn, steps, warmup, stream):
@@ -245,8 +262,8 @@ def qwen_sweep(args, device, stream, rank, world, dist):
     from sdc_b200.abft.distributed import shard_rows
 
     out = {}
-    for precision in ("fp8", "nvfp4"):
-        if args.format not in ("both", precision):
+    for precision in FORMATS:
+        if args.format not in ("all", precision):
             continue
         rows = {}
         total_flops = total_prot = total_plain = 0.0
@@ -276,11 +293,18 @@ def qwen_sweep(args, device, stream, rank, world, dist):
 
 def e2e_step(precision, host_a, host_b, device, weights, nonfinite, atol, rtol):
     """Public-API protected GEMM from pinned host bf16 buffers to host flags."""
-    from sdc_b200.gemm.quantization import quantize
+    from sdc_b200.gemm.quantization import quantize, quantize_blockwise
 
     ops = torch.ops.sdc_cutlass
     a = host_a.to(device, non_blocking=True)
     b = host_b.to(device, non_blocking=True)
+    if precision == "fp8_block":
+        qa, qb = quantize_blockwise(a, 1), quantize_blockwise(b, 128)
+        res = ops.abft_fp8_block_reference_mm(qa.codes.view(torch.float8_e4m3fn), qb.codes.view(torch.float8_e4m3fn),
+                                              qa.scales, qb.scales, weights, -1, -1, -1, 0, nonfinite)
+        out, obs, hit, pred, mag = res
+        packet = ops.abft_finalize_reference(obs, pred, mag, hit, nonfinite, b.shape[0], atol, rtol, None, False)
+        return packet[3].to("cpu"), out
     qa, qb = quantize(a, precision), quantize(b, precision)
     alpha = (qa.multiplier * qb.multiplier).reciprocal()
     if precision == "fp8":
@@ -316,8 +340,9 @@ def run_ours(args):
     stream = torch.cuda.current_stream(device)
     bf16_peak, hbm_peak, basis = measured_peaks()
     results = {}
-    for precision, size, seed in (("fp8", args.size or 8192, 1), ("nvfp4", args.size or 16384, 2)):
-        if args.format not in ("both", precision):
+    for precision, size, seed in (("fp8_block", args.size or 8192, 1), ("fp8", args.size or 8192, 3),
+                                  ("nvfp4", args.size or 16384, 2)):
+        if args.format not in ("all", precision):
             continue
         m = n = k = size
         prot = Protected(precision, m, n, k, device, seed + 1000 * rank)
@@ -346,9 +371,12 @@ def run_ours(args):
         step_paired, plain_paired = paired_overhead(prot, args.steps)
         t_fused = timed(prot.fused_only, args.steps, 2, stream)
         per_step = elapsed / args.steps
-        peak = bf16_peak * (2 if precision == "fp8" else 4)
+        fp8 = precision.startswith("fp8")
+        peak = bf16_peak * (2 if fp8 else 4)
+        profile = {("fp8_block", 8192): "gemm_fp8block_8192_abft.md",
+                   ("fp8", 8192): "gemm_fp8_8192_abft.md"}.get((precision, size))
         entry = {
-            "workload": f"{precision} M=N=K={size}" + (" tensorwise" if precision == "fp8" else " block16"),
+            "workload": f"{FORMATS[precision][1].split(' ', 1)[0]} M=N=K={size} {FORMATS[precision][1].split(' ', 1)[1]}",
             "tflops": world * flops / per_step / 1e12,
             "ms_per_step": per_step * 1e3,
             "unprotected_tflops": flops / plain_paired / 1e12,
@@ -357,13 +385,11 @@ def run_ours(args):
             "roofline": {"bound": "tensor", "achieved": flops / (t_fused / args.steps) / 1e12, "peak": peak,
                          "unit": "TFLOP/s", "frac": flops / (t_fused / args.steps) / 1e12 / peak,
                          "kernel": "protected GEMM (gemm_kernel with checksums, projection and prediction)",
-                         "traffic": (profiled_traffic("gemm_fp8_8192_abft.md")
-                                     if precision == "fp8" and size == 8192 else None),
-                         "traffic_source": "profiles/gemm_fp8_8192_abft.md (ncu dram bytes of one launch)"
-                                           if precision == "fp8" and size == 8192 else None,
+                         "traffic": profiled_traffic(profile) if profile else None,
+                         "traffic_source": f"profiles/{profile} (ncu dram bytes of one launch)" if profile else None,
                          "algorithmic_flops": flops,
-                         "peak_basis": f"{2 if precision == 'fp8' else 4}x {basis} bf16 dense burst "
-                                       f"({bf16_peak} TFLOP/s); nominal dense {4500 if precision == 'fp8' else 9000}"},
+                         "peak_basis": f"{2 if fp8 else 4}x {basis} bf16 dense burst "
+                                       f"({bf16_peak} TFLOP/s); nominal dense {4500 if fp8 else 9000}"},
             "clocks": clocks.summary(),
         }
         if rank == 0 and not args.no_detection:
@@ -396,22 +422,23 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return
-    head = results.get("fp8") or results["nvfp4"]
+    head = results.get("fp8_block") or results.get("fp8") or results["nvfp4"]
     line = {
         "metric": METRIC, "value": head["tflops"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "e4m3" if "fp8" in results else "e2m1", "data": "synthetic",
+        "vs_baseline": None, "dtype": "e2m1" if head is results.get("nvfp4") else "e4m3", "data": "synthetic",
         "config": {"workload": head["workload"] + " ABFT (Classic, K-slice input reference) + finalize",
                    "per_gpu": head["workload"].split(" ")[1],
                    "parallelism": f"M-shard x{world}, NCCL all-reduce of detection status",
-                   "l2": "working set (A+B codes, fp32 output) > 126 MB L2; no explicit flush"},
+                   "l2": "working set (A+B codes, output) > 126 MB L2; no explicit flush"},
         "overhead_pct": head["overhead_pct"], "unprotected_tflops": head["unprotected_tflops"],
         "roofline": head["roofline"], "clocks": head["clocks"],
         "gpu_launches": LAUNCHES_PER_STEP * args.steps,
         "e2e": head.get("e2e"), "detection": head.get("detection"),
     }
-    if "nvfp4" in results and "fp8" in results:
-        line["nvfp4"] = results["nvfp4"]
+    for key, name in (("fp8", "fp8_tensorwise"), ("nvfp4", "nvfp4")):
+        if key in results and results[key] is not head:
+            line[name] = results[key]
     if sweep is not None:
         line["qwen2.5_7b_linears"] = sweep
     if not args.no_cpu_baseline:
@@ -457,13 +484,16 @@ def run_reference(args):
         cpu_path.execute(a, b, atol=1e-3, rtol=1e-4)
     seconds = (time.perf_counter() - t0) / steps
     value = 2.0 * rows * n * k / seconds / 1e12
-    sample = f"fp32 {rows}x{n}x{k} row sample of the FP8 8192^3 workload per step"
+    sample = f"fp32 {rows}x{n}x{k} row sample of the 8192^3 workload per step"
     print(json.dumps({
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
         "steps": steps, "warmup": args.warmup, "ms_per_step": seconds * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "impl": "reference",
-        "config": {"workload": "fp8 M=N=K=8192 tensorwise ABFT (Classic) + finalize",
-                   "reference_path": "abft.execute fp32 CPU path (reference_mm=torch.mm), restated in oracle/cpu_path.py"},
+        "config": {"workload": "fp8 M=N=K=8192 block-scaled 1x128 / 128x128, bf16 out"
+                               " ABFT (Classic, K-slice input reference) + finalize",
+                   "reference_path": "abft.execute CPU path (reference_mm=torch.mm; the reference's only CPU "
+                                     "implementation computes the protected GEMM in fp32), restated in "
+                                     "oracle/cpu_path.py"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -476,7 +506,8 @@ def main():
     parser.add_argument("--steps", type=int, default=300)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--format", choices=["both", "fp8", "nvfp4"], default="both")
+    parser.add_argument("--format", choices=["all", "fp8_block", "fp8", "nvfp4"], default="all",
+                        help="fp8_block = config[1] (headline), fp8 = tensorwise FP8, nvfp4 = config[2]")
     parser.add_argument("--flips", type=int, default=64)
     parser.add_argument("--cpu-sample-rows", type=int, default=1024)
     parser.add_argument("--no-detection", action="store_true")

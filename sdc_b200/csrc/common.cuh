@@ -99,11 +99,13 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// The waiting thread may be suspended for up to the hint (1 ms) and is woken
+// when the phase completes, so waiters do not poll shared memory.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000000;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
       : "r"(smem_u32(bar)), "r"(phase)
@@ -120,7 +122,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, int32_t
   const uint64_t start = global_ns();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, phase)) {
-    if ((++spins & 255u) == 0u) {
+    if ((++spins & 15u) == 0u) {
       if (*abort) return false;
       if (global_ns() - start > kWaitLimitNs) {
         atomicCAS(watchdog, 0, code);
@@ -214,8 +216,11 @@ __device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
 }
 
 // Arrive on an mbarrier given by its cluster shared-memory address.
+// Arrive on a barrier of another CTA of the cluster (address from mapa).
+// Release at CTA scope: a cluster-scope release cost about a microsecond per
+// arrive on B200, which throttled every per-K-block handshake.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t columns) {

@@ -81,13 +81,29 @@ __host__ __device__ constexpr int smem_bytes(Kind k, bool pair = false) {
   return 1024 + num_stages(k, pair) * stage_bytes(k, pair) + kRedFloats * 4 + 256;
 }
 __host__ __device__ constexpr int num_acc(Kind k) { return k == Kind::kNvf4 ? 1 : 2; }
-// Warps: 0 TMA, 1 MMA, 2-5 epilogue, then 6-9 prediction (checked
-// K-slice launches) and 4 promotion warps (block-scaled FP8).
+// Warp roles. Tensorwise FP8 / NVFP4: 0 TMA, 1 MMA, 2-5 epilogue, 6-9
+// prediction (checked K-slice launches). Block-scaled FP8: 0 TMA, 1 MMA, 2-9
+// promotion + epilogue (two warps per TMEM lane quarter, one per 64-column
+// half of the tile), 10-13 prediction.
+constexpr int kEpi0 = 2;
+__host__ __device__ constexpr int acc_warps(bool blk) { return blk ? 8 : 4; }
+__host__ __device__ constexpr int pred_warp0(bool blk) { return kEpi0 + acc_warps(blk); }
 __host__ __device__ constexpr int num_threads(bool chk, bool blk = false) {
-  return 192 + (chk ? 128 : 0) + (blk ? 128 : 0);
+  return 32 * (pred_warp0(blk) + (chk ? 4 : 0));
 }
-__device__ __forceinline__ bool is_prediction_warp(int warp) { return warp >= 6 && warp < 10; }
-__device__ __forceinline__ int prediction_index(int warp) { return warp - 6; }
+template <bool BLK>
+__device__ __forceinline__ bool is_prediction_warp(int warp) {
+  return warp >= pred_warp0(BLK) && warp < pred_warp0(BLK) + 4;
+}
+template <bool BLK>
+__device__ __forceinline__ int prediction_index(int warp) { return warp - pred_warp0(BLK); }
+// Block-scaled FP8: 4 partial accumulators of 128 columns fill the 512 TMEM
+// columns; the promotion warps keep the tile totals in registers. The MMA and
+// promotion warps hand partials over in groups of 2 K blocks (one commit and
+// one release per group), so 2 groups are in flight.
+constexpr int kPartBufs = 4;
+constexpr int kGroupKb = 2;
+constexpr int kGroupSlots = kPartBufs / kGroupKb;
 
 struct Params {
   int32_t m, n, k, num_kb, tiles_m, tiles_n, num_tiles;
@@ -204,12 +220,13 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
   constexpr int kTileChunks = chunks(KIND);
   constexpr int kStageBytes = stage_bytes(KIND, PAIR);
   constexpr int kAcc = num_acc(KIND);
-  // Block-scaled FP8: the MMA writes each 128-wide K block into one of two
-  // partial accumulators (TMEM columns 256..511); promotion warps add
-  // scale_a * scale_b * partial into the tile total (columns 0..255, two
-  // buffers), which the epilogue then reads like an ordinary accumulator.
+  // Block-scaled FP8: the MMA writes each 128-wide K block into one of four
+  // partial accumulators (TMEM columns 0..511); the promotion warps add
+  // scale_a * scale_b * partial into tile totals held in their registers and
+  // run the epilogue from there.
   constexpr bool BLK = KIND == Kind::kFp8Block;
-  constexpr uint32_t kPartialCol = 256;
+  constexpr int kAccWarps = acc_warps(BLK);
+  constexpr uint32_t kAccThreads = 32 * kAccWarps;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -219,8 +236,8 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
   uint64_t* acc_full = empty + kS;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* part_full = acc_empty + 2;
-  uint64_t* part_empty = part_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(part_empty + 2);
+  uint64_t* part_empty = part_full + kPartBufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(part_empty + kPartBufs);
   volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(tmem_slot + 1);
   // Tiles whose epilogue has finished: paces the prediction warps.
   volatile uint32_t* tiles_done = tmem_slot + 2;
@@ -240,12 +257,15 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
       mbar_init(empty + s, 1);
     }
     for (int b = 0; b < 2; ++b) {
-      // Block-scaled: totals pass between this CTA's promotion and epilogue
-      // warps; otherwise the (leader's) MMA waits for both CTAs' epilogues.
-      mbar_init(acc_full + b, BLK ? 4 : 1);
-      mbar_init(acc_empty + b, (PAIR && !BLK) ? 8 : 4);
+      // The (leader's) MMA waits for both CTAs' epilogues.
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, PAIR ? 8 : 4);
+    }
+    for (int b = 0; b < kGroupSlots; ++b) {
+      // Block-scaled partial groups: the leader's MMA waits for both CTAs'
+      // promotion warps.
       mbar_init(part_full + b, 1);
-      mbar_init(part_empty + b, PAIR ? 8 : 4);
+      mbar_init(part_empty + b, PAIR ? 2 * kAccWarps : kAccWarps);
     }
     *abort_flag = 0;
     *tiles_done = 0;
@@ -274,6 +294,89 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
   if constexpr (PAIR) cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+
+  // One 32-column chunk of a finished tile (values after alpha), by the
+  // thread owning output row `row`: fault injection, nonfinite check, the
+  // observed checksum partials of the warp's 32 rows into `red`, the store.
+  auto emit_chunk = [&](float (&v)[32], int q, int row, bool row_ok, int c0, int chunk, const float* w,
+                        bool& nonfinite) {
+    if (C > 0 && p.fbit >= 0 && row == p.frow && p.fcol >= c0 && p.fcol < c0 + 32) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (c0 + j == p.fcol) v[j] = __uint_as_float(__float_as_uint(v[j]) ^ (1u << p.fbit));
+      }
+      *p.hit = 1;
+    }
+    if (C > 0 && p.nonfinite != nullptr && row_ok) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float out = BF16OUT ? bf16_bits_to_float(float_to_bf16_bits(v[j])) : v[j];
+        if (c0 + j < p.n && !isfinite(out)) nonfinite = true;
+      }
+    }
+    if constexpr (C > 0) {
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        float x[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) x[j] = w[c] * v[j];
+        red[((chunk * 4 + q) * C + c) * 32 + lane] = transpose_reduce32(x, lane);
+      }
+    }
+    if (row_ok) {
+      if constexpr (BF16OUT) {
+        uint16_t* d = static_cast<uint16_t*>(p.d) + static_cast<int64_t>(row) * p.n;
+        if (c0 + 32 <= p.n && (p.n & 7) == 0) {
+          uint32_t packed[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            packed[j] = static_cast<uint32_t>(float_to_bf16_bits(v[2 * j])) |
+                        (static_cast<uint32_t>(float_to_bf16_bits(v[2 * j + 1])) << 16);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(d + c0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (c0 + j < p.n) d[c0 + j] = float_to_bf16_bits(v[j]);
+          }
+        }
+      } else {
+        float* d = static_cast<float*>(p.d);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (c0 + j < p.n) d[static_cast<int64_t>(c0 + j) * p.m + row] = v[j];
+        }
+      }
+    }
+  };
+  // After every chunk of a tile: the observed checksum of each column is the
+  // sum of the four lane quarters' 32-row partials (all epilogue threads).
+  auto store_observed = [&](int mt, int n0, bool live) {
+    if constexpr (C > 0) {
+      named_barrier(1, kAccThreads);
+      if (live) {
+        const int e = static_cast<int>(threadIdx.x) - 32 * kEpi0;
+        for (int idx = e; idx < kTileChunks * C * 32; idx += kAccThreads) {
+          const int chunk = idx / (C * 32);
+          const int rem = idx - chunk * C * 32;
+          const int c = rem >> 5;
+          const int col = rem & 31;
+          float sum = 0.f;
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) sum += red[((chunk * 4 + qq) * C + c) * 32 + col];
+          const int gcol = n0 + chunk * 32 + col;
+          if (gcol < p.padded_n && mt < p.tiles_m) {
+            p.observed[(static_cast<int64_t>(c) * p.tiles_m + mt) * p.padded_n + gcol] = sum;
+          }
+        }
+      }
+      named_barrier(1, kAccThreads);
+    }
+  };
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -324,93 +427,154 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
     // ---------------- MMA issuer, block-scaled: one partial per K block ----------------
     if (lane == 0 && leader) {
       constexpr uint32_t idesc = idesc_e4m3(PAIR ? 2 * kBM : kBM, kTN);
-      uint32_t kbg = 0;
-      for (int t = work_first; t < p.num_work && !*abort_flag; t += work_step) {
-        for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
-          const int s = kbg % kS;
-          const uint32_t pb = kbg & 1u;
-          if (kbg >= 2) {
-            if (!mbar_wait(part_empty + pb, ((kbg >> 1) - 1) & 1, kWaitAccumFree, abort_flag, p.watchdog)) break;
+      uint32_t kbg = 0, gg = 0;
+      bool stop = false;
+      for (int t = work_first; t < p.num_work && !stop; t += work_step) {
+        // Groups of kGroupKb K blocks of one tile (the last may be shorter).
+        for (int kb0 = 0; kb0 < p.num_kb && !stop; kb0 += kGroupKb, ++gg) {
+          const uint32_t gs = gg % kGroupSlots;
+          if (gg >= kGroupSlots &&
+              !mbar_wait(part_empty + gs, ((gg / kGroupSlots) - 1) & 1, kWaitAccumFree, abort_flag, p.watchdog)) {
+            stop = true;
+            break;
           }
-          if (!mbar_wait(full + s, (kbg / kS) & 1, kWaitFull, abort_flag, p.watchdog)) break;
-          tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * kStageBytes);
-          const uint32_t sb = sa + kABytes;
-          const uint32_t d_tmem = tmem + kPartialCol + pb * kTN;
+          const int kb_end = min(kb0 + kGroupKb, p.num_kb);
+          for (int kb = kb0; kb < kb_end; ++kb, ++kbg) {
+            const int s = kbg % kS;
+            if (!mbar_wait(full + s, (kbg / kS) & 1, kWaitFull, abort_flag, p.watchdog)) {
+              stop = true;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(smem + s * kStageBytes);
+            const uint32_t sb = sa + kABytes;
+            const uint32_t d_tmem = tmem + (gs * kGroupKb + (kb - kb0)) * kTN;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint32_t acc = j > 0 ? 1u : 0u;
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t acc = j > 0 ? 1u : 0u;
+              if constexpr (PAIR) {
+                mma_f8f6f4_pair(d_tmem, sw128_desc(sa + 32 * j), sw128_desc(sb + 32 * j), idesc, acc);
+              } else {
+                mma_f8f6f4(d_tmem, sw128_desc(sa + 32 * j), sw128_desc(sb + 32 * j), idesc, acc);
+              }
+            }
             if constexpr (PAIR) {
-              mma_f8f6f4_pair(d_tmem, sw128_desc(sa + 32 * j), sw128_desc(sb + 32 * j), idesc, acc);
+              tc_commit_pair(empty + s, 0x3);
             } else {
-              mma_f8f6f4(d_tmem, sw128_desc(sa + 32 * j), sw128_desc(sb + 32 * j), idesc, acc);
+              tc_commit(empty + s);
             }
           }
+          if (stop) break;
           if constexpr (PAIR) {
-            tc_commit_pair(empty + s, 0x3);
-            tc_commit_pair(part_full + pb, 0x3);
+            tc_commit_pair(part_full + gs, 0x3);
           } else {
-            tc_commit(empty + s);
-            tc_commit(part_full + pb);
+            tc_commit(part_full + gs);
           }
         }
       }
     }
-  } else if (BLK && warp >= (CHK ? 10 : 6)) {
-    // ---------------- promotion (block-scaled): total += sa * sb * partial ----------------
-    const int q = warp & 3;
-    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    uint32_t kbg = 0;
-    int i = 0;
-    for (int t = work_first; t < p.num_work && !*abort_flag; t += work_step, ++i) {
-      int mt, nt;
-      work_coords<PAIR>(t, p, rank, mt, nt);
-      const int row = mt * kBM + q * 32 + lane;
-      const float* sa_row = p.sa + static_cast<int64_t>(row < p.m ? row : 0) * p.k_blocks;
-      const float* sb_blk = p.sb + static_cast<int64_t>(nt) * p.k_blocks;  // 128-wide tile = one B block
-      const uint32_t tb = static_cast<uint32_t>(i & 1);
-      bool ok = true;
-      if (i >= 2) {
-        ok = mbar_wait(acc_empty + tb, ((i >> 1) - 1) & 1, kWaitAccumFree, abort_flag, p.watchdog);
-        tc_fence_after();
-      }
-      for (int kb = 0; kb < p.num_kb && ok; ++kb, ++kbg) {
-        const uint32_t pb = kbg & 1u;
-        const float scale = __fmul_rn(row < p.m ? __ldg(sa_row + kb) : 0.f, __ldg(sb_blk + kb));
-        if (!mbar_wait(part_full + pb, (kbg >> 1) & 1, kWaitAccum, abort_flag, p.watchdog)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll 1
-        for (int chunk = 0; chunk < kTileChunks; ++chunk) {
-          uint32_t part[32], total[32];
-          tmem_ld_32x32b_x32(tmem + lane_base + kPartialCol + pb * kTN + chunk * 32, part);
-          if (kb > 0) tmem_ld_32x32b_x32(tmem + lane_base + tb * kTN + chunk * 32, total);
-          tmem_ld_wait();
+  } else if (BLK && warp >= kEpi0 && warp < kEpi0 + kAccWarps) {
+    // ------- promotion + epilogue (block-scaled): total += sa * sb * partial -------
+    if constexpr (BLK) {
+      constexpr int kHalfCols = kTN / 2;
+      const int q = warp & 3;                // TMEM lane quarter this warp may access
+      const int half = (warp - kEpi0) >> 2;  // 64-column half of the tile
+      const uint32_t lane_base = (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(half * kHalfCols);
+      uint32_t gg = 0;
+      int i = 0;
+      for (int t = work_first; t < p.num_work; t += work_step, ++i) {
+        int mt, nt;
+        work_coords<PAIR>(t, p, rank, mt, nt);
+        const int n0 = nt * kTN;
+        const int row = mt * kBM + q * 32 + lane;
+        const bool row_ok = row < p.m;
+        float w[C > 0 ? C : 1];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float x = __uint_as_float(part[j]);
-            total[j] = __float_as_uint(kb > 0 ? fmaf(scale, x, __uint_as_float(total[j])) : __fmul_rn(scale, x));
-          }
-          tmem_st_32x32b_x32(tmem + lane_base + tb * kTN + chunk * 32, total);
+        for (int c = 0; c < C; ++c) w[c] = row_ok ? p.weights[static_cast<int64_t>(c) * p.m + row] : 0.f;
+        const float* sa_row = p.sa + static_cast<int64_t>(row_ok ? row : 0) * p.k_blocks;
+        const float* sb_blk = p.sb + static_cast<int64_t>(nt) * p.k_blocks;  // 128-wide tile = one B block
+        // Column pairs (2j, 2j + 1) of this warp's half; -0 keeps
+        // fma(s, x, total) equal to s * x (sign of zero included) on the first block.
+        float2 total[kHalfCols / 2];
+#pragma unroll
+        for (int j = 0; j < kHalfCols / 2; ++j) total[j] = make_float2(-0.f, -0.f);
+        // This group's scales; the next group's load under this group's wait.
+        float sa_next[kGroupKb], sb_next[kGroupKb];
+#pragma unroll
+        for (int e = 0; e < kGroupKb; ++e) {
+          const bool in = e < p.num_kb;
+          sa_next[e] = in && row_ok ? __ldg(sa_row + e) : 0.f;
+          sb_next[e] = in ? __ldg(sb_blk + e) : 0.f;
         }
-        tmem_st_wait();
-        // The partial is consumed: hand it back to the MMA warp.
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          if constexpr (PAIR) {
-            mbar_arrive_cluster(mapa_shared(part_empty + pb, 0));
-          } else {
-            mbar_arrive(part_empty + pb);
+        bool ok = !*abort_flag;
+        for (int kb0 = 0; kb0 < p.num_kb && ok; kb0 += kGroupKb, ++gg) {
+          float2 s2[kGroupKb];
+#pragma unroll
+          for (int e = 0; e < kGroupKb; ++e) {
+            const float scale = __fmul_rn(sa_next[e], sb_next[e]);
+            s2[e] = make_float2(scale, scale);
+            const int kn = kb0 + kGroupKb + e;
+            if (kn < p.num_kb) {
+              sa_next[e] = row_ok ? __ldg(sa_row + kn) : 0.f;
+              sb_next[e] = __ldg(sb_blk + kn);
+            }
+          }
+          const int n_in = min(kGroupKb, p.num_kb - kb0);
+          const uint32_t gs = gg % kGroupSlots;
+          if (!mbar_wait(part_full + gs, (gg / kGroupSlots) & 1, kWaitAccum, abort_flag, p.watchdog)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int e = 0; e < kGroupKb; ++e) {
+            if (e < n_in) {
+              const uint32_t col = lane_base + static_cast<uint32_t>((gs * kGroupKb + e) * kTN);
+              uint32_t lo[32], hi[32];
+              tmem_ld_32x32b_x32(tmem + col, lo);
+              tmem_ld_32x32b_x32(tmem + col + 32, hi);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                total[j] =
+                    fma2(s2[e], make_float2(__uint_as_float(lo[2 * j]), __uint_as_float(lo[2 * j + 1])), total[j]);
+                total[16 + j] = fma2(s2[e], make_float2(__uint_as_float(hi[2 * j]), __uint_as_float(hi[2 * j + 1])),
+                                     total[16 + j]);
+              }
+            }
+          }
+          // The group's partials are in registers: hand the buffers back to
+          // the (leader's) MMA warp.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (PAIR) {
+              mbar_arrive_cluster(mapa_shared(part_empty + gs, 0));
+            } else {
+              mbar_arrive(part_empty + gs);
+            }
           }
         }
+        const bool live = !named_barrier_or(1, kAccThreads, !ok || *abort_flag != 0);
+        if (live) {
+          bool nonfinite = false;
+#pragma unroll
+          for (int cc = 0; cc < kHalfCols / 32; ++cc) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              v[2 * j] = total[cc * 16 + j].x;
+              v[2 * j + 1] = total[cc * 16 + j].y;
+            }
+            const int chunk = half * (kHalfCols / 32) + cc;
+            emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite);
+          }
+          if (nonfinite) atomicExch(p.nonfinite, 1);
+        }
+        store_observed(mt, n0, live);
+        if (threadIdx.x == 32 * kEpi0) *tiles_done = static_cast<uint32_t>(i + 1);
+        if (!live) break;
       }
-      if (!ok) break;
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acc_full + tb);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -476,10 +640,10 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
         }
       }
     }
-  } else if (warp < 6) {
+  } else if (!BLK && warp >= kEpi0 && warp < kEpi0 + kAccWarps) {
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const float alpha = BLK ? 1.f : *p.alpha;  // block scales are applied by the promotion warps
+    const float alpha = *p.alpha;
     int i = 0;
     for (int t = work_first; t < p.num_work; t += work_step, ++i) {
       int mt, nt;
@@ -492,7 +656,7 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
       for (int c = 0; c < C; ++c) w[c] = row_ok ? p.weights[static_cast<int64_t>(c) * p.m + row] : 0.f;
       const int b = i % kAcc;
       const bool ready = mbar_wait(acc_full + b, (i / kAcc) & 1, kWaitAccum, abort_flag, p.watchdog);
-      const bool live = !named_barrier_or(1, 128, !ready || *abort_flag != 0);
+      const bool live = !named_barrier_or(1, kAccThreads, !ready || *abort_flag != 0);
       tc_fence_after();
       if (live) {
         bool nonfinite = false;
@@ -507,104 +671,33 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-              if constexpr (PAIR && !BLK) {
+              if constexpr (PAIR) {
                 mbar_arrive_cluster(mapa_shared(acc_empty + b, 0));  // the leader's MMA waits on both CTAs
               } else {
                 mbar_arrive(acc_empty + b);
               }
             }
           }
-          const int c0 = n0 + chunk * 32;
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(alpha, __uint_as_float(r[j]));
-          if (C > 0 && p.fbit >= 0 && row == p.frow && p.fcol >= c0 && p.fcol < c0 + 32) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (c0 + j == p.fcol) v[j] = __uint_as_float(__float_as_uint(v[j]) ^ (1u << p.fbit));
-            }
-            *p.hit = 1;
-          }
-          if (C > 0 && p.nonfinite != nullptr && row_ok) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float out = BF16OUT ? bf16_bits_to_float(float_to_bf16_bits(v[j])) : v[j];
-              if (c0 + j < p.n && !isfinite(out)) nonfinite = true;
-            }
-          }
-          if constexpr (C > 0) {
-#pragma unroll
-            for (int c = 0; c < C; ++c) {
-              float x[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) x[j] = w[c] * v[j];
-              red[((chunk * 4 + q) * C + c) * 32 + lane] = transpose_reduce32(x, lane);
-            }
-          }
-          if (row_ok) {
-            if constexpr (BF16OUT) {
-              uint16_t* d = static_cast<uint16_t*>(p.d) + static_cast<int64_t>(row) * p.n;
-              if (c0 + 32 <= p.n && (p.n & 7) == 0) {
-                uint32_t packed[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  packed[j] = static_cast<uint32_t>(float_to_bf16_bits(v[2 * j])) |
-                              (static_cast<uint32_t>(float_to_bf16_bits(v[2 * j + 1])) << 16);
-                }
-                uint4* dst = reinterpret_cast<uint4*>(d + c0);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-                }
-              } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                  if (c0 + j < p.n) d[c0 + j] = float_to_bf16_bits(v[j]);
-                }
-              }
-            } else {
-              float* d = static_cast<float*>(p.d);
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                if (c0 + j < p.n) d[static_cast<int64_t>(c0 + j) * p.m + row] = v[j];
-              }
-            }
-          }
+          emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite);
         }
         if (nonfinite) atomicExch(p.nonfinite, 1);
       }
-      if constexpr (C > 0) {
-        named_barrier(1, 128);
-        if (live) {
-          const int e = threadIdx.x - 64;
-          for (int idx = e; idx < kTileChunks * C * 32; idx += 128) {
-            const int chunk = idx / (C * 32);
-            const int rem = idx - chunk * C * 32;
-            const int c = rem >> 5;
-            const int col = rem & 31;
-            float sum = 0.f;
-#pragma unroll
-            for (int qq = 0; qq < 4; ++qq) sum += red[((chunk * 4 + qq) * C + c) * 32 + col];
-            const int gcol = n0 + chunk * 32 + col;
-            if (gcol < p.padded_n && mt < p.tiles_m) {
-              p.observed[(static_cast<int64_t>(c) * p.tiles_m + mt) * p.padded_n + gcol] = sum;
-            }
-          }
-        }
-        named_barrier(1, 128);
-      }
-      if (threadIdx.x == 64) *tiles_done = static_cast<uint32_t>(i + 1);
+      store_observed(mt, n0, live);
+      if (threadIdx.x == 32 * kEpi0) *tiles_done = static_cast<uint32_t>(i + 1);
       if (!live) break;
     }
   } else if constexpr (CHK) {
-    if (is_prediction_warp(warp)) {
-      // ---------------- input-side prediction (warps 6..9) ----------------
+    if (is_prediction_warp<BLK>(warp)) {
+      // ---------------- input-side prediction (4 warps) ----------------
       // Independent of the MMA pipeline: for each of this CTA's tiles, the
       // slices s = mt, mt + Tm, ... (ascending) of the tile's 256 B rows are
       // read from global memory (hot in L2: the same column block is streaming
       // through this SM) and folded into fma chains with q_full.
       // 0..127: the tile's B rows ct (and ct + 128 for 256-wide tiles).
-      const int ct = prediction_index(warp) * 32 + lane;
+      const int ct = prediction_index<BLK>(warp) * 32 + lane;
       constexpr int kRowsPerThread = kTN / 128;
       const float alpha = BLK ? 1.f : *p.alpha;
       const int num_slices = (p.k + kSliceK - 1) / kSliceK;
@@ -638,7 +731,7 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
       {
         const int g = lane & 3, l = lane >> 2;
         const int64_t items = static_cast<int64_t>(num_slices) * p.q_bands;
-        const int64_t first_item = static_cast<int64_t>(blockIdx.x) * 4 + prediction_index(warp);
+        const int64_t first_item = static_cast<int64_t>(blockIdx.x) * 4 + prediction_index<BLK>(warp);
         const int64_t item_step = static_cast<int64_t>(gridDim.x) * 4;
         const int64_t my_items = first_item < items ? (items - 1 - first_item) / item_step + 1 : 0;
         int64_t j = 0;
