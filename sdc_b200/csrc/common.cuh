@@ -399,6 +399,19 @@ __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Per-warpgroup register reallocation: every warp of the warpgroup executes
+// the same instruction, in warp-uniform control flow. The increases of a CTA
+// must fit in what it was launched with (threads x registers at launch) minus
+// what the decreases free, or the increasing warps wait forever.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N));
+}
+
 // Named barrier that also ORs a predicate across the participating threads,
 // so every thread leaves with the same decision (e.g. "some wait failed").
 __device__ __forceinline__ bool named_barrier_or(uint32_t id, uint32_t count, bool pred) {

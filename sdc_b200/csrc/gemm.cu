@@ -82,12 +82,20 @@ __host__ __device__ constexpr int smem_bytes(Kind k, bool pair = false) {
 }
 __host__ __device__ constexpr int num_acc(Kind k) { return k == Kind::kNvf4 ? 1 : 2; }
 // Warp roles. Tensorwise FP8 / NVFP4: 0 TMA, 1 MMA, 2-5 epilogue, 6-9
-// prediction (checked K-slice launches). Block-scaled FP8: 0 TMA, 1 MMA, 2-9
-// promotion + epilogue (two warps per TMEM lane quarter, one per 64-column
-// half of the tile), 10-13 prediction.
-constexpr int kEpi0 = 2;
+// prediction (checked K-slice launches). Block-scaled FP8: 0 TMA, 1 MMA, 2-3
+// idle, 4-11 promotion + epilogue (two warps per TMEM lane quarter, one per
+// 64-column half of the tile), 12-15 prediction: roles on warpgroup
+// boundaries, so that checked launches can move registers from warpgroup 0
+// to the promotion warps (setmaxnreg).
+__host__ __device__ constexpr int epi_warp0(bool blk) { return blk ? 4 : 2; }
 __host__ __device__ constexpr int acc_warps(bool blk) { return blk ? 8 : 4; }
-__host__ __device__ constexpr int pred_warp0(bool blk) { return kEpi0 + acc_warps(blk); }
+__host__ __device__ constexpr int pred_warp0(bool blk) { return epi_warp0(blk) + acc_warps(blk); }
+// Checked block-scaled launches: 512 threads start with 128 registers each
+// (the whole register file). Warpgroup 0 drops to 40 and the two promotion
+// warpgroups rise to 168; the prediction warpgroup keeps 128:
+// 40 + 168 + 168 + 128 = 504 <= 4 x 128.
+constexpr uint32_t kLowRegs = 40;
+constexpr uint32_t kPromoteRegs = 168;
 __host__ __device__ constexpr int num_threads(bool chk, bool blk = false) {
   return 32 * (pred_warp0(blk) + (chk ? 4 : 0));
 }
@@ -226,6 +234,7 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
   // run the epilogue from there.
   constexpr bool BLK = KIND == Kind::kFp8Block;
   constexpr int kAccWarps = acc_warps(BLK);
+  constexpr int kEpi0 = epi_warp0(BLK);
   constexpr uint32_t kAccThreads = 32 * kAccWarps;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -242,7 +251,8 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
   // Tiles whose epilogue has finished: paces the prediction warps.
   volatile uint32_t* tiles_done = tmem_slot + 2;
 
-  const int warp = threadIdx.x >> 5;
+  // Warp-uniform by construction (setmaxnreg needs provably uniform branches).
+  const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x >> 5), 0);
   const int lane = threadIdx.x & 31;
   // CTA pairs: rank 0 (the leader) issues the MMAs for both CTAs; its
   // barriers count both CTAs' loads and epilogues.
@@ -378,6 +388,9 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
     }
   };
 
+  if (warp < kEpi0) {
+    // Warps 0-1 (block-scaled: warpgroup 0, warps 2-3 idle).
+    if constexpr (BLK && CHK) setmaxnreg_dec<kLowRegs>();
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
@@ -473,9 +486,75 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
         }
       }
     }
-  } else if (BLK && warp >= kEpi0 && warp < kEpi0 + kAccWarps) {
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && leader) {
+      constexpr int kMmaM = PAIR ? 2 * kBM : kBM;
+      constexpr uint32_t idesc = KIND == Kind::kFp8 ? idesc_e4m3(kMmaM, kTN) : idesc_nvf4(kMmaM, kTN);
+      uint32_t kbg = 0;
+      int i = 0;
+      for (int t = work_first; t < p.num_work && !*abort_flag; t += work_step, ++i) {
+        const int b = i % kAcc;
+        if (i >= kAcc) {
+          if (!mbar_wait(acc_empty + b, ((i / kAcc) - 1) & 1, kWaitAccumFree, abort_flag, p.watchdog)) break;
+          tc_fence_after();
+        }
+        const uint32_t d_tmem = tmem + b * kTN;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
+          const int s = kbg % kS;
+          if (!mbar_wait(full + s, (kbg / kS) & 1, kWaitFull, abort_flag, p.watchdog)) break;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * kStageBytes);
+          const uint32_t sb = sa + kABytes;
+          if constexpr (KIND == Kind::kNvf4) {
+            // Pairs: one copy moves each CTA's staged scales into its own TMEM.
+            const uint32_t ssfa = sb + kBStage;
+            const uint32_t ssfb = ssfa + kSfaBytes;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              tmem_cp_32x128b_x4<PAIR>(tmem + kSfaCol + 4 * j, sf_desc(ssfa + 512 * j));
+#pragma unroll
+              for (int g = 0; g < sfb_groups(KIND); ++g) {
+                tmem_cp_32x128b_x4<PAIR>(tmem + kSfbCol + 4 * (sfb_groups(KIND) * j + g),
+                                         sf_desc(ssfb + 2048 * g + 512 * j));
+              }
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint64_t adesc = sw128_desc(sa + 32 * j);
+            const uint64_t bdesc = sw128_desc(sb + 32 * j);
+            const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
+            if constexpr (KIND == Kind::kFp8) {
+              if constexpr (PAIR) {
+                mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, acc);
+              } else {
+                mma_f8f6f4(d_tmem, adesc, bdesc, idesc, acc);
+              }
+            } else {
+              mma_nvf4<PAIR>(d_tmem, adesc, bdesc, idesc, tmem + kSfaCol + 4 * j,
+                             tmem + kSfbCol + 4 * sfb_groups(KIND) * j, acc);
+            }
+          }
+          // Frees the stage in both CTAs (pairs) once these MMAs have read it.
+          if constexpr (PAIR) {
+            tc_commit_pair(empty + s, 0x3);
+          } else {
+            tc_commit(empty + s);
+          }
+        }
+        if constexpr (PAIR) {
+          tc_commit_pair(acc_full + b, 0x3);
+        } else {
+          tc_commit(acc_full + b);
+        }
+      }
+    }
+    }
+  } else if (BLK && warp < kEpi0 + kAccWarps) {
     // ------- promotion + epilogue (block-scaled): total += sa * sb * partial -------
     if constexpr (BLK) {
+      if constexpr (CHK) setmaxnreg_inc<kPromoteRegs>();
       constexpr int kHalfCols = kTN / 2;
       const int q = warp & 3;                // TMEM lane quarter this warp may access
       const int half = (warp - kEpi0) >> 2;  // 64-column half of the tile
@@ -576,71 +655,7 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
         if (!live) break;
       }
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0 && leader) {
-      constexpr int kMmaM = PAIR ? 2 * kBM : kBM;
-      constexpr uint32_t idesc = KIND == Kind::kFp8 ? idesc_e4m3(kMmaM, kTN) : idesc_nvf4(kMmaM, kTN);
-      uint32_t kbg = 0;
-      int i = 0;
-      for (int t = work_first; t < p.num_work && !*abort_flag; t += work_step, ++i) {
-        const int b = i % kAcc;
-        if (i >= kAcc) {
-          if (!mbar_wait(acc_empty + b, ((i / kAcc) - 1) & 1, kWaitAccumFree, abort_flag, p.watchdog)) break;
-          tc_fence_after();
-        }
-        const uint32_t d_tmem = tmem + b * kTN;
-        for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
-          const int s = kbg % kS;
-          if (!mbar_wait(full + s, (kbg / kS) & 1, kWaitFull, abort_flag, p.watchdog)) break;
-          tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * kStageBytes);
-          const uint32_t sb = sa + kABytes;
-          if constexpr (KIND == Kind::kNvf4) {
-            // Pairs: one copy moves each CTA's staged scales into its own TMEM.
-            const uint32_t ssfa = sb + kBStage;
-            const uint32_t ssfb = ssfa + kSfaBytes;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              tmem_cp_32x128b_x4<PAIR>(tmem + kSfaCol + 4 * j, sf_desc(ssfa + 512 * j));
-#pragma unroll
-              for (int g = 0; g < sfb_groups(KIND); ++g) {
-                tmem_cp_32x128b_x4<PAIR>(tmem + kSfbCol + 4 * (sfb_groups(KIND) * j + g),
-                                         sf_desc(ssfb + 2048 * g + 512 * j));
-              }
-            }
-          }
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint64_t adesc = sw128_desc(sa + 32 * j);
-            const uint64_t bdesc = sw128_desc(sb + 32 * j);
-            const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
-            if constexpr (KIND == Kind::kFp8) {
-              if constexpr (PAIR) {
-                mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, acc);
-              } else {
-                mma_f8f6f4(d_tmem, adesc, bdesc, idesc, acc);
-              }
-            } else {
-              mma_nvf4<PAIR>(d_tmem, adesc, bdesc, idesc, tmem + kSfaCol + 4 * j,
-                             tmem + kSfbCol + 4 * sfb_groups(KIND) * j, acc);
-            }
-          }
-          // Frees the stage in both CTAs (pairs) once these MMAs have read it.
-          if constexpr (PAIR) {
-            tc_commit_pair(empty + s, 0x3);
-          } else {
-            tc_commit(empty + s);
-          }
-        }
-        if constexpr (PAIR) {
-          tc_commit_pair(acc_full + b, 0x3);
-        } else {
-          tc_commit(acc_full + b);
-        }
-      }
-    }
-  } else if (!BLK && warp >= kEpi0 && warp < kEpi0 + kAccWarps) {
+  } else if (!BLK && warp < kEpi0 + kAccWarps) {
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const float alpha = *p.alpha;
