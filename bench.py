@@ -447,8 +447,9 @@ def run_ours(args):
     os.write(result_fd, (json.dumps(line) + "\n").encode())
 
 
-def cpu_baseline(rows):
-    """The reference's CPU/torch ABFT path on a row sample of the FP8 workload."""
+def cpu_baseline(rows, min_seconds=10.0):
+    """The reference's CPU/torch ABFT path on rows of the 8192^3 workload
+    (all 8192 by default), repeated until about ``min_seconds`` of CPU work."""
     from oracle import cpu_path
 
     torch.set_num_threads(os.cpu_count() or 1)
@@ -457,12 +458,18 @@ def cpu_baseline(rows):
     a = torch.randn(rows, k, generator=g)
     b = torch.randn(k, n, generator=g)
     cpu_path.execute(a[:64], b[:, :64], block_k=256)  # warm the BLAS
+    calls = 0
     t0 = time.perf_counter()
-    _, report, _ = cpu_path.execute(a, b, atol=1e-3, rtol=1e-4, block_k=256)
-    seconds = time.perf_counter() - t0
-    return {"value": 2.0 * rows * n * k / seconds / 1e12, "unit": UNIT, "cores": torch.get_num_threads(),
-            "kind": "port", "sample": f"fp32 {rows}x{n}x{k} row sample of the 8192^3 workload, Classic, "
-                                      f"1 protected GEMM ({seconds:.2f} s)", "detected": report["detected"]}
+    while True:
+        _, report, _ = cpu_path.execute(a, b, atol=1e-3, rtol=1e-4, block_k=256)
+        calls += 1
+        seconds = time.perf_counter() - t0
+        if seconds >= min_seconds:
+            break
+    return {"value": 2.0 * rows * n * k * calls / seconds / 1e12, "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"fp32 {rows}x{n}x{k} ({rows} of the 8192 rows of the workload), Classic, "
+                                      f"{calls} protected GEMMs in {seconds:.1f} s",
+            "detected": report["detected"]}
 
 
 def run_reference(args):
@@ -484,7 +491,7 @@ def run_reference(args):
         cpu_path.execute(a, b, atol=1e-3, rtol=1e-4)
     seconds = (time.perf_counter() - t0) / steps
     value = 2.0 * rows * n * k / seconds / 1e12
-    sample = f"fp32 {rows}x{n}x{k} row sample of the 8192^3 workload per step"
+    sample = f"fp32 {rows}x{n}x{k} ({rows} of the 8192 rows of the workload) per step"
     print(json.dumps({
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
         "steps": steps, "warmup": args.warmup, "ms_per_step": seconds * 1e3, "higher_is_better": True,
@@ -509,7 +516,7 @@ def main():
     parser.add_argument("--format", choices=["all", "fp8_block", "fp8", "nvfp4"], default="all",
                         help="fp8_block = config[1] (headline), fp8 = tensorwise FP8, nvfp4 = config[2]")
     parser.add_argument("--flips", type=int, default=64)
-    parser.add_argument("--cpu-sample-rows", type=int, default=1024)
+    parser.add_argument("--cpu-sample-rows", type=int, default=8192)
     parser.add_argument("--no-detection", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")

@@ -216,57 +216,74 @@ int grid_for(int64_t work) {
 // d = amax(|x|) / 448 (1 when amax == 0); codes = e4m3_rn_satfinite(x / d),
 // so x ~ code * d. BR = 1 (activations, one warp per block) or 128 (weights,
 // one CTA per block).
+// Block-scaled FP8 cast: d = amax(|block|) / 448 (1 for an all-zero block),
+// code = e4m3_rn_satfinite(x / d).
+// BR = 1 (1 x 128 blocks): 16 lanes per block, 8 consecutive elements (one or
+// two 16-byte loads) per lane, two blocks per warp.
+// BR = 128 (128 x 128 blocks): one CTA per block; every warp-wide load and
+// store covers two rows of the block contiguously.
 template <int DT, int BR>
 __global__ void __launch_bounds__(kQuantThreads)
     fp8_block_cast(const void* x, int64_t rows, int64_t cols, uint8_t* codes, float* scales) {
   const int64_t kblocks = cols / 128;
+  const int lane = threadIdx.x & 31;
   if constexpr (BR == 1) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t blk = static_cast<int64_t>(blockIdx.x) * (kQuantThreads / 32) + warp;
-    if (blk >= rows * kblocks) return;
+    const int64_t blk = static_cast<int64_t>(blockIdx.x) * (kQuantThreads / 16) + (threadIdx.x >> 4);
+    if (blk >= rows * kblocks) return;  // whole 16-lane groups leave together
     const int64_t r = blk / kblocks, kb = blk - r * kblocks;
-    const int64_t base = r * cols + kb * 128 + lane * 4;
-    float v[4];
+    const int64_t base = r * cols + kb * 128 + (threadIdx.x & 15) * 8;
+    float v[8];
+    load8<DT>(x, base, v);
     uint32_t bits = 0;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      v[e] = load_elem<DT>(x, base + e);
-      bits = max(bits, abs_bits(v[e]));
-    }
-    for (int o = 16; o > 0; o >>= 1) bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, o));
+    for (int e = 0; e < 8; ++e) bits = max(bits, abs_bits(v[e]));
+    const uint32_t group = 0xFFFFu << (lane & 16);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) bits = max(bits, __shfl_xor_sync(group, bits, o));
     const float amax = __uint_as_float(bits);
     const float d = amax == 0.f ? 1.f : __fdiv_rn(amax, 448.f);
-    const uint32_t lo = cvt_e4m3x2(__fdiv_rn(v[0], d), __fdiv_rn(v[1], d));
-    const uint32_t hi = cvt_e4m3x2(__fdiv_rn(v[2], d), __fdiv_rn(v[3], d));
-    *reinterpret_cast<uint32_t*>(codes + base) = lo | (hi << 16);
-    if (lane == 0) scales[r * kblocks + kb] = d;
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[j] = cvt_e4m3x2(__fdiv_rn(v[2 * j], d), __fdiv_rn(v[2 * j + 1], d));
+    *reinterpret_cast<uint2*>(codes + base) = make_uint2(w[0] | (w[1] << 16), w[2] | (w[3] << 16));
+    if ((threadIdx.x & 15) == 0) scales[r * kblocks + kb] = d;
   } else {
     __shared__ uint32_t warp_max[kQuantThreads / 32];
+    const int warp = threadIdx.x >> 5;
     const int64_t rb = blockIdx.x / kblocks, kb = blockIdx.x - rb * kblocks;
-    const int64_t r = rb * 128 + (threadIdx.x >> 1);
-    const int64_t base = r * cols + kb * 128 + (threadIdx.x & 1) * 64;
-    const bool in = r < rows;
-    float v[64];
+    // 16 lanes per row (8 columns each, 16-byte loads), two rows per warp and
+    // instruction; warp w owns rows 16w..16w+15 of the block.
+    const int64_t row0 = rb * 128 + warp * 16 + (lane >> 4);
+    const int64_t col = kb * 128 + (lane & 15) * 8;
+    float v[8][8];
     uint32_t bits = 0;
 #pragma unroll
-    for (int e = 0; e < 64; ++e) {
-      v[e] = in ? load_elem<DT>(x, base + e) : 0.f;
-      bits = max(bits, abs_bits(v[e]));
+    for (int i = 0; i < 8; ++i) {
+      if (row0 + 2 * i < rows) {
+        load8<DT>(x, (row0 + 2 * i) * cols + col, v[i]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) bits = max(bits, abs_bits(v[i][e]));
     }
+#pragma unroll
     for (int o = 16; o > 0; o >>= 1) bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, o));
-    if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = bits;
+    if (lane == 0) warp_max[warp] = bits;
     __syncthreads();
     bits = 0;
 #pragma unroll
     for (int w = 0; w < kQuantThreads / 32; ++w) bits = max(bits, warp_max[w]);
     const float amax = __uint_as_float(bits);
     const float d = amax == 0.f ? 1.f : __fdiv_rn(amax, 448.f);
-    if (in) {
 #pragma unroll
-      for (int e = 0; e < 64; e += 4) {
-        const uint32_t lo = cvt_e4m3x2(__fdiv_rn(v[e], d), __fdiv_rn(v[e + 1], d));
-        const uint32_t hi = cvt_e4m3x2(__fdiv_rn(v[e + 2], d), __fdiv_rn(v[e + 3], d));
-        *reinterpret_cast<uint32_t*>(codes + base + e) = lo | (hi << 16);
+    for (int i = 0; i < 8; ++i) {
+      if (row0 + 2 * i < rows) {
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = cvt_e4m3x2(__fdiv_rn(v[i][2 * j], d), __fdiv_rn(v[i][2 * j + 1], d));
+        *reinterpret_cast<uint2*>(codes + (row0 + 2 * i) * cols + col) = make_uint2(w[0] | (w[1] << 16), w[2] | (w[3] << 16));
       }
     }
     if (threadIdx.x == 0) scales[rb * kblocks + kb] = d;
@@ -388,10 +405,12 @@ extern "C" int sdc_quantize_fp8_block(const void* x, int dtype, int64_t rows, in
   SDC_REQUIRE(rows > 0 && cols > 0 && cols % 128 == 0, "block-scaled FP8 needs rows > 0 and cols % 128 == 0");
   SDC_REQUIRE(block_rows == 1 || block_rows == 128, "block-scaled FP8 blocks are 1 x 128 or 128 x 128");
   SDC_REQUIRE(x != nullptr && codes != nullptr && scales != nullptr, "quantize pointers must not be null");
-  SDC_REQUIRE(reinterpret_cast<uintptr_t>(codes) % 4 == 0, "FP8 codes must be 4-byte aligned");
+  SDC_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(codes) % 8 == 0 &&
+                  reinterpret_cast<uintptr_t>(scales) % 4 == 0,
+              "block-scaled FP8 input must be 16-byte aligned, codes 8-byte and scales 4-byte aligned");
   const int64_t kblocks = cols / 128;
   if (block_rows == 1) {
-    const unsigned grid = static_cast<unsigned>(ceil_div(rows * kblocks, kQuantThreads / 32));
+    const unsigned grid = static_cast<unsigned>(ceil_div(rows * kblocks, kQuantThreads / 16));
     if (dtype == 0) fp8_block_cast<0, 1><<<grid, kQuantThreads, 0, stream>>>(x, rows, cols, codes, scales);
     else fp8_block_cast<1, 1><<<grid, kQuantThreads, 0, stream>>>(x, rows, cols, codes, scales);
   } else {
