@@ -81,30 +81,40 @@ __host__ __device__ constexpr int smem_bytes(Kind k, bool pair = false) {
   return 1024 + num_stages(k, pair) * stage_bytes(k, pair) + kRedFloats * 4 + 256;
 }
 __host__ __device__ constexpr int num_acc(Kind k) { return k == Kind::kNvf4 ? 1 : 2; }
-// Warp roles. Tensorwise FP8 / NVFP4: 0 TMA, 1 MMA, 2-5 epilogue, 6-9
-// prediction (checked K-slice launches). Block-scaled FP8: 0 TMA, 1 MMA, 2-3
-// idle, 4-11 promotion + epilogue (two warps per TMEM lane quarter, one per
-// 64-column half of the tile), 12-15 prediction: roles on warpgroup
-// boundaries, so that checked launches can move registers from warpgroup 0
-// to the promotion warps (setmaxnreg).
-__host__ __device__ constexpr int epi_warp0(bool blk) { return blk ? 4 : 2; }
-__host__ __device__ constexpr int acc_warps(bool blk) { return blk ? 8 : 4; }
-__host__ __device__ constexpr int pred_warp0(bool blk) { return epi_warp0(blk) + acc_warps(blk); }
-// Checked block-scaled launches: 512 threads start with 128 registers each
-// (the whole register file). Warpgroup 0 drops to 40 and the two promotion
-// warpgroups rise to 168; the prediction warpgroup keeps 128:
-// 40 + 168 + 168 + 128 = 504 <= 4 x 128.
+// Warp roles. Tensorwise FP8: 0 TMA, 1 MMA, 2-5 epilogue, 6-9 prediction
+// (checked K-slice launches). Wide kinds (NVFP4, block-scaled FP8): 0 TMA,
+// 1 MMA, 2-3 idle, 4-11 epilogue (block-scaled: promotion + epilogue), two
+// warps per TMEM lane quarter, each owning one half of the tile's columns,
+// 12-15 prediction: roles on warpgroup boundaries, so that registers can move
+// from warpgroup 0 to the epilogue warps (setmaxnreg). NVFP4 has a single
+// accumulator: its epilogue warps load their whole half of it before the
+// math, so the next tile's MMAs start after the loads, not after the stores.
+__host__ __device__ constexpr bool is_wide(Kind k) { return k != Kind::kFp8; }
+__host__ __device__ constexpr int epi_warp0(bool wide) { return wide ? 4 : 2; }
+__host__ __device__ constexpr int acc_warps(bool wide) { return wide ? 8 : 4; }
+__host__ __device__ constexpr int pred_warp0(bool wide) { return epi_warp0(wide) + acc_warps(wide); }
+// Register split of the wide kinds (registers per thread, by warpgroup):
+// checked launches start 512 threads with 128 each (the whole register file);
+// warpgroup 0 drops to 40, the two epilogue warpgroups rise to 168 and the
+// prediction warpgroup keeps 128: 40 + 168 + 168 + 128 = 504 <= 4 x 128.
+// Unchecked launches start 384 threads with 168: 40 + 224 + 224 = 488 <= 3 x 168.
+// launch_impl checks the launch's register count against this before
+// launching (an increase that does not fit would wait forever).
 constexpr uint32_t kLowRegs = 40;
-constexpr uint32_t kPromoteRegs = 168;
-__host__ __device__ constexpr int num_threads(bool chk, bool blk = false) {
-  return 32 * (pred_warp0(blk) + (chk ? 4 : 0));
+__host__ __device__ constexpr uint32_t epilogue_regs(bool chk) { return chk ? 168 : 224; }
+__host__ __device__ constexpr uint32_t required_regs_per_thread(bool chk) {
+  // Registers of the whole CTA after the split, divided by its threads (rounded up).
+  return chk ? (kLowRegs + 2 * epilogue_regs(true) + 128 + 3) / 4 : (kLowRegs + 2 * epilogue_regs(false) + 2) / 3;
 }
-template <bool BLK>
+__host__ __device__ constexpr int num_threads(bool chk, bool wide = false) {
+  return 32 * (pred_warp0(wide) + (chk ? 4 : 0));
+}
+template <bool WIDE>
 __device__ __forceinline__ bool is_prediction_warp(int warp) {
-  return warp >= pred_warp0(BLK) && warp < pred_warp0(BLK) + 4;
+  return warp >= pred_warp0(WIDE) && warp < pred_warp0(WIDE) + 4;
 }
-template <bool BLK>
-__device__ __forceinline__ int prediction_index(int warp) { return warp - pred_warp0(BLK); }
+template <bool WIDE>
+__device__ __forceinline__ int prediction_index(int warp) { return warp - pred_warp0(WIDE); }
 // Block-scaled FP8: 4 partial accumulators of 128 columns fill the 512 TMEM
 // columns; the promotion warps keep the tile totals in registers. The MMA and
 // promotion warps hand partials over in groups of 2 K blocks (one commit and
@@ -218,7 +228,7 @@ __device__ __forceinline__ bool prediction_grid_barrier(uint32_t* counter, uint3
 __device__ __forceinline__ uint64_t sf_desc(uint32_t addr) { return smem_desc(addr, 0, 128, 0); }
 
 template <Kind KIND, int C, bool BF16OUT, bool CHK, bool PAIR>
-__global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
+__global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ CUtensorMap tm_sfa,
                 const __grid_constant__ CUtensorMap tm_sfb, const Params p) {
@@ -233,8 +243,9 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
   // scale_a * scale_b * partial into tile totals held in their registers and
   // run the epilogue from there.
   constexpr bool BLK = KIND == Kind::kFp8Block;
-  constexpr int kAccWarps = acc_warps(BLK);
-  constexpr int kEpi0 = epi_warp0(BLK);
+  constexpr bool WIDE = is_wide(KIND);
+  constexpr int kAccWarps = acc_warps(WIDE);
+  constexpr int kEpi0 = epi_warp0(WIDE);
   constexpr uint32_t kAccThreads = 32 * kAccWarps;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -269,7 +280,7 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
     for (int b = 0; b < 2; ++b) {
       // The (leader's) MMA waits for both CTAs' epilogues.
       mbar_init(acc_full + b, 1);
-      mbar_init(acc_empty + b, PAIR ? 8 : 4);
+      mbar_init(acc_empty + b, PAIR ? 2 * kAccWarps : kAccWarps);
     }
     for (int b = 0; b < kGroupSlots; ++b) {
       // Block-scaled partial groups: the leader's MMA waits for both CTAs'
@@ -318,11 +329,15 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
       *p.hit = 1;
     }
     if (C > 0 && p.nonfinite != nullptr && row_ok) {
+      // Non-finite as stored: fp32 from 0x7F800000 up; the round-to-nearest
+      // bf16 cast overflows from |x| >= 0x7F7F8000 (the tie above the largest
+      // finite bf16 rounds to the even pattern, +inf).
+      uint32_t largest = 0;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const float out = BF16OUT ? bf16_bits_to_float(float_to_bf16_bits(v[j])) : v[j];
-        if (c0 + j < p.n && !isfinite(out)) nonfinite = true;
+        if (c0 + j < p.n) largest = max(largest, __float_as_uint(v[j]) & 0x7FFFFFFFu);
       }
+      if (largest >= (BF16OUT ? 0x7F7F8000u : 0x7F800000u)) nonfinite = true;
     }
     if constexpr (C > 0) {
 #pragma unroll
@@ -389,8 +404,8 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
   };
 
   if (warp < kEpi0) {
-    // Warps 0-1 (block-scaled: warpgroup 0, warps 2-3 idle).
-    if constexpr (BLK && CHK) setmaxnreg_dec<kLowRegs>();
+    // Warps 0-1 (wide kinds: warpgroup 0, warps 2-3 idle).
+    if constexpr (WIDE) setmaxnreg_dec<kLowRegs>();
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
@@ -554,7 +569,7 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
   } else if (BLK && warp < kEpi0 + kAccWarps) {
     // ------- promotion + epilogue (block-scaled): total += sa * sb * partial -------
     if constexpr (BLK) {
-      if constexpr (CHK) setmaxnreg_inc<kPromoteRegs>();
+      setmaxnreg_inc<epilogue_regs(CHK)>();
       constexpr int kHalfCols = kTN / 2;
       const int q = warp & 3;                // TMEM lane quarter this warp may access
       const int half = (warp - kEpi0) >> 2;  // 64-column half of the tile
@@ -656,8 +671,11 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
       }
     }
   } else if (!BLK && warp < kEpi0 + kAccWarps) {
-    // ---------------- epilogue (warps 2..5) ----------------
+    // ---------------- epilogue ----------------
+    if constexpr (WIDE) setmaxnreg_inc<epilogue_regs(CHK)>();
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    constexpr int kWarpChunks = kTileChunks * 4 / kAccWarps;  // 32-column chunks per warp
+    const int first_chunk = ((warp - kEpi0) >> 2) * kWarpChunks;
     const float alpha = *p.alpha;
     int i = 0;
     for (int t = work_first; t < p.num_work; t += work_step, ++i) {
@@ -673,30 +691,48 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
       const bool ready = mbar_wait(acc_full + b, (i / kAcc) & 1, kWaitAccum, abort_flag, p.watchdog);
       const bool live = !named_barrier_or(1, kAccThreads, !ready || *abort_flag != 0);
       tc_fence_after();
+      const uint32_t acc_col = (static_cast<uint32_t>(q * 32) << 16) + b * kTN;
+      // All of this warp's accumulator columns are in registers: hand the
+      // buffer back to the (leader's) MMA warp before the remaining math.
+      auto release = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (PAIR) {
+            mbar_arrive_cluster(mapa_shared(acc_empty + b, 0));  // the leader's MMA waits on both CTAs
+          } else {
+            mbar_arrive(acc_empty + b);
+          }
+        }
+      };
       if (live) {
         bool nonfinite = false;
-#pragma unroll 1
-        for (int chunk = 0; chunk < kTileChunks; ++chunk) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + b * kTN + chunk * 32, r);
-          tmem_ld_wait();
-          if (chunk == kTileChunks - 1) {
-            // All of this warp's accumulator columns are in registers: hand
-            // the buffer back to the MMA warp before the remaining math.
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-              if constexpr (PAIR) {
-                mbar_arrive_cluster(mapa_shared(acc_empty + b, 0));  // the leader's MMA waits on both CTAs
-              } else {
-                mbar_arrive(acc_empty + b);
-              }
-            }
-          }
-          float v[32];
+        if constexpr (WIDE) {
+          uint32_t r[kWarpChunks][32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(alpha, __uint_as_float(r[j]));
-          emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite);
+          for (int cc = 0; cc < kWarpChunks; ++cc) tmem_ld_32x32b_x32(tmem + acc_col + (first_chunk + cc) * 32, r[cc]);
+          tmem_ld_wait();
+          release();
+#pragma unroll
+          for (int cc = 0; cc < kWarpChunks; ++cc) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(alpha, __uint_as_float(r[cc][j]));
+            const int chunk = first_chunk + cc;
+            emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite);
+          }
+        } else {
+#pragma unroll 1
+          for (int chunk = 0; chunk < kTileChunks; ++chunk) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem + acc_col + chunk * 32, r);
+            tmem_ld_wait();
+            if (chunk == kTileChunks - 1) release();
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(alpha, __uint_as_float(r[j]));
+            emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite);
+          }
         }
         if (nonfinite) atomicExch(p.nonfinite, 1);
       }
@@ -705,14 +741,14 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
       if (!live) break;
     }
   } else if constexpr (CHK) {
-    if (is_prediction_warp<BLK>(warp)) {
+    if (is_prediction_warp<WIDE>(warp)) {
       // ---------------- input-side prediction (4 warps) ----------------
       // Independent of the MMA pipeline: for each of this CTA's tiles, the
       // slices s = mt, mt + Tm, ... (ascending) of the tile's 256 B rows are
       // read from global memory (hot in L2: the same column block is streaming
       // through this SM) and folded into fma chains with q_full.
       // 0..127: the tile's B rows ct (and ct + 128 for 256-wide tiles).
-      const int ct = prediction_index<BLK>(warp) * 32 + lane;
+      const int ct = prediction_index<WIDE>(warp) * 32 + lane;
       constexpr int kRowsPerThread = kTN / 128;
       const float alpha = BLK ? 1.f : *p.alpha;
       const int num_slices = (p.k + kSliceK - 1) / kSliceK;
@@ -746,7 +782,7 @@ __global__ void __launch_bounds__(num_threads(CHK, KIND == Kind::kFp8Block), 1)
       {
         const int g = lane & 3, l = lane >> 2;
         const int64_t items = static_cast<int64_t>(num_slices) * p.q_bands;
-        const int64_t first_item = static_cast<int64_t>(blockIdx.x) * 4 + prediction_index<BLK>(warp);
+        const int64_t first_item = static_cast<int64_t>(blockIdx.x) * 4 + prediction_index<WIDE>(warp);
         const int64_t item_step = static_cast<int64_t>(gridDim.x) * 4;
         const int64_t my_items = first_item < items ? (items - 1 - first_item) / item_step + 1 : 0;
         int64_t j = 0;
@@ -1063,7 +1099,7 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   auto kernel = gemm_kernel<KIND, C, BF16OUT, CHK, PAIR>;
   constexpr int smem = smem_bytes(KIND, PAIR);
   cudaLaunchConfig_t config{};
-  config.blockDim = dim3(num_threads(CHK, KIND == Kind::kFp8Block));
+  config.blockDim = dim3(num_threads(CHK, is_wide(KIND)));
   config.dynamicSmemBytes = smem;
   config.stream = stream;
   cudaLaunchAttribute attribute[2];
@@ -1083,6 +1119,15 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   SDC_CUDA_CHECK(cudaGetDevice(&device));
   int fit = device >= 0 && device < 64 ? resident[device] : 0;
   if (fit == 0) {
+    if constexpr (is_wide(KIND)) {
+      // The register split (setmaxnreg) must fit in what the kernel is
+      // launched with, or the increasing warps would wait forever.
+      cudaFuncAttributes attr{};
+      SDC_CUDA_CHECK(cudaFuncGetAttributes(&attr, kernel));
+      if (attr.numRegs < static_cast<int>(required_regs_per_thread(CHK))) {
+        return fail(SDC_ERR_CUDA, "GEMM kernel was built with too few registers for its register split");
+      }
+    }
     SDC_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     if constexpr (PAIR) {
       config.gridDim = dim3(2);
