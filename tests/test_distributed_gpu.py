@@ -1,9 +1,10 @@
 """Row-sharded native ABFT over NCCL on two GPUs (skipped with fewer).
 
 Each rank protects its 128-aligned row shard of A on its own GPU with the
-fused FP8/NVFP4 kernels; its output rows must equal the same rows of the
-unsharded protected GEMM bit for bit (the A multiplier is the global amax
-one), and a fault on one shard must be detected and located by every rank.
+fused FP8/NVFP4/block-scaled FP8 kernels; its output rows must equal the same
+rows of the unsharded protected GEMM bit for bit (the A multiplier is the
+global amax one; block scales are per row), and a fault on one shard must be
+detected and located by every rank.
 NVLS is off (NCCL_NVLS_ENABLE=0): the exchange is one tiny all-reduce.
 """
 import os
@@ -23,6 +24,8 @@ def _free_port():
 
 
 def _worker(rank, world, port, precision, results):
+    precision, scaling = {"fp8": ("fp8", "tensorwise"), "nvfp4": ("nvfp4", "block16"),
+                          "fp8_block": ("fp8", "blockwise")}[precision]
     import datetime
 
     import torch.distributed as dist
@@ -36,13 +39,13 @@ def _worker(rank, world, port, precision, results):
         from sdc_b200.abft import execute
         from sdc_b200.abft.distributed import execute_sharded, shard_rows
 
-        scaling = {"fp8": "tensorwise", "nvfp4": "block16"}[precision]
         g = torch.Generator(device=device).manual_seed(21)
         m, n, k = 640, 384, 512
         a = torch.randn(m, k, device=device, generator=g)
         b = torch.randn(k, n, device=device, generator=g)
         cfg = {"method": "classic", "implementation": "native", "reference_mode": "input_fused",
-               "on_error": "report", "atol": 1e-3, "rtol": 1e-4, "locate": True}
+               "on_error": "report", "atol": 1e-3, "rtol": 1e-4, "locate": True,
+               "reference_layout": "kslice" if scaling == "blockwise" else "tile"}
         full, _ = execute(a, b, precision, scaling, abft_config=cfg)
         start, stop = shard_rows(m, world, rank)
         out, report = execute_sharded(a[start:stop], b, precision, scaling, cfg)
@@ -66,7 +69,7 @@ def _worker(rank, world, port, precision, results):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("precision", ["fp8", "nvfp4"])
+@pytest.mark.parametrize("precision", ["fp8", "nvfp4", "fp8_block"])
 def test_sharded_native_rows_bit_exact_and_verdict_global(precision):
     import torch.multiprocessing as mp
 
