@@ -246,7 +246,33 @@ def detection_campaign(prot, flips, seed):
     return {"flips": flips, "detected": detected, "detectable": detectable,
             "recall_all": detected / max(flips, 1), "recall_detectable": min(detected, detectable) / max(detectable, 1),
             "by_class": {k: {"detected": v[0], "flips": v[1]} for k, v in by_class.items()},
-            "clean_runs": clean_runs + 1, "false_positives": false_positives + int(bool(clean_packet[3][0]))}
+            "clean_runs": clean_runs + 1, "false_positives": false_positives + int(bool(clean_packet[3][0])),
+            "schedule": fault_schedule(prot, residual0, threshold0, seed)}
+
+
+def fault_schedule(prot, residual0, threshold0, seed, gemms=1000, rate=1e-3):
+    """The configurations' schedule: ``gemms`` protected GEMMs, each carrying
+    one seeded accumulator flip with probability ``rate`` (uniform row,
+    column and bit in [0, 32)); every GEMM's verdict is read back."""
+    g = torch.Generator().manual_seed(seed + 7919)
+    faulted = detected = detectable = false_positives = 0
+    for _ in range(gemms):
+        fault = (-1, -1, -1)
+        if float(torch.rand((), generator=g)) < rate:
+            fault = (int(torch.randint(0, prot.m, (1,), generator=g)), int(torch.randint(0, prot.n, (1,), generator=g)),
+                     int(torch.randint(0, 32, (1,), generator=g)))
+        _, packet = prot.step(fault)
+        flag = bool(packet[3][0])
+        if fault[0] < 0:
+            false_positives += flag
+            continue
+        faulted += 1
+        detected += flag
+        col = fault[1]
+        delta = (packet[1][:, col] - residual0[:, col]).abs()
+        detectable += bool((delta > threshold0[:, col]).any()) or bool(packet[3][1])
+    return {"gemms": gemms, "rate": rate, "faulted": faulted, "detected": detected, "detectable": detectable,
+            "false_positives": false_positives, "clean": gemms - faulted}
 
 
 # Qwen2.5-7B linear layers at T = 16384 tokens: (name, M, N, K).
@@ -507,6 +533,149 @@ def run_reference(args):
     }), flush=True)
 
 
+# Qwen2.5-0.5B shapes (configuration 5): layers, hidden, intermediate, heads, KV heads, vocab.
+QWEN05B = dict(num_hidden_layers=24, hidden_size=896, intermediate_size=4864, num_attention_heads=14,
+               num_key_value_heads=2, vocab_size=151936, rope_theta=1e6, rms_norm_eps=1e-6,
+               tie_word_embeddings=True, max_position_embeddings=32768)
+
+
+def build_train_model(device, seed, layers=None, shapes=None):
+    """Random-init Qwen2 causal LM (transformers config, fp32 master weights)
+    with every nn.Linear replaced by the protected NVFP4 linear."""
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    from sdc_b200.gemm.linear import install
+
+    cfg = dict(QWEN05B if shapes is None else shapes)
+    if layers is not None:
+        cfg["num_hidden_layers"] = layers
+    torch.manual_seed(seed)
+    model = Qwen2ForCausalLM(Qwen2Config(**cfg, attn_implementation="sdpa")).to(device)
+    abft = {"method": "classic", "implementation": "native", "reference_mode": "input_fused",
+            "reference_layout": "kslice", "on_error": "report", "recovery": "recompute", "locate": True,
+            "atol": 1e-3, "rtol": 1e-4}
+    install(model, "nvfp4", "block16", abft_config=abft, report_max_records=4096)
+    return model
+
+
+def train_reports(model):
+    """(layer, role, detected, located, fault_hit) per protected GEMM call recorded since the last reset."""
+    from sdc_b200.gemm.linear import ProtectedLinear
+
+    protection = next(m.protection for m in model.modules() if isinstance(m, ProtectedLinear))
+    rows = []
+    for report in protection.reports:
+        ctx = report.context
+        rows.append((ctx.get("layer"), ctx.get("role"), bool(report.detected), bool(report.located),
+                     int(report.fault_hit.reshape(-1)[0]) if report.fault_hit is not None else 0))
+    protection.reports.clear()
+    return protection, rows
+
+
+def run_train(args):
+    """Configuration 5: one data-parallel training step of a Qwen2.5-0.5B-shaped
+    model with NVFP4 ABFT on every linear (forward, dgrad, wgrad GEMMs),
+    synthetic uniform token ids, seeded Bernoulli accumulator faults per GEMM;
+    detections are counted per layer and role. Prints one JSON line."""
+    from sdc_b200.abft.config import parse_fault_config
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    result_fd = os.dup(1)
+    os.dup2(2, 1)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    model = build_train_model(device, 1234)
+    if dist is not None:
+        model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local])
+    optimizer = torch.optim.AdamW(model.parameters(), lr=1e-4)
+    batch, seq = args.micro_batch, args.seq_len
+    g = torch.Generator(device=device).manual_seed(100 + rank)
+    tokens = torch.randint(0, QWEN05B["vocab_size"], (batch, seq), device=device, generator=g)
+    schedule = torch.Generator().manual_seed(7 + rank)
+    stream = torch.cuda.current_stream(device)
+    core = model.module if dist is not None else model
+    gemms_per_step = None
+    per_layer = {}
+    faults = detected = 0
+
+    def step():
+        optimizer.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = model(input_ids=tokens, labels=tokens).loss
+        loss.backward()
+        optimizer.step()
+        return loss
+
+    def arm_faults(protection, first_call, count):
+        # One seeded Bernoulli(rate) draw per GEMM of the coming step; the
+        # session injects at most one fault per step (the first drawn).
+        hits = (torch.rand(count, generator=schedule) < args.fault_rate).nonzero().flatten().tolist()
+        if not hits:
+            protection.fault = parse_fault_config(None)
+            return None
+        call = first_call + hits[0] + 1
+        bit = int(torch.randint(0, 32, (1,), generator=schedule))
+        protection.fault = parse_fault_config({"location": "accumulator", "row": int(torch.randint(0, 128, (1,), generator=schedule)),
+                                               "col": int(torch.randint(0, 128, (1,), generator=schedule)),
+                                               "bit": bit, "call_index": call})
+        return call
+
+    losses = []
+    for i in range(args.warmup + args.steps):
+        protection, _ = train_reports(core)
+        if gemms_per_step is not None and i >= args.warmup:
+            faults += arm_faults(protection, protection.call_index, gemms_per_step) is not None
+        if i == args.warmup:
+            torch.cuda.synchronize()
+            if dist is not None:
+                dist.barrier()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+        first = protection.call_index
+        losses.append(step())
+        protection, rows = train_reports(core)
+        gemms_per_step = protection.call_index - first
+        if i >= args.warmup:
+            for layer, role, det, loc, hit in rows:
+                if det:
+                    key = f"{layer}:{role}"
+                    per_layer[key] = per_layer.get(key, 0) + 1
+                    detected += 1
+    end.record(stream)
+    end.synchronize()
+    elapsed = start.elapsed_time(end) / 1e3
+    if dist is not None:
+        t = torch.tensor([elapsed, faults, detected], device=device, dtype=torch.float64)
+        dist.all_reduce(t[:1], op=dist.ReduceOp.MAX)
+        dist.all_reduce(t[1:], op=dist.ReduceOp.SUM)
+        elapsed, faults, detected = float(t[0]), int(t[1]), int(t[2])
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    tokens_per_step = batch * seq * world
+    line = {"metric": "Qwen2.5-0.5B NVFP4 ABFT training step throughput", "value": tokens_per_step * args.steps / elapsed,
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "e2m1", "data": "synthetic",
+            "config": {"workload": "configuration 5: Qwen2.5-0.5B shapes (24 layers, hidden 896, intermediate 4864, "
+                                   "14/2 heads of dim 64, vocab 151936), random init, uniform token ids",
+                       "micro_batch": batch, "seq_len": seq, "parallelism": f"dp{world}",
+                       "protected_gemms_per_step": gemms_per_step, "fault_rate_per_gemm": args.fault_rate},
+            "faults_injected": faults, "detections": detected, "detections_per_layer_role": per_layer,
+            "loss_first": float(losses[0]), "loss_last": float(losses[-1])}
+    sys.stdout.flush()
+    os.write(result_fd, (json.dumps(line) + "\n").encode())
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
@@ -522,6 +691,11 @@ def main():
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-sweep", action="store_true", help="skip the Qwen2.5-7B linear-shape sweep")
     parser.add_argument("--sweep-steps", type=int, default=5)
+    parser.add_argument("--workload", choices=["gemm", "train"], default="gemm",
+                        help="gemm: the ABFT GEMM benchmark (default); train: configuration 5 training step")
+    parser.add_argument("--micro-batch", type=int, default=8)
+    parser.add_argument("--seq-len", type=int, default=2048)
+    parser.add_argument("--fault-rate", type=float, default=1e-4)
     parser.add_argument("--size", type=int, default=0,
                         help="override M=N=K of both workloads (profiling captures; not a bench line)")
     args = parser.parse_args()
@@ -529,6 +703,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "train":
+        run_train(args)
     else:
         run_ours(args)
 
