@@ -640,7 +640,7 @@ def run_train(args):
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             start.record(stream)
         first = protection.call_index
-        losses.append(step())
+        losses.append(step().detach())
         protection, rows = train_reports(core)
         gemms_per_step = protection.call_index - first
         if i >= args.warmup:
