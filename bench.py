@@ -458,7 +458,7 @@ def run_ours(args):
         }
         if rank == 0 and not args.no_detection:
             entry["detection"] = detection_campaign(prot, args.flips, seed)
-        if rank == 0 and not args.no_e2e:
+        if not args.no_e2e:  # every rank: its own shard end to end, time = max over ranks
             host_a = torch.randn(m, k, dtype=torch.bfloat16).pin_memory()
             host_b = torch.randn(n, k, dtype=torch.bfloat16).pin_memory()
             w = prot.weights
@@ -467,9 +467,13 @@ def run_ours(args):
             t0 = time.perf_counter()
             e_time = e2e_run(precision, host_a, host_b, device, w, prot.nonfinite, prot.atol, prot.rtol, e_steps,
                              stream)
-            entry["e2e"] = {"value": flops / e_time / 1e12, "unit": UNIT,
-                            "h2d_bytes_per_step": host_a.numel() * 2 + host_b.numel() * 2,
-                            "d2h_bytes_per_step": 5, "host_wall_s_per_step": (time.perf_counter() - t0) / e_steps,
+            if dist is not None:
+                t = torch.tensor([e_time], device=device)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                e_time = float(t.item())
+            entry["e2e"] = {"value": world * flops / e_time / 1e12, "unit": UNIT,
+                            "h2d_bytes_per_step": world * (host_a.numel() * 2 + host_b.numel() * 2),
+                            "d2h_bytes_per_step": world * 5, "host_wall_s_per_step": (time.perf_counter() - t0) / e_steps,
                             "pipeline": "step i+1's host-to-device copies overlap step i's compute (two buffer sets)"}
         results[precision] = entry
         del prot
@@ -499,7 +503,7 @@ def run_ours(args):
             line[name] = results[key]
     if sweep is not None:
         line["qwen2.5_7b_linears"] = sweep
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(args.cpu_sample_rows)
     sys.stdout.flush()
     os.write(result_fd, (json.dumps(line) + "\n").encode())
