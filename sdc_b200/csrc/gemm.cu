@@ -1,24 +1,35 @@
 // Persistent tcgen05 GEMMs for sm_100a with the ABFT checksums fused.
 //
-// One CTA per SM loops over 128 x 256 output tiles (one reference M-tile of
-// 128 rows per tile, so every observed-checksum partial comes from one CTA)
-// in a grouped raster order that keeps a band of A and B tiles resident in
-// L2. Warp roles:
+// One CTA (or CTA pair, cta_group::2, when M > 128) per SM loops over output
+// tiles of 128 rows per CTA (one reference M-tile, so every observed-checksum
+// partial comes from one CTA) in a grouped raster order that keeps a band of
+// A and the B tiles resident in L2. Tile widths: 256 columns (FP8, NVFP4),
+// 128 (block-scaled FP8). Warp roles:
 //   warp 0      TMA producer: 128-byte-swizzled K-major A/B stages (and the
-//               512-byte NVFP4 scale atoms) into a 4-stage ring.
-//   warp 1      allocates tensor memory; one thread issues tcgen05.mma
-//               (kind::f8f6f4 e4m3, or kind::mxf4nvf4.block16 with scales
-//               copied to TMEM by tcgen05.cp) into a 128x256 fp32
-//               accumulator. FP8 double-buffers the accumulator (2 x 256
-//               columns) so a tile's epilogue overlaps the next mainloop.
-//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, alpha * acc,
-//               optional accumulator bit flip, column checksums
-//               sum_rows w_c[row] * v (butterfly transpose-reduce across
-//               lanes, fixed-order sum across the four row quarters),
+//               512-byte NVFP4 scale atoms) into a ring; in pairs each CTA
+//               loads its A rows and half of the tile's B rows, completing
+//               on the leader's barrier.
+//   warp 1      allocates tensor memory; one thread (the leader's, in pairs)
+//               issues tcgen05.mma: kind::f8f6f4 e4m3, or kind::mxf4nvf4.block16
+//               with scales copied to TMEM by tcgen05.cp. FP8 double-buffers
+//               a 256-column fp32 accumulator so a tile's epilogue overlaps
+//               the next mainloop; NVFP4 has one (the scales take the rest of
+//               TMEM); block-scaled FP8 writes one partial per 128-wide K
+//               block into four rotating 128-column buffers.
+//   epilogue    FP8: warps 2-5, one per TMEM lane quarter, 32 columns at a
+//               time. NVFP4 and block-scaled FP8 ("wide" kinds): warps 4-11,
+//               two per lane quarter, each owning half of the tile's columns;
+//               NVFP4's warps load their whole half before the math, so the
+//               next tile's MMAs only wait for the loads; block-scaled FP8's
+//               warps first promote every partial into register-resident
+//               totals (total += fl(sa * sb) * partial). Then per 32-column
+//               chunk: alpha * acc, optional accumulator bit flip, column
+//               checksums sum_rows w_c[row] * v (butterfly transpose-reduce
+//               across lanes, fixed-order sum across the four row quarters),
 //               non-finite check of the converted output, output store.
-//   warps 6-9   (K-slice layout only) input-side prediction, independent of
-//               the MMA pipeline, in three phases separated by grid-wide
-//               barriers (the launch is cooperative, so every CTA is
+//   prediction  (K-slice layout only; warps 6-9, wide kinds 12-15)
+//               input-side prediction, independent of the MMA pipeline, in
+//               three phases separated by grid-wide barriers (every CTA is
 //               resident; each wait is bounded):
 //                 1. projection partials of A: each warp takes (64-wide K
 //                    chunk, 512-row band) items and writes
@@ -30,6 +41,8 @@
 //                    with B[n, k] and |q|, |B| (B rows read from L2).
 //               In total one extra pass over A and one over B, overlapped
 //               with the tensor-core mainloop.
+// Wide kinds run their roles on warpgroup boundaries and move registers with
+// setmaxnreg (warpgroup 0 down, the epilogue warpgroups up).
 // Epilogue semantics follow src/cutlass_gemm/csrc/abft/common/
 // sm120_epilogue.cuh:52-151 of the reference (inject after alpha, observe
 // before the output cast). Every wait is bounded (common.cuh).
