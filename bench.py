@@ -587,8 +587,11 @@ def build_train_model(device, seed, layers=None, shapes=None):
         cfg["num_hidden_layers"] = layers
     torch.manual_seed(seed)
     model = Qwen2ForCausalLM(Qwen2Config(**cfg, attn_implementation="sdpa")).to(device)
+    # Detect and log (the configuration asks for detections per layer); no
+    # recovery, so no GEMM waits on its own verdict and the host never syncs
+    # inside the step.
     abft = {"method": "classic", "implementation": "native", "reference_mode": "input_fused",
-            "reference_layout": "kslice", "on_error": "report", "recovery": "recompute", "locate": True,
+            "reference_layout": "kslice", "on_error": "report", "recovery": "none", "locate": True,
             "atol": 1e-3, "rtol": 1e-4}
     install(model, "nvfp4", "block16", abft_config=abft, report_max_records=4096)
     return model
