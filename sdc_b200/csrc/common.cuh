@@ -113,6 +113,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   return done != 0;
 }
 
+// Teardown wait for this thread's own asynchronous work (copies or MMAs in
+// flight) before the CTA releases its shared or tensor memory: ignores the
+// abort flag (an aborted CTA must still let its in-flight work land), gives
+// up after kDrainLimitNs. Returns whether the phase completed.
+constexpr uint64_t kDrainLimitNs = 100000000ull;
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t phase) {
+  const uint64_t start = global_ns();
+  while (!mbar_try_wait(bar, phase)) {
+    if (global_ns() - start > kDrainLimitNs) return false;
+  }
+  return true;
+}
+
 // Waits for `phase` of `bar` with a time limit. Returns false (and records
 // `code` in the watchdog word and in `*abort`) when the limit expires or when
 // another role of the CTA already aborted.

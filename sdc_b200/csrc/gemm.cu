@@ -270,7 +270,8 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* part_full = acc_empty + 2;
   uint64_t* part_empty = part_full + kPartBufs;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(part_empty + kPartBufs);
+  uint64_t* mma_done = part_empty + kPartBufs;  // the MMA thread's final commit (teardown)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(tmem_slot + 1);
   // Tiles whose epilogue has finished: paces the prediction warps.
   volatile uint32_t* tiles_done = tmem_slot + 2;
@@ -301,6 +302,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
       mbar_init(part_full + b, 1);
       mbar_init(part_empty + b, PAIR ? 2 * kAccWarps : kAccWarps);
     }
+    mbar_init(mma_done, 1);
     *abort_flag = 0;
     *tiles_done = 0;
     fence_barrier_init();
@@ -463,6 +465,14 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
           }
         }
       }
+      // Teardown: the last stages issued have landed (after a clean run the
+      // MMA already consumed them), so no copy writes shared memory after
+      // the CTA leaves. A pair's loads all complete on the leader's barriers.
+      if (leader) {
+        for (uint32_t j = kbg > static_cast<uint32_t>(kS) ? kbg - kS : 0u; j < kbg; ++j) {
+          mbar_drain(full + j % kS, (j / kS) & 1);
+        }
+      }
     }
   } else if (warp == 1 && BLK) {
     // ---------------- MMA issuer, block-scaled: one partial per K block ----------------
@@ -513,6 +523,13 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
           }
         }
       }
+      // Teardown: every MMA issued has completed before TMEM is released.
+      if constexpr (PAIR) {
+        tc_commit_pair(mma_done, 0x1);
+      } else {
+        tc_commit(mma_done);
+      }
+      mbar_drain(mma_done, 0);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -577,6 +594,13 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
           tc_commit(acc_full + b);
         }
       }
+      // Teardown: every MMA issued has completed before TMEM is released.
+      if constexpr (PAIR) {
+        tc_commit_pair(mma_done, 0x1);
+      } else {
+        tc_commit(mma_done);
+      }
+      mbar_drain(mma_done, 0);
     }
     }
   } else if (BLK && warp < kEpi0 + kAccWarps) {
