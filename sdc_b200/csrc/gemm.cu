@@ -90,8 +90,15 @@ __host__ __device__ constexpr int stage_bytes(Kind k, bool pair = false) {
 __host__ __device__ constexpr int num_stages(Kind k, bool pair) {
   return pair ? (k == Kind::kFp8 ? 6 : k == Kind::kFp8Block ? 8 : 5) : kStages;
 }
-__host__ __device__ constexpr int smem_bytes(Kind k, bool pair = false) {
-  return 1024 + num_stages(k, pair) * stage_bytes(k, pair) + kRedFloats * 4 + 256;
+// Checked e4m3 launches stage the prediction's B slices (tile rows x one
+// 64-byte K slice) in shared memory with their own TMA copies: a warp-wide
+// read there costs 4 shared-memory wavefronts where a global load of 32 rows
+// cost 32 L1 sectors (measured: most of the protected FP8 kernel's overhead).
+__host__ __device__ constexpr int pred_slice_bytes(Kind k, bool chk) {
+  return (chk && is_e4m3(k)) ? tile_n(k) * 64 : 0;
+}
+__host__ __device__ constexpr int smem_bytes(Kind k, bool pair = false, bool chk = false) {
+  return 1024 + num_stages(k, pair) * stage_bytes(k, pair) + kRedFloats * 4 + pred_slice_bytes(k, chk) + 512;
 }
 __host__ __device__ constexpr int num_acc(Kind k) { return k == Kind::kNvf4 ? 1 : 2; }
 // Warp roles. Tensorwise FP8: 0 TMA, 1 MMA, 2-5 epilogue, 6-9 prediction
@@ -264,14 +271,17 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   float* red = reinterpret_cast<float*>(smem + kS * kStageBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + kRedFloats);
+  // 1024-byte aligned: the stages and the reduction area are multiples of 1 KiB.
+  uint8_t* pred_slice = reinterpret_cast<uint8_t*>(red + kRedFloats);
+  uint64_t* full = reinterpret_cast<uint64_t*>(pred_slice + pred_slice_bytes(KIND, CHK));
   uint64_t* empty = full + kS;
   uint64_t* acc_full = empty + kS;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* part_full = acc_empty + 2;
   uint64_t* part_empty = part_full + kPartBufs;
   uint64_t* mma_done = part_empty + kPartBufs;  // the MMA thread's final commit (teardown)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* pred_full = mma_done + 1;            // the prediction's B slice has landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pred_full + 1);
   volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(tmem_slot + 1);
   // Tiles whose epilogue has finished: paces the prediction warps.
   volatile uint32_t* tiles_done = tmem_slot + 2;
@@ -303,6 +313,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
       mbar_init(part_empty + b, PAIR ? 2 * kAccWarps : kAccWarps);
     }
     mbar_init(mma_done, 1);
+    mbar_init(pred_full, 1);
     *abort_flag = 0;
     *tiles_done = 0;
     fence_barrier_init();
@@ -313,6 +324,8 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
     if constexpr (KIND == Kind::kNvf4) {
       tma_prefetch(&tm_sfa);
       tma_prefetch(&tm_sfb);
+    } else if constexpr (CHK) {
+      tma_prefetch(&tm_sfb);  // e4m3: the prediction's B-slice map
     }
   }
   if (warp == 1) {
@@ -935,8 +948,14 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
       // ---- phase 3: predictions of this CTA's tiles ----
       const uint32_t last = my_tiles > 0 ? my_tiles - 1 : 0u;
       uint32_t jt = 0;
-      for (int t = work_first; t < p.num_work && !*abort_flag; t += work_step, ++jt) {
-        if (!pace(half + jt * (last > half ? last - half : 0u) / (my_tiles > 0 ? my_tiles : 1u))) break;
+      uint32_t slices_staged = 0;  // B slices copied to shared memory (e4m3)
+      bool copy_in_flight = false;  // thread ct == 0: a slice copy not yet seen landing
+      bool stopped = false;
+      // Every decision to leave is taken by all 128 prediction threads
+      // together (named_barrier_or), since the slice loop synchronises them.
+      for (int t = work_first; t < p.num_work; t += work_step, ++jt) {
+        const bool paced = pace(half + jt * (last > half ? last - half : 0u) / (my_tiles > 0 ? my_tiles : 1u));
+        if (named_barrier_or(2, 128, !paced || *abort_flag != 0)) break;
         int mt, nt;
         work_coords<PAIR>(t, p, rank, mt, nt);
         if (mt >= p.tiles_m) continue;
@@ -950,16 +969,41 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
           constexpr int kChunksPerSlice = is_e4m3(KIND) ? 4 : 2;  // 16-byte chunks per row
           uint4 raw[kRowsPerThread][kChunksPerSlice];
           uint32_t sfw[kRowsPerThread];
+          bool landed = true;
+          if constexpr (is_e4m3(KIND)) {
+            // One thread copies the slice (rows past N and K past the row
+            // read as zeros); every prediction thread waits for it. The
+            // previous slice's reads ended at the barrier below.
+            if (ct == 0) {
+              fence_proxy_async_smem();
+              mbar_arrive_expect_tx(pred_full, static_cast<uint32_t>(pred_slice_bytes(KIND, CHK)));
+              tma_load_2d(pred_slice, &tm_sfb, pred_full, k0, nt * kTN);
+              copy_in_flight = true;
+            }
+            landed = mbar_wait(pred_full, slices_staged & 1u, kWaitProjection, abort_flag, p.watchdog);
+            if (ct == 0 && landed) copy_in_flight = false;
+            ++slices_staged;
+          }
 #pragma unroll
           for (int h = 0; h < kRowsPerThread; ++h) {
             const int64_t r = static_cast<int64_t>(nt) * kTN + ct + 128 * h;
             const bool row_in = r < p.n;
-            const uint8_t* src = p.b + r * row_bytes + (is_e4m3(KIND) ? k0 : k0 / 2);
+            if constexpr (is_e4m3(KIND)) {
+              // 64-byte swizzle: chunk c of slice row q sits at q*64 + ((c ^ ((q >> 1) & 3)) << 4).
+              const int q = ct + 128 * h;
 #pragma unroll
-            for (int ch = 0; ch < kChunksPerSlice; ++ch) {
-              const int byte = (is_e4m3(KIND) ? k0 : k0 / 2) + ch * 16;
-              raw[h][ch] = (row_in && byte < row_bytes) ? __ldg(reinterpret_cast<const uint4*>(src) + ch)
-                                                         : make_uint4(0, 0, 0, 0);
+              for (int ch = 0; ch < kChunksPerSlice; ++ch) {
+                raw[h][ch] = landed ? *reinterpret_cast<const uint4*>(pred_slice + q * 64 + ((ch ^ ((q >> 1) & 3)) << 4))
+                                    : make_uint4(0, 0, 0, 0);
+              }
+            } else {
+              const uint8_t* src = p.b + r * row_bytes + k0 / 2;
+#pragma unroll
+              for (int ch = 0; ch < kChunksPerSlice; ++ch) {
+                const int byte = k0 / 2 + ch * 16;
+                raw[h][ch] = (row_in && byte < row_bytes) ? __ldg(reinterpret_cast<const uint4*>(src) + ch)
+                                                           : make_uint4(0, 0, 0, 0);
+              }
             }
             if constexpr (KIND == Kind::kNvf4) {
               const int64_t off = ((r >> 7) * k_atoms + (k0 >> 6)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4;
@@ -967,6 +1011,13 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
             } else if constexpr (BLK) {
               // The scale of this row's 128 x 128 block holding the slice.
               sfw[h] = row_in ? __float_as_uint(__ldg(p.sb + (r >> 7) * p.k_blocks + (k0 >> 7))) : 0u;
+            }
+          }
+          if constexpr (is_e4m3(KIND)) {
+            // The slice is in registers (or its copy failed everywhere).
+            if (named_barrier_or(2, 128, !landed)) {
+              stopped = true;
+              break;
             }
           }
           // q_full is zero-padded to a multiple of 64 K, so loads need no guard;
@@ -1023,6 +1074,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
             }
           }
         }
+        if (stopped) break;
 #pragma unroll
         for (int h = 0; h < kRowsPerThread; ++h) {
           const int col = nt * kTN + ct + 128 * h;
@@ -1037,6 +1089,9 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
           }
         }
       }
+      // Teardown: a slice copy that was never seen landing lands before the
+      // CTA releases its shared memory.
+      if (copy_in_flight) mbar_drain(pred_full, (slices_staged - 1u) & 1u);
     }
   }
 
@@ -1096,6 +1151,16 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   } else {
     tsa = ta;
     tsb = tb;
+    if constexpr (CHK) {
+      // The prediction's B slices: the tile's rows x 64 bytes of K, 64-byte
+      // swizzle (conflict-free 16-byte reads of 8 consecutive rows).
+      const uint64_t dims[2] = {static_cast<uint64_t>(k_bytes), static_cast<uint64_t>(g.n)};
+      const uint64_t strides[1] = {static_cast<uint64_t>(k_bytes)};
+      const uint32_t box[2] = {static_cast<uint32_t>(kSliceK), static_cast<uint32_t>(tile_n(KIND))};
+      int rc = encode_tensor_map(&tsb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(g.b), dims, strides,
+                                 box, CU_TENSOR_MAP_SWIZZLE_64B);
+      if (rc != SDC_OK) return rc;
+    }
   }
   Params p{};
   p.m = static_cast<int32_t>(g.m);
@@ -1134,7 +1199,8 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   p.watchdog = watchdog_ptr();
   if (p.watchdog == nullptr) return fail(SDC_ERR_CUDA, "watchdog symbol unavailable");
   auto kernel = gemm_kernel<KIND, C, BF16OUT, CHK, PAIR>;
-  constexpr int smem = smem_bytes(KIND, PAIR);
+  constexpr int smem = smem_bytes(KIND, PAIR, CHK);
+  static_assert(smem <= 232448, "shared memory beyond the 227 KiB per-CTA limit");
   cudaLaunchConfig_t config{};
   config.blockDim = dim3(num_threads(CHK, is_wide(KIND)));
   config.dynamicSmemBytes = smem;
