@@ -296,11 +296,13 @@ def qwen_sweep(args, device, stream, rank, world, dist):
         for name, m, n, k in QWEN_SHAPES:
             start, stop = shard_rows(m, world, rank)
             prot = Protected(precision, stop - start, n, k, device, 7 + rank, b_std=0.02)
-            t = torch.tensor([timed(prot.step, args.sweep_steps, 3, stream),
-                              timed(prot.unprotected, args.sweep_steps, 3, stream)], device=device)
+            # Paired, alternating blocks (as for the headline), so that both
+            # arms see the same clocks under the power cap.
+            step_t, plain_t = paired_overhead(prot, 3 * args.sweep_steps, rounds=3)
+            t = torch.tensor([step_t, plain_t], device=device)
             if dist is not None:
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            t_prot, t_plain = (float(v) / args.sweep_steps for v in t.tolist())
+            t_prot, t_plain = (float(v) for v in t.tolist())
             flops = 2.0 * m * n * k
             rows[name] = {"m": m, "n": n, "k": k, "tflops": flops / t_prot / 1e12,
                           "unprotected_tflops": flops / t_plain / 1e12,
@@ -313,7 +315,8 @@ def qwen_sweep(args, device, stream, rank, world, dist):
         out[precision] = {"layers": rows, "tflops": total_flops / total_prot / 1e12,
                           "overhead_pct": 100.0 * (total_prot / total_plain - 1.0)}
     out["config"] = (f"T=16384 tokens, activations N(0,1), weights N(0,0.02), bf16 before quantisation; "
-                     f"M sharded over {world} rank(s); {args.sweep_steps} timed steps per shape")
+                     f"M sharded over {world} rank(s); 3 alternating blocks of {args.sweep_steps} protected and "
+                     f"{args.sweep_steps} unprotected steps per shape")
     return out
 
 
@@ -729,7 +732,7 @@ def main():
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-sweep", action="store_true", help="skip the Qwen2.5-7B linear-shape sweep")
-    parser.add_argument("--sweep-steps", type=int, default=5)
+    parser.add_argument("--sweep-steps", type=int, default=10)
     parser.add_argument("--workload", choices=["gemm", "train"], default="gemm",
                         help="gemm: the ABFT GEMM benchmark (default); train: configuration 5 training step")
     parser.add_argument("--micro-batch", type=int, default=8)
