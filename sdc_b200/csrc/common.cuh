@@ -566,4 +566,12 @@ __device__ __forceinline__ uint16_t float_to_bf16_bits(float f) {
   return out;
 }
 
+// Two floats to bf16 (round to nearest even) in one instruction: lo in bits
+// 0-15, hi in bits 16-31.
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+  uint32_t out;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(out) : "f"(hi), "f"(lo));
+  return out;
+}
+
 }  // namespace sdc

@@ -356,16 +356,50 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
       }
       *p.hit = 1;
     }
-    if (C > 0 && p.nonfinite != nullptr && row_ok) {
-      // Non-finite as stored: fp32 from 0x7F800000 up; the round-to-nearest
-      // bf16 cast overflows from |x| >= 0x7F7F8000 (the tie above the largest
-      // finite bf16 rounds to the even pattern, +inf).
+    if constexpr (BF16OUT) {
+      // The output as stored first: one round-to-nearest conversion per
+      // column pair. Its words also give the non-finite test: a bf16 exponent
+      // of all ones is inf or NaN as stored (the cast overflows from
+      // |x| >= 0x7F7F8000, the tie above the largest finite bf16 rounding to
+      // the even pattern, +inf); adding 0x80 to an all-ones exponent field
+      // sets the half's top bit, and no other exponent does.
+      uint32_t packed[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) packed[j] = bf16x2_bits(v[2 * j], v[2 * j + 1]);
+      const bool full = c0 + 32 <= p.n;
+      if (C > 0 && p.nonfinite != nullptr && row_ok) {
+        uint32_t flag = 0;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const uint32_t keep = full ? 0xFFFFFFFFu
+                                     : ((c0 + 2 * j < p.n ? 0x0000FFFFu : 0u) | (c0 + 2 * j + 1 < p.n ? 0xFFFF0000u : 0u));
+          flag |= ((packed[j] & keep) & 0x7F807F80u) + 0x00800080u;
+        }
+        if (flag & 0x80008000u) nonfinite = true;
+      }
+      if (row_ok) {
+        uint16_t* d = static_cast<uint16_t*>(p.d) + static_cast<int64_t>(row) * p.n;
+        if (full && (p.n & 7) == 0) {
+          uint4* dst = reinterpret_cast<uint4*>(d + c0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (c0 + j < p.n) d[c0 + j] = static_cast<uint16_t>((j & 1) ? packed[j >> 1] >> 16 : packed[j >> 1]);
+          }
+        }
+      }
+    } else if (C > 0 && p.nonfinite != nullptr && row_ok) {
+      // Non-finite as stored: fp32 from 0x7F800000 up.
       uint32_t largest = 0;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         if (c0 + j < p.n) largest = max(largest, __float_as_uint(v[j]) & 0x7FFFFFFFu);
       }
-      if (largest >= (BF16OUT ? 0x7F7F8000u : 0x7F800000u)) nonfinite = true;
+      if (largest >= 0x7F800000u) nonfinite = true;
     }
     if constexpr (C > 0) {
 #pragma unroll
@@ -376,28 +410,8 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
         red[((chunk * 4 + q) * C + c) * 32 + lane] = transpose_reduce32(x, lane);
       }
     }
-    if (row_ok) {
-      if constexpr (BF16OUT) {
-        uint16_t* d = static_cast<uint16_t*>(p.d) + static_cast<int64_t>(row) * p.n;
-        if (c0 + 32 <= p.n && (p.n & 7) == 0) {
-          uint32_t packed[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            packed[j] = static_cast<uint32_t>(float_to_bf16_bits(v[2 * j])) |
-                        (static_cast<uint32_t>(float_to_bf16_bits(v[2 * j + 1])) << 16);
-          }
-          uint4* dst = reinterpret_cast<uint4*>(d + c0);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (c0 + j < p.n) d[c0 + j] = float_to_bf16_bits(v[j]);
-          }
-        }
-      } else {
+    if constexpr (!BF16OUT) {
+      if (row_ok) {
         float* d = static_cast<float*>(p.d);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {

@@ -173,6 +173,30 @@ def test_nonfinite_injection_is_flagged():
     assert not torch.isfinite(out[128, 128].float())
 
 
+@pytest.mark.parametrize("before, stored_inf", [(0x3F7F8000, True), (0x3F7F7FFF, False)])
+def test_nonfinite_at_the_bf16_overflow_boundary(before, stored_inf):
+    """An output whose fp32 value is finite but rounds to bf16 inf is flagged;
+    the largest value that rounds to a finite bf16 is not. Flipping bit 30 of
+    0x3F7F8000 gives 0x7F7F8000, the tie above the largest finite bf16, which
+    rounds to the even pattern, +inf."""
+    m, n, k = 136, 144, 128
+    a = torch.zeros(m, k, device=DEV)
+    b = torch.zeros(n, k, device=DEV)
+    a[:, 0] = 1
+    b[:, 0] = 1
+    value = torch.tensor([before], dtype=torch.int32).view(torch.float32).item()
+    sa = torch.full((m, 1), value, device=DEV)
+    sb = torch.ones(2, 1, device=DEV)
+    args = (a.to(torch.float8_e4m3fn), b.to(torch.float8_e4m3fn), sa, sb)
+    nonfinite = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out, _, hit = ops.abft_fp8_block_mm(*args, torch.ones(2, m, device=DEV), 128, 128, 30, 0, nonfinite)
+    assert hit.item() == 1
+    assert nonfinite.item() == int(stored_inf)
+    assert torch.isfinite(out[128, 128].float()).item() != stored_inf
+    out[128, 128] = 0
+    assert torch.isfinite(out.float()).all() and nonfinite.item() == int(stored_inf)
+
+
 @pytest.mark.parametrize("bad", ["k", "scale_shape", "scale_dtype"])
 def test_invalid_block_operands_rejected(bad):
     a, b, sa, sb = _block_case(136, 144, 256, dyadic=True)
