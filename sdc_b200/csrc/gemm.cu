@@ -369,11 +369,15 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
       const bool full = c0 + 32 <= p.n;
       if (C > 0 && p.nonfinite != nullptr && row_ok) {
         uint32_t flag = 0;
+        if (full) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const uint32_t keep = full ? 0xFFFFFFFFu
-                                     : ((c0 + 2 * j < p.n ? 0x0000FFFFu : 0u) | (c0 + 2 * j + 1 < p.n ? 0xFFFF0000u : 0u));
-          flag |= ((packed[j] & keep) & 0x7F807F80u) + 0x00800080u;
+          for (int j = 0; j < 16; ++j) flag |= (packed[j] & 0x7F807F80u) + 0x00800080u;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const uint32_t keep = (c0 + 2 * j < p.n ? 0x0000FFFFu : 0u) | (c0 + 2 * j + 1 < p.n ? 0xFFFF0000u : 0u);
+            flag |= ((packed[j] & keep) & 0x7F807F80u) + 0x00800080u;
+          }
         }
         if (flag & 0x80008000u) nonfinite = true;
       }
