@@ -194,10 +194,13 @@ __device__ __forceinline__ void work_coords(int w, const Params& p, uint32_t ran
   }
 }
 
-// Lane j of the warp returns sum over the 32 lanes of x[j] (x is consumed).
-__device__ __forceinline__ float transpose_reduce32(float (&x)[32], int lane) {
+// Butterfly transpose-reduce over the lane bits below N: lane j returns the
+// sum, over the lanes that differ from it only in those bits, of x[j % N]
+// (x is consumed). With N = 32 that is the sum over the warp of x[j].
+template <int N>
+__device__ __forceinline__ float transpose_reduce(float (&x)[N], int lane) {
 #pragma unroll
-  for (int width = 16; width >= 1; width >>= 1) {
+  for (int width = N / 2; width >= 1; width >>= 1) {
     const bool upper = (lane & width) != 0;
 #pragma unroll
     for (int i = 0; i < width; ++i) {
@@ -406,13 +409,21 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
       if (largest >= 0x7F800000u) nonfinite = true;
     }
     if constexpr (C > 0) {
+      // Column sums of w_c[row] * v over the warp's 32 rows. The first
+      // butterfly level (lane bit 16) runs for all channels at once: the
+      // selects of v are shared, and the kept half's weight fuses into the
+      // add. Lane j ends with column j.
+      const bool upper = (lane & 16) != 0;
+      float x[C][16];
 #pragma unroll
-      for (int c = 0; c < C; ++c) {
-        float x[32];
+      for (int i = 0; i < 16; ++i) {
+        const float sent = upper ? v[i] : v[i + 16];
+        const float kept = upper ? v[i + 16] : v[i];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) x[j] = w[c] * v[j];
-        red[((chunk * 4 + q) * C + c) * 32 + lane] = transpose_reduce32(x, lane);
+        for (int c = 0; c < C; ++c) x[c][i] = fmaf(w[c], kept, __shfl_xor_sync(0xffffffffu, w[c] * sent, 16));
       }
+#pragma unroll
+      for (int c = 0; c < C; ++c) red[((chunk * 4 + q) * C + c) * 32 + lane] = transpose_reduce(x[c], lane);
     }
     if constexpr (!BF16OUT) {
       if (row_ok) {
