@@ -198,9 +198,10 @@ def profiled_traffic(name):
     return total
 
 
-# Kernels this library launches per protected step: the GEMM (projection and
-# K-slice prediction fused into it) + finalize_columns + finalize_flags.
-LAUNCHES_PER_STEP = 3
+# Kernels this library launches per protected step: the K-slice projection
+# of A (kslice_project + kslice_band_sum), the GEMM (prediction fused into
+# it), finalize_columns + finalize_flags.
+LAUNCHES_PER_STEP = 5
 
 
 def timed(fn, steps, warmup, stream):

@@ -52,9 +52,10 @@ enum sdc_reference_layout {
   /* predicted/magnitude[c, t, col] = contribution of the 64-wide K slices s
    * with s % Tm == t, summed over ALL rows. The sum over t equals the TILE
    * layout's sum over t (up to fp32 rounding); finalize is unchanged. The
-   * projection w^T A and the propagation run inside the GEMM launch (one
-   * extra read of A and of B, overlapped with the tensor-core mainloop)
-   * instead of ~C/32 of the GEMM on CUDA cores. */
+   * projection w^T A is one streaming pass over A before the GEMM, and the
+   * propagation runs inside the GEMM launch (one extra read of B, overlapped
+   * with the tensor-core mainloop) instead of ~C/32 of the GEMM on CUDA
+   * cores. */
   SDC_LAYOUT_KSLICE = 1
 };
 
@@ -67,6 +68,13 @@ int sdc_device_check(int device);
  * kernel gave up a bounded wait since the last call, otherwise the code of the
  * first wait that expired. Synchronises `stream`. */
 int sdc_read_device_error(sdc_stream_t stream, int32_t* code);
+/* Test hook (no counterpart in the reference): wait_limit_ns != 0 replaces the
+ * 2 s limit of every bounded wait in later GEMM launches; pace_extra > 0 is
+ * added to the prediction warps' pacing targets, which makes their wait
+ * unreachable so that it expires. (0, 0) restores normal operation. Lets a
+ * test check that an expired wait is reported in-band (hit bit 1, detected)
+ * without hanging or faulting the GPU. */
+int sdc_test_set_watchdog(uint64_t wait_limit_ns, int32_t pace_extra);
 
 /* ---- quantisation (src/cutlass_gemm/quantization.py:99-162) ------------ */
 
@@ -133,7 +141,10 @@ int sdc_nvfp4_gemm(const uint8_t* a_packed, const uint8_t* b_packed,
  *   nonfinite  nullable int32[1]; zeroed, then set to 1 when a converted
  *              in-bounds output element is not finite.
  *   observed   fp32 [C,Tm,Np]: sum over the tile's rows of w_c[row]*value.
- *   hit        int32[1]: 1 when the fault was applied.
+ *   hit        int32[1]: bit 0 set when the fault was applied; bit 1 set when
+ *              the launch gave up a bounded wait (its outputs and partials
+ *              are incomplete; finalize then reports detected and
+ *              nonfinite, and `nonfinite`, when given, is set to 1).
  * Input-fused variants also write predicted = alpha * w^T A B and
  * magnitude = |alpha| * |w|^T |A| |B| partials in `reference_layout`.
  */

@@ -66,6 +66,32 @@ static float value_at(int kind, const uint8_t* x, const uint8_t* sf, int64_t row
   return code * decode_e4m3(sf[sf_offset(row, kk / 16, k)]);
 }
 
+/* All k values of one operand row (same values as value_at, one row at a time). */
+static void decode_row(int kind, const uint8_t* x, const uint8_t* sf, int64_t row, int64_t k, float* out) {
+  static float lut[256];
+  static int lut_ready = 0;
+  if (!lut_ready) {
+    for (int i = 0; i < 256; ++i) lut[i] = decode_e4m3((uint8_t)i);
+    lut_ready = 1;
+  }
+  if (kind == 0) {
+    const uint8_t* r = x + row * k;
+    for (int64_t kk = 0; kk < k; ++kk) out[kk] = lut[r[kk]];
+  } else if (kind >= 2) {
+    const float* scales = (const float*)sf;
+    const int64_t srow = kind == 2 ? row : row / 128;
+    const uint8_t* r = x + row * k;
+    for (int64_t kk = 0; kk < k; ++kk) out[kk] = lut[r[kk]] * scales[srow * (k / 128) + kk / 128];
+  } else {
+    const uint8_t* r = x + row * (k / 2);
+    for (int64_t kk = 0; kk < k; ++kk) {
+      const uint8_t byte = r[kk / 2];
+      const float code = decode_e2m1((kk & 1) ? (byte >> 4) : (byte & 15));
+      out[kk] = code * lut[sf[sf_offset(row, kk / 16, k)]];
+    }
+  }
+}
+
 /* q layout: [(c*2 + h) * tiles * k + t * k + kk]. */
 static void encode_tiles(int kind, const uint8_t* a, const uint8_t* sfa, int64_t m, int64_t k,
                          const float* w, int channels, float* q) {
@@ -122,51 +148,62 @@ int oracle_kslice_reference(int kind, const uint8_t* a, const uint8_t* sfa, cons
                             int channels, float alpha, float* pred, float* mag, int64_t padded_n) {
   const int64_t tiles = (m + 127) / 128;
   const int64_t slices = (k + 63) / 64;
-  float* qf = (float*)malloc(sizeof(float) * channels * 2 * k);
-  if (!qf) return 1;
-  /* q over all rows in the GEMM prediction warps' order: bands of 512 rows;
-   * in a band, 8 row lanes l each run an fma chain over rows
-   * band_start + l, + 8, ... (ascending), combined as
-   * ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)); q = ((band_0 + band_1)
-   * + ...) + band_last. */
+  float* qf = (float*)calloc((size_t)channels * 2 * k, sizeof(float));
+  float* lanes = (float*)malloc(sizeof(float) * channels * 2 * 8 * k); /* [c][h][lane][k] */
+  float* row_v = (float*)malloc(sizeof(float) * k);
+  if (!qf || !lanes || !row_v) {
+    free(qf);
+    free(lanes);
+    free(row_v);
+    return 1;
+  }
+  /* q over all rows in the projection kernel's order: bands of 512 rows; in a
+   * band, 8 row lanes l each run an fma chain over rows band_start + l, + 8,
+   * ... (ascending), combined as ((p0 + p1) + (p2 + p3)) + ((p4 + p5) +
+   * (p6 + p7)); q = ((band_0 + band_1) + ...) + band_last. Rows are walked in
+   * order (each fma chain keeps its own accumulator), which is the same
+   * arithmetic as walking each chain separately. */
   const int64_t bands = (m + 511) / 512;
-  for (int c = 0; c < channels; ++c) {
-    for (int64_t kk = 0; kk < k; ++kk) {
-      float q[2] = {0.f, 0.f};
-      for (int64_t b = 0; b < bands; ++b) {
-        const int64_t begin = b * 512, end = begin + 512 < m ? begin + 512 : m;
-        float lanes[2][8];
-        for (int l = 0; l < 8; ++l) {
-          float e = 0.f, g = 0.f;
-          for (int64_t row = begin + l; row < end; row += 8) {
-            const float v = value_at(kind, a, sfa, row, kk, k);
-            const float wv = w[c * m + row];
-            e = fmaf(wv, v, e);
-            g = fmaf(fabsf(wv), fabsf(v), g);
-          }
-          lanes[0][l] = e;
-          lanes[1][l] = g;
-        }
-        for (int h = 0; h < 2; ++h) {
-          const float* p = lanes[h];
-          const float band = ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
-          q[h] = b == 0 ? band : q[h] + band;
+  for (int64_t bnd = 0; bnd < bands; ++bnd) {
+    const int64_t begin = bnd * 512, end = begin + 512 < m ? begin + 512 : m;
+    memset(lanes, 0, sizeof(float) * channels * 2 * 8 * k);
+    for (int64_t row = begin; row < end; ++row) {
+      const int l = (int)((row - begin) & 7);
+      decode_row(kind, a, sfa, row, k, row_v);
+      for (int c = 0; c < channels; ++c) {
+        const float wv = w[c * m + row], wa = fabsf(wv);
+        float* e = lanes + ((c * 2 + 0) * 8 + l) * k;
+        float* g = lanes + ((c * 2 + 1) * 8 + l) * k;
+        for (int64_t kk = 0; kk < k; ++kk) {
+          e[kk] = fmaf(wv, row_v[kk], e[kk]);
+          g[kk] = fmaf(wa, fabsf(row_v[kk]), g[kk]);
         }
       }
-      qf[(c * 2 + 0) * k + kk] = q[0];
-      qf[(c * 2 + 1) * k + kk] = q[1];
+    }
+    for (int c = 0; c < channels; ++c) {
+      for (int h = 0; h < 2; ++h) {
+        const float* p = lanes + (c * 2 + h) * 8 * k;
+        float* q = qf + (c * 2 + h) * k;
+        for (int64_t kk = 0; kk < k; ++kk) {
+          const float band = ((p[0 * k + kk] + p[1 * k + kk]) + (p[2 * k + kk] + p[3 * k + kk])) +
+                             ((p[4 * k + kk] + p[5 * k + kk]) + (p[6 * k + kk] + p[7 * k + kk]));
+          q[kk] = bnd == 0 ? band : q[kk] + band;
+        }
+      }
     }
   }
-  for (int c = 0; c < channels; ++c) {
-    for (int64_t slot = 0; slot < tiles; ++slot) {
-      for (int64_t col = 0; col < padded_n; ++col) {
+  for (int64_t col = 0; col < padded_n; ++col) {
+    if (col < n) decode_row(kind == 2 ? 3 : kind, b, sfb, col, k, row_v);
+    for (int c = 0; c < channels; ++c) {
+      const float* qe = qf + (c * 2 + 0) * k;
+      const float* qa = qf + (c * 2 + 1) * k;
+      for (int64_t slot = 0; slot < tiles; ++slot) {
         float r = 0.f, s = 0.f;
         if (col < n) {
           for (int64_t sl = slot; sl < slices; sl += tiles) {
             for (int64_t kk = sl * 64; kk < sl * 64 + 64 && kk < k; ++kk) {
-              const float v = value_at(kind == 2 ? 3 : kind, b, sfb, col, kk, k);
-              r = fmaf(qf[(c * 2 + 0) * k + kk], v, r);
-              s = fmaf(qf[(c * 2 + 1) * k + kk], fabsf(v), s);
+              r = fmaf(qe[kk], row_v[kk], r);
+              s = fmaf(qa[kk], fabsf(row_v[kk]), s);
             }
           }
         }
@@ -176,6 +213,109 @@ int oracle_kslice_reference(int kind, const uint8_t* a, const uint8_t* sfa, cons
     }
   }
   free(qf);
+  free(lanes);
+  free(row_v);
+  return 0;
+}
+
+/* TILE layout for a subset of M-tiles: pred/mag [C][ntiles][padded_n], entry
+ * (c, i, col) equal to oracle_tile_reference's (c, tiles[i], col). Makes the
+ * per-tile parity check affordable at the benchmark sizes. */
+int oracle_tile_reference_subset(int kind, const uint8_t* a, const uint8_t* sfa, const uint8_t* b,
+                                 const uint8_t* sfb, int64_t m, int64_t n, int64_t k, const float* w,
+                                 int channels, float alpha, const int64_t* tiles, int64_t ntiles, float* pred,
+                                 float* mag, int64_t padded_n) {
+  float* q = (float*)calloc((size_t)ntiles * channels * 2 * k, sizeof(float)); /* [i][c][h][k] */
+  float* bv = (float*)malloc(sizeof(float) * k);
+  if (!q || !bv) {
+    free(q);
+    free(bv);
+    return 1;
+  }
+  for (int64_t i = 0; i < ntiles; ++i) {
+    const int64_t t = tiles[i];
+    for (int64_t r = 0; r < 128 && t * 128 + r < m; ++r) {
+      const int64_t row = t * 128 + r;
+      decode_row(kind, a, sfa, row, k, bv);
+      for (int c = 0; c < channels; ++c) {
+        const float wt = w[c * m + row], wa = fabsf(wt);
+        float* qe = q + ((i * channels + c) * 2 + 0) * k;
+        float* qa = q + ((i * channels + c) * 2 + 1) * k;
+        for (int64_t kk = 0; kk < k; ++kk) {
+          qe[kk] = fmaf(wt, bv[kk], qe[kk]);
+          qa[kk] = fmaf(wa, fabsf(bv[kk]), qa[kk]);
+        }
+      }
+    }
+  }
+  for (int64_t col = 0; col < padded_n; ++col) {
+    if (col < n) decode_row(kind == 2 ? 3 : kind, b, sfb, col, k, bv);
+    for (int64_t i = 0; i < ntiles; ++i) {
+      for (int c = 0; c < channels; ++c) {
+        const float* qe = q + ((i * channels + c) * 2 + 0) * k;
+        const float* qa = q + ((i * channels + c) * 2 + 1) * k;
+        float r = 0.f, s = 0.f;
+        if (col < n) {
+          for (int64_t kk = 0; kk < k; ++kk) {
+            r = fmaf(qe[kk], bv[kk], r);
+            s = fmaf(qa[kk], fabsf(bv[kk]), s);
+          }
+        }
+        pred[(c * ntiles + i) * padded_n + col] = alpha * r;
+        mag[(c * ntiles + i) * padded_n + col] = fabsf(alpha) * s;
+      }
+    }
+  }
+  free(q);
+  free(bv);
+  return 0;
+}
+
+/* Observed column checksums in the sm_100a epilogue's reduction order (an
+ * sdc_b200 extension; the reference's in-tile order, CUTLASS's
+ * Sm90RowReduction, is unpinned). v: the fp32 values the epilogue checksums
+ * (alpha * accumulator, after the fault XOR), row-major [m, n]. Per 128-row
+ * tile, 32-row quarter q (rows 32q..32q+31, lane L = row % 32) and 32-column
+ * chunk (columns 32j..32j+31, column index i within it):
+ *   level 16: lane L with bit 4 equal to bit 4 of i holds
+ *             fmaf(w[L], v[L][i], fl(w[L^16] * v[L^16][i]));
+ *   levels 8, 4, 2, 1: lane L keeps the columns whose bit matches its own and
+ *             adds the partner lane's (L ^ width) value: fl(own + partner);
+ *   lane i ends with column i's quarter sum S_q;
+ * observed[c][t][col] = (((0 + S_0) + S_1) + S_2) + S_3, columns < padded_n
+ * (columns >= n contribute zeros; rows >= m have weight 0). */
+int oracle_observed_epilogue(const float* v, int64_t m, int64_t n, const float* w, int channels,
+                             float* observed, int64_t padded_n) {
+  const int64_t tiles = (m + 127) / 128;
+  for (int c = 0; c < channels; ++c) {
+    for (int64_t t = 0; t < tiles; ++t) {
+      for (int64_t col = 0; col < padded_n; ++col) {
+        const int i = (int)(col & 31);
+        float sum = 0.f;
+        for (int q = 0; q < 4; ++q) {
+          float lane_val[32];
+          float wl[32], vl[32];
+          for (int L = 0; L < 32; ++L) {
+            const int64_t row = t * 128 + q * 32 + L;
+            const int in = row < m && col < n;
+            wl[L] = row < m ? w[c * m + row] : 0.f;
+            vl[L] = in ? v[row * n + col] : 0.f;
+          }
+          for (int L = 0; L < 32; ++L) {
+            const float partner = wl[L ^ 16] * vl[L ^ 16];
+            lane_val[L] = fmaf(wl[L], vl[L], partner);
+          }
+          for (int width = 8; width >= 1; width >>= 1) {
+            float next[32];
+            for (int L = 0; L < 32; ++L) next[L] = lane_val[L] + lane_val[L ^ width];
+            memcpy(lane_val, next, sizeof(next));
+          }
+          sum = sum + lane_val[i];
+        }
+        observed[(c * tiles + t) * padded_n + col] = sum;
+      }
+    }
+  }
   return 0;
 }
 

@@ -41,6 +41,12 @@ def lib():
         _lib.oracle_gemm_f64.argtypes = [ctypes.c_int, u8, u8, u8, u8, i64, i64, i64,
                                          ctypes.POINTER(ctypes.c_double)]
         _lib.oracle_gemm_f64.restype = ctypes.c_int
+        _lib.oracle_tile_reference_subset.argtypes = [ctypes.c_int, u8, u8, u8, u8, i64, i64, i64, f32, ctypes.c_int,
+                                                      ctypes.c_float, ctypes.POINTER(ctypes.c_int64), i64, f32, f32,
+                                                      i64]
+        _lib.oracle_tile_reference_subset.restype = ctypes.c_int
+        _lib.oracle_observed_epilogue.argtypes = [f32, i64, i64, f32, ctypes.c_int, f32, i64]
+        _lib.oracle_observed_epilogue.restype = ctypes.c_int
     return _lib
 
 
@@ -97,3 +103,77 @@ def gemm_f64(kind, a, sfa, b, sfb, m, n, k):
     if rc:
         raise MemoryError("oracle allocation failed")
     return out
+
+
+def tile_reference_subset(kind, a, sfa, b, sfb, m, n, k, weights, alpha, padded_n, tiles):
+    """TILE-layout predicted/magnitude for the listed M-tiles only: [C, len(tiles), padded_n]."""
+    weights = np.ascontiguousarray(weights, dtype=np.float32)
+    channels = weights.shape[0]
+    tiles = np.ascontiguousarray(tiles, dtype=np.int64)
+    pred = np.zeros((channels, tiles.size, padded_n), np.float32)
+    mag = np.zeros_like(pred)
+    pa, ka = _ptr(a)
+    pb, kb = _ptr(b)
+    psa, ksa = _ptr(sfa)
+    psb, ksb = _ptr(sfb)
+    f32 = ctypes.POINTER(ctypes.c_float)
+    rc = lib().oracle_tile_reference_subset(KINDS[kind], pa, psa, pb, psb, m, n, k, weights.ctypes.data_as(f32),
+                                            channels, ctypes.c_float(np.float32(alpha)),
+                                            tiles.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), tiles.size,
+                                            pred.ctypes.data_as(f32), mag.ctypes.data_as(f32), padded_n)
+    if rc:
+        raise MemoryError("oracle allocation failed")
+    return pred, mag
+
+
+def observed_epilogue(values, weights, padded_n):
+    """Observed checksum partials [C, Tm, padded_n] of the fp32 values [m, n]
+    the epilogue summed, in the sm_100a epilogue's exact reduction order."""
+    values = np.ascontiguousarray(values, dtype=np.float32)
+    weights = np.ascontiguousarray(weights, dtype=np.float32)
+    m, n = values.shape
+    channels = weights.shape[0]
+    out = np.zeros((channels, (m + 127) // 128, padded_n), np.float32)
+    f32 = ctypes.POINTER(ctypes.c_float)
+    lib().oracle_observed_epilogue(values.ctypes.data_as(f32), m, n, weights.ctypes.data_as(f32), channels,
+                                   out.ctypes.data_as(f32), padded_n)
+    return out
+
+
+def decoded(kind, codes, scales, rows, k, operand="a", start=0, stop=None):
+    """Exact fp32 values of rows [start, stop) of a quantised operand with
+    ``rows`` rows and K = k: e4m3 codes; packed e2m1 codes times their ue4m3
+    scale (atom layout); or block-scaled e4m3 codes times their fp32 scale
+    (1 x 128 for operand "a", 128 x 128 for "b")."""
+    from . import formats
+    from .quant import scale_layout
+
+    stop = rows if stop is None else stop
+    if kind == "fp8":
+        return formats.e4m3_decode(np.asarray(codes, np.uint8).reshape(rows, k)[start:stop])
+    if kind == "fp8_block":
+        block_rows = 1 if operand == "a" else 128
+        scales = np.asarray(scales, np.float32)
+        idx = np.arange(start, stop) // block_rows
+        expanded = np.repeat(scales[idx], 128, axis=1)
+        return (formats.e4m3_decode(np.asarray(codes, np.uint8).reshape(rows, k)[start:stop]) * expanded).astype(
+            np.float32)
+    packed = np.asarray(codes, np.uint8).reshape(rows, k // 2)[start:stop]
+    vals = formats.e2m1_decode(formats.unpack_e2m1(packed))
+    s = formats.e4m3_decode(np.asarray(scales, np.uint8)[scale_layout(rows, k)[start:stop]])
+    return (vals.reshape(stop - start, k // 16, 16) * s[..., None]).reshape(stop - start, k).astype(np.float32)
+
+
+def gemm_rows_f64(kind, a, sfa, b, sfb, m, n, k, rows, chunk=2048):
+    """Float64 reference rows of the decoded product (exact products, the sum
+    in float64) and the same rows of |A| |B| (for error bounds): ([r, n], [r, n])."""
+    rows = np.asarray(rows, np.int64)
+    av = np.concatenate([decoded(kind, a, sfa, m, k, "a", int(r), int(r) + 1) for r in rows]).astype(np.float64)
+    out = np.zeros((rows.size, n))
+    bound = np.zeros((rows.size, n))
+    for c0 in range(0, n, chunk):
+        c1 = min(n, c0 + chunk)
+        bv = decoded(kind, b, sfb, n, k, "b", c0, c1).astype(np.float64)
+        out[:, c0:c1] = av @ bv.T
+        bound[:, c0:c1] = np.abs(av) @ np.abs(bv).T
+    return out, bound

@@ -127,21 +127,18 @@ ReferenceProblem reference_problem(const GemmProblem& g, float* predicted, float
   return r;
 }
 
-// Input-fused ABFT GEMM: TILE layout = GEMM, then the per-tile projection and
-// propagation on CUDA cores; K-SLICE layout = projection of A first, then the
-// GEMM with the propagation fused into its checksum warps.
+// Input-fused ABFT GEMM: TILE layout = per-tile projection, GEMM, then the
+// propagation on CUDA cores; K-SLICE layout = projection of A over all rows
+// (a streaming kernel), then the GEMM with the propagation fused into its
+// prediction warps.
 int run_input_fused(GemmProblem g, float* predicted, float* magnitude, int layout, void* workspace,
                     size_t workspace_bytes, cudaStream_t stream) {
   SDC_REQUIRE(predicted != nullptr && magnitude != nullptr, "predicted/magnitude must not be null");
   const ReferenceProblem r = reference_problem(g, predicted, magnitude, layout, workspace, workspace_bytes);
   if (layout == SDC_LAYOUT_KSLICE) {
-    // Projection and prediction both run inside the GEMM's prediction warps.
-    int rc = check_problem(r);
+    int rc = launch_kslice_projection(r, stream);
     if (rc != SDC_OK) return rc;
-    const KsliceScratch scratch = kslice_scratch(r);
-    g.q_full = scratch.q_full;
-    g.q_part = scratch.q_part;
-    g.grid_sync = scratch.grid_sync;
+    g.q_full = kslice_scratch(r).q_full;
     g.predicted = predicted;
     g.magnitude = magnitude;
     return launch_gemm(g, stream);

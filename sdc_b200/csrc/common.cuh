@@ -69,6 +69,15 @@ enum WatchdogCode : int32_t {
 // 2 seconds of globaltimer nanoseconds; a healthy wait ends in microseconds.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
+// Per-launch watchdog parameters: the wait limit, and a pacing offset that
+// only the test hook sdc_test_set_watchdog changes (it makes the prediction
+// warps' pacing wait unreachable, so a test can watch a bounded wait expire).
+struct WatchdogSettings {
+  uint64_t wait_limit_ns;
+  int32_t pace_extra;
+};
+WatchdogSettings watchdog_settings();
+
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -130,18 +139,40 @@ __device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t phase) {
 // `code` in the watchdog word and in `*abort`) when the limit expires or when
 // another role of the CTA already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, int32_t code,
-                                          volatile int32_t* abort, int32_t* watchdog) {
+                                          volatile int32_t* abort, int32_t* watchdog,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, phase)) return true;
   const uint64_t start = global_ns();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, phase)) {
     if ((++spins & 15u) == 0u) {
       if (*abort) return false;
-      if (global_ns() - start > kWaitLimitNs) {
+      if (global_ns() - start > limit_ns) {
         atomicCAS(watchdog, 0, code);
         *abort = code;
         return false;
       }
+    }
+  }
+  return true;
+}
+
+// As mbar_wait, but gives up only when its own limit expires, not when
+// another role aborted. The TMA producers use it: the two producers of a CTA
+// pair receive the same stage releases (the leader's MMA commits to both), so
+// as long as neither leaves early they issue exactly the same stages and the
+// leader's teardown drain covers every copy still in flight in either CTA.
+__device__ __forceinline__ bool mbar_wait_own_limit(uint64_t* bar, uint32_t phase, int32_t code,
+                                                    volatile int32_t* abort, int32_t* watchdog,
+                                                    uint64_t limit_ns) {
+  if (mbar_try_wait(bar, phase)) return true;
+  const uint64_t start = global_ns();
+  uint32_t spins = 0;
+  while (!mbar_try_wait(bar, phase)) {
+    if ((++spins & 15u) == 0u && global_ns() - start > limit_ns) {
+      atomicCAS(watchdog, 0, code);
+      *abort = code;
+      return false;
     }
   }
   return true;

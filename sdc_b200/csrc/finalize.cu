@@ -72,7 +72,11 @@ __global__ void __launch_bounds__(kColumnThreads) finalize_columns(FinalizeParam
       if (t & 2) state |= kDetected | kNonfinite;
     }
   } else if (block == 0 && threadIdx.x == 0) {
-    if (*p.hit_in != 0) state |= kHit;
+    // hit bit 0: the fault was applied; bit 1: the GEMM launch gave up a
+    // bounded wait, so its partials are incomplete and the call must not pass.
+    const int32_t hit = *p.hit_in;
+    if (hit & 1) state |= kHit;
+    if (hit & 2) state |= kDetected | kNonfinite;
     if (*p.nonfinite_in != 0) state |= kDetected | kNonfinite;
   }
 

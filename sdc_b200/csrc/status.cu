@@ -28,6 +28,14 @@ int32_t* watchdog_ptr() {
 
 namespace {
 thread_local std::string t_last_error;
+// Test hook state (sdc_test_set_watchdog): 0 = the production limit.
+std::atomic<uint64_t> g_test_wait_limit_ns{0};
+std::atomic<int32_t> g_test_pace_extra{0};
+}  // namespace
+
+WatchdogSettings watchdog_settings() {
+  const uint64_t limit = g_test_wait_limit_ns.load(std::memory_order_relaxed);
+  return {limit != 0 ? limit : kWaitLimitNs, g_test_pace_extra.load(std::memory_order_relaxed)};
 }
 
 void set_error(const std::string& message) { t_last_error = message; }
@@ -128,6 +136,13 @@ int sdc_device_check(int device) {
                      "sdc_b200 kernels are built for sm_100a (B200); device is sm_" +
                          std::to_string(major) + std::to_string(minor));
   }
+  return SDC_OK;
+}
+
+int sdc_test_set_watchdog(uint64_t wait_limit_ns, int32_t pace_extra) {
+  if (pace_extra < 0) return sdc::fail(SDC_ERR_INVALID, "pace_extra must be >= 0");
+  sdc::g_test_wait_limit_ns.store(wait_limit_ns, std::memory_order_relaxed);
+  sdc::g_test_pace_extra.store(pace_extra, std::memory_order_relaxed);
   return SDC_OK;
 }
 

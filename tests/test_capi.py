@@ -58,6 +58,8 @@ def test_argument_contracts_are_checked_before_launch():
     assert rc == capi.SDC_ERR_INVALID and "fault" in capi.last_error()
     rc = lib.sdc_quantize_fp8_block(fake, 0, 4, 128, 64, fake, fake, None)
     assert rc == capi.SDC_ERR_INVALID and "1 x 128 or 128 x 128" in capi.last_error()
+    assert lib.sdc_test_set_watchdog(0, -1) == capi.SDC_ERR_INVALID and "pace_extra" in capi.last_error()
+    assert lib.sdc_test_set_watchdog(0, 0) == capi.SDC_OK
     assert lib.sdc_abft_finalize_workspace_bytes(0, 300, 4) == 2 * ((300 + 63) // 64) * 4
     assert lib.sdc_abft_workspace_bytes(0, 256, 64, 128, 0) == 2 * 2 * 2 * 128 * 4
 

@@ -500,27 +500,26 @@ def test_end_to_end_detect_locate_correct(precision):
     weights = torch.stack((torch.ones(m, device=DEV), torch.arange(1, m + 1, device=DEV, dtype=torch.float32)))
     clean, *_ = reference(*args, weights, -1, -1, -1)
     row, col = 389, 201
-    # An exponent bit that is clear in the clean value: the flip scales it by
-    # 2^(2^(bit-23)) but keeps the row-weighted checksum finite.
+    # The highest exponent bit below 30 that is clear in the clean value: the
+    # flip scales it by 2^(2^(bit-23)), far above every threshold (so the ratio
+    # locator must succeed), and keeps the row-weighted checksum finite.
     bits = int(np.array([clean[row, col].float().item()], np.float32).view(np.uint32)[0])
-    bit = next(b for b in range(25, 30) if not bits & (1 << b))
+    bit = next(b for b in range(29, 24, -1) if not bits & (1 << b))
     nonfinite = torch.zeros(1, dtype=torch.int32, device=DEV)
     out, obs, hit, pred, mag = reference(*args, weights, row, col, bit, 0, nonfinite)
     packet = ops.abft_finalize_reference(obs, pred, mag, hit, nonfinite, n, 1e-3, 1e-4, None, True)
     assert packet[3][0].item() and not packet[3][1].item()
     location, located = ops.abft_locate(packet[1], packet[2], packet[3], m)
     ok, loc = oabft.locate(_np(packet[1]), _np(packet[2]), True, False, m)
-    assert located.item() == ok
-    assert location.tolist() == list(loc)
-    if ok:
-        assert location.tolist() == [row, col]
-        fixed = out.clone()
-        if precision == "fp8":
-            corrected = ops.abft_fp8_correct(*args, location, located, fixed)
-        else:
-            corrected = ops.abft_nvfp4_correct(*args, location, located, fixed)
-        assert corrected.item()
-        torch.testing.assert_close(fixed.float(), clean.float(), rtol=1e-2, atol=1e-3)
+    assert ok and located.item()
+    assert location.tolist() == list(loc) == [row, col]
+    fixed = out.clone()
+    if precision == "fp8":
+        corrected = ops.abft_fp8_correct(*args, location, located, fixed)
+    else:
+        corrected = ops.abft_nvfp4_correct(*args, location, located, fixed)
+    assert corrected.item()
+    torch.testing.assert_close(fixed.float(), clean.float(), rtol=1e-2, atol=1e-3)
     clean_packet = ops.abft_finalize_reference(*reference(*args, weights, -1, -1, -1, 0, nonfinite)[1:2],
                                                pred, mag, torch.zeros_like(hit), nonfinite, n, 1e-3, 1e-4, None, True)
     assert not clean_packet[3][0].item()
