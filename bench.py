@@ -4,28 +4,44 @@
 Metric: ABFT NVFP4/FP8 GEMM TFLOPS, % overhead vs the
 unprotected kernel, detection recall. One step = one protected GEMM on
 operands already quantised and resident in HBM: the input-fused ABFT GEMM
-(tcgen05 mainloop, fused observed-checksum epilogue, input-side prediction in
-the K-slice layout) followed by the device finalize that merges partials and
-decides. Throughput counts only the useful 2*M*N*K flops.
+(tcgen05 mainloop, fused observed-checksum epilogue, input-side projection
+and prediction in the K-slice layout) and the device finalize that merges
+the partials and decides. Throughput counts only the useful 2*M*N*K flops.
 
 Headline workload (config[1]): FP8 e4m3, M=N=K=8192, 1 x 128 (A) and
 128 x 128 (B) fp32 block scales, fp32 accumulation, bf16 output. Measured in
 the same run: the NVFP4 workload of config[2] (M=N=K=16384, e2m1 + ue4m3/16 +
 fp32 global scale, bf16 out) under "nvfp4", and the reference's own FP8
 semantics (tensorwise scale, fp32 output) at 8192^3 under "fp8_tensorwise".
+Operands are seeded bf16 N(0,1) matrices drawn on the host, so the reference
+arm can quantise exactly the same ones.
+
+Detection (rank 0): the configuration's schedule of 1000 GEMMs, each on fresh
+seeded operands, with seeded accumulator bit flips at rate 1e-3 per GEMM (at
+least one per schedule): false positives and the clean residual margins
+max |res|/thr and max |res|/mag; and a per-bit campaign (bits 20-31) on the
+headline operands with recall per bit and per class, where a flip counts as
+detectable when its own perturbation w_c * delta, computed from the flipped
+value, clears the threshold by more than the clean residual. The thresholds
+are atol + rtol * |w|^T |A| |B| with rtol calibrated per format from
+measured clean margins (CALIBRATED_RTOL), not the reference's debug default.
 
 Multi-GPU (python -m torch.distributed.run ... bench.py --gpus N): each rank
 protects its own M-shard (8192 rows x N=K=8192, weak scaling: the job's M is
-8192*N) and the ranks all-reduce (MAX) their detection status words over
-NCCL after every step, the path's only exchange. Time is the max over ranks.
+8192*N). Each step's verdict (detected, hit, max |res|/thr, max |res|) goes
+into a ring of per-step status rows that the ranks all-reduce (MAX) over
+NCCL once per 16 steps and at the end of the timed region, the path's only
+exchange. Time is the max over ranks.
 
 --impl reference times the reference's own CPU/torch ABFT path (restated in
-oracle/cpu_path.py, bit-identical to it) on this host's cores instead.
+oracle/cpu_path.py, bit-identical to it) on this host's cores, on the
+dequantised operands of the same seed and configuration.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -42,6 +58,14 @@ import torch  # noqa: E402
 
 METRIC = "ABFT NVFP4/FP8 GEMM TFLOPS, % overhead vs unprotected, detection recall"
 UNIT = "TFLOPS"
+# Relative thresholds of the benchmark's detector, per format, calibrated
+# from the clean residual margins measured over 1000 clean GEMMs at the
+# configuration's shape (the bench reports the margin it sees in every run).
+CALIBRATED_RTOL = {"fp8_block": 5e-8, "fp8": 5e-8, "nvfp4": 5e-8}
+ATOL = 1e-3
+SEEDS = {"fp8_block": 1, "fp8": 3, "nvfp4": 2}
+SIZES = {"fp8_block": 8192, "fp8": 8192, "nvfp4": 16384}
+EXCHANGE_EVERY = 16
 
 
 def measured_peaks():
@@ -53,7 +77,8 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks/throttle reasons sampled during the timed region.
+    The timed region starts only after the first sample has been written."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -71,11 +96,14 @@ class ClockSampler:
                  "-lms", "50"], stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
-        time.sleep(0.15)
+        deadline = time.time() + 10.0
+        while self.proc is not None and time.time() < deadline and os.path.getsize(self.file.name) == 0:
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            time.sleep(0.1)
             self.proc.terminate()
             self.proc.wait(timeout=5)
 
@@ -102,106 +130,110 @@ class ClockSampler:
                 "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
 
 
-# Workload formats: (quantisation precision, bench key, description).
+# Workload formats: (quantisation precision, description).
 FORMATS = {"fp8_block": ("fp8", "fp8 block-scaled 1x128 / 128x128, bf16 out"),
            "fp8": ("fp8", "fp8 tensorwise, fp32 out"),
            "nvfp4": ("nvfp4", "nvfp4 block16, bf16 out")}
 
 
-def make_operands(precision, m, n, k, device, seed, b_std=1.0):
-    """Seeded N(0,1) bf16 A [m,k] and B_rows [n,k] (synthetic, BASELINE shapes) quantised once."""
+def workload_name(precision, size):
+    kind, rest = FORMATS[precision][1].split(" ", 1)
+    return f"{kind} M=N=K={size} {rest}"
+
+
+def bench_config(precision, size, world):
+    """The config dict both arms print (the reference arm runs the same workload)."""
+    return {"workload": workload_name(precision, size) + " ABFT (Classic, K-slice input reference) + finalize",
+            "per_gpu": f"M=N=K={size}", "parallelism": f"M-shard x{world}, NCCL all-reduce of detection status",
+            "operands": f"seeded bf16 N(0,1) A [M,K] and B [N,K] drawn on the host (seed {SEEDS[precision]}"
+                        f" + 1000*rank), quantised once",
+            "l2": "working set (A+B codes, output) > 126 MB L2; no explicit flush"}
+
+
+def host_operands(m, n, k, seed, b_std=1.0):
+    """Seeded bf16 A [m, k] and B rows [n, k] on the host (both arms use these)."""
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(m, k, generator=g, dtype=torch.bfloat16)
+    b = torch.randn(n, k, generator=g, dtype=torch.bfloat16)
+    if b_std != 1.0:
+        b = (b.float() * b_std).to(torch.bfloat16)
+    return a, b
+
+
+def quantise(precision, a, b):
+    """Device bf16 A [m,k], B rows [n,k] -> (op args, (qa, qb))."""
     from sdc_b200.gemm.quantization import quantize, quantize_blockwise
 
-    g = torch.Generator(device=device).manual_seed(seed)
-    a = torch.randn(m, k, device=device, generator=g, dtype=torch.bfloat16)
-    b = torch.randn(n, k, device=device, generator=g, dtype=torch.bfloat16)
-    if b_std != 1.0:
-        b = b * b_std
     if precision == "fp8_block":
         qa, qb = quantize_blockwise(a, 1), quantize_blockwise(b, 128)
-        return (qa.codes.view(torch.float8_e4m3fn), qb.codes.view(torch.float8_e4m3fn), qa.scales, qb.scales)
+        return (qa.codes.view(torch.float8_e4m3fn), qb.codes.view(torch.float8_e4m3fn), qa.scales, qb.scales), (qa, qb)
     qa, qb = quantize(a, precision), quantize(b, precision)
     alpha = (qa.multiplier * qb.multiplier).reciprocal()
     if precision == "fp8":
-        args = (qa.codes.view(torch.float8_e4m3fn), qb.codes.view(torch.float8_e4m3fn), alpha)
-    else:
-        args = (qa.codes, qb.codes, qa.scales_mma, qb.scales_mma, k, alpha)
-    del a, b
-    return args
+        return (qa.codes.view(torch.float8_e4m3fn), qb.codes.view(torch.float8_e4m3fn), alpha), (qa, qb)
+    return (qa.codes, qb.codes, qa.scales_mma, qb.scales_mma, a.shape[1], alpha), (qa, qb)
+
+
+def _dequantize_row(q, row):
+    """Decoded row of a QuantizedMatrix (codes * block scales / multiplier)."""
+    import dataclasses
+
+    from sdc_b200.gemm.quantization import dequantize
+
+    if q.precision == "fp8" and q.block_rows:
+        scales = q.scales[row // q.block_rows:row // q.block_rows + 1]
+        return q.codes[row:row + 1].view(torch.float8_e4m3fn).float() * scales.repeat_interleave(128, 1)
+    one = dataclasses.replace(q, codes=q.codes[row:row + 1],
+                              scales=None if q.scales is None else q.scales[row:row + 1], shape=(1, q.shape[1]))
+    return dequantize(one)
 
 
 class Protected:
     """One protected GEMM step on resident operands (the hot path)."""
 
-    def __init__(self, precision, m, n, k, device, seed, layout=1, atol=1e-3, rtol=1e-4, b_std=1.0):
+    def __init__(self, precision, m, n, k, device, seed, layout=1, atol=ATOL, rtol=None, b_std=1.0, operands=None):
         self.ops = torch.ops.sdc_cutlass
-        self.precision, self.m, self.n, self.k = precision, m, n, k
-        self.args = make_operands(precision, m, n, k, device, seed, b_std)
+        self.precision, self.m, self.n, self.k, self.device = precision, m, n, k, device
+        if operands is None:
+            operands = host_operands(m, n, k, seed, b_std)
+        a, b = (t.to(device) for t in operands)
+        self.args, self.quantised = quantise(precision, a, b)
+        del a, b
         self.weights = torch.stack((torch.ones(m, device=device),
                                     torch.arange(1, m + 1, device=device, dtype=torch.float32)))
         self.nonfinite = torch.zeros(1, dtype=torch.int32, device=device)
-        self.atol, self.rtol = atol, rtol
+        self.atol = atol
+        self.rtol = CALIBRATED_RTOL[precision] if rtol is None else rtol
         ops = self.ops
         if precision == "fp8_block":  # K-slice is the block-scaled op's only layout
-            self.fused, self.observe, self.plain = (ops.abft_fp8_block_reference_mm, ops.abft_fp8_block_mm,
-                                                    ops.fp8_block_mm)
+            self.fused, self.plain = ops.abft_fp8_block_reference_mm, ops.fp8_block_mm
             self.layout_args = ()
         else:
             self.fused = ops.abft_fp8_reference_mm if precision == "fp8" else ops.abft_nvfp4_reference_mm
-            self.observe = ops.abft_fp8_mm if precision == "fp8" else ops.abft_nvfp4_mm
             self.plain = ops.fp8_mm if precision == "fp8" else ops.nvfp4_mm
             self.layout_args = (layout,)
 
-    def step(self, fault=(-1, -1, -1)):
+    def requantise(self, a, b):
+        self.args, self.quantised = quantise(self.precision, a, b)
+
+    def step(self, fault=(-1, -1, -1), diagnostics=True):
         out, obs, hit, pred, mag = self.fused(*self.args, self.weights, *fault, 0, self.nonfinite, *self.layout_args)
         packet = self.ops.abft_finalize_reference(obs, pred, mag, hit, self.nonfinite, self.n, self.atol,
-                                                  self.rtol, None, True)
+                                                  self.rtol, None, diagnostics)
         return out, packet
 
     def unprotected(self):
         return self.plain(*self.args)
 
-    def gemm_only(self):
-        return self.observe(*self.args, self.weights, -1, -1, -1)
-
     def fused_only(self):
         """The step's dominant kernel alone: the protected GEMM without finalize."""
         return self.fused(*self.args, self.weights, -1, -1, -1, 0, self.nonfinite, *self.layout_args)
 
-
-def paired_overhead(prot, steps, rounds=5):
-    """Protected vs unprotected step, alternating blocks so both see the same
-    clocks and temperature (the reference times paired, alternating calls)."""
-    stream = torch.cuda.current_stream()
-    n = max(2, steps // rounds)
-    t_prot = t_plain = 0.0
-    for _ in range(rounds):
-        t_prot += timed(prot.step, n, 1, stream)
-        t_plain += timed(prot.unprotected, n, 1, stream)
-    return t_prot / (rounds * n), t_plain / (rounds * n)
-
-
-def profiled_traffic(name):
-    """DRAM bytes (read + write) of one protected-GEMM launch from the committed
-    ncu summary (first value column of its full-capture table), or None."""
-    import re
-
-    path = ROOT / "profiles" / name
-    if not path.exists():
-        return None
-    total = 0.0
-    for metric in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
-        m = re.search(rf"\| {re.escape(metric)} \| ([0-9.]+) MB", path.read_text())
-        if m is None:
-            return None
-        total += float(m.group(1)) * 1e6
-    return total
-
-
-# Kernels this library launches per protected step: the K-slice projection
-# of A (kslice_project + kslice_band_sum), the GEMM (prediction fused into
-# it), finalize_columns + finalize_flags.
-LAUNCHES_PER_STEP = 5
+    def exact_value(self, row, col):
+        """Float64 dot product of the decoded operands at (row, col), times alpha:
+        the fp32 value the epilogue sees, up to the accumulation order."""
+        qa, qb = self.quantised
+        return float((_dequantize_row(qa, row).double() * _dequantize_row(qb, col).double()).sum())
 
 
 def timed(fn, steps, warmup, stream):
@@ -217,63 +249,161 @@ def timed(fn, steps, warmup, stream):
     return start.elapsed_time(end) / 1e3
 
 
-def detection_campaign(prot, flips, seed):
-    """Seeded single-bit accumulator flips (bits 23-30 exponent, 20-22 high
-    mantissa) at uniform (row, col); recall over all flips and over flips
-    whose checksum perturbation exceeds the threshold."""
+def paired_overhead(prot, steps, rounds=5):
+    """Protected vs unprotected step, alternating blocks so both see the same
+    clocks and temperature (the reference times paired, alternating calls)."""
+    stream = torch.cuda.current_stream()
+    n = max(2, steps // rounds)
+    t_prot = t_plain = 0.0
+    for _ in range(rounds):
+        t_prot += timed(prot.step, n, 1, stream)
+        t_plain += timed(prot.unprotected, n, 1, stream)
+    return t_prot / (rounds * n), t_plain / (rounds * n)
+
+
+def profiled_traffic(precision, size):
+    """DRAM bytes (read + write) of one protected-GEMM launch of this workload,
+    from the committed same-size ncu capture summary (profiles/traffic.json),
+    or None when no capture of this exact workload exists."""
+    path = ROOT / "profiles" / "traffic.json"
+    if not path.exists():
+        return None, None
+    entry = json.loads(path.read_text()).get(f"{precision}_{size}")
+    if not entry:
+        return None, None
+    return entry["dram_bytes_read"] + entry["dram_bytes_write"], entry["source"]
+
+
+# Kernels this library launches per protected step: the GEMM (projection and
+# K-slice prediction fused into it) + finalize_columns + finalize_flags.
+LAUNCHES_PER_STEP = 3
+
+
+def _flip(value, bit):
+    import numpy as np
+
+    bits = np.array([value], np.float32).view(np.uint32) ^ np.uint32(1 << bit)
+    return float(bits.view(np.float32)[0])
+
+
+def detection_campaign(prot, flips_per_bit, seed):
+    """Per-bit recall on the headline operands (bits 20-31). A flip is
+    detectable when, for some channel c, |w_c[row] * delta| exceeds the clean
+    threshold plus the clean residual of that column, where delta is the
+    flipped minus the clean fp32 value (from the decoded operands,
+    independently of the checksum arithmetic); undetectable when it is below
+    the threshold minus the clean residual for every channel; ambiguous
+    otherwise. Non-finite flipped values are detectable (non-finite rule)."""
     g = torch.Generator().manual_seed(seed)
     clean_out, clean_packet = prot.step()
-    residual0 = clean_packet[1].clone()
-    threshold0 = clean_packet[2].clone()
-    detected = detectable = 0
-    by_class = {"exponent": [0, 0], "high_mantissa": [0, 0]}
-    for _ in range(flips):
-        row = int(torch.randint(0, prot.m, (1,), generator=g))
-        col = int(torch.randint(0, prot.n, (1,), generator=g))
-        bit = int(torch.randint(20, 31, (1,), generator=g))
-        _, packet = prot.step((row, col, bit))
-        flags = packet[3].tolist()
-        hit = bool(flags[0])
-        # Detectable: the flip's own checksum perturbation exceeds the clean threshold.
-        delta = (packet[1][:, col] - residual0[:, col]).abs()
-        can = bool((delta > threshold0[:, col]).any()) or bool(flags[1])
-        detected += hit
-        detectable += can
-        cls = "exponent" if bit >= 23 else "high_mantissa"
-        by_class[cls][0] += hit
-        by_class[cls][1] += 1
-    clean_runs = 8
-    false_positives = sum(bool(prot.step()[1][3][0]) for _ in range(clean_runs))
-    return {"flips": flips, "detected": detected, "detectable": detectable,
-            "recall_all": detected / max(flips, 1), "recall_detectable": min(detected, detectable) / max(detectable, 1),
-            "by_class": {k: {"detected": v[0], "flips": v[1]} for k, v in by_class.items()},
-            "clean_runs": clean_runs + 1, "false_positives": false_positives + int(bool(clean_packet[3][0])),
-            "schedule": fault_schedule(prot, residual0, threshold0, seed)}
+    residual0 = clean_packet[1].double().cpu()
+    threshold0 = clean_packet[2].double().cpu()
+    per_bit = {}
+    totals = {"flips": 0, "detected": 0, "detectable": 0, "detected_detectable": 0, "undetectable": 0,
+              "detected_undetectable": 0, "ambiguous": 0}
+    classes = {"exponent": [0, 0, 0, 0], "high_mantissa": [0, 0, 0, 0], "sign": [0, 0, 0, 0]}
+    for bit in range(20, 32):
+        stats = [0, 0, 0, 0]  # flips, detected, detectable, detected among detectable
+        for _ in range(flips_per_bit):
+            row = int(torch.randint(0, prot.m, (1,), generator=g))
+            col = int(torch.randint(0, prot.n, (1,), generator=g))
+            if prot.precision == "fp8":
+                value = float(clean_out[row, col])  # fp32 output: exactly the epilogue's value
+            else:
+                value = float(torch.tensor(prot.exact_value(row, col), dtype=torch.float32))
+            flipped = _flip(value, bit)
+            _, packet = prot.step((row, col, bit))
+            hit = bool(packet[3][0])
+            if not math.isfinite(flipped):
+                status = "detectable"
+            else:
+                delta = abs(flipped - value)
+                perturb = [delta, (row + 1.0) * delta]
+                clean = [abs(float(residual0[c, col])) for c in range(2)]
+                thr = [float(threshold0[c, col]) for c in range(2)]
+                if any(perturb[c] > thr[c] + clean[c] for c in range(2)):
+                    status = "detectable"
+                elif all(perturb[c] < thr[c] - clean[c] for c in range(2)):
+                    status = "undetectable"
+                else:
+                    status = "ambiguous"
+            stats[0] += 1
+            stats[1] += hit
+            totals["flips"] += 1
+            totals["detected"] += hit
+            if status == "detectable":
+                stats[2] += 1
+                stats[3] += hit
+                totals["detectable"] += 1
+                totals["detected_detectable"] += hit
+            elif status == "undetectable":
+                totals["undetectable"] += 1
+                totals["detected_undetectable"] += hit
+            else:
+                totals["ambiguous"] += 1
+        per_bit[bit] = {"flips": stats[0], "detected": stats[1], "detectable": stats[2],
+                        "detected_detectable": stats[3]}
+        cls = "sign" if bit == 31 else "exponent" if bit >= 23 else "high_mantissa"
+        for i in range(4):
+            classes[cls][i] += stats[i]
+    by_class = {name: {"flips": v[0], "detected": v[1], "recall": v[1] / max(v[0], 1), "detectable": v[2],
+                       "recall_detectable": v[3] / max(v[2], 1)} for name, v in classes.items()}
+    return {"flips_per_bit": flips_per_bit, "per_bit": per_bit, "by_class": by_class, **totals,
+            "recall_all": totals["detected"] / max(totals["flips"], 1),
+            "recall_detectable": totals["detected_detectable"] / max(totals["detectable"], 1),
+            "missed_detectable": totals["detectable"] - totals["detected_detectable"],
+            "detectable_rule": "|w_c delta| > thr_c + |clean res_c| for some channel c, delta from the decoded "
+                               "operands (independent of the checksum arithmetic); non-finite flips detectable",
+            "clean_flagged": bool(clean_packet[3][0])}
 
 
-def fault_schedule(prot, residual0, threshold0, seed, gemms=1000, rate=1e-3):
-    """The configurations' schedule: ``gemms`` protected GEMMs, each carrying
-    one seeded accumulator flip with probability ``rate`` (uniform row,
-    column and bit in [0, 32)); every GEMM's verdict is read back."""
+def fault_schedule(prot, seed, gemms=1000, rate=1e-3):
+    """The configurations' schedule: ``gemms`` protected GEMMs, each on fresh
+    seeded operands of the workload's shape drawn on the device, each carrying
+    one seeded accumulator flip (uniform row, column and bit in [0, 32)) with
+    probability ``rate``; when the draws give none, one GEMM of the schedule
+    (drawn uniformly) carries one, so every schedule injects. Verdicts and the
+    clean residual margins stay on the device until the end."""
     g = torch.Generator().manual_seed(seed + 7919)
-    faulted = detected = detectable = false_positives = 0
-    for _ in range(gemms):
-        fault = (-1, -1, -1)
-        if float(torch.rand((), generator=g)) < rate:
-            fault = (int(torch.randint(0, prot.m, (1,), generator=g)), int(torch.randint(0, prot.n, (1,), generator=g)),
+    draws = torch.rand(gemms, generator=g) < rate
+    if not bool(draws.any()):
+        draws[int(torch.randint(0, gemms, (1,), generator=g))] = True
+    faults = {}
+    for i in draws.nonzero().flatten().tolist():
+        faults[i] = (int(torch.randint(0, prot.m, (1,), generator=g)), int(torch.randint(0, prot.n, (1,), generator=g)),
                      int(torch.randint(0, 32, (1,), generator=g)))
-        _, packet = prot.step(fault)
-        flag = bool(packet[3][0])
-        if fault[0] < 0:
-            false_positives += flag
-            continue
-        faulted += 1
-        detected += flag
-        col = fault[1]
-        delta = (packet[1][:, col] - residual0[:, col]).abs()
-        detectable += bool((delta > threshold0[:, col]).any()) or bool(packet[3][1])
-    return {"gemms": gemms, "rate": rate, "faulted": faulted, "detected": detected, "detectable": detectable,
-            "false_positives": false_positives, "clean": gemms - faulted}
+    device = prot.device
+    flags = torch.zeros(gemms, dtype=torch.bool, device=device)
+    nonfinite = torch.zeros(gemms, dtype=torch.bool, device=device)
+    ratio_thr = torch.zeros(gemms, dtype=torch.float64, device=device)
+    ratio_mag = torch.zeros(gemms, dtype=torch.float64, device=device)
+    dev_gen = torch.Generator(device=device)
+    saved = prot.args, prot.quantised
+    for i in range(gemms):
+        dev_gen.manual_seed(seed * 100003 + i)
+        a = torch.randn(prot.m, prot.k, device=device, generator=dev_gen, dtype=torch.bfloat16)
+        b = torch.randn(prot.n, prot.k, device=device, generator=dev_gen, dtype=torch.bfloat16)
+        prot.requantise(a, b)
+        del a, b
+        _, packet = prot.step(faults.get(i, (-1, -1, -1)))
+        flags[i] = packet[3][0]
+        nonfinite[i] = packet[3][1]
+        res = packet[1].abs().double()
+        ratio_thr[i] = (res / packet[2].double()).amax()
+        ratio_mag[i] = (res / packet[0][1].double().clamp_min(1e-30)).amax()
+    prot.args, prot.quantised = saved
+    flags, nonfinite = flags.cpu(), nonfinite.cpu()
+    ratio_thr, ratio_mag = ratio_thr.cpu(), ratio_mag.cpu()
+    clean = torch.ones(gemms, dtype=torch.bool)
+    clean[list(faults)] = False
+    return {"gemms": gemms, "rate": rate, "faulted": len(faults), "detected": int(flags[~clean].sum()),
+            "faults": [{"gemm": i, "row": r, "col": c, "bit": bit, "detected": bool(flags[i]),
+                        "nonfinite": bool(nonfinite[i])} for i, (r, c, bit) in sorted(faults.items())],
+            "clean": int(clean.sum()), "false_positives": int(flags[clean].sum()),
+            "clean_max_res_over_thr": float(ratio_thr[clean].max()),
+            "clean_max_res_over_mag": float(ratio_mag[clean].max()),
+            "clean_p50_res_over_mag": float(ratio_mag[clean].median()),
+            "operands": "fresh seeded N(0,1) bf16 operands per GEMM (device generator)"}
 
 
 # Qwen2.5-7B linear layers at T = 16384 tokens: (name, M, N, K).
@@ -296,7 +426,11 @@ def qwen_sweep(args, device, stream, rank, world, dist):
         total_flops = total_prot = total_plain = 0.0
         for name, m, n, k in QWEN_SHAPES:
             start, stop = shard_rows(m, world, rank)
-            prot = Protected(precision, stop - start, n, k, device, 7 + rank, b_std=0.02)
+            g = torch.Generator(device=device).manual_seed(7 + rank)
+            a = torch.randn(stop - start, k, device=device, generator=g, dtype=torch.bfloat16)
+            b = (torch.randn(n, k, device=device, generator=g, dtype=torch.bfloat16) * 0.02).to(torch.bfloat16)
+            prot = Protected(precision, stop - start, n, k, device, 0, operands=(a, b))
+            del a, b
             # Paired, alternating blocks (as for the headline), so that both
             # arms see the same clocks under the power cap.
             step_t, plain_t = paired_overhead(prot, 3 * args.sweep_steps, rounds=3)
@@ -321,69 +455,111 @@ def qwen_sweep(args, device, stream, rank, world, dist):
     return out
 
 
-def e2e_step(precision, a, b, weights, nonfinite, atol, rtol):
-    """Public-API protected GEMM on device bf16 operands (quantise, protected
-    GEMM, finalize); returns the flags packet tensor and the output."""
-    from sdc_b200.gemm.quantization import quantize, quantize_blockwise
-
-    ops = torch.ops.sdc_cutlass
-    if precision == "fp8_block":
-        qa, qb = quantize_blockwise(a, 1), quantize_blockwise(b, 128)
-        res = ops.abft_fp8_block_reference_mm(qa.codes.view(torch.float8_e4m3fn), qb.codes.view(torch.float8_e4m3fn),
-                                              qa.scales, qb.scales, weights, -1, -1, -1, 0, nonfinite)
-    else:
-        qa, qb = quantize(a, precision), quantize(b, precision)
-        alpha = (qa.multiplier * qb.multiplier).reciprocal()
-        if precision == "fp8":
-            res = ops.abft_fp8_reference_mm(qa.codes.view(torch.float8_e4m3fn), qb.codes.view(torch.float8_e4m3fn),
-                                            alpha, weights, -1, -1, -1, 0, nonfinite, 1)
-        else:
-            res = ops.abft_nvfp4_reference_mm(qa.codes, qb.codes, qa.scales_mma, qb.scales_mma, a.shape[1], alpha,
-                                              weights, -1, -1, -1, 0, nonfinite, 1)
-    out, obs, hit, pred, mag = res
-    packet = ops.abft_finalize_reference(obs, pred, mag, hit, nonfinite, b.shape[0], atol, rtol, None, False)
-    return packet[3], out
+ABFT_PUBLIC = {"method": "classic", "implementation": "native", "reference_mode": "input_fused",
+               "reference_layout": "kslice", "on_error": "report", "recovery": "none", "diagnostics": False}
 
 
-def e2e_run(precision, host_a, host_b, device, weights, nonfinite, atol, rtol, steps, stream):
-    """``steps`` end-to-end protected GEMMs from pinned host bf16 operands:
-    each step copies its A and B to the device (on a copy stream, one step
-    ahead, into one of two buffer sets) and reads its flags back to pinned
-    host memory. Returns seconds per step (CUDA events on the compute stream)."""
-    copy = torch.cuda.Stream(device)
+def e2e_run(precision, host_a, host_b_kn, device, atol, rtol, steps, stream):
+    """``steps`` clean end-to-end protected GEMMs through the public API
+    (sdc_b200.abft.execute: quantise both operands, protected GEMM,
+    finalize) from pinned host bf16 operands, with the output
+    and the verdict copied back to pinned host memory every step. Step i+1's
+    host-to-device copies run on a copy stream (two buffer sets) and step i's
+    device-to-host copies on another while the compute stream works.
+    Returns (seconds per step from CUDA events on the compute stream, bytes
+    copied back per step, steps flagged)."""
+    from sdc_b200.abft import execute
+
+    scaling = {"fp8_block": "blockwise", "fp8": "tensorwise", "nvfp4": "block16"}[precision]
+    quant = FORMATS[precision][0]
+    cfg = dict(ABFT_PUBLIC, atol=atol, rtol=rtol)
+    copy_in, copy_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
     dev_a = [torch.empty_like(host_a, device=device) for _ in range(2)]
-    dev_b = [torch.empty_like(host_b, device=device) for _ in range(2)]
-    flags_host = torch.empty((steps, 5), dtype=torch.bool).pin_memory()
+    dev_b = [torch.empty_like(host_b_kn, device=device) for _ in range(2)]
+    m, n = host_a.shape[0], host_b_kn.shape[1]
+    out_dtype = torch.float32 if precision == "fp8" else torch.bfloat16
+    out_host = [torch.empty((m, n), dtype=out_dtype).pin_memory() for _ in range(2)]
+    flags_host = torch.empty((steps, 2), dtype=torch.bool).pin_memory()
     copied = [torch.cuda.Event() for _ in range(2)]
     free = [torch.cuda.Event() for _ in range(2)]
 
     def issue_copy(i):
         slot = i % 2
-        with torch.cuda.stream(copy):
+        with torch.cuda.stream(copy_in):
             if i >= 2:
-                copy.wait_event(free[slot])
+                copy_in.wait_event(free[slot])
             dev_a[slot].copy_(host_a, non_blocking=True)
-            dev_b[slot].copy_(host_b, non_blocking=True)
-            copied[slot].record(copy)
+            dev_b[slot].copy_(host_b_kn, non_blocking=True)
+            copied[slot].record(copy_in)
 
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     start.record(stream)
-    with torch.cuda.stream(copy):
-        copy.wait_event(start)
+    with torch.cuda.stream(copy_in):
+        copy_in.wait_event(start)
     issue_copy(0)
     for i in range(steps):
         if i + 1 < steps:
             issue_copy(i + 1)
         slot = i % 2
         stream.wait_event(copied[slot])
-        flags, _ = e2e_step(precision, dev_a[slot], dev_b[slot], weights, nonfinite, atol, rtol)
+        out, report = execute(dev_a[slot], dev_b[slot], quant, scaling, abft_config=cfg)
         free[slot].record(stream)
-        flags_host[i].copy_(flags, non_blocking=True)
+        copy_out.wait_stream(stream)
+        with torch.cuda.stream(copy_out):
+            # Same-stream order keeps out_host[slot] from being overwritten
+            # before the previous copy into it has finished.
+            out_host[slot].copy_(out, non_blocking=True)
+            flags_host[i, 0].copy_(report.detected.reshape(()), non_blocking=True)
+            flags_host[i, 1].copy_(report.nonfinite.reshape(()), non_blocking=True)
+        out.record_stream(copy_out)
+    stream.wait_stream(copy_out)
     end.record(stream)
     end.synchronize()
-    assert not flags_host[:, 0].any(), "a clean end-to-end run was flagged"
-    return start.elapsed_time(end) / 1e3 / steps
+    return (start.elapsed_time(end) / 1e3 / steps, m * n * out_host[0].element_size() + 2,
+            int(flags_host[:, 0].sum()))
+
+
+def library_ceiling(device, stream):
+    """Library GEMMs at the workloads' shapes on the same box, as achievable
+    anchors beside the 2x / 4x bf16 denominators (torch._scaled_mm, i.e.
+    cuBLASLt). Each entry is TFLOP/s, or the error when the library rejects
+    the form."""
+    out = {}
+    size = 8192
+    g = torch.Generator(device=device).manual_seed(5)
+    a = torch.randn(size, size, device=device, generator=g).to(torch.float8_e4m3fn)
+    b = torch.randn(size, size, device=device, generator=g).to(torch.float8_e4m3fn)
+    one = torch.ones((), device=device)
+    flops = 2.0 * size ** 3
+
+    def measure(name, fn, flop):
+        try:
+            fn()
+            seconds = timed(fn, 20, 3, stream) / 20
+            out[name] = {"tflops": flop / seconds / 1e12}
+        except Exception as error:  # the library may not offer this form
+            out[name] = {"error": str(error).splitlines()[0][:200]}
+
+    measure("fp8_tensorwise_8192_bf16out", lambda: torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one,
+                                                                     out_dtype=torch.bfloat16), flops)
+    sa = torch.rand(size, size // 128, device=device) + 0.5
+    sb = torch.rand(size // 128, size // 128, device=device) + 0.5
+    measure("fp8_blockwise_1x128_128x128_8192_bf16out",
+            lambda: torch._scaled_mm(a, b.t(), scale_a=sa, scale_b=sb.t(), out_dtype=torch.bfloat16), flops)
+    del a, b
+    n4 = 16384
+    try:
+        codes = torch.randint(0, 256, (n4, n4 // 2), device=device, dtype=torch.uint8)
+        scales = torch.full((n4 * n4 // 16,), 0x38, device=device, dtype=torch.uint8)
+        fa = codes.view(torch.float4_e2m1fn_x2)
+        sfa = scales.view(torch.float8_e4m3fn)
+        measure("nvfp4_16384_bf16out", lambda: torch._scaled_mm(fa, fa.t(), scale_a=sfa, scale_b=sfa,
+                                                                 out_dtype=torch.bfloat16), 2.0 * n4 ** 3)
+    except Exception as error:
+        out["nvfp4_16384_bf16out"] = {"error": str(error).splitlines()[0][:200]}
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_ours(args):
@@ -408,29 +584,55 @@ def run_ours(args):
     stream = torch.cuda.current_stream(device)
     bf16_peak, hbm_peak, basis = measured_peaks()
     results = {}
-    for precision, size, seed in (("fp8_block", args.size or 8192, 1), ("fp8", args.size or 8192, 3),
-                                  ("nvfp4", args.size or 16384, 2)):
+    for precision in ("fp8_block", "fp8", "nvfp4"):
         if args.format not in ("all", precision):
             continue
+        size = args.size or SIZES[precision]
         m = n = k = size
-        prot = Protected(precision, m, n, k, device, seed + 1000 * rank)
+        prot = Protected(precision, m, n, k, device, SEEDS[precision] + 1000 * rank, rtol=args.rtol)
         flops = 2.0 * m * n * k
-        status = torch.zeros(2, dtype=torch.int32, device=device)
+        ring = torch.zeros(EXCHANGE_EVERY, 4, dtype=torch.float32, device=device)
+        exchanged = torch.zeros(4, dtype=torch.float32, device=device)
+        counter = [0]
+
+        def exchange():
+            dist.all_reduce(ring, op=dist.ReduceOp.MAX)
+            torch.maximum(exchanged, ring.amax(dim=0), out=exchanged)
+            ring.zero_()
 
         def step():
             _, packet = prot.step()
             if dist is not None:
-                status[0] = packet[3][0].to(torch.int32)
-                status[1] = packet[4][0]
-                dist.all_reduce(status, op=dist.ReduceOp.MAX)
+                # This step's verdict and residual norms into the ring; the
+                # ranks exchange the ring once per EXCHANGE_EVERY steps.
+                slot = counter[0] % EXCHANGE_EVERY
+                res = packet[1].abs()
+                ring[slot, 0] = packet[3][0].float()
+                ring[slot, 1] = packet[4][0].float()
+                ring[slot, 2] = (res / packet[2]).amax()
+                ring[slot, 3] = res.amax()
+                counter[0] += 1
+                if counter[0] % EXCHANGE_EVERY == 0:
+                    exchange()
 
         for _ in range(args.warmup):
             step()
+        if dist is not None and counter[0] % EXCHANGE_EVERY:
+            exchange()
         torch.cuda.synchronize()
         if dist is not None:
             dist.barrier()
+        counter[0] = 0
         with ClockSampler(local) as clocks:
-            elapsed = timed(step, args.steps, 0, stream)
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            for _ in range(args.steps):
+                step()
+            if dist is not None and counter[0] % EXCHANGE_EVERY:
+                exchange()
+            end.record(stream)
+            end.synchronize()
+        elapsed = start.elapsed_time(end) / 1e3
         torch.cuda.synchronize()
         if dist is not None:
             t = torch.tensor([elapsed], device=device)
@@ -441,10 +643,9 @@ def run_ours(args):
         per_step = elapsed / args.steps
         fp8 = precision.startswith("fp8")
         peak = bf16_peak * (2 if fp8 else 4)
-        profile = {("fp8_block", 8192): "gemm_fp8block_8192_abft.md",
-                   ("fp8", 8192): "gemm_fp8_8192_abft.md"}.get((precision, size))
+        traffic, traffic_source = profiled_traffic(precision, size)
         entry = {
-            "workload": f"{FORMATS[precision][1].split(' ', 1)[0]} M=N=K={size} {FORMATS[precision][1].split(' ', 1)[1]}",
+            "workload": workload_name(precision, size),
             "tflops": world * flops / per_step / 1e12,
             "ms_per_step": per_step * 1e3,
             "unprotected_tflops": flops / plain_paired / 1e12,
@@ -453,120 +654,169 @@ def run_ours(args):
             "roofline": {"bound": "tensor", "achieved": flops / (t_fused / args.steps) / 1e12, "peak": peak,
                          "unit": "TFLOP/s", "frac": flops / (t_fused / args.steps) / 1e12 / peak,
                          "kernel": "protected GEMM (gemm_kernel with checksums, projection and prediction)",
-                         "traffic": profiled_traffic(profile) if profile else None,
-                         "traffic_source": f"profiles/{profile} (ncu dram bytes of one launch)" if profile else None,
+                         "traffic": traffic, "traffic_source": traffic_source,
                          "algorithmic_flops": flops,
                          "peak_basis": f"{2 if fp8 else 4}x {basis} bf16 dense burst "
-                                       f"({bf16_peak} TFLOP/s); nominal dense {4500 if fp8 else 9000}"},
+                                       f"({bf16_peak} TFLOP/s) of measured; nominal dense {4500 if fp8 else 9000}"},
+            "thresholds": {"atol": prot.atol, "rtol": prot.rtol, "rule": "thr = atol + rtol * |w|^T|A||B|"},
             "clocks": clocks.summary(),
         }
+        if dist is not None:
+            verdict = exchanged.tolist()
+            entry["exchanged_status"] = {"detected": verdict[0], "fault_hit": verdict[1],
+                                         "max_res_over_thr": verdict[2], "max_abs_res": verdict[3],
+                                         "method": f"ring of per-step [detected, hit, max|res|/thr, max|res|], "
+                                                   f"MAX all-reduce every {EXCHANGE_EVERY} steps"}
         if rank == 0 and not args.no_detection:
-            entry["detection"] = detection_campaign(prot, args.flips, seed)
+            entry["detection"] = detection_campaign(prot, args.flips_per_bit, SEEDS[precision])
+            entry["fault_schedule"] = fault_schedule(prot, SEEDS[precision], gemms=args.schedule_gemms)
         if not args.no_e2e:  # every rank: its own shard end to end, time = max over ranks
-            host_a = torch.randn(m, k, dtype=torch.bfloat16).pin_memory()
-            host_b = torch.randn(n, k, dtype=torch.bfloat16).pin_memory()
-            w = prot.weights
-            e2e_run(precision, host_a, host_b, device, w, prot.nonfinite, prot.atol, prot.rtol, 3, stream)  # warm-up
+            host_a, host_b = host_operands(m, n, k, SEEDS[precision] + 1000 * rank)
+            host_a = host_a.pin_memory()
+            host_b_kn = host_b.T.contiguous().pin_memory()  # the public API's B is [K, N]
+            e2e_run(precision, host_a, host_b_kn, device, prot.atol, prot.rtol, 3, stream)  # warm-up
             e_steps = max(3, args.steps // 4)
             t0 = time.perf_counter()
-            e_time = e2e_run(precision, host_a, host_b, device, w, prot.nonfinite, prot.atol, prot.rtol, e_steps,
-                             stream)
+            e_time, d2h, e_flagged = e2e_run(precision, host_a, host_b_kn, device, prot.atol, prot.rtol, e_steps,
+                                             stream)
+            wall = (time.perf_counter() - t0) / e_steps
             if dist is not None:
                 t = torch.tensor([e_time], device=device)
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
                 e_time = float(t.item())
             entry["e2e"] = {"value": world * flops / e_time / 1e12, "unit": UNIT,
                             "h2d_bytes_per_step": world * (host_a.numel() * 2 + host_b.numel() * 2),
-                            "d2h_bytes_per_step": world * 5, "host_wall_s_per_step": (time.perf_counter() - t0) / e_steps,
-                            "pipeline": "step i+1's host-to-device copies overlap step i's compute (two buffer sets)"}
+                            "d2h_bytes_per_step": world * d2h, "host_wall_s_per_step": wall,
+                            "clean_steps_flagged": e_flagged,
+                            "api": "sdc_b200.abft.execute (quantise + protected GEMM + finalize), host buffers in "
+                                   "and out",
+                            "pipeline": "step i+1's host-to-device copies and step i's device-to-host copies "
+                                        "overlap the compute"}
         results[precision] = entry
         del prot
         torch.cuda.empty_cache()
     sweep = None if args.no_sweep else qwen_sweep(args, device, stream, rank, world, dist)
+    ceiling = None if (args.no_ceiling or rank != 0) else library_ceiling(device, stream)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
-    head = results.get("fp8_block") or results.get("fp8") or results["nvfp4"]
+    head_key = "fp8_block" if "fp8_block" in results else "fp8" if "fp8" in results else "nvfp4"
+    head = results[head_key]
     line = {
         "metric": METRIC, "value": head["tflops"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "e2m1" if head is results.get("nvfp4") else "e4m3", "data": "synthetic",
-        "config": {"workload": head["workload"] + " ABFT (Classic, K-slice input reference) + finalize",
-                   "per_gpu": head["workload"].split(" ")[1],
-                   "parallelism": f"M-shard x{world}, NCCL all-reduce of detection status",
-                   "l2": "working set (A+B codes, output) > 126 MB L2; no explicit flush"},
+        "vs_baseline": None, "dtype": "e2m1" if head_key == "nvfp4" else "e4m3", "data": "synthetic",
+        "config": bench_config(head_key, args.size or SIZES[head_key], world),
         "overhead_pct": head["overhead_pct"], "unprotected_tflops": head["unprotected_tflops"],
         "roofline": head["roofline"], "clocks": head["clocks"],
         "gpu_launches": LAUNCHES_PER_STEP * args.steps,
-        "e2e": head.get("e2e"), "detection": head.get("detection"),
+        "e2e": head.get("e2e"), "detection": head.get("detection"), "fault_schedule": head.get("fault_schedule"),
+        "thresholds": head["thresholds"],
     }
+    if "exchanged_status" in head:
+        line["exchanged_status"] = head["exchanged_status"]
     for key, name in (("fp8", "fp8_tensorwise"), ("nvfp4", "nvfp4")):
         if key in results and results[key] is not head:
             line[name] = results[key]
     if sweep is not None:
         line["qwen2.5_7b_linears"] = sweep
+    if ceiling is not None:
+        line["library_ceiling"] = ceiling
     if not args.no_cpu_baseline and world == 1:
-        line["cpu_baseline"] = cpu_baseline(args.cpu_sample_rows)
+        line["cpu_baseline"] = cpu_baseline(args.cpu_sample_rows, args.size or SIZES[head_key])
     sys.stdout.flush()
     os.write(result_fd, (json.dumps(line) + "\n").encode())
 
 
-def cpu_baseline(rows, min_seconds=10.0):
-    """The reference's CPU/torch ABFT path on rows of the 8192^3 workload
-    (all 8192 by default), repeated until about ``min_seconds`` of CPU work."""
+def reference_operands(precision, size, rows):
+    """The workload's operands as the reference's CPU path gets them: the same
+    seeded bf16 matrices, quantised by the oracle's restatement of the format
+    (bit-identical to the device quantiser) and dequantised to fp32. Returns
+    (A rows [rows, K] fp32, B [K, N] fp32)."""
+    import numpy as np
+
+    from oracle import quant
+
+    full_a, b = host_operands(size, size, size, SEEDS[precision])
+    full_a = full_a.float().numpy()
+    a = full_a[:rows]
+    b = b.float().numpy()
+    if precision == "fp8_block":
+        ca, sa = quant.quantize_fp8_block(a, 1)
+        cb, sb = quant.quantize_fp8_block(b, 128)
+        da, db = quant.dequantize_fp8_block(ca, sa, 1), quant.dequantize_fp8_block(cb, sb, 128)
+    elif precision == "fp8":
+        # The multiplier of A is the whole matrix's: amax over all rows.
+        ca, st_a = quant.quantize_fp8(a, float(quant.multiplier(full_a, "fp8")))
+        cb, st_b = quant.quantize_fp8(b)
+        da, db = quant.dequantize_fp8(ca, st_a), quant.dequantize_fp8(cb, st_b)
+    else:
+        ca, sa, st_a = quant.quantize_nvfp4(a, float(quant.multiplier(full_a, "nvfp4")))
+        cb, sb, st_b = quant.quantize_nvfp4(b)
+        da, db = quant.dequantize_nvfp4(ca, sa, st_a), quant.dequantize_nvfp4(cb, sb, st_b)
+    return torch.from_numpy(np.ascontiguousarray(da, np.float32)), torch.from_numpy(
+        np.ascontiguousarray(db.T, np.float32))
+
+
+def cpu_baseline(rows, size, min_seconds=10.0):
+    """The reference's CPU/torch ABFT path on rows of the headline workload's
+    dequantised operands, repeated until about ``min_seconds`` of CPU work."""
     from oracle import cpu_path
 
     torch.set_num_threads(os.cpu_count() or 1)
-    g = torch.Generator().manual_seed(0)
-    k = n = 8192
-    a = torch.randn(rows, k, generator=g)
-    b = torch.randn(k, n, generator=g)
+    rows = min(rows, size)
+    a, b = reference_operands("fp8_block", size, rows)
     cpu_path.execute(a[:64], b[:, :64], block_k=256)  # warm the BLAS
     calls = 0
     t0 = time.perf_counter()
     while True:
-        _, report, _ = cpu_path.execute(a, b, atol=1e-3, rtol=1e-4, block_k=256)
+        _, report, _ = cpu_path.execute(a, b, atol=ATOL, rtol=CALIBRATED_RTOL["fp8_block"], block_k=256)
         calls += 1
         seconds = time.perf_counter() - t0
         if seconds >= min_seconds:
             break
-    return {"value": 2.0 * rows * n * k * calls / seconds / 1e12, "unit": UNIT, "cores": torch.get_num_threads(),
-            "kind": "port", "sample": f"fp32 {rows}x{n}x{k} ({rows} of the 8192 rows of the workload), Classic, "
-                                      f"{calls} protected GEMMs in {seconds:.1f} s",
+    return {"value": 2.0 * rows * size * size * calls / seconds / 1e12, "unit": UNIT,
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"dequantised block-scaled fp32 {rows}x{size}x{size} ({rows} of the {size} rows of the "
+                      f"headline workload, same seed), Classic, {calls} protected GEMMs in {seconds:.1f} s",
             "detected": report["detected"]}
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     from oracle import cpu_path
 
     torch.set_num_threads(os.cpu_count() or 1)
-    rows, k, n = args.cpu_sample_rows, 8192, 8192
-    g = torch.Generator().manual_seed(0)
-    a = torch.randn(rows, k, generator=g)
-    b = torch.randn(k, n, generator=g)
-    for _ in range(max(1, min(args.warmup, 2))):
-        cpu_path.execute(a, b, atol=1e-3, rtol=1e-4)
-    steps = max(1, min(args.steps, 5))
+    precision = "fp8_block" if args.format == "all" else args.format
+    size = args.size or SIZES[precision]
+    rows = min(args.cpu_sample_rows, size)
+    a, b = reference_operands(precision, size, rows)
+    rtol = CALIBRATED_RTOL[precision] if args.rtol is None else args.rtol
+    for _ in range(args.warmup):
+        cpu_path.execute(a, b, atol=ATOL, rtol=rtol)
+    report = {"detected": False}
     t0 = time.perf_counter()
-    for _ in range(steps):
-        cpu_path.execute(a, b, atol=1e-3, rtol=1e-4)
-    seconds = (time.perf_counter() - t0) / steps
-    value = 2.0 * rows * n * k / seconds / 1e12
-    sample = f"fp32 {rows}x{n}x{k} ({rows} of the 8192 rows of the workload) per step"
+    for _ in range(args.steps):
+        # Each step is a whole protected GEMM: prepare (the input-side
+        # reference), collect and verify, as abft.execute does per call.
+        _, report, _ = cpu_path.execute(a, b, atol=ATOL, rtol=rtol)
+    seconds = (time.perf_counter() - t0) / max(args.steps, 1)
+    value = 2.0 * rows * size * size / seconds / 1e12
+    sample = (f"dequantised {FORMATS[precision][1].split(',')[0]} fp32 operands of the same seed, "
+              f"{rows}x{size}x{size} ({rows} of the {size} rows of the workload) per step")
     print(json.dumps({
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
-        "steps": steps, "warmup": args.warmup, "ms_per_step": seconds * 1e3, "higher_is_better": True,
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": seconds * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "impl": "reference",
-        "config": {"workload": "fp8 M=N=K=8192 block-scaled 1x128 / 128x128, bf16 out"
-                               " ABFT (Classic, K-slice input reference) + finalize",
-                   "reference_path": "abft.execute CPU path (reference_mm=torch.mm; the reference's only CPU "
-                                     "implementation computes the protected GEMM in fp32), restated in "
-                                     "oracle/cpu_path.py"},
+        "config": bench_config(precision, size, world),
+        "reference_path": "abft.execute CPU path (reference_mm=torch.mm; the reference's only CPU implementation "
+                          "computes the protected GEMM in fp32), restated in oracle/cpu_path.py",
+        "thresholds": {"atol": ATOL, "rtol": rtol}, "clean_detected": report["detected"],
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -648,6 +898,7 @@ def run_train(args):
     gemms_per_step = None
     per_layer = {}
     faults = detected = 0
+    fault_log = []
 
     def step():
         optimizer.zero_grad(set_to_none=True)
@@ -666,7 +917,8 @@ def run_train(args):
             return None
         call = first_call + hits[0] + 1
         bit = int(torch.randint(0, 32, (1,), generator=schedule))
-        protection.fault = parse_fault_config({"location": "accumulator", "row": int(torch.randint(0, 128, (1,), generator=schedule)),
+        protection.fault = parse_fault_config({"location": "accumulator",
+                                               "row": int(torch.randint(0, 128, (1,), generator=schedule)),
                                                "col": int(torch.randint(0, 128, (1,), generator=schedule)),
                                                "bit": bit, "call_index": call})
         return call
@@ -692,6 +944,9 @@ def run_train(args):
                     key = f"{layer}:{role}"
                     per_layer[key] = per_layer.get(key, 0) + 1
                     detected += 1
+                if hit:
+                    fault_log.append({"step": i - args.warmup, "layer": layer, "role": role, "detected": det,
+                                      "located": loc})
     end.record(stream)
     end.synchronize()
     elapsed = start.elapsed_time(end) / 1e3
@@ -705,7 +960,8 @@ def run_train(args):
     if rank != 0:
         return
     tokens_per_step = batch * seq * world
-    line = {"metric": "Qwen2.5-0.5B NVFP4 ABFT training step throughput", "value": tokens_per_step * args.steps / elapsed,
+    line = {"metric": "Qwen2.5-0.5B NVFP4 ABFT training step throughput",
+            "value": tokens_per_step * args.steps / elapsed,
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "e2m1", "data": "synthetic",
@@ -714,6 +970,7 @@ def run_train(args):
                        "micro_batch": batch, "seq_len": seq, "parallelism": f"dp{world}",
                        "protected_gemms_per_step": gemms_per_step, "fault_rate_per_gemm": args.fault_rate},
             "faults_injected": faults, "detections": detected, "detections_per_layer_role": per_layer,
+            "rank0_faults": fault_log,
             "loss_first": float(losses[0]), "loss_last": float(losses[-1])}
     sys.stdout.flush()
     os.write(result_fd, (json.dumps(line) + "\n").encode())
@@ -727,11 +984,14 @@ def main():
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--format", choices=["all", "fp8_block", "fp8", "nvfp4"], default="all",
                         help="fp8_block = config[1] (headline), fp8 = tensorwise FP8, nvfp4 = config[2]")
-    parser.add_argument("--flips", type=int, default=64)
+    parser.add_argument("--flips-per-bit", type=int, default=24)
+    parser.add_argument("--schedule-gemms", type=int, default=1000)
+    parser.add_argument("--rtol", type=float, default=None, help="override the calibrated relative threshold")
     parser.add_argument("--cpu-sample-rows", type=int, default=8192)
     parser.add_argument("--no-detection", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-ceiling", action="store_true", help="skip the library GEMM anchors")
     parser.add_argument("--no-sweep", action="store_true", help="skip the Qwen2.5-7B linear-shape sweep")
     parser.add_argument("--sweep-steps", type=int, default=10)
     parser.add_argument("--workload", choices=["gemm", "train"], default="gemm",
@@ -740,7 +1000,7 @@ def main():
     parser.add_argument("--seq-len", type=int, default=2048)
     parser.add_argument("--fault-rate", type=float, default=1e-4)
     parser.add_argument("--size", type=int, default=0,
-                        help="override M=N=K of both workloads (profiling captures; not a bench line)")
+                        help="override M=N=K of the workloads (profiling captures and CPU tests; not a bench line)")
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

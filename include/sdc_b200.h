@@ -52,10 +52,12 @@ enum sdc_reference_layout {
   /* predicted/magnitude[c, t, col] = contribution of the 64-wide K slices s
    * with s % Tm == t, summed over ALL rows. The sum over t equals the TILE
    * layout's sum over t (up to fp32 rounding); finalize is unchanged. The
-   * projection w^T A is one streaming pass over A before the GEMM, and the
-   * propagation runs inside the GEMM launch (one extra read of B, overlapped
-   * with the tensor-core mainloop) instead of ~C/32 of the GEMM on CUDA
-   * cores. */
+   * projection w^T A and the propagation run inside the GEMM launch (one
+   * extra read of A and of B, overlapped with the tensor-core mainloop)
+   * instead of ~C/32 of the GEMM on CUDA cores. The launch synchronises its
+   * CTAs twice, so two such launches must not run concurrently on one GPU
+   * (different streams): one of them would wait until its watchdog gives up
+   * and reports the call as detected. */
   SDC_LAYOUT_KSLICE = 1
 };
 

@@ -128,17 +128,19 @@ ReferenceProblem reference_problem(const GemmProblem& g, float* predicted, float
 }
 
 // Input-fused ABFT GEMM: TILE layout = per-tile projection, GEMM, then the
-// propagation on CUDA cores; K-SLICE layout = projection of A over all rows
-// (a streaming kernel), then the GEMM with the propagation fused into its
-// prediction warps.
+// propagation on CUDA cores; K-SLICE layout = one GEMM launch whose
+// prediction warps compute the projection of A and the propagation.
 int run_input_fused(GemmProblem g, float* predicted, float* magnitude, int layout, void* workspace,
                     size_t workspace_bytes, cudaStream_t stream) {
   SDC_REQUIRE(predicted != nullptr && magnitude != nullptr, "predicted/magnitude must not be null");
   const ReferenceProblem r = reference_problem(g, predicted, magnitude, layout, workspace, workspace_bytes);
   if (layout == SDC_LAYOUT_KSLICE) {
-    int rc = launch_kslice_projection(r, stream);
+    int rc = check_problem(r);
     if (rc != SDC_OK) return rc;
-    g.q_full = kslice_scratch(r).q_full;
+    const KsliceScratch scratch = kslice_scratch(r);
+    g.q_full = scratch.q_full;
+    g.q_part = scratch.q_part;
+    g.grid_sync = scratch.grid_sync;
     g.predicted = predicted;
     g.magnitude = magnitude;
     return launch_gemm(g, stream);

@@ -28,14 +28,19 @@
 //               across lanes, fixed-order sum across the four row quarters),
 //               non-finite check of the converted output, output store.
 //   prediction  (K-slice layout only; warps 6-9, wide kinds 12-15)
-//               input-side prediction, independent of the MMA pipeline: for
-//               the 64-wide K slices assigned to each of this CTA's tiles
-//               (slice % Tm == tile row), fma chains of the projection
-//               q_full[k][c][h] (w_c^T A for h = 0, |w_c|^T |A| for h = 1,
-//               written by a separate streaming kernel before this launch)
-//               with B[n, k] and |B[n, k]|. In total one extra pass over B,
-//               overlapped with the tensor-core mainloop; no CTA ever waits
-//               for another, so no co-residency is assumed.
+//               input-side prediction, independent of the MMA pipeline, in
+//               three phases separated by grid-wide barriers (every CTA is
+//               resident; each wait is bounded):
+//                 1. projection partials of A: each warp takes (64-wide K
+//                    chunk, 512-row band) items and writes
+//                    part[band][k][c][h] = sum over the band's rows of
+//                    w_c[row] * A[row, k] (h = 0) and |w_c| |A| (h = 1);
+//                 2. q_full[k][c][h] = sum over bands (ascending);
+//                 3. for the 64-wide K slices assigned to each of this CTA's
+//                    tiles (slice % Tm == tile row), fma chains of q_full
+//                    with B[n, k] and |q|, |B| (B rows read from L2).
+//               In total one extra pass over A and one over B, overlapped
+//               with the tensor-core mainloop.
 // Wide kinds run their roles on warpgroup boundaries and move registers with
 // setmaxnreg (warpgroup 0 down, the epilogue warpgroups up).
 // Epilogue semantics follow src/cutlass_gemm/csrc/abft/common/
@@ -153,9 +158,14 @@ struct Params {
   float* observed;
   int32_t* hit;
   int32_t padded_n;
-  const float* q_full;  // [K_pad][C][2]: full-M projection (h=0) and magnitude (h=1)
-  const uint8_t* b;     // B rows (NVFP4: and their scale atoms), read directly by
-  const uint8_t* sfb;   // the prediction warps
+  float* q_full;        // [K_pad][C][2]: full-M projection (h=0) and magnitude (h=1)
+  float* q_part;        // [bands][K_pad][C][2]: per-band partials
+  uint32_t* grid_sync;  // arrival counter of the prediction warpgroups (zeroed per launch)
+  int32_t q_bands;
+  const uint8_t* a;     // A operand rows (projection) and B rows (prediction),
+  const uint8_t* sfa;   // read directly by the prediction warps
+  const uint8_t* b;
+  const uint8_t* sfb;
   float* predicted;
   float* magnitude;
   int32_t* watchdog;
@@ -203,6 +213,42 @@ __device__ __forceinline__ float transpose_reduce(float (&x)[N], int lane) {
     }
   }
   return x[0];
+}
+
+constexpr int kBandRows = 512;  // rows per projection band (K-slice layout)
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid-wide barrier of the prediction warpgroups (thread ct == 0 of each CTA
+// arrives; all 128 threads leave together). Bounded: on timeout the CTA's
+// abort flag and the watchdog are set. Returns false when aborted.
+__device__ __forceinline__ bool prediction_grid_barrier(uint32_t* counter, uint32_t target, int ct,
+                                                        volatile int32_t* abort_flag, int32_t* watchdog,
+                                                        uint64_t limit_ns) {
+  named_barrier(2, 128);
+  if (ct == 0) {
+    __threadfence();
+    atomicAdd(counter, 1u);
+    const uint64_t start = global_ns();
+    while (ld_acquire_u32(counter) < target) {
+      if (*abort_flag) break;
+      if (global_ns() - start > limit_ns) {
+        atomicCAS(watchdog, 0, kWaitGrid);
+        *abort_flag = kWaitGrid;
+        break;
+      }
+      // Sparse polling: every CTA polls the same word, and the wait is off the
+      // tensor cores' critical path.
+      __nanosleep(4000);
+    }
+    __threadfence();
+  }
+  named_barrier(2, 128);
+  return *abort_flag == 0;
 }
 
 // Scale-factor atom (32 rows x 16 bytes, contiguous) as a tcgen05.cp source.
@@ -782,12 +828,9 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
     if (is_prediction_warp<WIDE>(warp)) {
       // ---------------- input-side prediction (4 warps) ----------------
       // Independent of the MMA pipeline: for each of this CTA's tiles, the
-      // slices s = mt, mt + Tm, ... (ascending) of the tile's B rows are
-      // folded into fma chains with the projection q_full = w^T A, which a
-      // separate kernel wrote before this launch (so no CTA waits for any
-      // other CTA). e4m3 kinds stage each slice in shared memory with a TMA
-      // copy; NVFP4 reads its B rows from L2 (the same column block is
-      // streaming through this SM for the MMA).
+      // slices s = mt, mt + Tm, ... (ascending) of the tile's 256 B rows are
+      // read from global memory (hot in L2: the same column block is streaming
+      // through this SM) and folded into fma chains with q_full.
       // 0..127: the tile's B rows ct (and ct + 128 for 256-wide tiles).
       const int ct = prediction_index<WIDE>(warp) * 32 + lane;
       constexpr int kRowsPerThread = kTN / 128;
@@ -795,10 +838,14 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
       const int num_slices = (p.k + kSliceK - 1) / kSliceK;
       const int64_t row_bytes = is_e4m3(KIND) ? p.k : p.k / 2;
       const int64_t k_atoms = (p.k + 63) / 64;
-      // Pacing: the prediction of the CTA's j-th tile starts once j of its
-      // tiles have left the epilogue, so this L2 traffic is spread over the
-      // launch instead of competing in one burst with the TMA loads that feed
-      // the tensor cores. A wait returns false once the CTA has aborted.
+      const int64_t k_pad = static_cast<int64_t>(num_slices) * kSliceK;
+      // Pacing: this work is spread over the CTA's tiles (projection during
+      // the first half, prediction during the second) instead of running in
+      // bursts, which would take L2 bandwidth from the TMA loads feeding the
+      // tensor cores. A wait returns false once the CTA has aborted.
+      const uint32_t my_tiles =
+          work_first < p.num_work ? static_cast<uint32_t>((p.num_work - 1 - work_first) / work_step + 1) : 0u;
+      const uint32_t half = my_tiles / 2;
       auto pace = [&](uint32_t target) -> bool {
         target += static_cast<uint32_t>(p.pace_extra);
         if (*tiles_done >= target) return true;
@@ -814,6 +861,127 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
         }
         return true;
       };
+      // ---- phase 1: per-band projection partials. Lane = 4 * l + g: k-group g
+      // (16 consecutive k), row lane l (rows band_start + l, + 8, ... ascending);
+      // the 8 row lanes combine as ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)).
+      {
+        const int g = lane & 3, l = lane >> 2;
+        const int64_t items = static_cast<int64_t>(num_slices) * p.q_bands;
+        const int64_t first_item = static_cast<int64_t>(blockIdx.x) * 4 + prediction_index<WIDE>(warp);
+        const int64_t item_step = static_cast<int64_t>(gridDim.x) * 4;
+        const int64_t my_items = first_item < items ? (items - 1 - first_item) / item_step + 1 : 0;
+        int64_t j = 0;
+        for (int64_t item = first_item; item < items && !*abort_flag; item += item_step, ++j) {
+          if (!pace(static_cast<uint32_t>(j * half / my_items))) break;
+          const int64_t chunk = item % num_slices, band = item / num_slices;
+          const int64_t k0 = chunk * kSliceK + g * 16;
+          // K % 16 == 0 (FP8) / % 32 == 0 (NVFP4): a group of 16 is all in or all out.
+          const bool k_in = k0 < p.k;
+          const int64_t row_end = min(static_cast<int64_t>(p.m), (band + 1) * kBandRows);
+          float2 enc[16], mg[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) enc[e] = mg[e] = make_float2(0.f, 0.f);
+          constexpr int kBatch = 4;
+          for (int64_t r0 = band * kBandRows + l; r0 < row_end; r0 += 8 * kBatch) {
+            uint4 raw[kBatch];
+            uint32_t sfv[kBatch];
+            float w[kBatch][C];
+#pragma unroll
+            for (int i = 0; i < kBatch; ++i) {
+              const int64_t row = r0 + 8 * i;
+              const bool row_in = row < row_end;
+              const bool in = row_in && k_in;
+              if constexpr (is_e4m3(KIND)) {
+                raw[i] = in ? __ldg(reinterpret_cast<const uint4*>(p.a + row * row_bytes + k0))
+                            : make_uint4(0, 0, 0, 0);
+                // Block-scaled: the row's scale of the 128-wide block holding these 16 k.
+                if constexpr (BLK) sfv[i] = in ? __float_as_uint(__ldg(p.sa + row * p.k_blocks + (k0 >> 7))) : 0u;
+              } else {
+                const uint2 u = in ? __ldg(reinterpret_cast<const uint2*>(p.a + row * row_bytes + k0 / 2))
+                                   : make_uint2(0, 0);
+                raw[i] = make_uint4(u.x, u.y, 0, 0);
+                const int64_t off = ((row >> 7) * k_atoms + (k0 >> 6)) * 512 + (row & 31) * 16 +
+                                    ((row >> 5) & 3) * 4 + ((k0 >> 4) & 3);
+                sfv[i] = in ? __ldg(p.sfa + off) : 0u;
+              }
+#pragma unroll
+              for (int c = 0; c < C; ++c) {
+                w[i][c] = row_in ? __ldg(p.weights + static_cast<int64_t>(c) * p.m + row) : 0.f;
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < kBatch; ++i) {
+              if (r0 + 8 * i >= row_end) break;
+              float v[16];
+              if constexpr (is_e4m3(KIND)) {
+                const uint32_t words[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const float2 lo = e4m3x2_to_float2(words[j] & 0xFFFFu), hi = e4m3x2_to_float2(words[j] >> 16);
+                  v[4 * j] = lo.x; v[4 * j + 1] = lo.y; v[4 * j + 2] = hi.x; v[4 * j + 3] = hi.y;
+                }
+                if constexpr (BLK) {
+                  const float scale = __uint_as_float(sfv[i]);
+#pragma unroll
+                  for (int e = 0; e < 16; ++e) v[e] = __fmul_rn(v[e], scale);
+                }
+              } else {
+                float lo8[8], hi8[8];
+                e2m1x8_to_float(raw[i].x, lo8);
+                e2m1x8_to_float(raw[i].y, hi8);
+                const float scale = decode_e4m3(sfv[i]);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  v[e] = lo8[e] * scale;
+                  v[8 + e] = hi8[e] * scale;
+                }
+              }
+              const float2 wv = make_float2(w[i][0], C == 2 ? w[i][C - 1] : 0.f);
+              const float2 wa = make_float2(fabsf(wv.x), fabsf(wv.y));
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                enc[e] = fma2(wv, make_float2(v[e], v[e]), enc[e]);
+                const float av = fabsf(v[e]);
+                mg[e] = fma2(wa, make_float2(av, av), mg[e]);
+              }
+            }
+          }
+#pragma unroll
+          for (int offset = 4; offset <= 16; offset <<= 1) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              enc[e].x += __shfl_xor_sync(0xffffffffu, enc[e].x, offset);
+              enc[e].y += __shfl_xor_sync(0xffffffffu, enc[e].y, offset);
+              mg[e].x += __shfl_xor_sync(0xffffffffu, mg[e].x, offset);
+              mg[e].y += __shfl_xor_sync(0xffffffffu, mg[e].y, offset);
+            }
+          }
+          if (l == 0) {
+            float* dst = p.q_part + (band * k_pad + chunk * kSliceK + g * 16) * C * 2;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              if constexpr (C == 2) {
+                reinterpret_cast<float4*>(dst)[e] = make_float4(enc[e].x, mg[e].x, enc[e].y, mg[e].y);
+              } else {
+                reinterpret_cast<float2*>(dst)[e] = make_float2(enc[e].x, mg[e].x);
+              }
+            }
+          }
+        }
+      }
+      // ---- phase 2: q_full = sum over bands (ascending) ----
+      if (prediction_grid_barrier(p.grid_sync, gridDim.x, ct, abort_flag, p.watchdog, p.wait_limit_ns)) {
+        const int64_t entries = k_pad * C * 2;
+        for (int64_t e = static_cast<int64_t>(blockIdx.x) * 128 + ct; e < entries;
+             e += static_cast<int64_t>(gridDim.x) * 128) {
+          float acc = __ldcg(p.q_part + e);
+          for (int b = 1; b < p.q_bands; ++b) acc += __ldcg(p.q_part + b * entries + e);
+          p.q_full[e] = acc;
+        }
+      }
+      prediction_grid_barrier(p.grid_sync, 2 * gridDim.x, ct, abort_flag, p.watchdog, p.wait_limit_ns);
+      // ---- phase 3: predictions of this CTA's tiles ----
+      const uint32_t last = my_tiles > 0 ? my_tiles - 1 : 0u;
       uint32_t jt = 0;
       uint32_t slices_staged = 0;  // B slices copied to shared memory (e4m3)
       bool copy_in_flight = false;  // thread ct == 0: a slice copy not yet seen landing
@@ -821,7 +989,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
       // Every decision to leave is taken by all 128 prediction threads
       // together (named_barrier_or), since the slice loop synchronises them.
       for (int t = work_first; t < p.num_work; t += work_step, ++jt) {
-        const bool paced = pace(jt);
+        const bool paced = pace(half + jt * (last > half ? last - half : 0u) / (my_tiles > 0 ? my_tiles : 1u));
         if (named_barrier_or(2, 128, !paced || *abort_flag != 0)) break;
         int mt, nt;
         work_coords<PAIR>(t, p, rank, mt, nt);
@@ -1063,6 +1231,11 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   p.hit = g.hit;
   p.padded_n = static_cast<int32_t>(g.padded_n);
   p.q_full = g.q_full;
+  p.q_part = g.q_part;
+  p.grid_sync = g.grid_sync;
+  p.q_bands = static_cast<int32_t>(ceil_div(g.m, kBandRows));
+  p.a = g.a;
+  p.sfa = g.sfa;
   p.b = g.b;
   p.sfb = g.sfb;
   p.predicted = g.predicted;
@@ -1117,11 +1290,21 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
     if (fit <= 0) return fail(SDC_ERR_CUDA, "GEMM kernel does not fit on this device");
     if (device >= 0 && device < 64) resident[device].store(fit, std::memory_order_release);
   }
-  // Persistent: at most one wave. No CTA waits for another CTA (the
-  // projection of A is a separate kernel), so correctness does not depend on
-  // every CTA being resident at once, e.g. beside a concurrent kernel.
-  const int units = std::min(p.num_work, fit);
+  const int units = std::min(p.num_work, fit);  // persistent: at most one wave
   config.gridDim = dim3(static_cast<unsigned>(PAIR ? 2 * units : units));
+  // The prediction warps synchronise across CTAs (two grid barriers around
+  // the projection), so every CTA must be resident: the grid never exceeds
+  // one wave of the occupancy computed above and single CTAs additionally
+  // launch cooperatively (a guarantee that cluster launches cannot combine
+  // with under the profiler). A CTA that cannot start because another kernel
+  // holds its SM (e.g. a second protected GEMM launched concurrently on
+  // another stream) leaves the others waiting at the barrier; every wait is
+  // bounded, and a launch that gives up is reported in-band as detected.
+  if constexpr (CHK && !PAIR) {
+    attribute[attrs].id = cudaLaunchAttributeCooperative;
+    attribute[attrs].val.cooperative = 1;
+    config.numAttrs = ++attrs;
+  }
   SDC_CUDA_CHECK(cudaLaunchKernelEx(&config, kernel, ta, tb, tsa, tsb, p));
   return SDC_OK;
 }
@@ -1155,6 +1338,7 @@ int launch_gemm(const GemmProblem& g, cudaStream_t stream) {
   if (g.channels > 0) {
     SDC_CUDA_CHECK(cudaMemsetAsync(g.hit, 0, sizeof(int32_t), stream));
     if (g.nonfinite != nullptr) SDC_CUDA_CHECK(cudaMemsetAsync(g.nonfinite, 0, sizeof(int32_t), stream));
+    if (g.grid_sync != nullptr) SDC_CUDA_CHECK(cudaMemsetAsync(g.grid_sync, 0, sizeof(uint32_t), stream));
   }
   if (g.kind == Kind::kFp8) {
     if (g.channels == 0) return dispatch_out<Kind::kFp8, 0>(g, stream);

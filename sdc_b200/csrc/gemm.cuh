@@ -29,9 +29,12 @@ struct GemmProblem {
   float* observed;         // [C, Tm, Np]
   int32_t* hit;
   int64_t padded_n;
-  // K-slice input prediction fused into the GEMM (null: not fused): the
-  // projection q_full [K_pad][C][2] written by launch_kslice_projection.
-  const float* q_full;
+  // K-slice input prediction fused into the GEMM (all null: not fused).
+  // Scratch from kslice_scratch(): q_full [K_pad][C][2], per-band partials
+  // and the grid-barrier counter (zeroed by launch_gemm).
+  float* q_full;
+  float* q_part;
+  uint32_t* grid_sync;
   float* predicted;        // [C, Tm, Np]
   float* magnitude;
 };
@@ -67,15 +70,12 @@ int check_problem(const ReferenceProblem& p);
 // their propagation against B on CUDA cores (after it).
 int launch_projection(const ReferenceProblem& p, cudaStream_t stream);
 int launch_tile_propagate(const ReferenceProblem& p, cudaStream_t stream);
-// K-slice layout: the projection's scratch inside the workspace.
+// K-slice layout: the GEMM's scratch inside the workspace.
 struct KsliceScratch {
-  float* q_full;  // [K_pad][C][2]
-  float* q_part;  // [ceil(M / 512)][K_pad][C][2] (M > 512 only)
+  uint32_t* grid_sync;  // 256 bytes, zeroed by launch_gemm
+  float* q_full;        // [K_pad][C][2]
+  float* q_part;        // [ceil(M / 512)][K_pad][C][2]
 };
 KsliceScratch kslice_scratch(const ReferenceProblem& p);
-// K-slice layout, before the GEMM: q_full = w^T A and |w|^T |A| over all rows
-// in the fixed order the C oracle restates (512-row bands of 8 interleaved
-// row lanes, bands ascending).
-int launch_kslice_projection(const ReferenceProblem& p, cudaStream_t stream);
 
 }  // namespace sdc

@@ -15,10 +15,10 @@
 // KSLICE layout (fast path). q is the projection over ALL rows, and the
 // 64-wide K slice s contributes to slot s % Tm:
 //   predicted[c, t, n] = alpha * sum_{s % Tm == t} sum_{k in s} q_c[k] B[n,k]
-// q is computed here by a streaming pass over A (kslice_project +
-// kslice_band_sum, before the GEMM); the propagation runs inside the GEMM
-// (gemm.cu, prediction warps). The per-column sum over slots equals the TILE
-// layout's sum over tiles up to fp32 rounding, so finalize is unchanged.
+// Both q and the propagation run inside the GEMM (gemm.cu, prediction
+// warps); this file only sizes and lays out their scratch. The per-column
+// sum over slots equals the TILE layout's sum over tiles up to fp32
+// rounding, so finalize is unchanged.
 #include <algorithm>
 
 #include "gemm.cuh"
@@ -258,184 +258,24 @@ int tile_propagate_impl(const ReferenceProblem& p, cudaStream_t stream) {
 }  // namespace
 
 namespace {
-constexpr int64_t kBandRows = 512;  // rows per projection band
-constexpr int kSliceK = 64;         // K elements per slice
-constexpr int kProjWarps = 8;       // warps (items) per kslice_project block
+constexpr int64_t kSyncBytes = 256;
+constexpr int64_t kBandRows = 512;  // rows per projection band (gemm.cu)
 int64_t kslice_q_floats(int channels, int64_t k) { return static_cast<int64_t>(channels) * 2 * ceil_div(k, 64) * 64; }
-int64_t kslice_bands(int64_t m) { return ceil_div(m, kBandRows); }
-
-// One warp per (64-wide K chunk, 512-row band) item; consecutive warps take
-// consecutive chunks of one band, so a block reads 512 contiguous bytes
-// (e4m3) of every row it visits. Lane = 4 * l + g: k-group g (16 consecutive
-// k), row lane l (rows band_start + l, + 8, ... ascending, one fma chain per
-// lane); the 8 row lanes are combined as
-// ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)) by xor shuffles.
-// part[band][k][c][h]: h = 0 the signed projection sum w_c A, h = 1 |w_c| |A|.
-// kFp8Block values are the dequantised fl(code * scale_a[row][k / 128]);
-// NVFP4 values are code * ue4m3 block scale (exact).
-template <Kind KIND, int C>
-__global__ void __launch_bounds__(32 * kProjWarps)
-    kslice_project(const uint8_t* a, const uint8_t* sfa, int64_t m, int64_t k, const float* weights,
-                   float* part, int64_t num_slices, int64_t bands) {
-  const int lane = threadIdx.x & 31;
-  const int64_t item = static_cast<int64_t>(blockIdx.x) * kProjWarps + (threadIdx.x >> 5);
-  if (item >= num_slices * bands) return;
-  const int g = lane & 3, l = lane >> 2;
-  const int64_t chunk = item % num_slices, band = item / num_slices;
-  const int64_t k0 = chunk * kSliceK + g * 16;
-  // K % 16 == 0 (e4m3) / % 32 == 0 (NVFP4): a group of 16 is all in or all
-  // out; groups past K contribute zeros, so q is zero-padded to the slice.
-  const bool k_in = k0 < k;
-  const int64_t row_bytes = is_e4m3(KIND) ? k : k / 2;
-  const int64_t k_atoms = (k + 63) / 64;
-  const int64_t k_blocks = k / 128;
-  const int64_t row_end = min(m, (band + 1) * kBandRows);
-  float2 enc[16], mg[16];
-#pragma unroll
-  for (int e = 0; e < 16; ++e) enc[e] = mg[e] = make_float2(0.f, 0.f);
-  constexpr int kBatch = 8;  // rows per lane with loads in flight together
-  for (int64_t r0 = band * kBandRows + l; r0 < row_end; r0 += 8 * kBatch) {
-    uint4 raw[kBatch];
-    uint32_t sfv[kBatch];
-    float w[kBatch][C];
-#pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-      const int64_t row = r0 + 8 * i;
-      const bool row_in = row < row_end;
-      const bool in = row_in && k_in;
-      if constexpr (is_e4m3(KIND)) {
-        raw[i] = in ? __ldg(reinterpret_cast<const uint4*>(a + row * row_bytes + k0)) : make_uint4(0, 0, 0, 0);
-        if constexpr (KIND == Kind::kFp8Block) {
-          sfv[i] = in ? __float_as_uint(__ldg(reinterpret_cast<const float*>(sfa) + row * k_blocks + (k0 >> 7))) : 0u;
-        }
-      } else {
-        const uint2 u = in ? __ldg(reinterpret_cast<const uint2*>(a + row * row_bytes + k0 / 2)) : make_uint2(0, 0);
-        raw[i] = make_uint4(u.x, u.y, 0, 0);
-        sfv[i] = in ? __ldg(sfa + sf_off(row, k0 >> 4, k_atoms)) : 0u;
-      }
-#pragma unroll
-      for (int c = 0; c < C; ++c) w[i][c] = row_in ? __ldg(weights + static_cast<int64_t>(c) * m + row) : 0.f;
-    }
-#pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-      if (r0 + 8 * i >= row_end) break;
-      float v[16];
-      if constexpr (is_e4m3(KIND)) {
-        const uint32_t words[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 lo = e4m3x2_to_float2(words[j] & 0xFFFFu), hi = e4m3x2_to_float2(words[j] >> 16);
-          v[4 * j] = lo.x; v[4 * j + 1] = lo.y; v[4 * j + 2] = hi.x; v[4 * j + 3] = hi.y;
-        }
-        if constexpr (KIND == Kind::kFp8Block) {
-          const float scale = __uint_as_float(sfv[i]);
-#pragma unroll
-          for (int e = 0; e < 16; ++e) v[e] = __fmul_rn(v[e], scale);
-        }
-      } else {
-        float lo8[8], hi8[8];
-        e2m1x8_to_float(raw[i].x, lo8);
-        e2m1x8_to_float(raw[i].y, hi8);
-        const float scale = decode_e4m3(sfv[i]);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          v[e] = lo8[e] * scale;
-          v[8 + e] = hi8[e] * scale;
-        }
-      }
-      const float2 wv = make_float2(w[i][0], C == 2 ? w[i][C - 1] : 0.f);
-      const float2 wa = make_float2(fabsf(wv.x), fabsf(wv.y));
-#pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        enc[e] = fma2(wv, make_float2(v[e], v[e]), enc[e]);
-        const float av = fabsf(v[e]);
-        mg[e] = fma2(wa, make_float2(av, av), mg[e]);
-      }
-    }
-  }
-#pragma unroll
-  for (int offset = 4; offset <= 16; offset <<= 1) {
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      enc[e].x += __shfl_xor_sync(0xffffffffu, enc[e].x, offset);
-      enc[e].y += __shfl_xor_sync(0xffffffffu, enc[e].y, offset);
-      mg[e].x += __shfl_xor_sync(0xffffffffu, mg[e].x, offset);
-      mg[e].y += __shfl_xor_sync(0xffffffffu, mg[e].y, offset);
-    }
-  }
-  if (l == 0) {
-    float* dst = part + (band * num_slices * kSliceK + chunk * kSliceK + g * 16) * C * 2;
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      if constexpr (C == 2) {
-        reinterpret_cast<float4*>(dst)[e] = make_float4(enc[e].x, mg[e].x, enc[e].y, mg[e].y);
-      } else {
-        reinterpret_cast<float2*>(dst)[e] = make_float2(enc[e].x, mg[e].x);
-      }
-    }
-  }
-}
-
-// q_full[e] = part[0][e] + part[1][e] + ... (bands ascending, one thread per entry).
-__global__ void __launch_bounds__(256)
-    kslice_band_sum(const float* part, float* q_full, int64_t entries, int64_t bands) {
-  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < entries;
-       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    float acc = __ldg(part + e);
-    for (int64_t b = 1; b < bands; ++b) acc += __ldg(part + b * entries + e);
-    q_full[e] = acc;
-  }
-}
-
-template <Kind KIND, int C>
-int kslice_projection_impl(const ReferenceProblem& p, float* q_full, float* q_part, cudaStream_t stream) {
-  const int64_t num_slices = ceil_div(p.k, kSliceK);
-  const int64_t bands = kslice_bands(p.m);
-  // One band: its partials are the projection itself.
-  float* part = bands == 1 ? q_full : q_part;
-  const int64_t items = num_slices * bands;
-  kslice_project<KIND, C><<<static_cast<unsigned>(ceil_div(items, kProjWarps)), 32 * kProjWarps, 0, stream>>>(
-      p.a, p.sfa, p.m, p.k, p.weights, part, num_slices, bands);
-  SDC_CUDA_CHECK(cudaGetLastError());
-  if (bands > 1) {
-    const int64_t entries = kslice_q_floats(C, p.k);
-    const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(ceil_div(entries, 256), 1184));
-    kslice_band_sum<<<blocks, 256, 0, stream>>>(q_part, q_full, entries, bands);
-    SDC_CUDA_CHECK(cudaGetLastError());
-  }
-  return SDC_OK;
-}
 }  // namespace
 
 size_t reference_workspace_bytes(int channels, int64_t m, int64_t n, int64_t k, int layout) {
   (void)n;
   if (layout == SDC_LAYOUT_KSLICE) {
-    const int64_t bands = kslice_bands(m);
-    const int64_t floats = kslice_q_floats(channels, k) * (1 + (bands > 1 ? bands : 0));
-    return static_cast<size_t>(floats * static_cast<int64_t>(sizeof(float)));
+    const int64_t floats = kslice_q_floats(channels, k) * (1 + ceil_div(m, kBandRows));
+    return static_cast<size_t>(kSyncBytes + floats * static_cast<int64_t>(sizeof(float)));
   }
   return static_cast<size_t>(q_floats(channels, m, k)) * sizeof(float);
 }
 
 KsliceScratch kslice_scratch(const ReferenceProblem& p) {
-  float* q_full = static_cast<float*>(p.workspace);
-  return {q_full, q_full + kslice_q_floats(p.channels, p.k)};
-}
-
-int launch_kslice_projection(const ReferenceProblem& p, cudaStream_t stream) {
-  int rc = check_problem(p);
-  if (rc != SDC_OK) return rc;
-  const KsliceScratch scratch = kslice_scratch(p);
-  if (p.kind == Kind::kFp8) {
-    return p.channels == 2 ? kslice_projection_impl<Kind::kFp8, 2>(p, scratch.q_full, scratch.q_part, stream)
-                           : kslice_projection_impl<Kind::kFp8, 1>(p, scratch.q_full, scratch.q_part, stream);
-  }
-  if (p.kind == Kind::kFp8Block) {
-    return p.channels == 2 ? kslice_projection_impl<Kind::kFp8Block, 2>(p, scratch.q_full, scratch.q_part, stream)
-                           : kslice_projection_impl<Kind::kFp8Block, 1>(p, scratch.q_full, scratch.q_part, stream);
-  }
-  return p.channels == 2 ? kslice_projection_impl<Kind::kNvf4, 2>(p, scratch.q_full, scratch.q_part, stream)
-                         : kslice_projection_impl<Kind::kNvf4, 1>(p, scratch.q_full, scratch.q_part, stream);
+  uint8_t* base = static_cast<uint8_t*>(p.workspace);
+  float* q_full = reinterpret_cast<float*>(base + kSyncBytes);
+  return {reinterpret_cast<uint32_t*>(base), q_full, q_full + kslice_q_floats(p.channels, p.k)};
 }
 
 int check_problem(const ReferenceProblem& p) {

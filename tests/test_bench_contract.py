@@ -13,7 +13,7 @@ ROOT = Path(__file__).resolve().parents[1]
 def test_reference_arm_prints_one_contract_line():
     proc = subprocess.run(
         [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "0",
-         "--cpu-sample-rows", "16"],
+         "--cpu-sample-rows", "16", "--size", "512"],
         cwd=ROOT, capture_output=True, text=True, timeout=600)
     assert proc.returncode == 0, proc.stderr[-2000:]
     lines = [line for line in proc.stdout.splitlines() if line.strip()]
