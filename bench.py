@@ -58,10 +58,13 @@ import torch  # noqa: E402
 
 METRIC = "ABFT NVFP4/FP8 GEMM TFLOPS, % overhead vs unprotected, detection recall"
 UNIT = "TFLOPS"
-# Relative thresholds of the benchmark's detector, per format, calibrated
-# from the clean residual margins measured over 1000 clean GEMMs at the
-# configuration's shape (the bench reports the margin it sees in every run).
-CALIBRATED_RTOL = {"fp8_block": 5e-8, "fp8": 5e-8, "nvfp4": 5e-8}
+# Relative thresholds of the benchmark's detector, per format. Calibrated on
+# B200 from 1000 clean GEMMs per format at the configuration's shape, each on
+# fresh seeded operands: the largest clean max |res| / |w|^T|A||B| was
+# 6.5e-10 (block-scaled FP8 8192^3), 9.2e-10 (tensorwise FP8 8192^3) and
+# 3.7e-10 (NVFP4 16384^3), so rtol = 1e-8 keeps a safety factor of at least
+# 10.8 (every run reports the margin it measures again in "fault_schedule").
+CALIBRATED_RTOL = {"fp8_block": 1e-8, "fp8": 1e-8, "nvfp4": 1e-8}
 ATOL = 1e-3
 SEEDS = {"fp8_block": 1, "fp8": 3, "nvfp4": 2}
 SIZES = {"fp8_block": 8192, "fp8": 8192, "nvfp4": 16384}
@@ -543,10 +546,23 @@ def library_ceiling(device, stream):
 
     measure("fp8_tensorwise_8192_bf16out", lambda: torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one,
                                                                      out_dtype=torch.bfloat16), flops)
+    # 1 x 128 activation and 128 x 128 weight scales: the scale layouts the
+    # library accepts differ between versions, so the known forms are tried.
     sa = torch.rand(size, size // 128, device=device) + 0.5
     sb = torch.rand(size // 128, size // 128, device=device) + 0.5
-    measure("fp8_blockwise_1x128_128x128_8192_bf16out",
-            lambda: torch._scaled_mm(a, b.t(), scale_a=sa, scale_b=sb.t(), out_dtype=torch.bfloat16), flops)
+    forms = (("row-major", lambda: (sa, sb)), ("a outer-dim-major", lambda: (sa.t().contiguous().t(), sb)),
+             ("both outer-dim-major", lambda: (sa.t().contiguous().t(), sb.t().contiguous().t())))
+    name = "fp8_blockwise_1x128_128x128_8192_bf16out"
+    errors = []
+    for form, scales in forms:
+        s_a, s_b = scales()
+        measure(name, lambda: torch._scaled_mm(a, b.t(), scale_a=s_a, scale_b=s_b, out_dtype=torch.bfloat16), flops)
+        if "tflops" in out[name]:
+            out[name]["scale_form"] = form
+            break
+        errors.append(f"{form}: {out[name]['error']}")
+    else:
+        out[name] = {"error": "; ".join(errors)}
     del a, b
     n4 = 16384
     try:
