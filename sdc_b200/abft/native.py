@@ -1,77 +1,116 @@
-"""Native ABFT executions: fused sm_100a GEMM + device finalize.
+"""Native executions: the fused sm_100a GEMM, the device finalize and locator.
 
-Mirrors src/abft/native.py of the reference (``_execute_native``,
-``execute_input_fused``, the builtin-weight cache and ``_tensors``): the host
-resolves the method's compiled policy once, the kernels never call Python
-hooks, and every decision stays a device tensor until the caller asks for it
-(``bool(detected)`` is the one host read, taken only when recovery or
-``on_error="raise"`` needs it). Extensions over the reference:
+The host resolves the method's compiled policy once per call; the kernels
+never call back into Python, and every decision stays a device tensor until
+a caller asks for it (recovery and ``on_error="raise"`` are the only host
+reads). One call is:
 
-* the prediction layout (``AbftConfig.reference_layout``) is passed to the
-  GEMM op; "kslice" computes the prediction inside the GEMM;
-* ``AbftConfig.locate`` runs the device Classic locator after finalize
-  (policy 0 only), filling ``located``/``location``;
-* ``recovery="correct"`` recomputes just the located element on the device
-  and falls back to the reference's full recompute + recheck otherwise.
+1. the builtin projection weights W [C, M] (``WeightCache``: made once per
+   policy, device and M, shared across streams with an event);
+2. the input-fused GEMM (``reference_layout`` "tile": the reference's
+   per-M-tile predicted partials; "kslice": computed inside the GEMM launch)
+   with the epilogue fault, if this call's fault fires;
+3. the device finalize (threshold atol + rtol * magnitude, or the method's
+   own thresholds), then optionally the device ratio locator (policy 0);
+4. on detection with ``recovery``: either the located element recomputed on
+   the device (``"correct"``), or a full recompute judged against the first
+   call's reference (``"recompute"``, and ``"correct"`` when nothing was
+   located); then the engine's shared tail (commit, diagnostics, raise).
 """
 from __future__ import annotations
 
 import time
 from collections import OrderedDict
-from contextlib import contextmanager, nullcontext
 from threading import Lock
 
 import torch
 
+from .engine import AbftReport, _finish, _injection, _Plan, _selected, _Timer, call_context
 from .methods import Classic, Sum, get_method
 
-_weights = OrderedDict()
-_weights_lock = Lock()
-_MAX_WEIGHT_ENTRIES = 32
-_MAX_WEIGHT_BYTES = 16 * 1024 * 1024
 
+class WeightCache:
+    """Least-recently-used cache of the builtin projection weights, bounded
+    by entry count and bytes. An entry remembers the stream that made it: a
+    consumer on another stream first waits for that work (event) and marks
+    the tensor as used on its own stream."""
 
-def _builtin_weights(method, prepared, cfg, policy):
-    """Projection weights for the builtin formulas, cached per (policy, stream,
-    m); plugin or overridden preparations are never cached."""
-    custom = any(name in vars(method) for name in ("projection_weights", "prepare_fused"))
-    if type(method) not in {Classic, Sum} or method.stateful or custom:
-        return method.prepare_fused(prepared, cfg)
-    device = torch.device(prepared.a.device)
-    stream = torch.cuda.current_stream(device)
-    key = (policy.algorithm, stream.device.index, prepared.m)
-    with _weights_lock:
-        entry = _weights.pop(key, None)
-        if entry is None:
-            weights = method.projection_weights(prepared).to(torch.float32).contiguous()
-            ready = torch.cuda.Event()
-            ready.record(stream)
-            entry = (weights, ready, stream.cuda_stream)
-        weights, ready, owner = entry
-        if weights.numel() * 4 <= _MAX_WEIGHT_BYTES:
-            _weights[key] = entry
-            while (len(_weights) > _MAX_WEIGHT_ENTRIES or
-                   sum(item[0].numel() * 4 for item in _weights.values()) > _MAX_WEIGHT_BYTES):
-                _weights.popitem(last=False)
-        if owner != stream.cuda_stream:
+    def __init__(self, max_entries=32, max_bytes=16 * 1024 * 1024):
+        self.max_entries, self.max_bytes = max_entries, max_bytes
+        self._entries = OrderedDict()  # key -> (weights, ready event, producing stream handle)
+        self._lock = Lock()
+
+    def peek(self, key):
+        with self._lock:
+            entry = self._entries.get(key)
+            return None if entry is None else entry[0]
+
+    def weights(self, method, prepared, policy):
+        device = torch.device(prepared.a.device)
+        stream = torch.cuda.current_stream(device)
+        key = (policy.algorithm, stream.device.index, prepared.m)
+        with self._lock:
+            entry = self._entries.pop(key, None)
+            if entry is None:
+                made = method.projection_weights(prepared).to(torch.float32).contiguous()
+                ready = torch.cuda.Event()
+                ready.record(stream)
+                entry = (made, ready, stream.cuda_stream)
+            if entry[0].numel() * 4 <= self.max_bytes:
+                self._entries[key] = entry
+                self._evict()
+        weights, ready, producer = entry
+        if producer != stream.cuda_stream:
             stream.wait_event(ready)
             weights.record_stream(stream)
-    return {"weights": weights, "m": prepared.m, "n": prepared.n}
+        return weights
+
+    def _evict(self):
+        while len(self._entries) > self.max_entries or sum(
+                item[0].numel() * 4 for item in self._entries.values()) > self.max_bytes:
+            self._entries.popitem(last=False)
 
 
-def _tensors(finalized, diagnostics):
-    reference, residual, threshold, flags, hit, location = finalized
+WEIGHTS = WeightCache()
+
+
+def _method_state(method, prepared, cfg, policy):
+    """Weights (and optional thresholds) of this call. Only unmodified
+    builtin methods use the cache; plugins prepare their own."""
+    customised = any(hook in vars(method) for hook in ("projection_weights", "prepare_fused"))
+    if type(method) in {Classic, Sum} and not method.stateful and not customised:
+        return {"weights": WEIGHTS.weights(method, prepared, policy), "m": prepared.m, "n": prepared.n}
+    return method.prepare_fused(prepared, cfg)
+
+
+def _check_state(state, prepared, policy):
+    weights = state["weights"]
+    if (weights.ndim != 2 or weights.shape != (policy.channels, prepared.m) or weights.dtype != torch.float32
+            or weights.device != prepared.a.device or not weights.is_contiguous()):
+        raise ValueError("Native method weights do not match compiled policy channels/format/device")
+    thresholds = state.get("thresholds")
+    if thresholds is not None and (not isinstance(thresholds, torch.Tensor) or thresholds.dtype != torch.float32
+                                   or thresholds.device != prepared.a.device or not thresholds.is_contiguous()
+                                   or thresholds.shape not in {(1,), (policy.channels, prepared.n)}):
+        raise ValueError("Native method thresholds must be contiguous FP32 [1] or [channels,N] on the operand "
+                         "device")
+    return weights, thresholds
+
+
+def _decisions(packet, statistics):
+    """Report tensors from a finalize packet (reference, residual, threshold,
+    flags, hit, location)."""
+    reference, residual, threshold, flags, hit, location = packet
     detected, nonfinite, located, recovered, recheck_failed = flags.unbind()
-    tensors = dict(detected=detected, nonfinite=nonfinite, located=located, recovered=recovered,
-                   recheck_failed=recheck_failed, fault_hit=hit, location=location)
-    if diagnostics:
+    tensors = {"detected": detected, "nonfinite": nonfinite, "located": located, "recovered": recovered,
+               "recheck_failed": recheck_failed, "fault_hit": hit, "location": location}
+    if statistics:
         tensors.update(residual=residual, threshold=threshold)
     return reference, tensors, (residual, threshold, flags)
 
 
-def _execute_native(prepared, cfg, fault, context, *, method=None, policy=None, profile_scope=None):
+def execute_input_fused(prepared, cfg, fault, context, *, method=None, policy=None, profile_scope=None):
     from .. import ops, require_device
-    from .engine import AbftError, AbftReport, _commit_method, _report_context, _selected
 
     if method is None:
         method = get_method(cfg.method)
@@ -80,107 +119,54 @@ def _execute_native(prepared, cfg, fault, context, *, method=None, policy=None, 
     policy = method.validate_execution(prepared, cfg) if policy is None else policy
     if cfg.reference_mode != "input_fused":
         raise NotImplementedError("native executions on B200 use the input_fused reference")
-    algorithm = policy.algorithm
-    locate = cfg.locate and algorithm == 0
-    need_statistics = cfg.diagnostics or method.needs_diagnostics or locate
+    locate = cfg.locate and policy.algorithm == 0
+    statistics = cfg.diagnostics or method.needs_diagnostics or locate
     require_device(prepared.a.device)
-    selected = _selected(fault, context)
-    injection = (-1, -1, -1)
-    if selected:
-        if fault.location != "accumulator":
-            raise ValueError("native fused GEMM accepts only accumulator faults")
-        if fault.row >= prepared.m or fault.col >= prepared.n or fault.bit >= 32:
-            raise ValueError("Accumulator fault coordinate/bit outside FP32 output")
-        injection = (fault.row, fault.col, fault.bit)
+    plan = _Plan(prepared, cfg, fault, context, method, policy, _selected(fault, context))
+    injection = _injection(prepared, fault, plan.selected, accumulator_only=True)
+    timer = _Timer(cfg.timing, prepared.a.device, profile_scope)
     started = time.perf_counter()
-    events = []
-    scope = profile_scope or nullcontext
 
-    @contextmanager
-    def phase(name):
-        with scope("abft." + name):
-            mark = None
-            if cfg.timing and prepared.a.is_cuda:
-                mark = torch.cuda.Event(enable_timing=True)
-                mark.record(torch.cuda.current_stream(prepared.a.device))
-            yield
-            if mark is not None:
-                end = torch.cuda.Event(enable_timing=True)
-                end.record(torch.cuda.current_stream(prepared.a.device))
-                events.append((name, mark, end))
+    with timer.phase("reference"):
+        plan.state = _method_state(method, prepared, cfg, policy)
+        weights, thresholds = _check_state(plan.state, prepared, policy)
 
-    with phase("reference"):
-        state = _builtin_weights(method, prepared, cfg, policy)
-        weights = state["weights"]
-        if (weights.ndim != 2 or weights.shape != (policy.channels, prepared.m) or
-                weights.dtype != torch.float32 or weights.device != prepared.a.device or
-                not weights.is_contiguous()):
-            raise ValueError("Native method weights do not match compiled policy channels/format/device")
-        thresholds = state.get("thresholds")
-        if thresholds is not None and (
-            not isinstance(thresholds, torch.Tensor) or thresholds.dtype != torch.float32 or
-            thresholds.device != prepared.a.device or not thresholds.is_contiguous() or
-            thresholds.shape not in {(1,), (policy.channels, prepared.n)}
-        ):
-            raise ValueError("Native method thresholds must be contiguous FP32 [1] or [channels,N] on the operand device")
-        finalize_args = (algorithm, thresholds)
-
-    def run(fault_tuple):
+    def gemm(injected):
         nonfinite = torch.empty(1, device=prepared.a.device, dtype=torch.int32)
         output, observed, hit, predicted, magnitude = prepared.collected_reference_native(
-            weights, fault_tuple, algorithm=algorithm, nonfinite=nonfinite, layout=cfg.reference_layout)
+            weights, injected, algorithm=policy.algorithm, nonfinite=nonfinite, layout=cfg.reference_layout)
         return output, (observed, predicted, magnitude, hit, nonfinite)
 
-    def finalize(evidence, first_reference):
-        return ops.abft_finalize_reference(*evidence, prepared.n, cfg.atol, cfg.rtol, first_reference,
-                                           need_statistics, *finalize_args)
+    def finalize(evidence, reference):
+        return ops.abft_finalize_reference(*evidence, prepared.n, cfg.atol, cfg.rtol, reference, statistics,
+                                           policy.algorithm, thresholds)
 
-    with phase("execute"):
-        output, evidence = run(injection)
-    with phase("finalize"):
-        reference, tensors, (residual, threshold, flags) = _tensors(finalize(evidence, None), need_statistics)
-    if locate:
-        with phase("locate"):
-            location, located = ops.abft_locate(residual, threshold, flags, prepared.m)
-            tensors.update(location=location, located=located)
-    state = {**state, "reference": reference}
+    with timer.phase("execute"):
+        output, evidence = gemm(injection)
+    with timer.phase("finalize"):
+        first_reference, tensors, (residual, threshold, flags) = _decisions(finalize(evidence, None), statistics)
     del evidence
-    report_context = _report_context(prepared, cfg, fault, context, selected, output, method)
-    report_context["reference_operand_reuse"] = "mainloop_shared_operands"
-    report_context["threshold_source"] = "method_state" if thresholds is not None else "config_atol_rtol"
-    report = AbftReport(tensors, report_context, cfg.method, "input_fused_native", events)
-    if cfg.recovery in {"recompute", "correct"} and bool(tensors["detected"].item()):
-        with phase("recover_recheck"):
-            if cfg.recovery == "correct" and locate and bool(tensors["located"].item()):
-                correct = (ops.abft_fp8_block_correct if getattr(prepared, "blockwise", False) else
-                           ops.abft_fp8_correct if prepared.precision == "fp8" else ops.abft_nvfp4_correct)
-                corrected = correct(*prepared._native_args(), tensors["location"], tensors["located"], output)
-                tensors["recovered"] = corrected
-                tensors["recheck_failed"] = ~corrected
-                report.context["recovery_action"] = "located_element_recomputed"
-            else:
-                replacement, retry_evidence = run((-1, -1, -1))
-                _, checked, _ = _tensors(finalize(retry_evidence, reference), need_statistics)
-                tensors["recheck_failed"] = checked["detected"]
-                tensors["recovered"] = ~checked["detected"]
-                if need_statistics:
-                    tensors["retry_residual"] = checked["residual"]
-                if not bool(checked["detected"].item()):
-                    output = replacement
-                report.context["recovery_action"] = "full_recompute"
-    with phase("state_update") if method.stateful or method.needs_diagnostics else nullcontext():
-        _commit_method(method, state, tensors, context, prepared)
-    if not cfg.diagnostics:
-        for key in ("residual", "threshold", "retry_residual"):
-            tensors.pop(key, None)
-    should_raise = (cfg.on_error == "raise" and bool(tensors["detected"].item())
-                    and not bool(tensors["recovered"].item()))
-    report.host_seconds = time.perf_counter() - started
-    if should_raise:
-        raise AbftError(report)
-    return output, report
+    if locate:
+        with timer.phase("locate"):
+            tensors["location"], tensors["located"] = ops.abft_locate(residual, threshold, flags, prepared.m)
+    plan.state = {**plan.state, "reference": first_reference}
+    described = call_context(prepared, cfg, fault, context, plan.selected, output, method)
+    described["reference_operand_reuse"] = "mainloop_shared_operands"
+    described["threshold_source"] = "method_state" if thresholds is not None else "config_atol_rtol"
+    report = AbftReport(tensors, described, cfg.method, "input_fused_native", timer.events)
 
+    def recheck():
+        if cfg.recovery == "correct" and locate and bool(tensors["located"].item()):
+            # Only the located element is recomputed, in place.
+            correct = (ops.abft_fp8_block_correct if getattr(prepared, "blockwise", False) else
+                       ops.abft_fp8_correct if prepared.precision == "fp8" else ops.abft_nvfp4_correct)
+            fixed = correct(*prepared._native_args(), tensors["location"], tensors["located"], output)
+            tensors["recovered"], tensors["recheck_failed"] = fixed, ~fixed
+            report.context["recovery_action"] = "located_element_recomputed"
+            return None, None
+        replacement, retry_evidence = gemm((-1, -1, -1))
+        _, checked, _ = _decisions(finalize(retry_evidence, first_reference), statistics)
+        report.context["recovery_action"] = "full_recompute"
+        return replacement, checked
 
-def execute_input_fused(prepared, cfg, fault, context, *, method=None, policy=None, profile_scope=None):
-    return _execute_native(prepared, cfg, fault, context, method=method, policy=policy,
-                           profile_scope=profile_scope)
+    return _finish(plan, report, output, recheck, timer, started)

@@ -1,13 +1,22 @@
-"""Caller-owned ABFT method instances, the physical call counter, checkpoints.
+"""Method instances retained across the GEMM calls of one protected model.
 
-Mirrors src/abft/session.py of the reference (``MethodSession``): every
-product request reserves a new ``call_index`` (activation-checkpoint replay
-included); stateless methods (Classic, Sum) share one instance with no scope
-bookkeeping, stream queries or locks on the hot path; stateful methods get one
-instance per execution profile (layer, role, precision, device, m, n, k and
-scale profile), reject concurrent entry, stream changes and CUDA-graph
-capture, and snapshot / restore their history through ``state_dict`` /
-``load_state_dict`` with the same checkpoint schema and validation rules.
+A ``MethodSession`` does two jobs for the Linear bridge:
+
+* it numbers every physical GEMM call (forward, dgrad, wgrad, and forwards
+  replayed by activation checkpointing), which is what a fault's
+  ``call_index`` refers to;
+* it hands the engine the method instance a call must use. Stateless methods
+  (classic, sum) share one instance and take no locks or stream queries on
+  the hot path. Stateful methods get one instance per execution profile
+  (layer, role, precision, device, shape, scale profile), are bound to one
+  CUDA stream per device, refuse concurrent entry and CUDA-graph capture, and
+  can be checkpointed with ``state_dict`` / ``load_state_dict``.
+
+The checkpoint dictionary uses the reference's schema (src/abft/session.py)
+so that checkpoints move between the two implementations: schema and config
+versions, a SHA-256 signature of the canonical configuration, the method's
+state metadata, the call counter, per-profile states and the state of a
+not-yet-used stateful instance.
 """
 from __future__ import annotations
 
@@ -15,7 +24,7 @@ import hashlib
 import json
 import math
 from contextlib import contextmanager, nullcontext
-from dataclasses import asdict
+from dataclasses import asdict, dataclass
 from threading import Lock
 
 import torch
@@ -25,19 +34,23 @@ from .methods import get_method
 
 SCHEMA_VERSION = 1
 CONFIG_VERSION = 1
-_SCOPE_FIELDS = frozenset({"layer", "role", "precision", "device", "m", "n", "k", "scale_profile"})
-_SCALING = {"fp32": "none", "bf16": "none", "fp8": "tensorwise", "nvfp4": "block16"}
-_CHECKPOINT_FIELDS = frozenset({"schema_version", "config_version", "config_signature", "method_metadata",
-                                "call_index", "instances", "pending_state"})
+CHECKPOINT_KEYS = frozenset({"schema_version", "config_version", "config_signature", "method_metadata",
+                             "call_index", "instances", "pending_state"})
+ROLES = frozenset({"forward", "dgrad", "wgrad"})
+DEFAULT_SCALING = {"fp32": "none", "bf16": "none", "fp8": "tensorwise", "nvfp4": "block16"}
 
 
-def _canonical(value):
+def _json(value):
     return json.dumps(value, sort_keys=True, separators=(",", ":"), allow_nan=False)
 
 
-def _frozen(value, seen=None):
-    """Detached copy of checkpointable state: dicts with str keys, lists,
-    tuples, scalars and plain tensors only; no cycles."""
+def _roundtrip(value):
+    return json.loads(_json(value))
+
+
+def _detached(value, _path=()):
+    """A checkpoint-safe deep copy: string-key dictionaries, lists, tuples,
+    scalars and plain tensors (cloned), without cycles."""
     if isinstance(value, torch.Tensor):
         copy = value.detach().clone()
         if type(copy) is not torch.Tensor:
@@ -48,26 +61,21 @@ def _frozen(value, seen=None):
     if type(value) not in (dict, list, tuple):
         raise ValueError("ABFT state must contain only dictionaries, lists, tuples, scalars and tensors; "
                          "save generator.get_state(), not a generator object")
-    seen = set() if seen is None else seen
-    if id(value) in seen:
+    if any(item is value for item in _path):
         raise ValueError("ABFT state must not contain cycles")
-    seen.add(id(value))
-    try:
-        if type(value) is dict:
-            if not all(type(key) is str for key in value):
-                raise ValueError("ABFT state dictionary keys must be strings")
-            return {key: _frozen(item, seen) for key, item in value.items()}
-        items = [_frozen(item, seen) for item in value]
-        return items if type(value) is list else tuple(items)
-    finally:
-        seen.discard(id(value))
+    path = _path + (value,)
+    if type(value) is dict:
+        if any(type(key) is not str for key in value):
+            raise ValueError("ABFT state dictionary keys must be strings")
+        return {key: _detached(item, path) for key, item in value.items()}
+    items = [_detached(item, path) for item in value]
+    return items if type(value) is list else tuple(items)
 
 
-def _metadata(method, name):
+def _method_metadata(method, name):
     if method is None:
         return {"name": name, "class": None, "stateful": False, "state_schema_version": 1}
-    stateful = getattr(method, "stateful", False)
-    version = getattr(method, "state_schema_version", 1)
+    stateful, version = getattr(method, "stateful", False), getattr(method, "state_schema_version", 1)
     if type(stateful) is not bool or type(version) is not int or version < 1:
         raise ValueError("ABFT method stateful/state_schema_version metadata is invalid")
     kind = type(method)
@@ -75,68 +83,118 @@ def _metadata(method, name):
             "state_schema_version": version}
 
 
-def _scope_key(scope):
-    """Validated hashable key of an execution profile."""
-    if type(scope) is not dict or set(scope) != _SCOPE_FIELDS:
-        raise ValueError("ABFT method scope metadata is invalid")
-    if not isinstance(scope["layer"], str) or scope["role"] not in {"forward", "dgrad", "wgrad"}:
-        raise ValueError("ABFT method layer/role scope is invalid")
-    if scope["precision"] not in _SCALING:
-        raise ValueError("ABFT method precision scope is invalid")
-    if not all(type(scope[d]) is int and scope[d] > 0 for d in ("m", "n", "k")):
-        raise ValueError("ABFT method shape scope is invalid")
-    if not isinstance(scope["device"], str) or str(torch.device(scope["device"])) != scope["device"]:
-        raise ValueError("ABFT method device scope is invalid")
-    profile = scope["scale_profile"]
-    if type(profile) is not dict or set(profile) != {"scaling", "global_scale", "input_dtypes"}:
-        raise ValueError("ABFT scale profile metadata is invalid")
-    if profile["scaling"] != _SCALING[scope["precision"]] and (scope["precision"], profile["scaling"]) != (
-            "fp8", "blockwise"):
-        raise ValueError("ABFT precision/scale profile mismatch")
-    scale = profile["global_scale"]
-    if scale != "amax" and (type(scale) not in (int, float) or not math.isfinite(scale) or scale <= 0):
-        raise ValueError("ABFT global scale profile is invalid")
-    dtypes = profile["input_dtypes"]
-    if not isinstance(dtypes, list) or len(dtypes) != 2 or not all(isinstance(d, str) for d in dtypes):
-        raise ValueError("ABFT input dtype profile is invalid")
-    return (scope["layer"], scope["role"], scope["precision"], scope["device"], scope["m"], scope["n"],
-            scope["k"], profile["scaling"], scale, *dtypes)
+@dataclass(frozen=True)
+class _Scope:
+    """One execution profile of a stateful method (hashable)."""
+
+    layer: str
+    role: str
+    precision: str
+    device: str
+    m: int
+    n: int
+    k: int
+    scaling: str
+    global_scale: object
+    dtypes: tuple
+
+    def record(self):
+        return {"layer": self.layer, "role": self.role, "precision": self.precision, "device": self.device,
+                "m": self.m, "n": self.n, "k": self.k,
+                "scale_profile": {"scaling": self.scaling, "global_scale": self.global_scale,
+                                  "input_dtypes": list(self.dtypes)}}
+
+    @classmethod
+    def parse(cls, record):
+        """Validated scope of a checkpoint (or freshly built) record."""
+        fields = {"layer", "role", "precision", "device", "m", "n", "k", "scale_profile"}
+        if type(record) is not dict or set(record) != fields:
+            raise ValueError("ABFT method scope metadata is invalid")
+        if not isinstance(record["layer"], str) or record["role"] not in ROLES:
+            raise ValueError("ABFT method layer/role scope is invalid")
+        precision = record["precision"]
+        if precision not in DEFAULT_SCALING:
+            raise ValueError("ABFT method precision scope is invalid")
+        if any(type(record[d]) is not int or record[d] <= 0 for d in ("m", "n", "k")):
+            raise ValueError("ABFT method shape scope is invalid")
+        device = record["device"]
+        if not isinstance(device, str) or str(torch.device(device)) != device:
+            raise ValueError("ABFT method device scope is invalid")
+        profile = record["scale_profile"]
+        if type(profile) is not dict or set(profile) != {"scaling", "global_scale", "input_dtypes"}:
+            raise ValueError("ABFT scale profile metadata is invalid")
+        scaling = profile["scaling"]
+        if scaling != DEFAULT_SCALING[precision] and (precision, scaling) != ("fp8", "blockwise"):
+            raise ValueError("ABFT precision/scale profile mismatch")
+        scale = profile["global_scale"]
+        if scale != "amax" and (type(scale) not in (int, float) or not math.isfinite(scale) or scale <= 0):
+            raise ValueError("ABFT global scale profile is invalid")
+        dtypes = profile["input_dtypes"]
+        if not isinstance(dtypes, list) or len(dtypes) != 2 or not all(isinstance(d, str) for d in dtypes):
+            raise ValueError("ABFT input dtype profile is invalid")
+        return cls(record["layer"], record["role"], precision, device, record["m"], record["n"], record["k"],
+                   scaling, scale, tuple(dtypes))
 
 
-def _call_context(layer, role, index, profile):
-    return {"layer": layer, "role": role, "call_index": index,
-            "execution_kind": "forward_or_recompute" if role == "forward" else "backward", "retry": 0,
+def _engine_context(layer, role, index, profile):
+    """The context the engine receives for one physical call."""
+    kind = "forward_or_recompute" if role == "forward" else "backward"
+    return {"layer": layer, "role": role, "call_index": index, "execution_kind": kind, "retry": 0,
             "scale_profile": profile}
 
 
 class MethodSession:
-    """Retains method instances across calls of one configuration."""
+    """Retains method instances across the calls of one configuration."""
 
     def __init__(self, config=None, fault=None):
-        # Normalise through canonical JSON so the signature is stable.
-        self.config = parse_abft_config(json.loads(_canonical(asdict(parse_abft_config(config)))))
-        self.fault = parse_fault_config(json.loads(_canonical(asdict(parse_fault_config(fault)))))
-        payload = {"version": CONFIG_VERSION, "abft": asdict(self.config), "fault": asdict(self.fault)}
-        self.config_signature = hashlib.sha256(_canonical(payload).encode()).hexdigest()
-        self._pending = get_method(self.config.method) if self.config.method != "none" else None
-        self.metadata = _metadata(self._pending, self.config.method)
+        # Canonical JSON round trip: the signature depends on values only.
+        self.config = parse_abft_config(_roundtrip(asdict(parse_abft_config(config))))
+        self.fault = parse_fault_config(_roundtrip(asdict(parse_fault_config(fault))))
+        signed = {"version": CONFIG_VERSION, "abft": asdict(self.config), "fault": asdict(self.fault)}
+        self.config_signature = hashlib.sha256(_json(signed).encode()).hexdigest()
+        self._spare = None if self.config.method == "none" else get_method(self.config.method)
+        self.metadata = _method_metadata(self._spare, self.config.method)
         self.stateful = self.metadata["stateful"]
         self.call_index = 0
-        self._entries = {}
-        self._streams = {}
-        self._lock = Lock() if self.stateful else None
+        self._by_scope = {}   # _Scope -> method instance (stateful only)
+        self._streams = {}    # device name -> the one stream its history advances on
+        self._guard = Lock() if self.stateful else None
+
+    # --- calls ---------------------------------------------------------------
+    @contextmanager
+    def call(self, a, b, precision, scaling, global_scale, layer, role):
+        """Reserve one physical call; yields (method instance, engine context)."""
+        profile = {"scaling": scaling, "global_scale": global_scale, "input_dtypes": [str(a.dtype), str(b.dtype)]}
+        if not self.stateful:
+            self.call_index += 1
+            yield self._spare, _engine_context(layer, role, self.call_index, profile)
+            return
+        with self._exclusive():
+            if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[0] or a.device != b.device:
+                raise ValueError("ABFT session requires compatible matrices on one device")
+            scope = _Scope.parse({"layer": layer, "role": role, "precision": precision, "device": str(a.device),
+                                  "m": int(a.shape[0]), "n": int(b.shape[1]), "k": int(a.shape[1]),
+                                  "scale_profile": _roundtrip(profile)})
+            self._bind_stream(a.device)
+            method = self._by_scope.get(scope)
+            if method is None:
+                method = self._spare if self._spare is not None else self._new_method()
+                self._spare = None
+                self._by_scope[scope] = method
+            self.call_index += 1
+            yield method, _engine_context(layer, role, self.call_index, _roundtrip(profile))
 
     @contextmanager
     def _exclusive(self):
-        if self._lock is None:
+        if self._guard is None:
             yield
             return
-        if not self._lock.acquire(blocking=False):
+        if not self._guard.acquire(blocking=False):
             raise RuntimeError("Stateful ABFT session does not support concurrent calls or snapshots")
         try:
             yield
         finally:
-            self._lock.release()
+            self._guard.release()
 
     def _bind_stream(self, device):
         if device.type == "cpu":
@@ -146,112 +204,82 @@ class MethodSession:
         if torch.cuda.is_current_stream_capturing():
             raise RuntimeError("Stateful ABFT history cannot be advanced by CUDA Graph replay")
         stream = torch.cuda.current_stream(device)
-        bound = self._streams.setdefault(str(device), stream)
-        if bound.cuda_stream != stream.cuda_stream:
+        if self._streams.setdefault(str(device), stream).cuda_stream != stream.cuda_stream:
             raise RuntimeError("Stateful ABFT history cannot be shared across CUDA streams")
 
-    @contextmanager
-    def call(self, a, b, precision, scaling, global_scale, layer, role):
-        """Reserve one physical call; yields (method instance, engine context)."""
-        profile = {"scaling": scaling, "global_scale": global_scale, "input_dtypes": [str(a.dtype), str(b.dtype)]}
-        if not self.stateful:
-            self.call_index += 1
-            yield self._pending, _call_context(layer, role, self.call_index, profile)
-            return
-        with self._exclusive():
-            if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[0] or a.device != b.device:
-                raise ValueError("ABFT session requires compatible matrices on one device")
-            scope = {"layer": layer, "role": role, "precision": precision, "device": str(a.device),
-                     "m": int(a.shape[0]), "n": int(b.shape[1]), "k": int(a.shape[1]),
-                     "scale_profile": profile}
-            key = _scope_key(scope)
-            self._bind_stream(a.device)
-            entry = self._entries.get(key)
-            if entry is None:
-                method = self._pending if self._pending is not None else get_method(self.config.method)
-                if _metadata(method, self.config.method) != self.metadata:
-                    raise ValueError("ABFT method factory changed its state metadata")
-                # The stored scope is a private copy: consumers may mutate the context.
-                entry = self._entries[key] = (json.loads(_canonical(scope)), method)
-                self._pending = None
-            self.call_index += 1
-            context_profile = {**profile, "input_dtypes": list(profile["input_dtypes"])}
-            yield entry[1], _call_context(layer, role, self.call_index, context_profile)
+    def _new_method(self, state=None):
+        method = get_method(self.config.method)
+        if _method_metadata(method, self.config.method) != self.metadata:
+            raise ValueError("ABFT method factory changed its state metadata")
+        if state is not None:
+            method.load_state_dict(_detached(state))
+        return method
 
+    # --- checkpoints -----------------------------------------------------------
     def state_dict(self):
         with self._exclusive():
-            instances = []
-            pending = None
+            instances, pending = [], None
             if self.stateful:
-                for scope, method in self._entries.values():
-                    stream = self._streams.get(scope["device"])
+                for scope, method in self._by_scope.items():
+                    stream = self._streams.get(scope.device)
                     with torch.cuda.stream(stream) if stream is not None else nullcontext():
-                        state = method.state_dict()
-                    if type(state) is not dict:
-                        raise ValueError("ABFT method state_dict must return a dictionary")
-                    instances.append({"scope": json.loads(_canonical(scope)), "state": _frozen(state)})
-                # Device clones finish before a caller serialises them.
-                for stream in self._streams.values():
+                        instances.append({"scope": scope.record(), "state": _detached(_own_state(method))})
+                for stream in self._streams.values():  # clones complete before the caller serialises
                     stream.synchronize()
-                if self._pending is not None:
-                    pending = self._pending.state_dict()
-                    if type(pending) is not dict:
-                        raise ValueError("ABFT method state_dict must return a dictionary")
-                    pending = _frozen(pending)
+                if self._spare is not None:
+                    pending = _detached(_own_state(self._spare))
             return {"schema_version": SCHEMA_VERSION, "config_version": CONFIG_VERSION,
                     "config_signature": self.config_signature, "method_metadata": dict(self.metadata),
                     "call_index": self.call_index, "instances": instances, "pending_state": pending}
 
     def load_state_dict(self, payload, *, device=None):
+        """Restore a checkpoint; on any error the live state is untouched."""
         with self._exclusive():
             self._check_header(payload)
             wanted = None if device is None else str(torch.device(device))
-            entries = {}
-            for item in payload["instances"]:
-                if type(item) is not dict or set(item) != {"scope", "state"} or type(item["state"]) is not dict:
+            restored = {}
+            for entry in payload["instances"]:
+                if type(entry) is not dict or set(entry) != {"scope", "state"} or type(entry["state"]) is not dict:
                     raise ValueError("ABFT method checkpoint entry is invalid")
-                scope = json.loads(_canonical(item["scope"]))
-                key = _scope_key(scope)
-                if key in entries or (wanted is not None and scope["device"] != wanted):
+                scope = _Scope.parse(_roundtrip(entry["scope"]))
+                if scope in restored or (wanted is not None and scope.device != wanted):
                     raise ValueError("ABFT checkpoint has duplicate or mismatched device scopes")
-                entries[key] = (scope, self._restored(item["state"]))
-            pending = None if self.stateful else self._pending
-            if self.stateful and not entries:
+                restored[scope] = self._new_method(entry["state"])
+            spare = self._spare if not self.stateful else None
+            if self.stateful and not restored:
                 if type(payload["pending_state"]) is not dict:
                     raise ValueError("Unused stateful ABFT method is missing its initial RNG/state")
-                pending = self._restored(payload["pending_state"])
+                spare = self._new_method(payload["pending_state"])
             elif payload["pending_state"] is not None:
                 raise ValueError("ABFT checkpoint contains incompatible pending method state")
             if self.stateful:
                 for stream in self._streams.values():
                     stream.synchronize()
-                for name in {scope["device"] for scope, _ in entries.values()}:
+                for name in {scope.device for scope in restored}:
                     if torch.device(name).type == "cuda":
                         torch.cuda.current_stream(torch.device(name)).synchronize()
-            # Only now does the live state change: a rejected checkpoint leaves it intact.
-            self._entries, self._pending, self._streams = entries, pending, {}
+            self._by_scope, self._spare, self._streams = restored, spare, {}
             self.call_index = payload["call_index"]
 
     def _check_header(self, payload):
-        if type(payload) is not dict or set(payload) != _CHECKPOINT_FIELDS:
+        if type(payload) is not dict or set(payload) != CHECKPOINT_KEYS:
             raise ValueError("ABFT session checkpoint schema is invalid")
-        metadata = payload["method_metadata"]
-        if (type(metadata) is not dict or set(metadata) != set(self.metadata) or
-                type(metadata["stateful"]) is not bool or type(metadata["state_schema_version"]) is not int):
+        meta = payload["method_metadata"]
+        if (type(meta) is not dict or set(meta) != set(self.metadata) or type(meta["stateful"]) is not bool
+                or type(meta["state_schema_version"]) is not int):
             raise ValueError("ABFT method/state schema does not match checkpoint")
-        if (type(payload["schema_version"]) is not int or type(payload["config_version"]) is not int or
-                payload["schema_version"] != SCHEMA_VERSION or payload["config_version"] != CONFIG_VERSION or
-                payload["config_signature"] != self.config_signature or metadata != self.metadata):
+        versions = (payload["schema_version"], payload["config_version"])
+        if (any(type(v) is not int for v in versions) or versions != (SCHEMA_VERSION, CONFIG_VERSION)
+                or payload["config_signature"] != self.config_signature or meta != self.metadata):
             raise ValueError("ABFT session configuration/method/state schema does not match checkpoint")
-        if (type(payload["call_index"]) is not int or payload["call_index"] < 0 or
-                type(payload["instances"]) is not list):
+        if type(payload["call_index"]) is not int or payload["call_index"] < 0 or type(payload["instances"]) is not list:
             raise ValueError("ABFT session call counter/instances are invalid")
         if not self.stateful and (payload["instances"] or payload["pending_state"] is not None):
             raise ValueError("Stateless ABFT methods must not restore adaptive history")
 
-    def _restored(self, state):
-        method = get_method(self.config.method)
-        if _metadata(method, self.config.method) != self.metadata:
-            raise ValueError("ABFT method factory changed its state metadata")
-        method.load_state_dict(_frozen(state))
-        return method
+
+def _own_state(method):
+    state = method.state_dict()
+    if type(state) is not dict:
+        raise ValueError("ABFT method state_dict must return a dictionary")
+    return state

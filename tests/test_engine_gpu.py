@@ -128,9 +128,9 @@ def test_native_weights_are_cached_per_stream():
     prepared = PreparedGemm.prepare(a, b, "fp8", "tensorwise")
     execute_prepared(prepared, _cfg())
     key = (0, torch.device(DEV).index or 0, 128)
-    first = native._weights[key][0]
+    first = native.WEIGHTS.peek(key)
     execute_prepared(prepared, _cfg())
-    assert native._weights[key][0] is first
+    assert first is not None and native.WEIGHTS.peek(key) is first
     assert torch.equal(first, get_method("classic").projection_weights(prepared))
 
 
