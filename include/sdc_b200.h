@@ -105,6 +105,22 @@ int sdc_quantize_nvfp4(const void* x, int dtype, int64_t rows, int64_t cols,
                        void* workspace, size_t workspace_bytes,
                        sdc_stream_t stream);
 
+/* Row-sharded quantisation (extension; no counterpart in the reference): the
+ * same casts as sdc_quantize_fp8 / sdc_quantize_nvfp4 with the "amax"
+ * multiplier of the WHOLE matrix, taken from a device fp32 scalar `amax`
+ * (max |x| over all shards, e.g. a MAX all-reduce of the shards' maxima), so
+ * a shard's codes equal the unsharded matrix's rows bit for bit with no host
+ * read of the maximum. No workspace. */
+int sdc_quantize_fp8_global_amax(const void* x, int dtype, int64_t rows,
+                                 int64_t cols, const float* amax,
+                                 uint8_t* codes, float* multiplier,
+                                 sdc_stream_t stream);
+int sdc_quantize_nvfp4_global_amax(const void* x, int dtype, int64_t rows,
+                                   int64_t cols, const float* amax,
+                                   uint8_t* codes, uint8_t* scales,
+                                   uint8_t* scales_mma, float* multiplier,
+                                   sdc_stream_t stream);
+
 /* ---- NVFP4 scale-factor layout (src/cutlass_gemm/csrc/gemm/nvfp4.cu:122-147)
  * Byte offset of natural scale (row, block) in the 128x4 atom layout, and the
  * layout's byte size for a [rows, k] operand. Host functions. */

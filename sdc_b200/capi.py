@@ -35,6 +35,8 @@ PROTOTYPES = {
     "sdc_quantize_workspace_bytes": (_size, [_i64, _i64]),
     "sdc_quantize_fp8": (_int, [_vp, _int, _i64, _i64, _int, _float, _vp, _vp, _vp, _size, _vp]),
     "sdc_quantize_nvfp4": (_int, [_vp, _int, _i64, _i64, _int, _float, _vp, _vp, _vp, _vp, _vp, _size, _vp]),
+    "sdc_quantize_fp8_global_amax": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _vp, _vp]),
+    "sdc_quantize_nvfp4_global_amax": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp]),
     "sdc_nvfp4_scale_offset": (_i64, [_i64, _i64, _i64]),
     "sdc_nvfp4_scale_size": (_i64, [_i64, _i64]),
     "sdc_nvfp4_scale_layout": (_int, [_i64, _i64, _vp]),

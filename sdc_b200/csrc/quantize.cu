@@ -396,6 +396,58 @@ int sdc_quantize_nvfp4(const void* x, int dtype, int64_t rows, int64_t cols, int
   return SDC_OK;
 }
 
+
+// Quantisation of one shard of a row-sharded matrix with the multiplier of
+// the whole matrix: `amax` is a device fp32 scalar holding max |x| over every
+// shard (e.g. a MAX all-reduce of the shards' maxima). The cast kernels
+// derive st from it exactly as from their own partial maxima (a non-negative
+// float's bits order like its value), so the codes equal the unsharded
+// matrix's rows bit for bit, with no host read of the maximum.
+int sdc_quantize_fp8_global_amax(const void* x, int dtype, int64_t rows, int64_t cols, const float* amax,
+                                 uint8_t* codes, float* multiplier, sdc_stream_t stream) {
+  using namespace sdc;
+  SDC_REQUIRE(dtype == 0 || dtype == 1, "quantize requires FP32 (0) or BF16 (1) input");
+  SDC_REQUIRE(rows > 0 && cols > 0, "quantize requires a nonempty matrix");
+  SDC_REQUIRE(x != nullptr && amax != nullptr && codes != nullptr && multiplier != nullptr,
+              "quantize pointers must not be null");
+  const int64_t count = rows * cols;
+  const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (reinterpret_cast<uintptr_t>(codes) % 16 == 0);
+  const uint32_t* bits = reinterpret_cast<const uint32_t*>(amax);
+  const int grid = grid_for(ceil_div(count, 16));
+  if (dtype == 0) {
+    fp8_cast<0><<<grid, kQuantThreads, 0, stream>>>(x, count, vec, bits, 1, true, 1.f, codes, multiplier);
+  } else {
+    fp8_cast<1><<<grid, kQuantThreads, 0, stream>>>(x, count, vec, bits, 1, true, 1.f, codes, multiplier);
+  }
+  SDC_CUDA_CHECK(cudaGetLastError());
+  return SDC_OK;
+}
+
+int sdc_quantize_nvfp4_global_amax(const void* x, int dtype, int64_t rows, int64_t cols, const float* amax,
+                                   uint8_t* codes, uint8_t* scales, uint8_t* scales_mma, float* multiplier,
+                                   sdc_stream_t stream) {
+  using namespace sdc;
+  SDC_REQUIRE(dtype == 0 || dtype == 1, "quantize requires FP32 (0) or BF16 (1) input");
+  SDC_REQUIRE(rows > 0 && cols > 0 && cols % 16 == 0, "nonempty input columns must be divisible by 16");
+  SDC_REQUIRE(x != nullptr && amax != nullptr && codes != nullptr && multiplier != nullptr,
+              "quantize pointers must not be null");
+  const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (reinterpret_cast<uintptr_t>(codes) % 8 == 0);
+  if (scales_mma != nullptr && (rows % 128 != 0 || cols % 64 != 0)) {
+    SDC_CUDA_CHECK(cudaMemsetAsync(scales_mma, 0, sdc_nvfp4_scale_size(rows, cols), stream));
+  }
+  const uint32_t* bits = reinterpret_cast<const uint32_t*>(amax);
+  const int grid = grid_for(rows * (cols / 16));
+  if (dtype == 0) {
+    nvfp4_cast<0><<<grid, kQuantThreads, 0, stream>>>(x, rows, cols, vec, bits, 1, true, 1.f, codes, scales,
+                                                      scales_mma, multiplier);
+  } else {
+    nvfp4_cast<1><<<grid, kQuantThreads, 0, stream>>>(x, rows, cols, vec, bits, 1, true, 1.f, codes, scales,
+                                                      scales_mma, multiplier);
+  }
+  SDC_CUDA_CHECK(cudaGetLastError());
+  return SDC_OK;
+}
+
 }  // extern "C"
 
 extern "C" int sdc_quantize_fp8_block(const void* x, int dtype, int64_t rows, int64_t cols, int block_rows,

@@ -434,14 +434,31 @@ int dtype_code(const Tensor& x) {
   return x.scalar_type() == at::kFloat ? 0 : 1;
 }
 
-std::tuple<Tensor, Tensor> quantize_fp8(const Tensor& x, std::optional<double> global_scale) {
+// `amax`: optional device fp32 scalar, max |x| of the whole (row-sharded)
+// matrix; when given, the "amax" multiplier comes from it instead of x.
+void check_global_amax(OptTensor amax, const Tensor& x, std::optional<double> global_scale) {
+  if (!amax.has_value()) return;
+  TORCH_CHECK(!global_scale.has_value(), "quantize takes a fixed global_scale or a global amax, not both");
+  TORCH_CHECK(amax->is_cuda() && amax->device() == x.device() && amax->scalar_type() == at::kFloat &&
+                  amax->numel() == 1 && amax->is_contiguous(),
+              "global amax must be a CUDA fp32 scalar on the input device");
+}
+
+std::tuple<Tensor, Tensor> quantize_fp8(const Tensor& x, std::optional<double> global_scale, OptTensor amax) {
   TORCH_CHECK(x.is_cuda() && x.dim() == 2, "quantize requires a two-dimensional CUDA tensor");
   const int dt = dtype_code(x);
   TORCH_CHECK(x.size(0) > 0 && x.size(1) > 0 && x.size(1) % 4 == 0, "nonempty input columns must be divisible by 4");
+  check_global_amax(amax, x, global_scale);
   const c10::cuda::CUDAGuard guard(x.device());
   Tensor xc = x.contiguous();
   auto codes = at::empty(x.sizes(), x.options().dtype(at::kByte));
   auto st = at::empty({}, x.options().dtype(at::kFloat));
+  if (amax.has_value()) {
+    check_status(sdc_quantize_fp8_global_amax(xc.const_data_ptr(), dt, x.size(0), x.size(1),
+                                              amax->const_data_ptr<float>(), codes.data_ptr<uint8_t>(),
+                                              st.data_ptr<float>(), stream_of(x)));
+    return {codes, st};
+  }
   const size_t ws_bytes = sdc_quantize_workspace_bytes(x.size(0), x.size(1));
   Tensor ws = workspace(x, ws_bytes);
   check_status(sdc_quantize_fp8(xc.const_data_ptr(), dt, x.size(0), x.size(1), global_scale.has_value() ? 0 : 1,
@@ -465,17 +482,25 @@ std::tuple<Tensor, Tensor> quantize_fp8_block(const Tensor& x, int64_t block_row
   return {codes, scales};
 }
 
-std::tuple<Tensor, Tensor, Tensor, Tensor> quantize_nvfp4(const Tensor& x, std::optional<double> global_scale) {
+std::tuple<Tensor, Tensor, Tensor, Tensor> quantize_nvfp4(const Tensor& x, std::optional<double> global_scale,
+                                                          OptTensor amax) {
   TORCH_CHECK(x.is_cuda() && x.dim() == 2, "quantize requires a two-dimensional CUDA tensor");
   const int dt = dtype_code(x);
   const int64_t rows = x.size(0), cols = x.size(1);
   TORCH_CHECK(rows > 0 && cols > 0 && cols % 16 == 0, "nonempty input columns must be divisible by 16");
+  check_global_amax(amax, x, global_scale);
   const c10::cuda::CUDAGuard guard(x.device());
   Tensor xc = x.contiguous();
   auto codes = at::empty({rows, cols / 2}, x.options().dtype(at::kByte));
   auto scales = at::empty({rows, cols / 16}, x.options().dtype(at::kByte));
   auto packed = at::empty({sdc_nvfp4_scale_size(rows, cols)}, x.options().dtype(at::kByte));
   auto st = at::empty({}, x.options().dtype(at::kFloat));
+  if (amax.has_value()) {
+    check_status(sdc_quantize_nvfp4_global_amax(xc.const_data_ptr(), dt, rows, cols, amax->const_data_ptr<float>(),
+                                                codes.data_ptr<uint8_t>(), scales.data_ptr<uint8_t>(),
+                                                packed.data_ptr<uint8_t>(), st.data_ptr<float>(), stream_of(x)));
+    return {codes, scales, packed, st};
+  }
   const size_t ws_bytes = sdc_quantize_workspace_bytes(rows, cols);
   Tensor ws = workspace(x, ws_bytes);
   check_status(sdc_quantize_nvfp4(xc.const_data_ptr(), dt, rows, cols, global_scale.has_value() ? 0 : 1,
@@ -621,8 +646,8 @@ TORCH_LIBRARY(sdc_cutlass, lib) {
   lib.def("abft_fp8_block_correct(Tensor a, Tensor b_rows, Tensor scale_a, Tensor scale_b, Tensor location, Tensor located, Tensor(a!) output) -> Tensor");
   lib.def("nvfp4_scale_layout(int m, int n, int k) -> (Tensor, Tensor, int, int)", &nvfp4_scale_layout);
   // sdc_b200 extensions.
-  lib.def("quantize_fp8(Tensor x, float? global_scale=None) -> (Tensor, Tensor)");
-  lib.def("quantize_nvfp4(Tensor x, float? global_scale=None) -> (Tensor, Tensor, Tensor, Tensor)");
+  lib.def("quantize_fp8(Tensor x, float? global_scale=None, Tensor? amax=None) -> (Tensor, Tensor)");
+  lib.def("quantize_nvfp4(Tensor x, float? global_scale=None, Tensor? amax=None) -> (Tensor, Tensor, Tensor, Tensor)");
   lib.def("nvfp4_pack_scales(Tensor scales, int k) -> Tensor");
   lib.def("abft_locate(Tensor residual, Tensor threshold, Tensor flags, int m) -> (Tensor, Tensor)");
   lib.def("abft_fp8_correct(Tensor a, Tensor b_rows, Tensor alpha, Tensor location, Tensor located, Tensor(a!) output) -> Tensor");

@@ -54,8 +54,13 @@ def _fixed_scale(policy):
 
 
 @torch.no_grad()
-def quantize(matrix, precision, global_scale="amax"):
-    """Quantize a 2-D CUDA FP32/BF16 matrix to FP8 (tensorwise) or NVFP4."""
+def quantize(matrix, precision, global_scale="amax", *, amax=None):
+    """Quantize a 2-D CUDA FP32/BF16 matrix to FP8 (tensorwise) or NVFP4.
+
+    ``amax`` (extension): a 0-d CUDA fp32 tensor holding max |x| of a larger
+    matrix this one is a row shard of; with the "amax" policy the multiplier
+    then comes from it (no host read), so the shard's codes equal the same
+    rows of the whole matrix quantised at once."""
     if matrix.device.type != "cuda" or matrix.ndim != 2:
         raise ValueError("quantize requires a two-dimensional CUDA tensor")
     if matrix.dtype not in {torch.float32, torch.bfloat16}:
@@ -68,11 +73,15 @@ def quantize(matrix, precision, global_scale="amax"):
     if rows == 0 or columns == 0 or columns % alignment:
         raise ValueError(f"nonempty input columns must be divisible by {alignment}")
     fixed = _fixed_scale(global_scale)
+    if amax is not None and fixed is not None:
+        raise ValueError("a global amax only applies to the amax policy")
     require_device(matrix.device)
+    if amax is not None:
+        amax = amax.detach().to(device=matrix.device, dtype=torch.float32).reshape(())
     if precision == "fp8":
-        codes, st = ops.quantize_fp8(matrix, fixed)
+        codes, st = ops.quantize_fp8(matrix, fixed, amax)
         return QuantizedMatrix(codes, None, st, precision, (rows, columns))
-    codes, scales, packed, st = ops.quantize_nvfp4(matrix, fixed)
+    codes, scales, packed, st = ops.quantize_nvfp4(matrix, fixed, amax)
     return QuantizedMatrix(codes, scales, st, precision, (rows, columns), packed)
 
 

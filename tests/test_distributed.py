@@ -65,6 +65,19 @@ def _scenario(name, rank, world):
         one = allreduce_status(tensors if rank == 1 else {}, 128 * rank)
         return {"both": [bool(both["located"]), both["location"].tolist()],
                 "one": [bool(one["located"]), one["location"].tolist(), bool(one["detected"])]}
+    if name == "norms":
+        residual = torch.tensor([[1.0, -4.0 * (rank + 1)], [0.5, 2.0]])
+        threshold = torch.tensor([[8.0, 8.0], [1.0, 64.0]])
+        verdict = allreduce_status({"detected": torch.tensor(False), "residual": residual,
+                                    "threshold": threshold}, 128 * rank)
+        quiet = allreduce_status({"detected": torch.tensor(rank == 0)}, 128 * rank)
+        return {"norms": [float(verdict["max_residual_over_threshold"]), float(verdict["max_abs_residual"])],
+                "quiet": [float(quiet["max_residual_over_threshold"]), bool(quiet["detected"]),
+                          int(quiet["shards_detected"])]}
+    if name == "explicit_offsets":
+        out, report = execute_sharded(rows, b, "fp32", "none", {"method": "classic", "on_error": "report"},
+                                      row_offset=start, total_rows=a.shape[0], **kwargs)
+        return {"rows": (start, stop), "out": out, "record": report.to_record()}
     if name == "multiplier":
         x = torch.randn(stop - start, 32, generator=torch.Generator().manual_seed(rank)) * (rank + 1)
         return {"st": global_multiplier(x, "fp8"), "local_amax": float(x.abs().amax()),
@@ -151,3 +164,21 @@ def test_global_multiplier_is_the_unsharded_amax_policy():
     expected = float(torch.tensor(448.0) / torch.tensor(amax))
     assert all(r["st"] == expected for r in results)
     assert all(r["st4"] == float(torch.tensor(2688.0) / torch.tensor(amax)) for r in results)
+
+
+def test_exchange_carries_residual_norms():
+    results = _run("norms")
+    for r in results:
+        # Rank 1's column 1: |res| 8 against threshold 8 (ratio 1); the largest |res| is 8.
+        assert r["norms"] == [1.0, 8.0]
+        # Without residuals the norms are reported as -1; flags still sum.
+        assert r["quiet"] == [-1.0, True, 1]
+
+
+def test_explicit_offsets_skip_the_size_exchange():
+    a, b = _operands()
+    for r in _run("explicit_offsets"):
+        start, stop = r["rows"]
+        assert torch.equal(r["out"], (a @ b)[start:stop])
+        assert r["record"]["context"]["row_offset"] == start and r["record"]["context"]["m"] == 300
+        assert r["record"]["detected"] is False
