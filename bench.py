@@ -264,6 +264,85 @@ def paired_overhead(prot, steps, rounds=5):
     return t_prot / (rounds * n), t_plain / (rounds * n)
 
 
+def timed_flushed(fns, iters, stream, flush):
+    """Mean device seconds per call of each function in ``fns``, one call at
+    a time with L2 flushed (a write larger than L2) before each, outside the
+    timed interval; the functions alternate so they share clocks."""
+    totals = [0.0] * len(fns)
+    for _ in range(iters):
+        for i, fn in enumerate(fns):
+            flush.add_(1)
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            fn()
+            end.record(stream)
+            end.synchronize()
+            totals[i] += start.elapsed_time(end) / 1e3
+    return [t / iters for t in totals]
+
+
+# Published augmented-mode timings of the reference at M=N=K=2048 on an RTX
+# 5090 (its own benchmark, BF16): augmented ABFT vs the unprotected GEMM.
+REFERENCE_AUGMENTED_2048 = {"gpu": "RTX 5090", "protected_us": 137.872, "unprotected_us": 98.895}
+
+
+def augmented_bf16(device, stream, sizes=(2048, 8192), iters=20):
+    """The augmented BF16 ABFT GEMM (Classic, compact form + packed finalize)
+    against the unprotected BF16 GEMM of this library at M=N=K = each size,
+    L2 flushed before every call; plus the clean calls' largest
+    |residual| / magnitude (what the relative threshold must clear)."""
+    from sdc_b200 import ops
+
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    bf16_peak, _, basis = measured_peaks()
+    out = {}
+    for size in sizes:
+        g = torch.Generator().manual_seed(size)
+        a = torch.randn(size, size, generator=g).to(torch.bfloat16).to(device)
+        b_kn = torch.randn(size, size, generator=g).to(torch.bfloat16).to(device).T.contiguous().T
+        rows = torch.arange(1, size + 1, device=device, dtype=torch.float32)
+        w = torch.stack((torch.ones_like(rows), rows)).to(torch.bfloat16)
+        worst = torch.zeros((), device=device)
+
+        def protected():
+            _, partials, flags = ops.abft_augmented_compact(a, b_kn, w, -1, -1, -1, 0)
+            packet = ops.abft_finalize(partials, flags, size, 0.0, 0.0, None, True, 0, None)
+            return partials, packet
+
+        def plain():
+            ops.mm(a, b_kn)
+
+        def library():  # cuBLAS through torch: an anchor for the plain GEMM, not this library
+            torch.matmul(a, b_kn)
+
+        for _ in range(3):
+            partials, packet = protected()
+            plain()
+            mag = partials[2].sum(dim=1)[:, :size]
+            torch.maximum(worst, (packet[1].abs() / mag.clamp_min(1e-30)).amax(), out=worst)
+        library()
+        t_prot, t_plain, t_lib = timed_flushed([protected, plain, library], iters, stream, flush)
+        flops = 2.0 * size ** 3
+        out[str(size)] = {
+            "protected_us": t_prot * 1e6, "unprotected_us": t_plain * 1e6, "time_ratio": t_prot / t_plain,
+            "overhead_pct": 100.0 * (t_prot / t_plain - 1.0),
+            "protected_tflops": flops / t_prot / 1e12, "unprotected_tflops": flops / t_plain / 1e12,
+            "unprotected_frac_of_bf16_peak": flops / t_plain / 1e12 / bf16_peak,
+            "cublas_bf16_us": t_lib * 1e6,
+            "clean_max_res_over_magnitude": float(worst),
+            "launches_per_call": {"protected": 4, "unprotected": 1},
+        }
+        del a, b_kn
+    out["method"] = (f"{iters} alternating calls each, L2 flushed before every call (256 MB write, untimed), "
+                     "CUDA events per call; protected = encode + augmented GEMM + finalize_columns + "
+                     "finalize_flags")
+    out["peak_basis"] = f"{basis} bf16 dense burst ({bf16_peak} TFLOP/s)"
+    out["reference_published_2048"] = {**REFERENCE_AUGMENTED_2048,
+                                       "time_ratio": REFERENCE_AUGMENTED_2048["protected_us"]
+                                       / REFERENCE_AUGMENTED_2048["unprotected_us"]}
+    return out
+
+
 def profiled_traffic(precision, size):
     """DRAM bytes (read + write) of one protected-GEMM launch of this workload,
     from the committed same-size ncu capture summary (profiles/traffic.json),
@@ -712,6 +791,7 @@ def run_ours(args):
         del prot
         torch.cuda.empty_cache()
     sweep = None if args.no_sweep else qwen_sweep(args, device, stream, rank, world, dist)
+    augmented = None if (args.no_augmented or rank != 0) else augmented_bf16(device, stream)
     ceiling = None if (args.no_ceiling or rank != 0) else library_ceiling(device, stream)
     if dist is not None:
         dist.barrier()
@@ -740,6 +820,8 @@ def run_ours(args):
         line["qwen2.5_7b_linears"] = sweep
     if ceiling is not None:
         line["library_ceiling"] = ceiling
+    if augmented is not None:
+        line["augmented_bf16"] = augmented
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(args.cpu_sample_rows, args.size or SIZES[head_key])
     sys.stdout.flush()
@@ -1010,6 +1092,7 @@ def main():
     parser.add_argument("--no-ceiling", action="store_true", help="skip the library GEMM anchors")
     parser.add_argument("--no-sweep", action="store_true", help="skip the Qwen2.5-7B linear-shape sweep")
     parser.add_argument("--sweep-steps", type=int, default=10)
+    parser.add_argument("--no-augmented", action="store_true", help="skip the augmented BF16 ABFT leg")
     parser.add_argument("--workload", choices=["gemm", "train"], default="gemm",
                         help="gemm: the ABFT GEMM benchmark (default); train: configuration 5 training step")
     parser.add_argument("--micro-batch", type=int, default=8)

@@ -244,6 +244,52 @@ int sdc_abft_fp8_block_reference_gemm(
     float* predicted, float* magnitude, void* workspace,
     size_t workspace_bytes, sdc_stream_t stream);
 
+/* ---- BF16 GEMM and augmented BF16 ABFT ------------------------------------
+ * bf16 operands (a [M,K] row-major, b_rows [N,K] row-major, K % 8 == 0),
+ * fp32 accumulation on the tensor cores, d = a . b_rows^T as bf16 [M,N]
+ * row-major. */
+
+/* Replaces sdc_cutlass_mm for bf16 operands
+ * (src/cutlass_gemm/csrc/gemm/fp32_bf16.cu:95-130; the reference's fp32
+ * variant stays outside this library). */
+int sdc_bf16_gemm(const uint16_t* a, const uint16_t* b_rows, int64_t m,
+                  int64_t n, int64_t k, uint16_t* d, sdc_stream_t stream);
+
+/* The encoding step of sdc_abft_bf16_augmented_gemm on its own (the
+ * reference forms these rows inside its augmented mainloop,
+ * src/cutlass_gemm/csrc/abft/fp32_bf16/bf16_augmented.h:200-320): for each
+ * 128-row M-tile t and channel c, q[t*C + c][k] = bf16 (round to nearest
+ * even) of the fp32 fma chain over the tile's rows in ascending order of
+ * w_c[row] * A[row][k]. a: bf16 [M, K] row-major, K % 8 == 0; weights: bf16
+ * [C, M]; q: bf16 [C * ceil(M/128), K]; a and q 16-byte aligned. */
+int sdc_abft_augment_encode(const uint16_t* a, int64_t m, int64_t k,
+                            int algorithm, const uint16_t* weights,
+                            uint16_t* q, sdc_stream_t stream);
+
+/* Workspace bytes of sdc_abft_bf16_augmented_gemm (256-byte aligned). */
+size_t sdc_abft_augmented_workspace_bytes(int algorithm, int64_t m,
+                                          int64_t k);
+
+/* Replaces sdc_cutlass_abft_augmented_mm and _compact
+ * (src/cutlass_gemm/csrc/abft/fp32_bf16/bf16_augmented.cu:12-162). The
+ * checksum rows of every 128-row M-tile t, q[t*C + c] = bf16(w_c^T A_t)
+ * (fp32 sum over the tile's rows, ascending), run as extra M-tiles of the
+ * same GEMM; their fp32 results are predicted[c, t, :]. The data tiles'
+ * epilogue applies the fault (XOR of bit `bit` of the fp32 value at
+ * (row, col)) and writes observed = sum_rows w_c v and the output-side
+ * magnitude sum_rows |w_c v|. weights: bf16 [C, M]. observed, predicted,
+ * magnitude: fp32 [C, Tm, Np], Np = ceil(N/128)*128 (padding zero). hit:
+ * nullable int32[1], zeroed, bit 0 = fault applied, bit 1 = a bounded wait
+ * expired. tile_flags: nullable int32 [Tm, ceil(N/128)], zeroed, ORed with
+ * bit 0 = fault applied and bit 1 = non-finite output in that block (the
+ * packed finalize's status input). */
+int sdc_abft_bf16_augmented_gemm(
+    const uint16_t* a, const uint16_t* b_rows, int64_t m, int64_t n, int64_t k,
+    int algorithm, const uint16_t* weights, int64_t row, int64_t col,
+    int64_t bit, uint16_t* d, float* observed, float* predicted,
+    float* magnitude, int32_t* hit, int32_t* tile_flags, void* workspace,
+    size_t workspace_bytes, sdc_stream_t stream);
+
 /* ---- finalize (src/cutlass_gemm/csrc/abft/common/finalize.cu:55-319) ------
  * Sums the per-tile partials of each (channel, column) in ascending tile
  * order with IEEE round-to-nearest adds, then applies the policy

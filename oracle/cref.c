@@ -342,3 +342,48 @@ int oracle_gemm_f64(int kind, const uint8_t* a, const uint8_t* sfa, const uint8_
   free(av);
   return 0;
 }
+
+/* Augmented BF16 encoding, the fixed order of the sdc_b200 augmented GEMM's
+ * encode kernel (the reference forms the same rows with tensor-core MMAs,
+ * src/cutlass_gemm/csrc/abft/fp32_bf16/bf16_augmented.h:216-320, whose
+ * internal summation order is unspecified): for each 128-row M-tile t,
+ * channel c and column kk,
+ *   acc = fmaf(w_c[row], A[row][kk], acc)   over the tile's rows ascending,
+ *   q[t * C + c][kk] = bf16(acc), rounded to nearest even.
+ * a: bf16 bits [m, k]; w: bf16 bits [C, m]; q: bf16 bits [C * tiles, k]. */
+static float bf16_value(uint16_t h) {
+  const uint32_t u = (uint32_t)h << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+static uint16_t bf16_round(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FFF; /* canonical NaN */
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+int oracle_augment_encode(const uint16_t* a, int64_t m, int64_t k, const uint16_t* w, int channels,
+                          uint16_t* q) {
+  const int64_t tiles = (m + 127) / 128;
+  float* acc = (float*)malloc(sizeof(float) * k);
+  if (!acc) return 1;
+  for (int64_t t = 0; t < tiles; ++t) {
+    const int64_t row_end = (t + 1) * 128 < m ? (t + 1) * 128 : m;
+    for (int c = 0; c < channels; ++c) {
+      for (int64_t kk = 0; kk < k; ++kk) acc[kk] = 0.f;
+      for (int64_t row = t * 128; row < row_end; ++row) {
+        const float wv = bf16_value(w[c * m + row]);
+        const uint16_t* ar = a + row * k;
+        for (int64_t kk = 0; kk < k; ++kk) acc[kk] = fmaf(wv, bf16_value(ar[kk]), acc[kk]);
+      }
+      uint16_t* out = q + (t * channels + c) * k;
+      for (int64_t kk = 0; kk < k; ++kk) out[kk] = bf16_round(acc[kk]);
+    }
+  }
+  free(acc);
+  return 0;
+}

@@ -47,6 +47,9 @@ def lib():
         _lib.oracle_tile_reference_subset.restype = ctypes.c_int
         _lib.oracle_observed_epilogue.argtypes = [f32, i64, i64, f32, ctypes.c_int, f32, i64]
         _lib.oracle_observed_epilogue.restype = ctypes.c_int
+        u16 = ctypes.POINTER(ctypes.c_uint16)
+        _lib.oracle_augment_encode.argtypes = [u16, i64, i64, u16, ctypes.c_int, u16]
+        _lib.oracle_augment_encode.restype = ctypes.c_int
     return _lib
 
 
@@ -177,3 +180,19 @@ def gemm_rows_f64(kind, a, sfa, b, sfb, m, n, k, rows, chunk=2048):
         out[:, c0:c1] = av @ bv.T
         bound[:, c0:c1] = np.abs(av) @ np.abs(bv).T
     return out, bound
+
+
+def augment_encode(a_bits, w_bits):
+    """Checksum rows of the augmented BF16 GEMM as bf16 bit patterns
+    [C * ceil(m/128), k] from bf16 bits A [m, k] and weights [C, m]."""
+    a_bits = np.ascontiguousarray(a_bits, dtype=np.uint16)
+    w_bits = np.ascontiguousarray(w_bits, dtype=np.uint16)
+    m, k = a_bits.shape
+    channels = w_bits.shape[0]
+    q = np.zeros((channels * ((m + 127) // 128), k), np.uint16)
+    u16 = ctypes.POINTER(ctypes.c_uint16)
+    rc = lib().oracle_augment_encode(a_bits.ctypes.data_as(u16), m, k, w_bits.ctypes.data_as(u16), channels,
+                                     q.ctypes.data_as(u16))
+    if rc:
+        raise MemoryError("oracle allocation failed")
+    return q

@@ -35,6 +35,7 @@ CUDA_SOURCES = [
     "gemm.cu",
     "api.cu",
     "locate.cu",
+    "augmented.cu",
 ]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

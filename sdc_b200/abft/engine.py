@@ -146,6 +146,7 @@ class _Timer:
 
 def call_context(prepared, cfg, fault, context, selected, output, method=None):
     """The report context: the caller's context plus what ran and how."""
+    augmented = cfg.reference_mode == "augmented"
     fused = cfg.reference_mode in {"input_fused", "augmented"}
     native = cfg.implementation == "native"
     policy = getattr(method, "compiled_policy", None)
@@ -156,17 +157,25 @@ def call_context(prepared, cfg, fault, context, selected, output, method=None):
         injection_point = "post_alpha_fp32_epilogue_before_output_cast"
     else:
         injection_point = "prepared_input_codes"
-    if native:
+    if augmented:
+        # BF16-rounded checksum rows and row numbers: no single-element ratio.
+        location = "disabled_for_low_precision_encoding"
+    elif native:
         location = "device_ratio_locator" if cfg.locate and channels == 2 else "disabled_for_native_policy"
     else:
         location = "disabled_for_detection_only_method" if channels == 1 else "single_output_element"
+    if augmented:
+        algorithm = "augmented_gemm"
+    else:
+        algorithm = "input_fused_fp32_projection" if fused else "separate_projection_arithmetic"
     described = {
         "fault": asdict(fault), "fault_selected": selected, "precision": prepared.precision,
         "scaling": getattr(prepared, "scaling", SCALING[prepared.precision]),
         "reference_mode": cfg.reference_mode, "implementation": cfg.implementation,
-        "threshold_scale": cfg.threshold_scale, "checksum_input_precision": "fp32",
-        "reference_algorithm": "input_fused_fp32_projection" if fused else "separate_projection_arithmetic",
-        "reference_layout": cfg.reference_layout if fused else None, "augmented_rows_per_data_tile": 0,
+        "threshold_scale": cfg.threshold_scale, "checksum_input_precision": "bf16" if augmented else "fp32",
+        "reference_algorithm": algorithm,
+        "reference_layout": cfg.reference_layout if fused and not augmented else None,
+        "augmented_rows_per_data_tile": channels if augmented else 0,
         "compiled_policy": policy.metadata() if policy is not None else None,
         "verification_backend": "cuda_policy" if native else "python_method",
         "compiled_reference_format": dict(policy.reference_formats).get(cfg.reference_mode) if policy else None,
@@ -258,10 +267,11 @@ def execute_prepared(prepared, abft_config=None, fault_config=None, context=None
     cfg, fault = parse_abft_config(abft_config), parse_fault_config(fault_config)
     seams = {"raw_fn": raw_fn, "reference_mm": reference_mm, "collector_fn": collector_fn,
              "reference_collector_fn": reference_collector_fn}
-    if cfg.reference_mode == "augmented":
-        raise NotImplementedError("the augmented (BF16) reference mode is outside the FP8/NVFP4 path")
-    if cfg.reference_mode == "input_fused":
-        if prepared.precision not in INPUT_REFERENCE_PRECISIONS and reference_collector_fn is None:
+    if cfg.reference_mode == "augmented" and prepared.precision != "bf16":
+        raise ValueError("augmented currently requires BF16 GEMM")
+    if cfg.reference_mode in {"input_fused", "augmented"}:
+        if (cfg.reference_mode == "input_fused" and prepared.precision not in INPUT_REFERENCE_PRECISIONS
+                and reference_collector_fn is None):
             raise NotImplementedError(f"input_fused reference is not implemented for {prepared.precision}")
         if fault.location in {"a", "b"}:
             raise ValueError("input_fused protects computation only; input memory faults require separate reference")
@@ -284,10 +294,10 @@ def execute_prepared(prepared, abft_config=None, fault_config=None, context=None
     policy = method.validate_execution(prepared, cfg) if method is not None else None
     plan = _Plan(prepared, cfg, fault, context, method, policy, selected)
     if cfg.implementation == "native":
-        from .native import execute_input_fused
+        from .native import execute_augmented, execute_input_fused
 
-        return execute_input_fused(prepared, cfg, fault, context, method=method, policy=policy,
-                                   profile_scope=profile_scope)
+        run = execute_augmented if cfg.reference_mode == "augmented" else execute_input_fused
+        return run(prepared, cfg, fault, context, method=method, policy=policy, profile_scope=profile_scope)
     return _run_reference(plan, seams, profile_scope)
 
 
@@ -297,7 +307,8 @@ def _run_reference(plan, seams, profile_scope):
     prepared, cfg, fault, method = plan.prepared, plan.cfg, plan.fault, plan.method
     device = prepared.a.device
     algorithm = plan.policy.algorithm if plan.policy is not None else 0
-    fused_reference = cfg.reference_mode == "input_fused"
+    augmented = cfg.reference_mode == "augmented"
+    fused_reference = cfg.reference_mode in {"input_fused", "augmented"}
     timer = _Timer(cfg.timing, device, profile_scope)
     started = time.perf_counter()
     if method is not None:
@@ -306,6 +317,8 @@ def _run_reference(plan, seams, profile_scope):
     with timer.phase("reference"):
         if method is None:
             plan.state = None
+        elif augmented:
+            plan.state = method.prepare_augmented(prepared, cfg)
         elif fused_reference:
             plan.state = method.prepare_fused(prepared, cfg)
         else:
@@ -327,6 +340,8 @@ def _run_reference(plan, seams, profile_scope):
         """(output, observed, hit, predicted, magnitude) of the input-fused GEMM."""
         if seams["reference_collector_fn"] is not None:
             return seams["reference_collector_fn"](operands, weights, injected)
+        if augmented:
+            return operands.augmented_native(weights, injected, algorithm=algorithm)
         return operands.collected_reference_native(weights, injected, algorithm=algorithm,
                                                    layout=cfg.reference_layout)
 

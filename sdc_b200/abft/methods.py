@@ -216,6 +216,15 @@ class ProjectionChecksum(AbftMethod):
     def prepare_fused(self, operands, config):
         return self._fresh_state(operands)
 
+    def prepare_augmented(self, operands, config):
+        """Encoding weights in the BF16 input format shared with A and the
+        checksum rows (rounded row numbers above 256 are not all distinct)."""
+        if operands.precision != "bf16":
+            raise ValueError("augmented currently requires BF16 GEMM")
+        state = self._fresh_state(operands, augmented=True)
+        state["weights"] = state["weights"].to(torch.bfloat16).contiguous()
+        return state
+
     def bind_reference(self, predicted_partials, magnitude_partials, state):
         return {**state, "expected": self.propagate(predicted_partials, state),
                 "magnitude": self.propagate(magnitude_partials, state)}

@@ -16,6 +16,11 @@ reads). One call is:
    the device (``"correct"``), or a full recompute judged against the first
    call's reference (``"recompute"``, and ``"correct"`` when nothing was
    located); then the engine's shared tail (commit, diagnostics, raise).
+
+The augmented BF16 mode (``execute_augmented``) follows the same steps with
+BF16 encoding weights, the compact augmented GEMM and the packed finalize.
+Both mirror src/abft/native.py of the reference (``_builtin_weights``,
+``_execute_native``).
 """
 from __future__ import annotations
 
@@ -45,18 +50,18 @@ class WeightCache:
             entry = self._entries.get(key)
             return None if entry is None else entry[0]
 
-    def weights(self, method, prepared, policy):
+    def weights(self, method, prepared, policy, dtype=torch.float32):
         device = torch.device(prepared.a.device)
         stream = torch.cuda.current_stream(device)
-        key = (policy.algorithm, stream.device.index, prepared.m)
+        key = (policy.algorithm, stream.device.index, prepared.m, dtype)
         with self._lock:
             entry = self._entries.pop(key, None)
             if entry is None:
-                made = method.projection_weights(prepared).to(torch.float32).contiguous()
+                made = method.projection_weights(prepared).to(dtype).contiguous()
                 ready = torch.cuda.Event()
                 ready.record(stream)
                 entry = (made, ready, stream.cuda_stream)
-            if entry[0].numel() * 4 <= self.max_bytes:
+            if entry[0].numel() * entry[0].element_size() <= self.max_bytes:
                 self._entries[key] = entry
                 self._evict()
         weights, ready, producer = entry
@@ -67,7 +72,7 @@ class WeightCache:
 
     def _evict(self):
         while len(self._entries) > self.max_entries or sum(
-                item[0].numel() * 4 for item in self._entries.values()) > self.max_bytes:
+                item[0].numel() * item[0].element_size() for item in self._entries.values()) > self.max_bytes:
             self._entries.popitem(last=False)
 
 
@@ -76,16 +81,20 @@ WEIGHTS = WeightCache()
 
 def _method_state(method, prepared, cfg, policy):
     """Weights (and optional thresholds) of this call. Only unmodified
-    builtin methods use the cache; plugins prepare their own."""
-    customised = any(hook in vars(method) for hook in ("projection_weights", "prepare_fused"))
+    builtin methods use the cache; plugins prepare their own. The augmented
+    mode encodes with BF16 weights (the input format of A)."""
+    augmented = cfg.reference_mode == "augmented"
+    customised = any(hook in vars(method) for hook in ("projection_weights", "prepare_fused", "prepare_augmented"))
     if type(method) in {Classic, Sum} and not method.stateful and not customised:
-        return {"weights": WEIGHTS.weights(method, prepared, policy), "m": prepared.m, "n": prepared.n}
-    return method.prepare_fused(prepared, cfg)
+        dtype = torch.bfloat16 if augmented else torch.float32
+        return {"weights": WEIGHTS.weights(method, prepared, policy, dtype), "m": prepared.m, "n": prepared.n,
+                **({"augmented": True} if augmented else {})}
+    return method.prepare_augmented(prepared, cfg) if augmented else method.prepare_fused(prepared, cfg)
 
 
-def _check_state(state, prepared, policy):
+def _check_state(state, prepared, policy, dtype=torch.float32):
     weights = state["weights"]
-    if (weights.ndim != 2 or weights.shape != (policy.channels, prepared.m) or weights.dtype != torch.float32
+    if (weights.ndim != 2 or weights.shape != (policy.channels, prepared.m) or weights.dtype != dtype
             or weights.device != prepared.a.device or not weights.is_contiguous()):
         raise ValueError("Native method weights do not match compiled policy channels/format/device")
     thresholds = state.get("thresholds")
@@ -164,6 +173,62 @@ def execute_input_fused(prepared, cfg, fault, context, *, method=None, policy=No
             tensors["recovered"], tensors["recheck_failed"] = fixed, ~fixed
             report.context["recovery_action"] = "located_element_recomputed"
             return None, None
+        replacement, retry_evidence = gemm((-1, -1, -1))
+        _, checked, _ = _decisions(finalize(retry_evidence, first_reference), statistics)
+        report.context["recovery_action"] = "full_recompute"
+        return replacement, checked
+
+    return _finish(plan, report, output, recheck, timer, started)
+
+
+def execute_augmented(prepared, cfg, fault, context, *, method=None, policy=None, profile_scope=None):
+    """The augmented BF16 execution: one launch computes the output, the
+    observed and output-magnitude partials (data tiles' epilogue) and the
+    predicted partials (the BF16 checksum rows as extra M-tiles), with
+    per-tile fault/non-finite flags; then the packed device finalize. No
+    locator: BF16-rounded checksum rows and row numbers cannot place a
+    single element. Recovery is the full recompute judged against the first
+    call's reference (``"correct"`` falls back to it, nothing is located)."""
+    from .. import ops, require_device
+
+    if method is None:
+        method = get_method(cfg.method)
+        if method.stateful:
+            raise ValueError("Stateful native methods require a retained method_instance or MethodSession")
+    policy = method.validate_execution(prepared, cfg) if policy is None else policy
+    if cfg.reference_mode != "augmented" or prepared.precision != "bf16":
+        raise ValueError("augmented currently requires BF16 GEMM")
+    statistics = cfg.diagnostics or method.needs_diagnostics
+    require_device(prepared.a.device)
+    plan = _Plan(prepared, cfg, fault, context, method, policy, _selected(fault, context))
+    injection = _injection(prepared, fault, plan.selected, accumulator_only=True)
+    timer = _Timer(cfg.timing, prepared.a.device, profile_scope)
+    started = time.perf_counter()
+
+    with timer.phase("reference"):
+        plan.state = _method_state(method, prepared, cfg, policy)
+        weights, thresholds = _check_state(plan.state, prepared, policy, torch.bfloat16)
+
+    def gemm(injected):
+        output, partials, tile_flags = prepared.augmented_compact(weights, injected, algorithm=policy.algorithm)
+        return output, (partials, tile_flags)
+
+    def finalize(evidence, reference):
+        return ops.abft_finalize(*evidence, prepared.n, cfg.atol, cfg.rtol, reference, statistics,
+                                 policy.algorithm, thresholds)
+
+    with timer.phase("execute"):
+        output, evidence = gemm(injection)
+    with timer.phase("finalize"):
+        first_reference, tensors, _ = _decisions(finalize(evidence, None), statistics)
+    del evidence
+    plan.state = {**plan.state, "reference": first_reference}
+    described = call_context(prepared, cfg, fault, context, plan.selected, output, method)
+    described["reference_operand_reuse"] = "checksum_rows_as_extra_m_tiles"
+    described["threshold_source"] = "method_state" if thresholds is not None else "config_atol_rtol"
+    report = AbftReport(tensors, described, cfg.method, "augmented_native", timer.events)
+
+    def recheck():
         replacement, retry_evidence = gemm((-1, -1, -1))
         _, checked, _ = _decisions(finalize(retry_evidence, first_reference), statistics)
         report.context["recovery_action"] = "full_recompute"

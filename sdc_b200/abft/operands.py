@@ -4,9 +4,11 @@ Mirrors src/abft/operands.py of the reference (``PreparedGemm``): the same
 fields, ``prepare`` (FP8/NVFP4 through this library's quantizer, B transposed
 to K-major rows), ``raw_native`` / ``collected_native`` /
 ``collected_reference_native`` op routing, the CPU-capable ``decode_block``
-and ``injected`` input-code bit flips (NVFP4 nibble rule). FP32/BF16 operands
-are kept for the separate reference mode and CPU tests; their native GEMMs
-are outside this path. Extension: FP8 ``scaling="blockwise"`` (1 x 128 A and
+and ``injected`` input-code bit flips (NVFP4 nibble rule). BF16 operands run on
+the tcgen05 BF16 GEMM (``raw_native``) and the augmented ABFT GEMM
+(``augmented_native`` / ``augmented_compact``); FP32 operands are kept for
+the separate reference mode and CPU tests, their native GEMMs are outside
+this path. Extension: FP8 ``scaling="blockwise"`` (1 x 128 A and
 128 x 128 B fp32 block scales in ``sfa``/``sfb``, no alpha) routes to the
 block-scaled ops, whose input-fused prediction has the K-slice layout only.
 """
@@ -62,9 +64,15 @@ class PreparedGemm:
         n = b.shape[1]
         if min(m, n, k) <= 0:
             raise ValueError("Empty GEMM is not supported")
-        if precision in {"fp32", "bf16"}:
-            dtype = torch.float32 if precision == "fp32" else torch.bfloat16
-            return cls(a.to(dtype), b.to(dtype), precision, m, n, k)
+        if precision == "bf16":
+            # The sm_100a GEMM reads A row-major and B as K-major rows, i.e.
+            # B [K, N] column-major: repack once here instead of every call.
+            a, b = a.to(torch.bfloat16).contiguous(), b.to(torch.bfloat16)
+            if not b.T.is_contiguous():
+                b = b.T.contiguous().T
+            return cls(a, b, precision, m, n, k)
+        if precision == "fp32":
+            return cls(a.float(), b.float(), precision, m, n, k)
         from .. import require_device
         from ..gemm.quantization import quantize, quantize_blockwise
 
@@ -121,6 +129,23 @@ class PreparedGemm:
             return ops.abft_fp8_block_reference_mm(*self._native_args(), weights, *fault, algorithm, nonfinite)
         op = ops.abft_fp8_reference_mm if self.precision == "fp8" else ops.abft_nvfp4_reference_mm
         return op(*self._native_args(), weights, *fault, algorithm, nonfinite, LAYOUTS[layout])
+
+    def augmented_native(self, weights, fault=(-1, -1, -1), *, algorithm=0):
+        """Output, observed, hit, predicted and magnitude partials of the
+        augmented BF16 GEMM (the checksum rows are extra M-tiles of the same
+        tcgen05 GEMM; magnitude is the output-side sum |w v|)."""
+        if self.precision != "bf16":
+            raise ValueError("augmented currently requires BF16 GEMM")
+        from .. import require_device
+        require_device(self.a.device)
+        return _ops().abft_augmented_mm(self.a, self.b, weights, *fault, algorithm)
+
+    def augmented_compact(self, weights, fault=(-1, -1, -1), *, algorithm=0):
+        """Output, packed partials [3, C, Tm, padded_N] and per-tile flags of
+        the augmented BF16 GEMM (the native engine's form)."""
+        if self.precision != "bf16":
+            raise ValueError("augmented currently requires BF16 GEMM")
+        return _ops().abft_augmented_compact(self.a, self.b, weights, *fault, algorithm)
 
     def decode_block(self, start, end):
         """Decoded fp32 A[:, start:end] and B[start:end, :] (works on the CPU)."""

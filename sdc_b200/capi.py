@@ -53,6 +53,11 @@ PROTOTYPES = {
     "sdc_abft_fp8_block_gemm": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
     "sdc_abft_fp8_block_reference_gemm": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _size, _vp]),
     "sdc_abft_correct_fp8_block": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
+    "sdc_bf16_gemm": (_int, [_vp, _vp, _i64, _i64, _i64, _vp, _vp]),
+    "sdc_abft_augment_encode": (_int, [_vp, _i64, _i64, _int, _vp, _vp, _vp]),
+    "sdc_abft_augmented_workspace_bytes": (_size, [_int, _i64, _i64]),
+    "sdc_abft_bf16_augmented_gemm": (_int, [_vp, _vp, _i64, _i64, _i64, _int, _vp, _i64, _i64, _i64, _vp, _vp, _vp,
+                                            _vp, _vp, _vp, _vp, _size, _vp]),
     "sdc_abft_finalize_workspace_bytes": (_size, [_int, _i64, _i64]),
     "sdc_abft_finalize": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _float, _float, _vp, _int, _int, _vp, _vp, _vp, _int, _vp, _vp, _vp, _vp, _size, _vp]),
     "sdc_abft_finalize_noalloc": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _float, _float, _vp, _int, _int, _vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),

@@ -338,6 +338,28 @@ __device__ __forceinline__ void mma_f8f6f4(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] . B[smem]^T, bf16 x bf16 -> fp32 (kind::f16);
+// PAIR: one MMA over the CTA pair (M = 256), issued by the leader.
+template <bool PAIR = false>
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  if constexpr (PAIR) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
+}
+
 // Block-scaled e2m1 x e2m1 with ue4m3 scales per 16 K (NVFP4), fp32
 // accumulate; PAIR: one MMA over the CTA pair (M = 256), issued by the leader.
 template <bool PAIR = false>
@@ -435,6 +457,12 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) { return smem_desc
 // Instruction descriptor of kind::f8f6f4 e4m3 x e4m3 -> fp32, K-major A and B.
 __host__ __device__ constexpr uint32_t idesc_e4m3(int m, int n) {
   return (1u << 4) /*D fp32*/ | (0u << 7) /*A e4m3*/ | (0u << 10) /*B e4m3*/ |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// Instruction descriptor of kind::f16 bf16 x bf16 -> fp32, K-major A and B.
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4) /*D fp32*/ | (1u << 7) /*A bf16*/ | (1u << 10) /*B bf16*/ |
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 

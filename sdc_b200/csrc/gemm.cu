@@ -77,7 +77,11 @@ constexpr int kGroupM = 16;        // M-tiles per raster group
 constexpr int kABytes = kBM * kBKBytes;
 constexpr int kSfaBytes = 4 * 512;
 constexpr int kSfbBytes = 4 * 512 * (kBN / 128);  // per k-block: 4 k-steps x the tile's B row groups
-constexpr int kRedFloats = kChunks * 4 * 2 * 32;
+// Reduced channels of the epilogue per 32-column chunk and row quarter: the
+// checksum channels (<= 2), plus as many output-magnitude channels for the
+// augmented bf16 GEMM.
+__host__ __device__ constexpr int red_channels(Kind k) { return k == Kind::kBf16 ? 4 : 2; }
+__host__ __device__ constexpr int red_floats(Kind k) { return kChunks * 4 * red_channels(k) * 32; }
 
 // CTA pairs: each CTA stages its 128 rows of A and 128 of the tile's 256 B
 // rows (NVFP4: plus its own A scales and all 256 rows' B scales); one
@@ -89,7 +93,7 @@ __host__ __device__ constexpr int stage_bytes(Kind k, bool pair = false) {
   return kABytes + b_stage_bytes(k, pair) + (k == Kind::kNvf4 ? kSfaBytes + kSfbBytes : 0);
 }
 __host__ __device__ constexpr int num_stages(Kind k, bool pair) {
-  return pair ? (k == Kind::kFp8 ? 6 : k == Kind::kFp8Block ? 8 : 5) : kStages;
+  return pair ? (k == Kind::kFp8 || k == Kind::kBf16 ? 6 : k == Kind::kFp8Block ? 8 : 5) : kStages;
 }
 // Checked e4m3 launches stage the prediction's B slices (tile rows x one
 // 64-byte K slice) in shared memory with their own TMA copies: a warp-wide
@@ -99,7 +103,7 @@ __host__ __device__ constexpr int pred_slice_bytes(Kind k, bool chk) {
   return (chk && is_e4m3(k)) ? tile_n(k) * 64 : 0;
 }
 __host__ __device__ constexpr int smem_bytes(Kind k, bool pair = false, bool chk = false) {
-  return 1024 + num_stages(k, pair) * stage_bytes(k, pair) + kRedFloats * 4 + pred_slice_bytes(k, chk) + 512;
+  return 1024 + num_stages(k, pair) * stage_bytes(k, pair) + red_floats(k) * 4 + pred_slice_bytes(k, chk) + 512;
 }
 __host__ __device__ constexpr int num_acc(Kind k) { return k == Kind::kNvf4 ? 1 : 2; }
 // Warp roles. Tensorwise FP8: 0 TMA, 1 MMA, 2-5 epilogue, 6-9 prediction
@@ -110,7 +114,7 @@ __host__ __device__ constexpr int num_acc(Kind k) { return k == Kind::kNvf4 ? 1 
 // from warpgroup 0 to the epilogue warps (setmaxnreg). NVFP4 has a single
 // accumulator: its epilogue warps load their whole half of it before the
 // math, so the next tile's MMAs start after the loads, not after the stores.
-__host__ __device__ constexpr bool is_wide(Kind k) { return k != Kind::kFp8; }
+__host__ __device__ constexpr bool is_wide(Kind k) { return k != Kind::kFp8 && k != Kind::kBf16; }
 __host__ __device__ constexpr int epi_warp0(bool wide) { return wide ? 4 : 2; }
 __host__ __device__ constexpr int acc_warps(bool wide) { return wide ? 8 : 4; }
 __host__ __device__ constexpr int pred_warp0(bool wide) { return epi_warp0(wide) + acc_warps(wide); }
@@ -171,6 +175,13 @@ struct Params {
   int32_t* watchdog;
   uint64_t wait_limit_ns;  // every bounded wait gives up after this long
   int32_t pace_extra;      // test hook: added to every pacing target (0 in use)
+  // Augmented bf16 GEMM: M-tiles tiles_m .. tiles_m_all - 1 hold the
+  // checksum rows (aug_rows of them, row t * C + c); tile_flags (nullable)
+  // [tiles_m][flag_cols] collects per-128-column status bits (ORed).
+  int32_t tiles_m_all;
+  int32_t aug_rows;
+  int32_t* tile_flags;
+  int32_t flag_cols;
 };
 
 __device__ __forceinline__ void raster(int t, int rows, int group_rows, int tiles_n, int& r, int& nt) {
@@ -190,10 +201,10 @@ template <bool PAIR>
 __device__ __forceinline__ void work_coords(int w, const Params& p, uint32_t rank, int& mt, int& nt) {
   if constexpr (PAIR) {
     int mt2;
-    raster(w, (p.tiles_m + 1) / 2, kGroupM / 2, p.tiles_n, mt2, nt);
+    raster(w, (p.tiles_m_all + 1) / 2, kGroupM / 2, p.tiles_n, mt2, nt);
     mt = 2 * mt2 + static_cast<int>(rank);
   } else {
-    raster(w, p.tiles_m, kGroupM, p.tiles_n, mt, nt);
+    raster(w, p.tiles_m_all, kGroupM, p.tiles_n, mt, nt);
   }
 }
 
@@ -270,6 +281,10 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
   // scale_a * scale_b * partial into tile totals held in their registers and
   // run the epilogue from there.
   constexpr bool BLK = KIND == Kind::kFp8Block;
+  // Augmented bf16 GEMM: checksum-row M-tiles, and the epilogue also reduces
+  // the output-side magnitude |w_c| |v| (R reduced channels in all).
+  constexpr bool AUG = KIND == Kind::kBf16 && C > 0;
+  constexpr int R = AUG ? 2 * C : C;
   constexpr bool WIDE = is_wide(KIND);
   constexpr int kAccWarps = acc_warps(WIDE);
   constexpr int kEpi0 = epi_warp0(WIDE);
@@ -279,7 +294,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
                                              ~static_cast<uintptr_t>(1023));
   float* red = reinterpret_cast<float*>(smem + kS * kStageBytes);
   // 1024-byte aligned: the stages and the reduction area are multiples of 1 KiB.
-  uint8_t* pred_slice = reinterpret_cast<uint8_t*>(red + kRedFloats);
+  uint8_t* pred_slice = reinterpret_cast<uint8_t*>(red + red_floats(KIND));
   uint64_t* full = reinterpret_cast<uint64_t*>(pred_slice + pred_slice_bytes(KIND, CHK));
   uint64_t* empty = full + kS;
   uint64_t* acc_full = empty + kS;
@@ -355,13 +370,14 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
   // thread owning output row `row`: fault injection, nonfinite check, the
   // observed checksum partials of the warp's 32 rows into `red`, the store.
   auto emit_chunk = [&](float (&v)[32], int q, int row, bool row_ok, int c0, int chunk, const float* w,
-                        bool& nonfinite) {
+                        bool& nonfinite, bool& faulted) {
     if (C > 0 && p.fbit >= 0 && row == p.frow && p.fcol >= c0 && p.fcol < c0 + 32) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         if (c0 + j == p.fcol) v[j] = __uint_as_float(__float_as_uint(v[j]) ^ (1u << p.fbit));
       }
       atomicOr(p.hit, 1);
+      faulted = true;
     }
     if constexpr (BF16OUT) {
       // The output as stored first: one round-to-nearest conversion per
@@ -374,7 +390,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
 #pragma unroll
       for (int j = 0; j < 16; ++j) packed[j] = bf16x2_bits(v[2 * j], v[2 * j + 1]);
       const bool full = c0 + 32 <= p.n;
-      if (C > 0 && p.nonfinite != nullptr && row_ok) {
+      if (C > 0 && (AUG || p.nonfinite != nullptr) && row_ok) {
         uint32_t flag = 0;
         if (full) {
 #pragma unroll
@@ -427,7 +443,23 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
         for (int c = 0; c < C; ++c) x[c][i] = fmaf(w[c], kept, __shfl_xor_sync(0xffffffffu, w[c] * sent, 16));
       }
 #pragma unroll
-      for (int c = 0; c < C; ++c) red[((chunk * 4 + q) * C + c) * 32 + lane] = transpose_reduce(x[c], lane);
+      for (int c = 0; c < C; ++c) red[((chunk * 4 + q) * R + c) * 32 + lane] = transpose_reduce(x[c], lane);
+      if constexpr (AUG) {
+        // Output-side magnitude sum_rows |w_c v| = sum_rows |w_c| |v|, in the
+        // same butterfly order as the observed sum.
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float sent = fabsf(upper ? v[i] : v[i + 16]);
+          const float kept = fabsf(upper ? v[i + 16] : v[i]);
+#pragma unroll
+          for (int c = 0; c < C; ++c) {
+            const float wa = fabsf(w[c]);
+            x[c][i] = fmaf(wa, kept, __shfl_xor_sync(0xffffffffu, wa * sent, 16));
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < C; ++c) red[((chunk * 4 + q) * R + C + c) * 32 + lane] = transpose_reduce(x[c], lane);
+      }
     }
     if constexpr (!BF16OUT) {
       if (row_ok) {
@@ -446,21 +478,40 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
       named_barrier(1, kAccThreads);
       if (live) {
         const int e = static_cast<int>(threadIdx.x) - 32 * kEpi0;
-        for (int idx = e; idx < kTileChunks * C * 32; idx += kAccThreads) {
-          const int chunk = idx / (C * 32);
-          const int rem = idx - chunk * C * 32;
-          const int c = rem >> 5;
+        for (int idx = e; idx < kTileChunks * R * 32; idx += kAccThreads) {
+          const int chunk = idx / (R * 32);
+          const int rem = idx - chunk * R * 32;
+          const int r = rem >> 5;
           const int col = rem & 31;
           float sum = 0.f;
 #pragma unroll
-          for (int qq = 0; qq < 4; ++qq) sum += red[((chunk * 4 + qq) * C + c) * 32 + col];
+          for (int qq = 0; qq < 4; ++qq) sum += red[((chunk * 4 + qq) * R + r) * 32 + col];
           const int gcol = n0 + chunk * 32 + col;
           if (gcol < p.padded_n && mt < p.tiles_m) {
-            p.observed[(static_cast<int64_t>(c) * p.tiles_m + mt) * p.padded_n + gcol] = sum;
+            // Channels r >= C (augmented only) are the output magnitudes.
+            float* plane = r < C ? p.observed : p.magnitude;
+            const int c = r < C ? r : r - C;
+            plane[(static_cast<int64_t>(c) * p.tiles_m + mt) * p.padded_n + gcol] = sum;
           }
         }
       }
       named_barrier(1, kAccThreads);
+    }
+  };
+  // Augmented bf16: the per-tile status (fault applied, non-finite output)
+  // of this CTA's 128 rows, ORed into both 128-column blocks of the tile.
+  // Every epilogue thread takes part (the decision is CTA-uniform).
+  auto store_tile_flags = [&](int mt, int nt, bool faulted, bool nonfinite) {
+    if constexpr (AUG) {
+      const bool any_fault = named_barrier_or(1, kAccThreads, faulted);
+      const bool any_nonfinite = named_barrier_or(1, kAccThreads, nonfinite);
+      if (p.tile_flags != nullptr && threadIdx.x == 32 * kEpi0 && mt < p.tiles_m) {
+        const int32_t word = (any_fault ? 1 : 0) | (any_nonfinite ? 2 : 0);
+        for (int half = 0; half < kTN / 128; ++half) {
+          const int block = nt * (kTN / 128) + half;
+          if (word != 0 && block < p.flag_cols) atomicOr(p.tile_flags + static_cast<int64_t>(mt) * p.flag_cols + block, word);
+        }
+      }
     }
   };
 
@@ -485,11 +536,16 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
           }
           uint8_t* sa = smem + s * kStageBytes;
           uint8_t* sb = sa + kABytes;
+          // Augmented bf16: the M-tiles after the data tiles read the checksum
+          // rows (tensor map tm_sfa), from row 0 of that matrix.
+          const bool aug_tile = AUG && mt >= p.tiles_m;
+          const CUtensorMap* map_a = aug_tile ? &tm_sfa : &tm_a;
+          const int32_t row_a = (aug_tile ? mt - p.tiles_m : mt) * kBM;
           if constexpr (PAIR) {
             // Both halves complete on the leader's barrier, which expects both.
             const uint32_t bar = mapa_shared(full + s, 0);
             if (leader) mbar_arrive_expect_tx(full + s, 2 * kStageBytes);
-            tma_load_2d_pair(sa, &tm_a, bar, kb * kBKBytes, mt * kBM);
+            tma_load_2d_pair(sa, map_a, bar, kb * kBKBytes, row_a);
             tma_load_2d_pair(sb, &tm_b, bar, kb * kBKBytes, nt * kTN + static_cast<int>(rank) * (kTN / 2));
             if constexpr (KIND == Kind::kNvf4) {
               // Own A scales; the B scales of all the tile's rows (each CTA's
@@ -502,7 +558,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
             continue;
           }
           mbar_arrive_expect_tx(full + s, kStageBytes);
-          tma_load_2d(sa, &tm_a, full + s, kb * kBKBytes, mt * kBM);
+          tma_load_2d(sa, map_a, full + s, kb * kBKBytes, row_a);
           tma_load_2d(sb, &tm_b, full + s, kb * kBKBytes, nt * kTN);
           if constexpr (KIND == Kind::kNvf4) {
             uint8_t* ssfa = sb + kBStage;
@@ -582,7 +638,9 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
     // ---------------- MMA issuer ----------------
     if (lane == 0 && leader) {
       constexpr int kMmaM = PAIR ? 2 * kBM : kBM;
-      constexpr uint32_t idesc = KIND == Kind::kFp8 ? idesc_e4m3(kMmaM, kTN) : idesc_nvf4(kMmaM, kTN);
+      constexpr uint32_t idesc = KIND == Kind::kFp8    ? idesc_e4m3(kMmaM, kTN)
+                                 : KIND == Kind::kBf16 ? idesc_bf16(kMmaM, kTN)
+                                                       : idesc_nvf4(kMmaM, kTN);
       uint32_t kbg = 0;
       int i = 0;
       for (int t = work_first; t < p.num_work && !*abort_flag; t += work_step, ++i) {
@@ -623,6 +681,9 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
               } else {
                 mma_f8f6f4(d_tmem, adesc, bdesc, idesc, acc);
               }
+            } else if constexpr (KIND == Kind::kBf16) {
+              // 16 bf16 K per MMA: 32 bytes of the swizzle atom, as for e4m3.
+              mma_bf16<PAIR>(d_tmem, adesc, bdesc, idesc, acc);
             } else {
               mma_nvf4<PAIR>(d_tmem, adesc, bdesc, idesc, tmem + kSfaCol + 4 * j,
                              tmem + kSfbCol + 4 * sfb_groups(KIND) * j, acc);
@@ -735,7 +796,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
         }
         const bool live = !named_barrier_or(1, kAccThreads, !ok || *abort_flag != 0);
         if (live) {
-          bool nonfinite = false;
+          bool nonfinite = false, faulted = false;
 #pragma unroll
           for (int cc = 0; cc < kHalfCols / 32; ++cc) {
             float v[32];
@@ -745,7 +806,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
               v[2 * j + 1] = total[cc * 16 + j].y;
             }
             const int chunk = half * (kHalfCols / 32) + cc;
-            emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite);
+            emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite, faulted);
           }
           if (nonfinite) atomicExch(p.nonfinite, 1);
         }
@@ -760,7 +821,8 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     constexpr int kWarpChunks = kTileChunks * 4 / kAccWarps;  // 32-column chunks per warp
     const int first_chunk = ((warp - kEpi0) >> 2) * kWarpChunks;
-    const float alpha = *p.alpha;
+    // bf16 GEMMs have no alpha: the fp32 accumulator is the value (times 1).
+    const float alpha = KIND == Kind::kBf16 ? 1.f : *p.alpha;
     int i = 0;
     for (int t = work_first; t < p.num_work; t += work_step, ++i) {
       int mt, nt;
@@ -768,6 +830,10 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
       const int m0 = mt * kBM, n0 = nt * kTN;
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < p.m;
+      // Augmented bf16: tiles past the data tiles hold checksum rows, whose
+      // results are the predicted partials (row t * C + c -> predicted[c][t]).
+      const bool checksum_tile = AUG && mt >= p.tiles_m;
+      const int aug_row = (mt - p.tiles_m) * kBM + q * 32 + lane;
       float w[C > 0 ? C : 1];
 #pragma unroll
       for (int c = 0; c < C; ++c) w[c] = row_ok ? p.weights[static_cast<int64_t>(c) * p.m + row] : 0.f;
@@ -789,8 +855,8 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
           }
         }
       };
+      bool nonfinite = false, faulted = false;
       if (live) {
-        bool nonfinite = false;
         if constexpr (WIDE) {
           uint32_t r[kWarpChunks][32];
 #pragma unroll
@@ -803,7 +869,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(alpha, __uint_as_float(r[cc][j]));
             const int chunk = first_chunk + cc;
-            emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite);
+            emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite, faulted);
           }
         } else {
 #pragma unroll 1
@@ -815,12 +881,25 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(alpha, __uint_as_float(r[j]));
-            emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite);
+            if (checksum_tile) {
+              if (aug_row < p.aug_rows) {
+                const int c = aug_row % (C > 0 ? C : 1), tile = aug_row / (C > 0 ? C : 1);
+                float* dst = p.predicted + (static_cast<int64_t>(c) * p.tiles_m + tile) * p.padded_n;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  const int col = n0 + chunk * 32 + j;
+                  if (col < p.padded_n) dst[col] = v[j];
+                }
+              }
+            } else {
+              emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite, faulted);
+            }
           }
         }
-        if (nonfinite) atomicExch(p.nonfinite, 1);
+        if (nonfinite && p.nonfinite != nullptr) atomicExch(p.nonfinite, 1);
       }
-      store_observed(mt, n0, live);
+      store_tile_flags(mt, nt, faulted, nonfinite);
+      store_observed(mt, n0, live && !checksum_tile);
       if (threadIdx.x == 32 * kEpi0) *tiles_done = static_cast<uint32_t>(i + 1);
       if (!live) break;
     }
@@ -1137,6 +1216,9 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
   if constexpr (C > 0) {
     if (threadIdx.x == 0 && *abort_flag != 0) {
       atomicOr(p.hit, 2);
+      // Augmented calls report through their tile flags: the non-finite bit
+      // of the first entry makes the packed finalize report detected.
+      if (AUG && p.tile_flags != nullptr) atomicOr(p.tile_flags, 2);
       if (p.nonfinite != nullptr) atomicExch(p.nonfinite, 1);
     }
   }
@@ -1155,7 +1237,8 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
 
 template <Kind KIND, int C, bool BF16OUT, bool CHK, bool PAIR>
 int launch_impl(const GemmProblem& g, cudaStream_t stream) {
-  const int64_t k_bytes = is_e4m3(KIND) ? g.k : g.k / 2;
+  constexpr bool AUG = KIND == Kind::kBf16 && C > 0;
+  const int64_t k_bytes = row_bytes_of(KIND, g.k);
   CUtensorMap ta{}, tb{}, tsa{}, tsb{};
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(k_bytes), static_cast<uint64_t>(g.m)};
@@ -1195,6 +1278,15 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   } else {
     tsa = ta;
     tsb = tb;
+    if constexpr (AUG) {
+      // The checksum rows of A, read by the M-tiles after the data tiles.
+      const uint64_t dims[2] = {static_cast<uint64_t>(k_bytes), static_cast<uint64_t>(g.aug_rows)};
+      const uint64_t strides[1] = {static_cast<uint64_t>(k_bytes)};
+      const uint32_t box[2] = {kBKBytes, kBM};
+      int rc = encode_tensor_map(&tsa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(g.q), dims, strides,
+                                 box, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc != SDC_OK) return rc;
+    }
     if constexpr (CHK) {
       // The prediction's B slices: the tile's rows x 64 bytes of K, 64-byte
       // swizzle (conflict-free 16-byte reads of 8 consecutive rows).
@@ -1212,9 +1304,13 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   p.k = static_cast<int32_t>(g.k);
   p.num_kb = static_cast<int32_t>(ceil_div(k_bytes, kBKBytes));
   p.tiles_m = static_cast<int32_t>(ceil_div(g.m, kBM));
+  p.tiles_m_all = p.tiles_m + (AUG ? static_cast<int32_t>(ceil_div(g.aug_rows, kBM)) : 0);
+  p.aug_rows = AUG ? static_cast<int32_t>(g.aug_rows) : 0;
+  p.tile_flags = g.tile_flags;
+  p.flag_cols = static_cast<int32_t>(g.flag_cols);
   p.tiles_n = static_cast<int32_t>(ceil_div(g.n, tile_n(KIND)));
-  p.num_tiles = p.tiles_m * p.tiles_n;
-  p.num_work = PAIR ? static_cast<int32_t>(ceil_div(p.tiles_m, 2)) * p.tiles_n : p.num_tiles;
+  p.num_tiles = p.tiles_m_all * p.tiles_n;
+  p.num_work = PAIR ? static_cast<int32_t>(ceil_div(p.tiles_m_all, 2)) * p.tiles_n : p.num_tiles;
   if constexpr (KIND == Kind::kFp8Block) {
     p.sa = reinterpret_cast<const float*>(g.sfa);
     p.sb = reinterpret_cast<const float*>(g.sfb);
@@ -1311,8 +1407,10 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
 
 template <Kind KIND, int C, bool BF16OUT, bool CHK>
 int dispatch_pair(const GemmProblem& g, cudaStream_t stream) {
-  // CTA pairs (256-row tiles) whenever there are two M-tiles.
-  if (g.m > kBM) return launch_impl<KIND, C, BF16OUT, CHK, true>(g, stream);
+  // CTA pairs (256-row tiles) whenever there are two M-tiles (checksum-row
+  // tiles of the augmented bf16 GEMM included).
+  const int64_t rows = ceil_div(g.m, kBM) * kBM + (KIND == Kind::kBf16 && C > 0 ? g.aug_rows : 0);
+  if (rows > kBM) return launch_impl<KIND, C, BF16OUT, CHK, true>(g, stream);
   return launch_impl<KIND, C, BF16OUT, CHK, false>(g, stream);
 }
 
@@ -1339,6 +1437,9 @@ int launch_gemm(const GemmProblem& g, cudaStream_t stream) {
     SDC_CUDA_CHECK(cudaMemsetAsync(g.hit, 0, sizeof(int32_t), stream));
     if (g.nonfinite != nullptr) SDC_CUDA_CHECK(cudaMemsetAsync(g.nonfinite, 0, sizeof(int32_t), stream));
     if (g.grid_sync != nullptr) SDC_CUDA_CHECK(cudaMemsetAsync(g.grid_sync, 0, sizeof(uint32_t), stream));
+    if (g.tile_flags != nullptr) {
+      SDC_CUDA_CHECK(cudaMemsetAsync(g.tile_flags, 0, sizeof(int32_t) * ceil_div(g.m, kBM) * g.flag_cols, stream));
+    }
   }
   if (g.kind == Kind::kFp8) {
     if (g.channels == 0) return dispatch_out<Kind::kFp8, 0>(g, stream);
@@ -1349,6 +1450,12 @@ int launch_gemm(const GemmProblem& g, cudaStream_t stream) {
     if (g.channels == 0) return dispatch_out<Kind::kFp8Block, 0>(g, stream);
     if (g.channels == 1) return dispatch_out<Kind::kFp8Block, 1>(g, stream);
     return dispatch_out<Kind::kFp8Block, 2>(g, stream);
+  }
+  if (g.kind == Kind::kBf16) {
+    // bf16 row-major output only; the protected form is the augmented GEMM.
+    if (g.channels == 0) return dispatch_pair<Kind::kBf16, 0, true, false>(g, stream);
+    if (g.channels == 1) return dispatch_pair<Kind::kBf16, 1, true, false>(g, stream);
+    return dispatch_pair<Kind::kBf16, 2, true, false>(g, stream);
   }
   if (g.channels == 0) return dispatch_out<Kind::kNvf4, 0>(g, stream);
   if (g.channels == 1) return dispatch_out<Kind::kNvf4, 1>(g, stream);

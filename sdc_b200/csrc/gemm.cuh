@@ -8,8 +8,15 @@ namespace sdc {
 // kFp8Block: e4m3 codes with fp32 dequantisation scales per 1 x 128 block of
 // A (sfa: float [M][K/128]) and per 128 x 128 block of B rows (sfb: float
 // [ceil(N/128)][K/128]); bf16 row-major output.
-enum class Kind : int { kFp8 = 0, kNvf4 = 1, kFp8Block = 2 };
-__host__ __device__ constexpr bool is_e4m3(Kind k) { return k != Kind::kNvf4; }
+// kBf16: bf16 operands (kind::f16 MMA, fp32 accumulation), bf16 row-major
+// output; its protected form is the augmented GEMM (checksum rows of A as
+// extra M-tiles, see GemmProblem::q).
+enum class Kind : int { kFp8 = 0, kNvf4 = 1, kFp8Block = 2, kBf16 = 3 };
+__host__ __device__ constexpr bool is_e4m3(Kind k) { return k == Kind::kFp8 || k == Kind::kFp8Block; }
+// Bytes of one operand row of K elements.
+__host__ __device__ constexpr int64_t row_bytes_of(Kind k, int64_t elems) {
+  return k == Kind::kNvf4 ? elems / 2 : k == Kind::kBf16 ? 2 * elems : elems;
+}
 
 struct GemmProblem {
   Kind kind;
@@ -37,6 +44,17 @@ struct GemmProblem {
   uint32_t* grid_sync;
   float* predicted;        // [C, Tm, Np]
   float* magnitude;
+  // Augmented bf16 GEMM (kBf16 with channels > 0): q holds the bf16 checksum
+  // rows of A, row t * C + c = bf16(w_c^T A over M-tile t), [aug_rows, K].
+  // They run as extra M-tiles after the data tiles; their fp32 results are
+  // written to `predicted`, and the data tiles' epilogue also writes the
+  // output-side magnitude sum_rows |w_c v| to `magnitude`. tile_flags
+  // (nullable, zeroed by launch_gemm): int32 [Tm, flag_cols] of bit 0 fault
+  // applied, bit 1 non-finite output, per 128-column block.
+  const uint8_t* q;
+  int64_t aug_rows;
+  int32_t* tile_flags;
+  int64_t flag_cols;
 };
 
 // Launches the GEMM (and its fused epilogue) on `stream`. Zeroes hit/nonfinite

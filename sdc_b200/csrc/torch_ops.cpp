@@ -609,18 +609,117 @@ Tensor abft_fp8_block_correct(const Tensor& a, const Tensor& b, const Tensor& sc
   TORCH_CHECK(false, "sdc_cutlass::", name,
               " (FP32/BF16 legacy kernels) is not part of the sdc_b200 FP8/NVFP4 hot path");
 }
-Tensor mm_stub(const Tensor&, const Tensor&) { out_of_scope("mm"); }
+// ------------------------------------------------------ bf16 / augmented ----
+
+// A [M,K] and B [K,N], each packed row-major or column-major (the layouts the
+// reference accepts); the sm_100a kernels take A row-major and B as rows
+// [N,K] (K-major), so the other layouts are repacked first.
+std::pair<Tensor, Tensor> bf16_operands(const Tensor& a, const Tensor& b, const char* what) {
+  for (const Tensor* t : {&a, &b}) {
+    for (int dim = 0; dim < 2; ++dim) {
+      TORCH_CHECK(t->size(dim) > 0 && t->size(dim) <= std::numeric_limits<int>::max() - 128, what,
+                  " dimensions must be positive and fit padded int32 extents");
+    }
+  }
+  const bool a_row = a.stride(1) == 1 && a.stride(0) == a.size(1);
+  const bool a_col = a.stride(0) == 1 && a.stride(1) == a.size(0);
+  const bool b_row = b.stride(1) == 1 && b.stride(0) == b.size(1);
+  const bool b_col = b.stride(0) == 1 && b.stride(1) == b.size(0);
+  TORCH_CHECK(a_row || a_col, what, " A requires packed row-major or column-major storage");
+  TORCH_CHECK(b_row || b_col, what, " B requires packed row-major or column-major storage");
+  TORCH_CHECK(a.size(1) % 8 == 0, what, " K must be a multiple of 8 on sm_100a (16-byte operand rows)");
+  // B column-major [K,N] is already B^T row-major [N,K].
+  return {a_row ? a : a.contiguous(), b_col ? b.t() : b.t().contiguous()};
+}
+
+const uint16_t* u16(const Tensor& t) { return static_cast<const uint16_t*>(t.const_data_ptr()); }
+
+Tensor mm(const Tensor& a, const Tensor& b) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda(), "A and B must be CUDA tensors");
+  TORCH_CHECK(a.device() == b.device(), "A and B must be on the same CUDA device");
+  TORCH_CHECK(a.layout() == at::kStrided && b.layout() == at::kStrided, "A and B must be strided tensors");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2, "A and B must be two-dimensional");
+  TORCH_CHECK(a.scalar_type() == b.scalar_type(), "A and B must have the same dtype");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16,
+              "sdc_b200 mm computes BF16 operands on the tensor cores (the reference's FP32 SIMT GEMM is not "
+              "part of this library)");
+  TORCH_CHECK(a.size(1) == b.size(0), "A and B inner dimensions must match");
+  const c10::cuda::CUDAGuard guard(a.device());
+  auto [ar, br] = bf16_operands(a, b, "BF16 GEMM");
+  const int64_t m = a.size(0), n = b.size(1), k = a.size(1);
+  auto out = at::empty({m, n}, a.options());
+  check_status(sdc_bf16_gemm(u16(ar), u16(br), m, n, k, static_cast<uint16_t*>(out.data_ptr()), stream_of(a)));
+  return out;
+}
+
+struct AugmentedOut {
+  Tensor d, observed, predicted, magnitude, hit, partials, tile_flags;
+};
+
+AugmentedOut run_augmented(const Tensor& a, const Tensor& b, const Tensor& weights, int64_t row, int64_t col,
+                           int64_t bit, int64_t algorithm, bool compact) {
+  const int c = channels_of(algorithm);
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && weights.is_cuda() && a.device() == b.device() &&
+                  a.device() == weights.device(),
+              "Augmented ABFT tensors must be on the same CUDA device");
+  TORCH_CHECK(a.layout() == at::kStrided && b.layout() == at::kStrided && a.dim() == 2 && b.dim() == 2,
+              "Augmented ABFT operands must be strided matrices");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16,
+              "Augmented ABFT currently requires BF16 operands");
+  TORCH_CHECK(a.size(1) == b.size(0), "Augmented ABFT inner dimensions must match");
+  TORCH_CHECK(weights.layout() == at::kStrided && weights.scalar_type() == at::kBFloat16 && weights.dim() == 2 &&
+                  weights.size(0) == c && weights.size(1) == a.size(0) && weights.is_contiguous(),
+              "Augmented ABFT weights must be contiguous BF16 [", c, ",M]");
+  TORCH_CHECK((row == -1 && col == -1 && bit == -1) ||
+                  (row >= 0 && row < a.size(0) && col >= 0 && col < b.size(1) && bit >= 0 && bit < 32),
+              "Augmented ABFT fault must be all -1, or a valid row/column and FP32 bit 0..31");
+  const c10::cuda::CUDAGuard guard(a.device());
+  auto [ar, br] = bf16_operands(a, b, "Augmented ABFT");
+  const int64_t m = a.size(0), n = b.size(1), k = a.size(1);
+  const int64_t tm = (m + 127) / 128, nt = (n + 127) / 128, np = nt * 128;
+  AugmentedOut o;
+  o.d = at::empty({m, n}, a.options());
+  const auto f32 = a.options().dtype(at::kFloat);
+  if (compact) {
+    o.partials = at::empty({3, c, tm, np}, f32);
+    o.observed = o.partials.select(0, 0);
+    o.predicted = o.partials.select(0, 1);
+    o.magnitude = o.partials.select(0, 2);
+    o.tile_flags = at::empty({tm, nt}, a.options().dtype(at::kInt));
+  } else {
+    o.observed = at::empty({c, tm, np}, f32);
+    o.predicted = at::empty_like(o.observed);
+    o.magnitude = at::empty_like(o.observed);
+    o.hit = at::empty({1}, a.options().dtype(at::kInt));
+  }
+  const size_t ws_bytes = sdc_abft_augmented_workspace_bytes(static_cast<int>(algorithm), m, k);
+  Tensor ws = workspace(a, ws_bytes + 256);
+  void* base = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(ws.data_ptr()) + 255) & ~uintptr_t{255});
+  check_status(sdc_abft_bf16_augmented_gemm(
+      u16(ar), u16(br), m, n, k, static_cast<int>(algorithm), u16(weights), row, col, bit,
+      static_cast<uint16_t*>(o.d.data_ptr()), o.observed.data_ptr<float>(), o.predicted.data_ptr<float>(),
+      o.magnitude.data_ptr<float>(), compact ? nullptr : o.hit.data_ptr<int32_t>(),
+      compact ? o.tile_flags.data_ptr<int32_t>() : nullptr, base, ws_bytes, stream_of(a)));
+  return o;
+}
+
+Out5 abft_augmented_mm(const Tensor& a, const Tensor& b, const Tensor& weights, int64_t row, int64_t col, int64_t bit,
+                       int64_t algorithm) {
+  AugmentedOut o = run_augmented(a, b, weights, row, col, bit, algorithm, false);
+  return {o.d, o.observed, o.hit, o.predicted, o.magnitude};
+}
+
+Out3 abft_augmented_compact(const Tensor& a, const Tensor& b, const Tensor& weights, int64_t row, int64_t col,
+                            int64_t bit, int64_t algorithm) {
+  AugmentedOut o = run_augmented(a, b, weights, row, col, bit, algorithm, true);
+  return {o.d, o.partials, o.tile_flags};
+}
+
 Out3 abft_mm_stub(const Tensor&, const Tensor&, const Tensor&, int64_t, int64_t, int64_t, int64_t, OptTensor) {
   out_of_scope("abft_mm");
 }
 Out5 abft_reference_mm_stub(const Tensor&, const Tensor&, const Tensor&, int64_t, int64_t, int64_t, int64_t, OptTensor) {
   out_of_scope("abft_reference_mm");
-}
-Out5 abft_augmented_mm_stub(const Tensor&, const Tensor&, const Tensor&, int64_t, int64_t, int64_t, int64_t) {
-  out_of_scope("abft_augmented_mm");
-}
-Out3 abft_augmented_compact_stub(const Tensor&, const Tensor&, const Tensor&, int64_t, int64_t, int64_t, int64_t) {
-  out_of_scope("abft_augmented_compact");
 }
 
 }  // namespace
@@ -655,11 +754,11 @@ TORCH_LIBRARY(sdc_cutlass, lib) {
 }
 
 TORCH_LIBRARY_IMPL(sdc_cutlass, CUDA, lib) {
-  lib.impl("mm", &mm_stub);
+  lib.impl("mm", &mm);
   lib.impl("abft_mm", &abft_mm_stub);
   lib.impl("abft_reference_mm", &abft_reference_mm_stub);
-  lib.impl("abft_augmented_mm", &abft_augmented_mm_stub);
-  lib.impl("abft_augmented_compact", &abft_augmented_compact_stub);
+  lib.impl("abft_augmented_mm", &abft_augmented_mm);
+  lib.impl("abft_augmented_compact", &abft_augmented_compact);
   lib.impl("fp8_mm", &fp8_mm);
   lib.impl("nvfp4_mm", &nvfp4_mm);
   lib.impl("abft_fp8_mm", &abft_fp8_mm);

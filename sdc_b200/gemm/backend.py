@@ -3,8 +3,8 @@
 Mirrors src/cutlass_gemm/backend.py of the reference: ``require_device``,
 ``_scale_layout``, ``_pack_scales`` and ``gemm(a, b, precision, scaling,
 global_scale)`` with the same precision/scaling pairs and output contracts
-(FP8: fp32 column-major; NVFP4: bf16 row-major). The FP32/BF16 legacy
-precisions of the reference are outside this path and raise. Extension:
+(FP8: fp32 column-major; NVFP4 and BF16: bf16 row-major). The reference's
+FP32 SIMT GEMM is outside this path and raises. Extension:
 FP8 with ``scaling="blockwise"`` (1 x 128 A / 128 x 128 B fp32 block scales,
 bf16 row-major output).
 """
@@ -39,10 +39,13 @@ def _pack_scales(scales, indices, size):
 
 
 def mm(a, b):
-    """The reference's FP32/BF16 GEMM entry: device-checked, then rejected
-    (those kernels are outside the FP8/NVFP4 path)."""
+    """The reference's FP32/BF16 GEMM entry: BF16 runs on the tcgen05 BF16
+    GEMM (fp32 accumulation, bf16 row-major output); the FP32 SIMT GEMM is
+    outside this library's path and raises after the device check."""
     require_device(a.device)
-    raise NotImplementedError("FP32/BF16 legacy GEMMs are not part of the sdc_b200 FP8/NVFP4 path")
+    if a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16:
+        return ops.mm(a, b)
+    raise NotImplementedError("FP32 legacy GEMMs are not part of the sdc_b200 path")
 
 
 def gemm(a, b, precision, scaling, global_scale="amax"):
