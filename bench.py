@@ -322,6 +322,30 @@ def augmented_bf16(device, stream, sizes=(2048, 8192), iters=20):
             torch.maximum(worst, (packet[1].abs() / mag.clamp_min(1e-30)).amax(), out=worst)
         library()
         t_prot, t_plain, t_lib = timed_flushed([protected, plain, library], iters, stream, flush)
+        # Host enqueue time of one eager call (no synchronisation inside).
+        host = []
+        for fn in (protected, plain):
+            torch.cuda.synchronize()
+            flush.add_(1)  # keeps the GPU busy so the enqueue never waits on it
+            t0 = time.perf_counter()
+            fn()
+            host.append(time.perf_counter() - t0)
+        torch.cuda.synchronize()
+        # The same calls captured once in CUDA graphs and replayed: device
+        # time without the host's per-call work.
+        graphs = []
+        for fn in (protected, plain):
+            side = torch.cuda.Stream(device)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                fn()
+            stream.wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                fn()
+            graphs.append(graph)
+        t_prot_graph, t_plain_graph = timed_flushed([g.replay for g in graphs], iters, stream, flush)
+        del graphs
         flops = 2.0 * size ** 3
         out[str(size)] = {
             "protected_us": t_prot * 1e6, "unprotected_us": t_plain * 1e6, "time_ratio": t_prot / t_plain,
@@ -329,6 +353,9 @@ def augmented_bf16(device, stream, sizes=(2048, 8192), iters=20):
             "protected_tflops": flops / t_prot / 1e12, "unprotected_tflops": flops / t_plain / 1e12,
             "unprotected_frac_of_bf16_peak": flops / t_plain / 1e12 / bf16_peak,
             "cublas_bf16_us": t_lib * 1e6,
+            "host_enqueue_us": {"protected": host[0] * 1e6, "unprotected": host[1] * 1e6},
+            "graph_replay": {"protected_us": t_prot_graph * 1e6, "unprotected_us": t_plain_graph * 1e6,
+                             "time_ratio": t_prot_graph / t_plain_graph},
             "clean_max_res_over_magnitude": float(worst),
             "launches_per_call": {"protected": 4, "unprotected": 1},
         }
@@ -791,7 +818,8 @@ def run_ours(args):
         del prot
         torch.cuda.empty_cache()
     sweep = None if args.no_sweep else qwen_sweep(args, device, stream, rank, world, dist)
-    augmented = None if (args.no_augmented or rank != 0) else augmented_bf16(device, stream)
+    augmented = None if (args.no_augmented or rank != 0) else augmented_bf16(
+        device, stream, tuple(int(x) for x in args.augmented_sizes.split(",")), args.augmented_iters)
     ceiling = None if (args.no_ceiling or rank != 0) else library_ceiling(device, stream)
     if dist is not None:
         dist.barrier()
@@ -1093,6 +1121,10 @@ def main():
     parser.add_argument("--no-sweep", action="store_true", help="skip the Qwen2.5-7B linear-shape sweep")
     parser.add_argument("--sweep-steps", type=int, default=10)
     parser.add_argument("--no-augmented", action="store_true", help="skip the augmented BF16 ABFT leg")
+    parser.add_argument("--augmented-only", action="store_true",
+                        help="run only the augmented BF16 leg and print its object (profiling; not a bench line)")
+    parser.add_argument("--augmented-sizes", default="2048,8192")
+    parser.add_argument("--augmented-iters", type=int, default=20)
     parser.add_argument("--workload", choices=["gemm", "train"], default="gemm",
                         help="gemm: the ABFT GEMM benchmark (default); train: configuration 5 training step")
     parser.add_argument("--micro-batch", type=int, default=8)
@@ -1103,7 +1135,13 @@ def main():
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
-    if args.impl == "reference":
+    if args.augmented_only:
+        device = torch.device("cuda", 0)
+        torch.cuda.set_device(device)
+        result = augmented_bf16(device, torch.cuda.current_stream(device),
+                                tuple(int(x) for x in args.augmented_sizes.split(",")), args.augmented_iters)
+        print(json.dumps({"augmented_bf16": result}))
+    elif args.impl == "reference":
         run_reference(args)
     elif args.workload == "train":
         run_train(args)

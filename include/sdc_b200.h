@@ -259,8 +259,9 @@ int sdc_bf16_gemm(const uint16_t* a, const uint16_t* b_rows, int64_t m,
  * reference forms these rows inside its augmented mainloop,
  * src/cutlass_gemm/csrc/abft/fp32_bf16/bf16_augmented.h:200-320): for each
  * 128-row M-tile t and channel c, q[t*C + c][k] = bf16 (round to nearest
- * even) of the fp32 fma chain over the tile's rows in ascending order of
- * w_c[row] * A[row][k]. a: bf16 [M, K] row-major, K % 8 == 0; weights: bf16
+ * even) of the sum, in ascending order, of eight fp32 fma chains of
+ * w_c[row] * A[row][k], each over a 16-row segment of the tile (rows
+ * ascending, rows >= M absent). a: bf16 [M, K] row-major, K % 8 == 0; weights: bf16
  * [C, M]; q: bf16 [C * ceil(M/128), K]; a and q 16-byte aligned. */
 int sdc_abft_augment_encode(const uint16_t* a, int64_t m, int64_t k,
                             int algorithm, const uint16_t* weights,
@@ -273,7 +274,7 @@ size_t sdc_abft_augmented_workspace_bytes(int algorithm, int64_t m,
 /* Replaces sdc_cutlass_abft_augmented_mm and _compact
  * (src/cutlass_gemm/csrc/abft/fp32_bf16/bf16_augmented.cu:12-162). The
  * checksum rows of every 128-row M-tile t, q[t*C + c] = bf16(w_c^T A_t)
- * (fp32 sum over the tile's rows, ascending), run as extra M-tiles of the
+ * (the order of sdc_abft_augment_encode), run as extra M-tiles of the
  * same GEMM; their fp32 results are predicted[c, t, :]. The data tiles'
  * epilogue applies the fault (XOR of bit `bit` of the fp32 value at
  * (row, col)) and writes observed = sum_rows w_c v and the output-side

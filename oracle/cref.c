@@ -348,8 +348,9 @@ int oracle_gemm_f64(int kind, const uint8_t* a, const uint8_t* sfa, const uint8_
  * src/cutlass_gemm/csrc/abft/fp32_bf16/bf16_augmented.h:216-320, whose
  * internal summation order is unspecified): for each 128-row M-tile t,
  * channel c and column kk,
- *   acc = fmaf(w_c[row], A[row][kk], acc)   over the tile's rows ascending,
- *   q[t * C + c][kk] = bf16(acc), rounded to nearest even.
+ *   s_j = fmaf(w_c[row], A[row][kk], s_j) over rows [16 j, 16 j + 16) of
+ *         the tile that are < m, ascending, from s_j = +0 (j = 0..7);
+ *   q[t * C + c][kk] = bf16(((s_0 + s_1) + s_2) + ... + s_7), nearest even.
  * a: bf16 bits [m, k]; w: bf16 bits [C, m]; q: bf16 bits [C * tiles, k]. */
 static float bf16_value(uint16_t h) {
   const uint32_t u = (uint32_t)h << 16;
@@ -369,21 +370,26 @@ static uint16_t bf16_round(float f) {
 int oracle_augment_encode(const uint16_t* a, int64_t m, int64_t k, const uint16_t* w, int channels,
                           uint16_t* q) {
   const int64_t tiles = (m + 127) / 128;
-  float* acc = (float*)malloc(sizeof(float) * k);
-  if (!acc) return 1;
+  float* seg = (float*)malloc(sizeof(float) * k * 8);
+  if (!seg) return 1;
   for (int64_t t = 0; t < tiles; ++t) {
-    const int64_t row_end = (t + 1) * 128 < m ? (t + 1) * 128 : m;
     for (int c = 0; c < channels; ++c) {
-      for (int64_t kk = 0; kk < k; ++kk) acc[kk] = 0.f;
-      for (int64_t row = t * 128; row < row_end; ++row) {
-        const float wv = bf16_value(w[c * m + row]);
-        const uint16_t* ar = a + row * k;
-        for (int64_t kk = 0; kk < k; ++kk) acc[kk] = fmaf(wv, bf16_value(ar[kk]), acc[kk]);
+      for (int64_t i = 0; i < k * 8; ++i) seg[i] = 0.f;
+      for (int j = 0; j < 8; ++j) {
+        for (int64_t row = t * 128 + 16 * j; row < t * 128 + 16 * j + 16 && row < m; ++row) {
+          const float wv = bf16_value(w[c * m + row]);
+          const uint16_t* ar = a + row * k;
+          for (int64_t kk = 0; kk < k; ++kk) seg[j * k + kk] = fmaf(wv, bf16_value(ar[kk]), seg[j * k + kk]);
+        }
       }
       uint16_t* out = q + (t * channels + c) * k;
-      for (int64_t kk = 0; kk < k; ++kk) out[kk] = bf16_round(acc[kk]);
+      for (int64_t kk = 0; kk < k; ++kk) {
+        float sum = seg[kk];
+        for (int j = 1; j < 8; ++j) sum = sum + seg[j * k + kk];
+        out[kk] = bf16_round(sum);
+      }
     }
   }
-  free(acc);
+  free(seg);
   return 0;
 }

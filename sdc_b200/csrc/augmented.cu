@@ -12,8 +12,9 @@
 // observed = sum_rows w_c v and the output-side magnitude sum_rows |w_c v|
 // (the augmented mode's threshold scale), after the optional fault XOR.
 //
-// Fixed summation order of the encoding (mirrored by the C oracle): one fp32
-// fma chain per (tile, channel, k) over the tile's rows in ascending order.
+// Fixed summation order of the encoding (mirrored by the C oracle): per
+// (tile, channel, k), eight fp32 fma chains over 16-row segments (rows
+// ascending), added in ascending segment order, one rounding to bf16.
 #include <algorithm>
 
 #include "gemm.cuh"
@@ -21,47 +22,63 @@
 namespace sdc {
 namespace {
 
-constexpr int kEncodeThreads = 128;
-constexpr int kEncodeK = 8;  // k per thread: one 16-byte bf16 load per row
+constexpr int kSegments = 8;                   // warps per block: row segments of a tile
+constexpr int kSegmentRows = 128 / kSegments;  // 16 rows per segment
+constexpr int kEncodeThreads = 32 * kSegments;
+constexpr int kEncodeK = 8;                    // k per lane: one 16-byte bf16 load per row
+constexpr int kBlockK = 32 * kEncodeK;         // 256 columns per block
 
-// Grid (ceil(K / 1024), Tm). Thread: 8 consecutive k of one M-tile. Block
-// x == 0 also writes the tile's weights as fp32 for the GEMM epilogue (when
-// w32 is not null).
+// Grid (ceil(K / 256), Tm), 256 threads. Warp s forms, for the block's 256
+// columns, the fp32 fma chain over rows [16 s, 16 s + 16) of the tile in
+// ascending order (its 16 row loads all in flight at once); the eight
+// segment sums are then added in ascending segment order (an empty segment
+// adds +0) and rounded once to bf16. Blocks x == 0 also write the tile's
+// weights as fp32 for the GEMM epilogue (when w32 is not null) and zero the
+// tile's status words (tile_flags row t, and hit once) that the GEMM ORs into.
 template <int C>
 __global__ void __launch_bounds__(kEncodeThreads)
-    augment_encode(const uint16_t* a, int64_t m, int64_t k, const uint16_t* w, uint16_t* q, float* w32) {
+    augment_encode(const uint16_t* a, int64_t m, int64_t k, const uint16_t* w, uint16_t* q, float* w32,
+                   int32_t* tile_flags, int64_t flag_cols, int32_t* hit) {
+  __shared__ float part[kSegments][C][kBlockK];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t = blockIdx.y;
   const int64_t row0 = t * 128;
-  const int64_t rows = std::min<int64_t>(128, m - row0);
-  if (blockIdx.x == 0 && w32 != nullptr) {
-    for (int64_t i = threadIdx.x; i < C * rows; i += kEncodeThreads) {
-      const int64_t c = i / rows, r = row0 + i % rows;
-      w32[c * m + r] = bf16_bits_to_float(w[c * m + r]);
+  const int rows = static_cast<int>(std::min<int64_t>(128, m - row0));
+  if (blockIdx.x == 0) {
+    if (w32 != nullptr) {
+      for (int i = threadIdx.x; i < C * rows; i += kEncodeThreads) {
+        const int64_t c = i / rows, r = row0 + i % rows;
+        w32[c * m + r] = bf16_bits_to_float(w[c * m + r]);
+      }
     }
+    if (tile_flags != nullptr) {
+      for (int64_t i = threadIdx.x; i < flag_cols; i += kEncodeThreads) tile_flags[t * flag_cols + i] = 0;
+    }
+    if (hit != nullptr && t == 0 && threadIdx.x == 0) *hit = 0;
   }
-  const int64_t k0 = (static_cast<int64_t>(blockIdx.x) * kEncodeThreads + threadIdx.x) * kEncodeK;
-  if (k0 >= k) return;
-  // acc[c][j]: channel c, k pair (k0 + 2j, k0 + 2j + 1) as one f32x2 fma lane pair.
+  const int64_t kb = static_cast<int64_t>(blockIdx.x) * kBlockK;
+  const int64_t k0 = kb + lane * kEncodeK;
+  // acc[c][j]: channel c, columns (k0 + 2j, k0 + 2j + 1) as one f32x2 lane pair.
   float2 acc[C][kEncodeK / 2];
 #pragma unroll
   for (int c = 0; c < C; ++c)
 #pragma unroll
     for (int j = 0; j < kEncodeK / 2; ++j) acc[c][j] = make_float2(0.f, 0.f);
-  constexpr int kBatch = 8;
-  for (int64_t r0 = 0; r0 < rows; r0 += kBatch) {
-    uint4 raw[kBatch];
-    float wv[kBatch][C];
+  const int seg0 = warp * kSegmentRows;
+  if (k0 < k) {  // K % 8 == 0: a lane's 8 columns are all inside or all outside
+    uint4 raw[kSegmentRows];
+    float wv[kSegmentRows][C];
 #pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-      const bool in = r0 + i < rows;
-      const int64_t r = row0 + r0 + i;
+    for (int i = 0; i < kSegmentRows; ++i) {
+      const bool in = seg0 + i < rows;
+      const int64_t r = row0 + seg0 + i;
       raw[i] = in ? __ldg(reinterpret_cast<const uint4*>(a + r * k + k0)) : make_uint4(0, 0, 0, 0);
 #pragma unroll
       for (int c = 0; c < C; ++c) wv[i][c] = in ? bf16_bits_to_float(__ldg(w + c * m + r)) : 0.f;
     }
 #pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-      if (r0 + i >= rows) break;
+    for (int i = 0; i < kSegmentRows; ++i) {
+      if (seg0 + i >= rows) break;  // rows past M are not terms (keeps a -0 chain -0)
       const uint32_t words[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -73,12 +90,22 @@ __global__ void __launch_bounds__(kEncodeThreads)
   }
 #pragma unroll
   for (int c = 0; c < C; ++c) {
-    uint4 out;
-    out.x = bf16x2_bits(acc[c][0].x, acc[c][0].y);
-    out.y = bf16x2_bits(acc[c][1].x, acc[c][1].y);
-    out.z = bf16x2_bits(acc[c][2].x, acc[c][2].y);
-    out.w = bf16x2_bits(acc[c][3].x, acc[c][3].y);
-    *reinterpret_cast<uint4*>(q + (t * C + c) * k + k0) = out;
+    float4* dst = reinterpret_cast<float4*>(&part[warp][c][lane * kEncodeK]);
+    dst[0] = make_float4(acc[c][0].x, acc[c][0].y, acc[c][1].x, acc[c][1].y);
+    dst[1] = make_float4(acc[c][2].x, acc[c][2].y, acc[c][3].x, acc[c][3].y);
+  }
+  __syncthreads();
+  // Column pairs: (channel, pair) = i over C * 128; segments added ascending.
+  for (int i = threadIdx.x; i < C * (kBlockK / 2); i += kEncodeThreads) {
+    const int c = i / (kBlockK / 2), col = 2 * (i % (kBlockK / 2));
+    if (kb + col >= k) continue;
+    float lo = part[0][c][col], hi = part[0][c][col + 1];
+#pragma unroll
+    for (int seg = 1; seg < kSegments; ++seg) {
+      lo = lo + part[seg][c][col];
+      hi = hi + part[seg][c][col + 1];
+    }
+    *reinterpret_cast<uint32_t*>(q + (t * C + c) * k + kb + col) = bf16x2_bits(lo, hi);
   }
 }
 
@@ -137,13 +164,12 @@ GemmProblem bf16_problem(const uint16_t* a, const uint16_t* b, int64_t m, int64_
 }
 
 int launch_encode(const uint16_t* a, int64_t m, int64_t k, int channels, const uint16_t* weights, uint16_t* q,
-                  float* w32, cudaStream_t stream) {
-  const dim3 grid(static_cast<unsigned>(ceil_div(k, kEncodeThreads * kEncodeK)),
-                  static_cast<unsigned>(ceil_div(m, 128)));
+                  float* w32, int32_t* tile_flags, int64_t flag_cols, int32_t* hit, cudaStream_t stream) {
+  const dim3 grid(static_cast<unsigned>(ceil_div(k, kBlockK)), static_cast<unsigned>(ceil_div(m, 128)));
   if (channels == 2) {
-    augment_encode<2><<<grid, kEncodeThreads, 0, stream>>>(a, m, k, weights, q, w32);
+    augment_encode<2><<<grid, kEncodeThreads, 0, stream>>>(a, m, k, weights, q, w32, tile_flags, flag_cols, hit);
   } else {
-    augment_encode<1><<<grid, kEncodeThreads, 0, stream>>>(a, m, k, weights, q, w32);
+    augment_encode<1><<<grid, kEncodeThreads, 0, stream>>>(a, m, k, weights, q, w32, tile_flags, flag_cols, hit);
   }
   SDC_CUDA_CHECK(cudaGetLastError());
   return SDC_OK;
@@ -178,7 +204,7 @@ int sdc_abft_augment_encode(const uint16_t* a, int64_t m, int64_t k, int algorit
               "Augmented encode A and q must be 16-byte aligned");
   int rc = check_current_device();
   if (rc != SDC_OK) return rc;
-  return launch_encode(a, m, k, channels, weights, q, nullptr, stream);
+  return launch_encode(a, m, k, channels, weights, q, nullptr, nullptr, 0, nullptr, stream);
 }
 
 size_t sdc_abft_augmented_workspace_bytes(int algorithm, int64_t m, int64_t k) {
@@ -207,7 +233,9 @@ int sdc_abft_bf16_augmented_gemm(const uint16_t* a, const uint16_t* b_rows, int6
   }
   const AugmentedScratch s = carve(workspace, channels, m, k);
   const int64_t tiles = ceil_div(m, 128);
-  rc = launch_encode(a, m, k, channels, weights, s.q, s.w32, stream);
+  // The encode kernel also zeroes hit and tile_flags (no memset launches).
+  rc = launch_encode(a, m, k, channels, weights, s.q, s.w32, tile_flags, ceil_div(n, 128),
+                     hit != nullptr ? hit : s.hit, stream);
   if (rc != SDC_OK) return rc;
   GemmProblem g = bf16_problem(a, b_rows, m, n, k, d);
   g.channels = channels;
@@ -224,6 +252,7 @@ int sdc_abft_bf16_augmented_gemm(const uint16_t* a, const uint16_t* b_rows, int6
   g.aug_rows = channels * tiles;
   g.tile_flags = tile_flags;
   g.flag_cols = ceil_div(n, 128);
+  g.status_zeroed = true;
   return launch_gemm(g, stream);
 }
 

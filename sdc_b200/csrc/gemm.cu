@@ -370,14 +370,14 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
   // thread owning output row `row`: fault injection, nonfinite check, the
   // observed checksum partials of the warp's 32 rows into `red`, the store.
   auto emit_chunk = [&](float (&v)[32], int q, int row, bool row_ok, int c0, int chunk, const float* w,
-                        bool& nonfinite, bool& faulted) {
+                        uint32_t& nonfinite, uint32_t& faulted) {
     if (C > 0 && p.fbit >= 0 && row == p.frow && p.fcol >= c0 && p.fcol < c0 + 32) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         if (c0 + j == p.fcol) v[j] = __uint_as_float(__float_as_uint(v[j]) ^ (1u << p.fbit));
       }
       atomicOr(p.hit, 1);
-      faulted = true;
+      faulted |= 1u << (chunk >> 2);  // bit per 128-column block of the tile
     }
     if constexpr (BF16OUT) {
       // The output as stored first: one round-to-nearest conversion per
@@ -402,7 +402,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
             flag |= ((packed[j] & keep) & 0x7F807F80u) + 0x00800080u;
           }
         }
-        if (flag & 0x80008000u) nonfinite = true;
+        if (flag & 0x80008000u) nonfinite |= 1u << (chunk >> 2);
       }
       if (row_ok) {
         uint16_t* d = static_cast<uint16_t*>(p.d) + static_cast<int64_t>(row) * p.n;
@@ -426,7 +426,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
       for (int j = 0; j < 32; ++j) {
         if (c0 + j < p.n) largest = max(largest, __float_as_uint(v[j]) & 0x7FFFFFFFu);
       }
-      if (largest >= 0x7F800000u) nonfinite = true;
+      if (largest >= 0x7F800000u) nonfinite |= 1u << (chunk >> 2);
     }
     if constexpr (C > 0) {
       // Column sums of w_c[row] * v over the warp's 32 rows. The first
@@ -498,18 +498,20 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
       named_barrier(1, kAccThreads);
     }
   };
-  // Augmented bf16: the per-tile status (fault applied, non-finite output)
-  // of this CTA's 128 rows, ORed into both 128-column blocks of the tile.
-  // Every epilogue thread takes part (the decision is CTA-uniform).
-  auto store_tile_flags = [&](int mt, int nt, bool faulted, bool nonfinite) {
+  // Augmented bf16: the status (bit 0 fault applied, bit 1 non-finite
+  // output) of each 128 x 128 block of this CTA's tile, ORed into its flag
+  // word. Every epilogue thread takes part (the decisions are CTA-uniform).
+  auto store_tile_flags = [&](int mt, int nt, uint32_t faulted, uint32_t nonfinite) {
     if constexpr (AUG) {
-      const bool any_fault = named_barrier_or(1, kAccThreads, faulted);
-      const bool any_nonfinite = named_barrier_or(1, kAccThreads, nonfinite);
-      if (p.tile_flags != nullptr && threadIdx.x == 32 * kEpi0 && mt < p.tiles_m) {
+#pragma unroll
+      for (int block = 0; block < kTN / 128; ++block) {
+        const bool any_fault = named_barrier_or(1, kAccThreads, (faulted >> block) & 1u);
+        const bool any_nonfinite = named_barrier_or(1, kAccThreads, (nonfinite >> block) & 1u);
+        const int col_block = nt * (kTN / 128) + block;
         const int32_t word = (any_fault ? 1 : 0) | (any_nonfinite ? 2 : 0);
-        for (int half = 0; half < kTN / 128; ++half) {
-          const int block = nt * (kTN / 128) + half;
-          if (word != 0 && block < p.flag_cols) atomicOr(p.tile_flags + static_cast<int64_t>(mt) * p.flag_cols + block, word);
+        if (p.tile_flags != nullptr && threadIdx.x == 32 * kEpi0 && mt < p.tiles_m && word != 0 &&
+            col_block < p.flag_cols) {
+          atomicOr(p.tile_flags + static_cast<int64_t>(mt) * p.flag_cols + col_block, word);
         }
       }
     }
@@ -796,7 +798,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
         }
         const bool live = !named_barrier_or(1, kAccThreads, !ok || *abort_flag != 0);
         if (live) {
-          bool nonfinite = false, faulted = false;
+          uint32_t nonfinite = 0, faulted = 0;
 #pragma unroll
           for (int cc = 0; cc < kHalfCols / 32; ++cc) {
             float v[32];
@@ -855,7 +857,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
           }
         }
       };
-      bool nonfinite = false, faulted = false;
+      uint32_t nonfinite = 0, faulted = 0;
       if (live) {
         if constexpr (WIDE) {
           uint32_t r[kWarpChunks][32];
@@ -1434,10 +1436,10 @@ int launch_gemm(const GemmProblem& g, cudaStream_t stream) {
   int rc = check_current_device();
   if (rc != SDC_OK) return rc;
   if (g.channels > 0) {
-    SDC_CUDA_CHECK(cudaMemsetAsync(g.hit, 0, sizeof(int32_t), stream));
+    if (!g.status_zeroed) SDC_CUDA_CHECK(cudaMemsetAsync(g.hit, 0, sizeof(int32_t), stream));
     if (g.nonfinite != nullptr) SDC_CUDA_CHECK(cudaMemsetAsync(g.nonfinite, 0, sizeof(int32_t), stream));
     if (g.grid_sync != nullptr) SDC_CUDA_CHECK(cudaMemsetAsync(g.grid_sync, 0, sizeof(uint32_t), stream));
-    if (g.tile_flags != nullptr) {
+    if (g.tile_flags != nullptr && !g.status_zeroed) {
       SDC_CUDA_CHECK(cudaMemsetAsync(g.tile_flags, 0, sizeof(int32_t) * ceil_div(g.m, kBM) * g.flag_cols, stream));
     }
   }

@@ -55,6 +55,9 @@ struct GemmProblem {
   int64_t aug_rows;
   int32_t* tile_flags;
   int64_t flag_cols;
+  // The caller zeroed hit and tile_flags on this stream already (launch_gemm
+  // then issues no memsets for them).
+  bool status_zeroed;
 };
 
 // Launches the GEMM (and its fused epilogue) on `stream`. Zeroes hit/nonfinite
