@@ -250,7 +250,7 @@ int sdc_abft_fp8_block_reference_gemm(
  * row-major. */
 
 /* Replaces sdc_cutlass_mm for bf16 operands
- * (src/cutlass_gemm/csrc/gemm/fp32_bf16.cu:95-130; the reference's fp32
+ * (src/cutlass_gemm/csrc/gemm/fp32_bf16.cu:34-125; the reference's fp32
  * variant stays outside this library). */
 int sdc_bf16_gemm(const uint16_t* a, const uint16_t* b_rows, int64_t m,
                   int64_t n, int64_t k, uint16_t* d, sdc_stream_t stream);

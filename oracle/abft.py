@@ -109,10 +109,10 @@ def locate(residual, threshold, detected, nonfinite, m):
 
 
 def classic_weights(m):
-    """Classic projection weights [ones; 1..M] (src/abft/methods.py:469-471)."""
+    """Classic projection weights [ones; 1..M] (src/abft/methods.py:162-164)."""
     return np.stack([np.ones(m, np.float32), np.arange(1, m + 1, dtype=np.float32)])
 
 
 def sum_weights(m):
-    """Sum projection weights (src/abft/methods.py:559-560)."""
+    """Sum projection weights (src/abft/methods.py:252-253)."""
     return np.ones((1, m), np.float32)

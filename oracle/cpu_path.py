@@ -2,12 +2,12 @@
 
 Restates ``abft.execute(a, b, "fp32", "none", abft_config={"method": "classic",
 ...}, reference_mm=torch.mm, collector_fn=collect)`` of the reference:
-  PreparedGemm.prepare fp32 (src/abft/operands.py:151-165),
-  Classic.prepare K-chunked expected/magnitude (src/abft/methods.py:488-503),
+  PreparedGemm.prepare fp32 (src/abft/operands.py:28-41),
+  Classic.prepare K-chunked expected/magnitude (src/abft/methods.py:181-197),
   the CPU collector of tests/abft/test_framework.py:14-22 (C = A @ B, XOR of
   one fp32 bit, partials = W @ C),
-  Classic.propagate / verify incl. the ratio locator (src/abft/methods.py:505-544),
-  and the recompute-and-recheck retry (src/abft/engine.py:274-293).
+  Classic.propagate / verify incl. the ratio locator (src/abft/methods.py:198-241),
+  and the recompute-and-recheck retry (src/abft/engine.py:274-291).
 The torch CPU ops are the same ones the reference calls, so results are bit
 for bit those of the reference on the same machine. This is the timed CPU
 baseline of bench.py and the checker of the config-1 golden trials.

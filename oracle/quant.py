@@ -1,9 +1,9 @@
 """Quantisation and scale layout, restated in numpy. Test infrastructure only.
 
 Follows src/cutlass_gemm/quantization.py of the reference:
-  _multiplier (:180-191), quantize FP8 (:194-221), NVFP4 (:223-243),
-  dequantize (:246-266);
-the scale scatter of src/cutlass_gemm/backend.py:383-393; and the CUTLASS
+  _multiplier (:99-112), quantize FP8 (:114-140), NVFP4 (:141-165),
+  dequantize (:166-185);
+the scale scatter of src/cutlass_gemm/backend.py:124-127; and the CUTLASS
 Sm1xxBlkScaledConfig<16> K-major layout the reference's
 src/cutlass_gemm/csrc/gemm/nvfp4.cu:122-147 evaluates (pinned against CUTLASS
 itself in tests/golden/sf_layout.json).

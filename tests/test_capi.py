@@ -90,6 +90,7 @@ EXTENDED = {
 
 
 def test_torch_op_schemas_match_reference_bindings():
+    sdc_b200.load()
     for name, schema in REFERENCE_SCHEMAS.items():
         assert str(getattr(torch.ops.sdc_cutlass, name).default._schema) == "sdc_cutlass::" + schema
     for name, schema in BLOCK_SCALED.items():

@@ -374,7 +374,7 @@ def _dyadic_weights(m):
 
 
 def _varying_case(precision, m, n, k):
-    """Heterogeneous block scales (tests/cutlass_gemm/test_nvfp4_input_reference_gpu.py:121-139)."""
+    """Heterogeneous block scales (tests/cutlass_gemm/test_nvfp4_input_reference_gpu.py:60-81)."""
     def values(rows, phase):
         row = torch.arange(rows, device=DEV)[:, None]
         col = torch.arange(k, device=DEV)[None, :]
