@@ -40,6 +40,9 @@ __global__ void __launch_bounds__(kEncodeThreads)
     augment_encode(const uint16_t* a, int64_t m, int64_t k, const uint16_t* w, uint16_t* q, float* w32,
                    int32_t* tile_flags, int64_t flag_cols, int32_t* hit) {
   __shared__ float part[kSegments][C][kBlockK];
+  // The GEMM launched next may begin its data tiles now (it waits for this
+  // grid before it reads anything this kernel writes).
+  griddep_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t = blockIdx.y;
   const int64_t row0 = t * 128;

@@ -472,6 +472,14 @@ __host__ __device__ constexpr uint32_t idesc_nvf4(int m, int n) {
          (0u << 23) /*scale ue4m3*/ | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// Programmatic dependent launch. griddep_wait: until the grid this one was
+// launched after (as a programmatic dependent) has completed and its writes
+// are visible; returns at once for a grid launched normally.
+// griddep_launch_dependents: this block allows the next grid on the stream
+// (if launched as a dependent) to start launching.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 // Named barrier among `count` threads (ids 1..15; 0 is __syncthreads).
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -7,10 +7,13 @@
 // bits cross thread-block boundaries. Work is memory bound (3 partial planes
 // read once); the grid is one thread per (channel, column) so loads of
 // consecutive columns coalesce, and a second one-block kernel ORs the
-// per-block status words, so no float atomics or host syncs are involved.
+// per-block status words into the five flags: the last block of the grid to
+// finish (an atomic ticket) does it, so the finalize is one launch, with no
+// float atomics and no host syncs.
 // The partials are staged through shared memory by all warps of a block so
 // that many loads are in flight, while the additions stay serial per column.
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -43,7 +46,20 @@ struct FinalizeParams {
   const float* thresholds;
   bool scalar_threshold;
   int32_t* block_states;
+  int64_t blocks;            // grid size: the ticket value of the last block
+  uint32_t* ticket;          // this launch's arrival counter, zero on entry
+  uint8_t* flags;
+  int32_t* hit_out;
+  int64_t* location;
 };
+
+// Arrival counters of the finalize launches on a device. A launch takes the
+// slot its host-side sequence number selects (mod kTicketSlots); its last
+// block returns the counter to zero, so a slot is clean again before it
+// comes round (far more launches than that are never in flight at once; a
+// captured graph replays its slot sequentially).
+constexpr int kTicketSlots = 4096;
+static __device__ uint32_t g_finalize_tickets[kTicketSlots];
 
 // Block = 64 columns of one channel. All 8 warps stage the partials of 32
 // tiles at a time in shared memory (warp w stages column group w % 2 of the
@@ -139,36 +155,62 @@ __global__ void __launch_bounds__(kColumnThreads) finalize_columns(FinalizeParam
   for (int offset = 16; offset > 0; offset >>= 1) state |= __shfl_xor_sync(0xffffffffu, state, offset);
   if (lane == 0) warp_state[warp] = state;
   __syncthreads();
+  __shared__ bool last;
   if (threadIdx.x == 0) {
     unsigned combined = 0;
     for (int w = 0; w < kColumnThreads / 32; ++w) combined |= warp_state[w];
     p.block_states[block] = static_cast<int32_t>(combined);
+    // Publish the state before taking a ticket; the block that takes the
+    // last ticket sees every other block's state.
+    __threadfence();
+    last = atomicAdd(p.ticket, 1u) == static_cast<uint32_t>(p.blocks - 1);
   }
-}
-
-__global__ void __launch_bounds__(kFinalizeThreads)
-    finalize_flags(const int32_t* block_states, int64_t blocks, uint8_t* flags, int32_t* hit_out,
-                   int64_t* location) {
-  unsigned state = 0;
-  for (int64_t i = threadIdx.x; i < blocks; i += kFinalizeThreads) {
-    state |= static_cast<unsigned>(block_states[i]);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  unsigned all = 0;
+  for (int64_t i = threadIdx.x; i < p.blocks; i += kColumnThreads) {
+    all |= static_cast<unsigned>(__ldcg(p.block_states + i));
   }
-  for (int offset = 16; offset > 0; offset >>= 1) state |= __shfl_xor_sync(0xffffffffu, state, offset);
-  __shared__ unsigned warp_state[kFinalizeThreads / 32];
-  if ((threadIdx.x & 31) == 0) warp_state[threadIdx.x >> 5] = state;
+  for (int offset = 16; offset > 0; offset >>= 1) all |= __shfl_xor_sync(0xffffffffu, all, offset);
+  if (lane == 0) warp_state[warp] = all;
   __syncthreads();
   if (threadIdx.x == 0) {
     unsigned combined = 0;
-    for (int w = 0; w < kFinalizeThreads / 32; ++w) combined |= warp_state[w];
-    flags[0] = (combined & kDetected) ? 1 : 0;
-    flags[1] = (combined & kNonfinite) ? 1 : 0;
-    flags[2] = 0;  // located: reported by sdc_abft_locate, not by the policy decision
-    flags[3] = 0;  // recovered: owned by the caller's retry transaction
-    flags[4] = 0;  // recheck_failed: owned by the caller's retry transaction
-    hit_out[0] = (combined & kHit) ? 1 : 0;
-    location[0] = -1;
-    location[1] = -1;
+    for (int w = 0; w < kColumnThreads / 32; ++w) combined |= warp_state[w];
+    p.flags[0] = (combined & kDetected) ? 1 : 0;
+    p.flags[1] = (combined & kNonfinite) ? 1 : 0;
+    p.flags[2] = 0;  // located: reported by sdc_abft_locate, not by the policy decision
+    p.flags[3] = 0;  // recovered: owned by the caller's retry transaction
+    p.flags[4] = 0;  // recheck_failed: owned by the caller's retry transaction
+    p.hit_out[0] = (combined & kHit) ? 1 : 0;
+    p.location[0] = -1;
+    p.location[1] = -1;
+    *p.ticket = 0;  // the slot is clean for its next launch
   }
+}
+
+// The device address of this launch's ticket (slot chosen on the host).
+int finalize_ticket(uint32_t** out) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex lock;
+  static uint32_t* base[kMaxDevices] = {};
+  static std::atomic<uint64_t> sequence{0};
+  int device = 0;
+  SDC_CUDA_CHECK(cudaGetDevice(&device));
+  if (device < 0 || device >= kMaxDevices) return fail(SDC_ERR_INVALID, "device index out of range");
+  uint32_t* slots = nullptr;
+  {
+    std::lock_guard<std::mutex> guard(lock);
+    if (base[device] == nullptr) {
+      void* ptr = nullptr;
+      SDC_CUDA_CHECK(cudaGetSymbolAddress(&ptr, g_finalize_tickets));
+      base[device] = static_cast<uint32_t*>(ptr);
+    }
+    slots = base[device];
+  }
+  *out = slots + sequence.fetch_add(1, std::memory_order_relaxed) % kTicketSlots;
+  return SDC_OK;
 }
 
 int64_t finalize_blocks(int channels, int64_t n) {
@@ -233,15 +275,18 @@ int sdc_abft_finalize(int algorithm, const float* observed, const float* predict
   p.thresholds = thresholds;
   p.scalar_threshold = scalar_threshold != 0;
   p.block_states = static_cast<int32_t*>(workspace);
+  p.blocks = blocks;
+  p.flags = flags;
+  p.hit_out = hit_out;
+  p.location = location;
+  const int rc = finalize_ticket(&p.ticket);
+  if (rc != SDC_OK) return rc;
   const dim3 grid(static_cast<unsigned>(ceil_div(n, kFinalizeThreads)), channels);
   if (channels == 2) {
     finalize_columns<2><<<grid, kColumnThreads, 0, stream>>>(p);
   } else {
     finalize_columns<1><<<grid, kColumnThreads, 0, stream>>>(p);
   }
-  SDC_CUDA_CHECK(cudaGetLastError());
-  finalize_flags<<<1, kFinalizeThreads, 0, stream>>>(p.block_states, blocks, flags, hit_out,
-                                                       location);
   SDC_CUDA_CHECK(cudaGetLastError());
   return SDC_OK;
 }

@@ -525,6 +525,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
     if (lane == 0) {
       uint32_t kbg = 0;
       bool stop = false;
+      bool encoded = false;  // augmented: the encode grid's rows are visible
       for (int t = work_first; t < p.num_work && !stop; t += work_step) {
         int mt, nt;
         work_coords<PAIR>(t, p, rank, mt, nt);
@@ -541,6 +542,12 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
           // Augmented bf16: the M-tiles after the data tiles read the checksum
           // rows (tensor map tm_sfa), from row 0 of that matrix.
           const bool aug_tile = AUG && mt >= p.tiles_m;
+          if (aug_tile && !encoded) {
+            // Launched as a programmatic dependent of the encode kernel: the
+            // checksum rows exist once that grid has completed.
+            griddep_wait();
+            encoded = true;
+          }
           const CUtensorMap* map_a = aug_tile ? &tm_sfa : &tm_a;
           const int32_t row_a = (aug_tile ? mt - p.tiles_m : mt) * kBM;
           if constexpr (PAIR) {
@@ -825,6 +832,9 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
     const int first_chunk = ((warp - kEpi0) >> 2) * kWarpChunks;
     // bf16 GEMMs have no alpha: the fp32 accumulator is the value (times 1).
     const float alpha = KIND == Kind::kBf16 ? 1.f : *p.alpha;
+    // Augmented: the weights and the zeroed status words come from the encode
+    // grid this launch may overlap (programmatic dependent launch).
+    if constexpr (AUG) griddep_wait();
     int i = 0;
     for (int t = work_first; t < p.num_work; t += work_step, ++i) {
       int mt, nt;
@@ -1217,6 +1227,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
   // launch as detected, so an aborted GEMM can never pass as clean.
   if constexpr (C > 0) {
     if (threadIdx.x == 0 && *abort_flag != 0) {
+      if constexpr (AUG) griddep_wait();  // after the encode grid zeroed the status
       atomicOr(p.hit, 2);
       // Augmented calls report through their tile flags: the non-finite bit
       // of the first entry makes the packed finalize report detected.
@@ -1350,13 +1361,21 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   config.blockDim = dim3(num_threads(CHK, is_wide(KIND)));
   config.dynamicSmemBytes = smem;
   config.stream = stream;
-  cudaLaunchAttribute attribute[2];
+  cudaLaunchAttribute attribute[3];
   int attrs = 0;
   if constexpr (PAIR) {
     attribute[attrs].id = cudaLaunchAttributeClusterDimension;
     attribute[attrs].val.clusterDim.x = 2;
     attribute[attrs].val.clusterDim.y = 1;
     attribute[attrs].val.clusterDim.z = 1;
+    ++attrs;
+  }
+  if constexpr (AUG) {
+    // The augmented GEMM follows its encode kernel on the stream and may
+    // start while that grid finishes: its data tiles need nothing from it,
+    // and the warps that do (checksum-row loads, epilogue) wait for it.
+    attribute[attrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute[attrs].val.programmaticStreamSerializationAllowed = 1;
     ++attrs;
   }
   config.attrs = attribute;

@@ -127,7 +127,7 @@ def test_native_weights_are_cached_per_stream():
     a, b = _operands(128, 128, 128)
     prepared = PreparedGemm.prepare(a, b, "fp8", "tensorwise")
     execute_prepared(prepared, _cfg())
-    key = (0, torch.device(DEV).index or 0, 128)
+    key = (0, torch.device(DEV).index or 0, 128, torch.float32)
     first = native.WEIGHTS.peek(key)
     execute_prepared(prepared, _cfg())
     assert first is not None and native.WEIGHTS.peek(key) is first
