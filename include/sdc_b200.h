@@ -52,12 +52,14 @@ enum sdc_reference_layout {
   /* predicted/magnitude[c, t, col] = contribution of the 64-wide K slices s
    * with s % Tm == t, summed over ALL rows. The sum over t equals the TILE
    * layout's sum over t (up to fp32 rounding); finalize is unchanged. The
-   * projection w^T A and the propagation run inside the GEMM launch (one
-   * extra read of A and of B, overlapped with the tensor-core mainloop)
-   * instead of ~C/32 of the GEMM on CUDA cores. The launch synchronises its
-   * CTAs twice, so two such launches must not run concurrently on one GPU
-   * (different streams): one of them would wait until its watchdog gives up
-   * and reports the call as detected. */
+   * projection w^T A and the propagation run inside the GEMM launch (one extra read of A and of B, overlapped with the tensor-core
+   * mainloop) instead of ~C/32 of the GEMM on CUDA cores; that launch
+   * synchronises its CTAs twice, so two such launches must not run
+   * concurrently on one GPU (different streams): one of them would wait until
+   * its watchdog gives up and reports the call as detected. NVFP4 launches
+   * with M <= 4096 and N >= 16 M run them as two kernels before an
+   * observed-only GEMM instead (no such restriction), with bit-identical
+   * results. */
   SDC_LAYOUT_KSLICE = 1
 };
 
@@ -77,6 +79,13 @@ int sdc_read_device_error(sdc_stream_t stream, int32_t* code);
  * test check that an expired wait is reported in-band (hit bit 1, detected)
  * without hanging or faulting the GPU. */
 int sdc_test_set_watchdog(uint64_t wait_limit_ns, int32_t pace_extra);
+/* Test hook (no counterpart in the reference): how later K-slice launches
+ * compute their prediction. 0 (default) chooses by shape: NVFP4 with
+ * M <= 4096 rows and N >= 16 M runs the projection and the prediction as two
+ * kernels before an observed-only GEMM, everything else inside the GEMM;
+ * 1 forces the in-GEMM path, 2 the two kernels. Both give bit-identical
+ * partials; the hook lets a test check it. */
+int sdc_test_set_kslice_path(int mode);
 
 /* ---- quantisation (src/cutlass_gemm/quantization.py:99-162) ------------ */
 

@@ -157,15 +157,15 @@ int oracle_kslice_reference(int kind, const uint8_t* a, const uint8_t* sfa, cons
     free(row_v);
     return 1;
   }
-  /* q over all rows in the projection kernel's order: bands of 512 rows; in a
+  /* q over all rows in the projection kernel's order: bands of 128 rows; in a
    * band, 8 row lanes l each run an fma chain over rows band_start + l, + 8,
    * ... (ascending), combined as ((p0 + p1) + (p2 + p3)) + ((p4 + p5) +
    * (p6 + p7)); q = ((band_0 + band_1) + ...) + band_last. Rows are walked in
    * order (each fma chain keeps its own accumulator), which is the same
    * arithmetic as walking each chain separately. */
-  const int64_t bands = (m + 511) / 512;
+  const int64_t bands = (m + 127) / 128;
   for (int64_t bnd = 0; bnd < bands; ++bnd) {
-    const int64_t begin = bnd * 512, end = begin + 512 < m ? begin + 512 : m;
+    const int64_t begin = bnd * 128, end = begin + 128 < m ? begin + 128 : m;
     memset(lanes, 0, sizeof(float) * channels * 2 * 8 * k);
     for (int64_t row = begin; row < end; ++row) {
       const int l = (int)((row - begin) & 7);

@@ -36,6 +36,7 @@ CUDA_SOURCES = [
     "api.cu",
     "locate.cu",
     "augmented.cu",
+    "kslice.cu",
 ]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -32,6 +32,7 @@ PROTOTYPES = {
     "sdc_device_check": (_int, [_int]),
     "sdc_read_device_error": (_int, [_vp, _vp]),
     "sdc_test_set_watchdog": (_int, [ctypes.c_uint64, ctypes.c_int32]),
+    "sdc_test_set_kslice_path": (_int, [_int]),
     "sdc_quantize_workspace_bytes": (_size, [_i64, _i64]),
     "sdc_quantize_fp8": (_int, [_vp, _int, _i64, _i64, _int, _float, _vp, _vp, _vp, _size, _vp]),
     "sdc_quantize_nvfp4": (_int, [_vp, _int, _i64, _i64, _int, _float, _vp, _vp, _vp, _vp, _vp, _size, _vp]),

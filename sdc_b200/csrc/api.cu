@@ -129,7 +129,8 @@ ReferenceProblem reference_problem(const GemmProblem& g, float* predicted, float
 
 // Input-fused ABFT GEMM: TILE layout = per-tile projection, GEMM, then the
 // propagation on CUDA cores; K-SLICE layout = one GEMM launch whose
-// prediction warps compute the projection of A and the propagation.
+// prediction warps compute the projection of A and the propagation, or, for
+// a short M, the two standalone K-slice kernels and an observed-only GEMM.
 int run_input_fused(GemmProblem g, float* predicted, float* magnitude, int layout, void* workspace,
                     size_t workspace_bytes, cudaStream_t stream) {
   SDC_REQUIRE(predicted != nullptr && magnitude != nullptr, "predicted/magnitude must not be null");
@@ -138,6 +139,13 @@ int run_input_fused(GemmProblem g, float* predicted, float* magnitude, int layou
     int rc = check_problem(r);
     if (rc != SDC_OK) return rc;
     const KsliceScratch scratch = kslice_scratch(r);
+    if (kslice_standalone(r)) {
+      rc = check_current_device();
+      if (rc != SDC_OK) return rc;
+      rc = launch_kslice_standalone(r, scratch, stream);
+      if (rc != SDC_OK) return rc;
+      return launch_gemm(g, stream);  // q_full unset: observed-only epilogue
+    }
     g.q_full = scratch.q_full;
     g.q_part = scratch.q_part;
     g.grid_sync = scratch.grid_sync;

@@ -49,7 +49,7 @@
 #include <algorithm>
 #include <atomic>
 
-#include "gemm.cuh"
+#include "kslice.cuh"
 
 namespace sdc {
 namespace {
@@ -58,7 +58,6 @@ constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBKBytes = 128;  // one 128-byte swizzle atom of K per stage
 constexpr int kStages = 4;
-constexpr int kSliceK = 64;    // K elements per input-checksum slice
 constexpr uint32_t kTmemCols = 512;
 // Tile width in output columns. NVFP4 keeps 256 as well: a 128-wide tile
 // would leave room for two accumulators next to the block scales, but the
@@ -73,6 +72,7 @@ constexpr uint32_t kSfaCol = 256;  // 4 k-steps x 4 columns
 constexpr uint32_t kSfbCol = 272;  // 4 k-steps x 4 columns x B row groups
 constexpr int kChunks = kBN / 32;  // the widest tile's 32-column chunks
 constexpr int kGroupM = 16;        // M-tiles per raster group
+constexpr int64_t kPacedItems = 4;  // projection items per warp above which they are paced
 
 constexpr int kABytes = kBM * kBKBytes;
 constexpr int kSfaBytes = 4 * 512;
@@ -226,7 +226,6 @@ __device__ __forceinline__ float transpose_reduce(float (&x)[N], int lane) {
   return x[0];
 }
 
-constexpr int kBandRows = 512;  // rows per projection band (K-slice layout)
 
 __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
   uint32_t v;
@@ -952,112 +951,22 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
         }
         return true;
       };
-      // ---- phase 1: per-band projection partials. Lane = 4 * l + g: k-group g
-      // (16 consecutive k), row lane l (rows band_start + l, + 8, ... ascending);
-      // the 8 row lanes combine as ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)).
+      // ---- phase 1: per-band projection partials (project_item, kslice.cuh),
+      // spread over the first half of the CTA's tiles.
       {
-        const int g = lane & 3, l = lane >> 2;
+        const ProjectionView view{p.a, p.sa, p.sfa, p.weights, p.m, p.k, p.k_blocks, num_slices, p.q_part};
         const int64_t items = static_cast<int64_t>(num_slices) * p.q_bands;
         const int64_t first_item = static_cast<int64_t>(blockIdx.x) * 4 + prediction_index<WIDE>(warp);
         const int64_t item_step = static_cast<int64_t>(gridDim.x) * 4;
         const int64_t my_items = first_item < items ? (items - 1 - first_item) / item_step + 1 : 0;
         int64_t j = 0;
         for (int64_t item = first_item; item < items && !*abort_flag; item += item_step, ++j) {
-          if (!pace(static_cast<uint32_t>(j * half / my_items))) break;
-          const int64_t chunk = item % num_slices, band = item / num_slices;
-          const int64_t k0 = chunk * kSliceK + g * 16;
-          // K % 16 == 0 (FP8) / % 32 == 0 (NVFP4): a group of 16 is all in or all out.
-          const bool k_in = k0 < p.k;
-          const int64_t row_end = min(static_cast<int64_t>(p.m), (band + 1) * kBandRows);
-          float2 enc[16], mg[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) enc[e] = mg[e] = make_float2(0.f, 0.f);
-          constexpr int kBatch = 4;
-          for (int64_t r0 = band * kBandRows + l; r0 < row_end; r0 += 8 * kBatch) {
-            uint4 raw[kBatch];
-            uint32_t sfv[kBatch];
-            float w[kBatch][C];
-#pragma unroll
-            for (int i = 0; i < kBatch; ++i) {
-              const int64_t row = r0 + 8 * i;
-              const bool row_in = row < row_end;
-              const bool in = row_in && k_in;
-              if constexpr (is_e4m3(KIND)) {
-                raw[i] = in ? __ldg(reinterpret_cast<const uint4*>(p.a + row * row_bytes + k0))
-                            : make_uint4(0, 0, 0, 0);
-                // Block-scaled: the row's scale of the 128-wide block holding these 16 k.
-                if constexpr (BLK) sfv[i] = in ? __float_as_uint(__ldg(p.sa + row * p.k_blocks + (k0 >> 7))) : 0u;
-              } else {
-                const uint2 u = in ? __ldg(reinterpret_cast<const uint2*>(p.a + row * row_bytes + k0 / 2))
-                                   : make_uint2(0, 0);
-                raw[i] = make_uint4(u.x, u.y, 0, 0);
-                const int64_t off = ((row >> 7) * k_atoms + (k0 >> 6)) * 512 + (row & 31) * 16 +
-                                    ((row >> 5) & 3) * 4 + ((k0 >> 4) & 3);
-                sfv[i] = in ? __ldg(p.sfa + off) : 0u;
-              }
-#pragma unroll
-              for (int c = 0; c < C; ++c) {
-                w[i][c] = row_in ? __ldg(p.weights + static_cast<int64_t>(c) * p.m + row) : 0.f;
-              }
-            }
-#pragma unroll
-            for (int i = 0; i < kBatch; ++i) {
-              if (r0 + 8 * i >= row_end) break;
-              float v[16];
-              if constexpr (is_e4m3(KIND)) {
-                const uint32_t words[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  const float2 lo = e4m3x2_to_float2(words[j] & 0xFFFFu), hi = e4m3x2_to_float2(words[j] >> 16);
-                  v[4 * j] = lo.x; v[4 * j + 1] = lo.y; v[4 * j + 2] = hi.x; v[4 * j + 3] = hi.y;
-                }
-                if constexpr (BLK) {
-                  const float scale = __uint_as_float(sfv[i]);
-#pragma unroll
-                  for (int e = 0; e < 16; ++e) v[e] = __fmul_rn(v[e], scale);
-                }
-              } else {
-                float lo8[8], hi8[8];
-                e2m1x8_to_float(raw[i].x, lo8);
-                e2m1x8_to_float(raw[i].y, hi8);
-                const float scale = decode_e4m3(sfv[i]);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                  v[e] = lo8[e] * scale;
-                  v[8 + e] = hi8[e] * scale;
-                }
-              }
-              const float2 wv = make_float2(w[i][0], C == 2 ? w[i][C - 1] : 0.f);
-              const float2 wa = make_float2(fabsf(wv.x), fabsf(wv.y));
-#pragma unroll
-              for (int e = 0; e < 16; ++e) {
-                enc[e] = fma2(wv, make_float2(v[e], v[e]), enc[e]);
-                const float av = fabsf(v[e]);
-                mg[e] = fma2(wa, make_float2(av, av), mg[e]);
-              }
-            }
-          }
-#pragma unroll
-          for (int offset = 4; offset <= 16; offset <<= 1) {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              enc[e].x += __shfl_xor_sync(0xffffffffu, enc[e].x, offset);
-              enc[e].y += __shfl_xor_sync(0xffffffffu, enc[e].y, offset);
-              mg[e].x += __shfl_xor_sync(0xffffffffu, mg[e].x, offset);
-              mg[e].y += __shfl_xor_sync(0xffffffffu, mg[e].y, offset);
-            }
-          }
-          if (l == 0) {
-            float* dst = p.q_part + (band * k_pad + chunk * kSliceK + g * 16) * C * 2;
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              if constexpr (C == 2) {
-                reinterpret_cast<float4*>(dst)[e] = make_float4(enc[e].x, mg[e].x, enc[e].y, mg[e].y);
-              } else {
-                reinterpret_cast<float2*>(dst)[e] = make_float2(enc[e].x, mg[e].x);
-              }
-            }
-          }
+          // A few items (a short M) run at once: pacing only matters when
+          // the projection is large enough to take L2 bandwidth from the
+          // mainloop's loads.
+          if (my_items > kPacedItems && !pace(static_cast<uint32_t>(j * half / my_items))) break;
+          const int64_t band = item / num_slices, chunk = item % num_slices;
+          project_item<KIND, C>(view, band, chunk, lane, band_partial<C>(view, band, chunk));
         }
       }
       // ---- phase 2: q_full = sum over bands (ascending) ----
@@ -1073,6 +982,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
       prediction_grid_barrier(p.grid_sync, 2 * gridDim.x, ct, abort_flag, p.watchdog, p.wait_limit_ns);
       // ---- phase 3: predictions of this CTA's tiles ----
       const uint32_t last = my_tiles > 0 ? my_tiles - 1 : 0u;
+      const uint32_t start = min(static_cast<uint32_t>(*tiles_done), last);
       uint32_t jt = 0;
       uint32_t slices_staged = 0;  // B slices copied to shared memory (e4m3)
       bool copy_in_flight = false;  // thread ct == 0: a slice copy not yet seen landing
@@ -1080,7 +990,9 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
       // Every decision to leave is taken by all 128 prediction threads
       // together (named_barrier_or), since the slice loop synchronises them.
       for (int t = work_first; t < p.num_work; t += work_step, ++jt) {
-        const bool paced = pace(half + jt * (last > half ? last - half : 0u) / (my_tiles > 0 ? my_tiles : 1u));
+        // Spread over the tiles still to come when the projection finished
+        // (the second half for a long M, almost all of them for a short one).
+        const bool paced = pace(start + jt * (last > start ? last - start : 0u) / (my_tiles > 0 ? my_tiles : 1u));
         if (named_barrier_or(2, 128, !paced || *abort_flag != 0)) break;
         int mt, nt;
         work_coords<PAIR>(t, p, rank, mt, nt);

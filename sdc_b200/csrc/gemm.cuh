@@ -98,5 +98,12 @@ struct KsliceScratch {
   float* q_part;        // [ceil(M / 512)][K_pad][C][2]
 };
 KsliceScratch kslice_scratch(const ReferenceProblem& p);
+// NVFP4 with a short M (rows <= kStandaloneMaxRows) and N >= 16 M: the
+// projection and the K-slice prediction run as two kernels spread over the
+// whole GPU before an observed-only GEMM, with bit-identical partials
+// (kslice.cu); otherwise they stay inside the GEMM, behind its tiles.
+constexpr int64_t kStandaloneMaxRows = 4096;
+bool kslice_standalone(const ReferenceProblem& p);
+int launch_kslice_standalone(const ReferenceProblem& p, const KsliceScratch& s, cudaStream_t stream);
 
 }  // namespace sdc

@@ -21,7 +21,7 @@
 // rounding, so finalize is unchanged.
 #include <algorithm>
 
-#include "gemm.cuh"
+#include "kslice.cuh"
 
 namespace sdc {
 namespace {
@@ -259,7 +259,6 @@ int tile_propagate_impl(const ReferenceProblem& p, cudaStream_t stream) {
 
 namespace {
 constexpr int64_t kSyncBytes = 256;
-constexpr int64_t kBandRows = 512;  // rows per projection band (gemm.cu)
 int64_t kslice_q_floats(int channels, int64_t k) { return static_cast<int64_t>(channels) * 2 * ceil_div(k, 64) * 64; }
 }  // namespace
 

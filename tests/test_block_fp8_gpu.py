@@ -103,15 +103,26 @@ def test_random_output_within_accumulation_bound(shape):
 
 
 @pytest.mark.parametrize("shape", [(136, 144, 128), (300, 200, 384), (2048, 2048, 512), (2560, 4352, 2048),
-                                   (640, 33024, 1024)])
-def test_kslice_prediction_bit_exact_vs_oracle(shape):
+                                   (640, 33024, 1024), (5000, 640, 512)])
+@pytest.mark.parametrize("path", [1, 2])
+def test_kslice_prediction_bit_exact_vs_oracle(shape, path):
+    # path 1: the prediction inside the GEMM; path 2: the two standalone
+    # kernels before an observed-only GEMM (the default for M <= 4096).
+    from sdc_b200 import capi
+
     m, n, k = shape
     args = _block_case(m, n, k, seed=11)
     rows = torch.arange(m, device=DEV, dtype=torch.int64)
     weights = torch.stack(((rows * 7 % 29 - 14).float() / 8, (rows * 11 % 37 - 18).float() / 16))
     base = ops.fp8_block_mm(*args)
     fused_out, fused_obs, fused_hit = ops.abft_fp8_block_mm(*args, weights, -1, -1, -1)
-    out, obs, hit, pred, mag = ops.abft_fp8_block_reference_mm(*args, weights, -1, -1, -1)
+    lib = capi.lib()
+    try:
+        capi.check(lib.sdc_test_set_kslice_path(path))
+        out, obs, hit, pred, mag = ops.abft_fp8_block_reference_mm(*args, weights, -1, -1, -1)
+        torch.cuda.synchronize()
+    finally:
+        capi.check(lib.sdc_test_set_kslice_path(0))
     assert torch.equal(out, base) and torch.equal(fused_out, base) and torch.equal(obs, fused_obs)
     assert hit.item() == fused_hit.item() == 0
     assert obs.shape == pred.shape == (2, (m + 127) // 128, ((n + 127) // 128) * 128)

@@ -2,7 +2,8 @@
 
 Every wait in the GEMM kernels gives up after a time limit and unwinds. The
 test hook ``sdc_test_set_watchdog`` shortens that limit to 1 ms and makes the
-prediction warps' pacing target unreachable (a flag that nothing sets), so
+prediction warps' pacing target unreachable (a flag that nothing sets; the
+in-GEMM prediction path is forced with ``sdc_test_set_kslice_path``), so
 the wait runs out on purpose; nothing faults or hangs the GPU. The launch
 must then report itself through its own outputs: bit 1 of ``hit``, the
 non-finite flag, and finalize's verdict detected + nonfinite, plus the
@@ -66,6 +67,16 @@ def _call(kind, m, n, k):
 def test_expired_wait_is_reported_in_band(kind, shape):
     run = _call(kind, *shape)
     assert _watchdog() == 0
+    # The pacing wait belongs to the in-GEMM prediction path (these short M
+    # would otherwise run the standalone K-slice kernels, which never wait).
+    capi.check(capi.lib().sdc_test_set_kslice_path(1))
+    try:
+        _expire_and_recover(run)
+    finally:
+        capi.check(capi.lib().sdc_test_set_kslice_path(0))
+
+
+def _expire_and_recover(run):
     clean, hit, nonfinite, flags, hit_out = run()
     assert hit == 0 and nonfinite == 0 and flags == [False] * 5
     try:
