@@ -225,6 +225,27 @@ class Protected:
     def requantise(self, a, b):
         self.args, self.quantised = quantise(self.precision, a, b)
 
+    def step_rows(self, fault=(-1, -1, -1)):
+        """The step with row checksums: the protected GEMM whose epilogue also
+        sums the output rows, the row prediction alpha * A (B^T e), the
+        finalize and the two-dimensional locator."""
+        if self.precision == "fp8_block":
+            a, b, sa, sb = self.args
+            rows_args = (2, a, sa, b, sb, self.k, None)
+        elif self.precision == "fp8":
+            a, b, alpha = self.args
+            rows_args = (0, a, None, b, None, self.k, alpha)
+        else:
+            a, b, sa, sb, k, alpha = self.args
+            rows_args = (1, a, sa, b, sb, k, alpha)
+        out, obs, hit, pred, mag, row_obs, row_pred, row_mag = self.ops.abft_reference_rows_mm(
+            *rows_args, self.weights, *fault, 0, self.nonfinite, 1)
+        packet = self.ops.abft_finalize_reference(obs, pred, mag, hit, self.nonfinite, self.n, self.atol,
+                                                  self.rtol, None, True)
+        location, located, row_flags, _, _ = self.ops.abft_locate2d(row_obs, row_pred, row_mag, self.atol,
+                                                                    self.rtol, packet[1], packet[2], packet[3])
+        return out, packet, (location, located, row_flags)
+
     def step(self, fault=(-1, -1, -1), diagnostics=True):
         out, obs, hit, pred, mag = self.fused(*self.args, self.weights, *fault, 0, self.nonfinite, *self.layout_args)
         packet = self.ops.abft_finalize_reference(obs, pred, mag, hit, self.nonfinite, self.n, self.atol,
@@ -471,6 +492,49 @@ def detection_campaign(prot, flips_per_bit, seed):
             "detectable_rule": "|w_c delta| > thr_c + |clean res_c| for some channel c, delta from the decoded "
                                "operands (independent of the checksum arithmetic); non-finite flips detectable",
             "clean_flagged": bool(clean_packet[3][0])}
+
+
+def row_checksum_leg(prot, steps, seed, flips=48, rounds=5):
+    """Row checksums with two-dimensional localisation: the step's cost
+    against the column-only step and the unprotected GEMM (paired
+    alternating blocks), and a localisation campaign of single accumulator
+    flips (bits 23-30 at seeded positions): of the flips the columns
+    detected, how many the row/column pair located at the exact element,
+    against the two-channel ratio locator on the same packets."""
+    stream = torch.cuda.current_stream()
+    n = max(2, steps // rounds)
+    t_rows = t_cols = t_plain = 0.0
+    for _ in range(rounds):
+        t_rows += timed(prot.step_rows, n, 1, stream)
+        t_cols += timed(prot.step, n, 1, stream)
+        t_plain += timed(prot.unprotected, n, 1, stream)
+    t_rows, t_cols, t_plain = (t / (rounds * n) for t in (t_rows, t_cols, t_plain))
+    g = torch.Generator().manual_seed(seed)
+    counts = {"flips": 0, "column_detected": 0, "row_detected": 0, "located_2d": 0, "located_2d_exact": 0,
+              "located_ratio": 0, "located_ratio_exact": 0}
+    _, clean_packet, (_, clean_located, clean_rows) = prot.step_rows()
+    for i in range(flips):
+        row = int(torch.randint(0, prot.m, (1,), generator=g))
+        col = int(torch.randint(0, prot.n, (1,), generator=g))
+        bit = 23 + i % 8
+        _, packet, (location, located, row_flags) = prot.step_rows((row, col, bit))
+        ratio_location, ratio_located = prot.ops.abft_locate(packet[1], packet[2], packet[3], prot.m)
+        counts["flips"] += 1
+        if not bool(packet[3][0]):
+            continue
+        counts["column_detected"] += 1
+        counts["row_detected"] += bool(row_flags[0])
+        counts["located_2d"] += bool(located)
+        counts["located_2d_exact"] += location.tolist() == [row, col]
+        counts["located_ratio"] += bool(ratio_located)
+        counts["located_ratio_exact"] += ratio_location.tolist() == [row, col]
+    return {"ms_per_step": t_rows * 1e3, "column_only_ms_per_step": t_cols * 1e3,
+            "unprotected_ms_per_step": t_plain * 1e3,
+            "overhead_pct": 100.0 * (t_rows / t_plain - 1.0),
+            "added_over_column_only_pct": 100.0 * (t_rows / t_cols - 1.0),
+            "clean_flagged": bool(clean_packet[3][0]) or bool(clean_rows[0]) or bool(clean_located),
+            "localisation": counts,
+            "method": "paired alternating blocks; flips of the fp32 accumulator, bits 23-30, seeded positions"}
 
 
 def fault_schedule(prot, seed, gemms=1000, rate=1e-3):
@@ -799,6 +863,8 @@ def run_ours(args):
         if rank == 0 and not args.no_detection:
             entry["detection"] = detection_campaign(prot, args.flips_per_bit, SEEDS[precision])
             entry["fault_schedule"] = fault_schedule(prot, SEEDS[precision], gemms=args.schedule_gemms)
+        if rank == 0 and not args.no_rows:
+            entry["row_checksums"] = row_checksum_leg(prot, args.steps, SEEDS[precision] + 7)
         if not args.no_e2e:  # every rank: its own shard end to end, time = max over ranks
             host_a, host_b = host_operands(m, n, k, SEEDS[precision] + 1000 * rank)
             host_a = host_a.pin_memory()
@@ -844,7 +910,7 @@ def run_ours(args):
         "roofline": head["roofline"], "clocks": head["clocks"],
         "gpu_launches": LAUNCHES_PER_STEP * args.steps,
         "e2e": head.get("e2e"), "detection": head.get("detection"), "fault_schedule": head.get("fault_schedule"),
-        "thresholds": head["thresholds"],
+        "thresholds": head["thresholds"], "row_checksums": head.get("row_checksums"),
     }
     if "exchanged_status" in head:
         line["exchanged_status"] = head["exchanged_status"]
@@ -1164,6 +1230,8 @@ def main():
     parser.add_argument("--no-sweep", action="store_true", help="skip the Qwen2.5-7B linear-shape sweep")
     parser.add_argument("--sweep-steps", type=int, default=10)
     parser.add_argument("--no-augmented", action="store_true", help="skip the augmented BF16 ABFT leg")
+    parser.add_argument("--no-rows", action="store_true",
+                        help="skip the row-checksum (two-dimensional localisation) leg")
     parser.add_argument("--augmented-only", action="store_true",
                         help="run only the augmented BF16 leg and print its object (profiling; not a bench line)")
     parser.add_argument("--augmented-sizes", default="2048,8192")

@@ -63,6 +63,13 @@ enum sdc_reference_layout {
   SDC_LAYOUT_KSLICE = 1
 };
 
+/* Operand kinds of the generic (kind-dispatched) entry points. */
+enum sdc_kind {
+  SDC_KIND_FP8 = 0,       /* e4m3 tensorwise: scales unused, alpha device scalar */
+  SDC_KIND_NVFP4 = 1,     /* packed e2m1 + ue4m3 scale atoms, alpha device scalar */
+  SDC_KIND_FP8_BLOCK = 2  /* e4m3 + fp32 1x128 (A) / 128x128 (B) block scales, no alpha */
+};
+
 /* ---- library / device ------------------------------------------------- */
 
 const char* sdc_last_error(void);
@@ -299,6 +306,57 @@ int sdc_abft_bf16_augmented_gemm(
     int64_t bit, uint16_t* d, float* observed, float* predicted,
     float* magnitude, int32_t* hit, int32_t* tile_flags, void* workspace,
     size_t workspace_bytes, sdc_stream_t stream);
+
+/* ---- row checksums and two-dimensional localisation (extension) ---------
+ * The reference checks column sums only; these add C.e against A.(B^T e):
+ * the GEMM epilogue also writes row_observed[b][m] = sum of row m's fp32
+ * values (after the fault) over the 64 columns of block b, ascending, from
+ * +0; sdc_abft_row_reference forms predicted_rows = alpha * A . u and
+ * magnitude_rows = |alpha| * |A| . u_abs with u = e^T B, u_abs = e^T |B| (the
+ * K-slice projection of B with unit weights); sdc_abft_locate2d decides the
+ * rows like finalize decides the columns (threshold atol + rtol * magnitude,
+ * no FMA, strict >, non-finite fails) and locates (row, col) when exactly one
+ * row and one column fail and nothing is non-finite. */
+
+/* The input-fused GEMM of `kind` (a_scales/b_scales as the kind's entry point
+ * takes them) plus row_observed fp32 [ceil(N/64)][M]. Other arguments as
+ * sdc_abft_{fp8,nvfp4,fp8_block}_reference_gemm. */
+int sdc_abft_reference_gemm_rows(
+    int kind, const uint8_t* a, const void* a_scales, const uint8_t* b_rows,
+    const void* b_scales, int64_t m, int64_t n, int64_t k, const float* alpha,
+    int algorithm, const float* weights, int64_t row, int64_t col, int64_t bit,
+    int32_t* nonfinite, void* d, float* observed, int32_t* hit,
+    float* predicted, float* magnitude, int reference_layout,
+    float* row_observed, void* workspace, size_t workspace_bytes,
+    sdc_stream_t stream);
+
+/* Workspace of sdc_abft_row_reference (u, u_abs for K rounded up to 64). */
+size_t sdc_abft_row_workspace_bytes(int64_t k);
+/* predicted_rows / magnitude_rows fp32 [M] of `kind`; alpha null for
+ * SDC_KIND_FP8_BLOCK. */
+int sdc_abft_row_reference(int kind, const uint8_t* a, const void* a_scales,
+                           const uint8_t* b_rows, const void* b_scales,
+                           int64_t m, int64_t n, int64_t k, const float* alpha,
+                           float* predicted_rows, float* magnitude_rows,
+                           void* workspace, size_t workspace_bytes,
+                           sdc_stream_t stream);
+
+/* Workspace of sdc_abft_locate2d. */
+size_t sdc_abft_locate2d_workspace_bytes(void);
+/* col_residual / col_threshold / col_flags: finalize's diagnostics outputs
+ * ([C, N] and u8[5]). Writes row_residual / row_threshold [M] (nullable),
+ * location int64[2] and located u8[1] (the element when exactly one row and
+ * one column fail, else -1 / 0), row_flags u8[2] (a row failed, a row was
+ * non-finite). */
+int sdc_abft_locate2d(const float* row_observed, int64_t row_blocks,
+                      const float* predicted_rows, const float* magnitude_rows,
+                      int64_t m, float atol, float rtol,
+                      const float* col_residual, const float* col_threshold,
+                      int algorithm, int64_t n, const uint8_t* col_flags,
+                      float* row_residual, float* row_threshold,
+                      int64_t* location, uint8_t* located, uint8_t* row_flags,
+                      void* workspace, size_t workspace_bytes,
+                      sdc_stream_t stream);
 
 /* ---- finalize (src/cutlass_gemm/csrc/abft/common/finalize.cu:55-319) ------
  * Sums the per-tile partials of each (channel, column) in ascending tile

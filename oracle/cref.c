@@ -393,3 +393,102 @@ int oracle_augment_encode(const uint16_t* a, int64_t m, int64_t k, const uint16_
   free(seg);
   return 0;
 }
+
+/* Row checksums (the sdc_b200 extension; the reference checks columns only).
+ *
+ * oracle_row_observed: out[b][row] = sum of v[row][col] over the 64 columns
+ * col of block b that are < n, ascending, from +0 (the GEMM epilogue's order).
+ * v: fp32 [m][n] row-major; out: [ceil(n/64)][m]. */
+int oracle_row_observed(const float* v, int64_t m, int64_t n, float* out) {
+  const int64_t blocks = (n + 63) / 64;
+  for (int64_t b = 0; b < blocks; ++b) {
+    for (int64_t row = 0; row < m; ++row) {
+      float s = 0.f;
+      for (int64_t col = b * 64; col < b * 64 + 64 && col < n; ++col) s = s + v[row * n + col];
+      out[b * m + row] = s;
+    }
+  }
+  return 0;
+}
+
+/* oracle_row_reference: u[k] = e^T B, u_abs[k] = e^T |B| over the n rows of
+ * B in the K-slice projection's order (bands of 128 rows; in a band, 8 row
+ * lanes l each run an fma chain over rows begin + l, + 8, ...; combined as
+ * ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)); bands ascending) with
+ * unit weights; then for each row m of A, 32 lane chains: lane j runs
+ * acc_j = fmaf(A[m][k], u[k], acc_j) (and the |A| u_abs chain) over the
+ * 16-element groups g = j, j + 32, ... (k ascending), combined by a butterfly
+ * (p[j] = p[j] + p[j ^ w] for w = 16, 8, 4, 2, 1; the result is p[0]);
+ * pred[m] = alpha * acc, mag[m] = |alpha| * acc_abs. kind: 0 FP8, 1 NVFP4,
+ * 2 block-scaled FP8 (B's scales per 128 x 128 block). */
+int oracle_row_reference(int kind, const uint8_t* a, const uint8_t* sfa, const uint8_t* b, const uint8_t* sfb,
+                         int64_t m, int64_t n, int64_t k, float alpha, float* pred, float* mag) {
+  float* u = (float*)calloc((size_t)k, sizeof(float));
+  float* ua = (float*)calloc((size_t)k, sizeof(float));
+  float* lanes = (float*)malloc(sizeof(float) * 2 * 8 * k);
+  float* row_v = (float*)malloc(sizeof(float) * k);
+  if (!u || !ua || !lanes || !row_v) {
+    free(u);
+    free(ua);
+    free(lanes);
+    free(row_v);
+    return 1;
+  }
+  const int bkind = kind == 2 ? 3 : kind;
+  const int64_t bands = (n + 127) / 128;
+  for (int64_t bnd = 0; bnd < bands; ++bnd) {
+    const int64_t begin = bnd * 128, end = begin + 128 < n ? begin + 128 : n;
+    memset(lanes, 0, sizeof(float) * 2 * 8 * k);
+    for (int64_t row = begin; row < end; ++row) {
+      const int l = (int)((row - begin) & 7);
+      decode_row(bkind, b, sfb, row, k, row_v);
+      float* e = lanes + (0 * 8 + l) * k;
+      float* g = lanes + (1 * 8 + l) * k;
+      for (int64_t kk = 0; kk < k; ++kk) {
+        e[kk] = fmaf(1.f, row_v[kk], e[kk]);
+        g[kk] = fmaf(1.f, fabsf(row_v[kk]), g[kk]);
+      }
+    }
+    for (int h = 0; h < 2; ++h) {
+      const float* p = lanes + h * 8 * k;
+      float* q = h == 0 ? u : ua;
+      for (int64_t kk = 0; kk < k; ++kk) {
+        const float band = ((p[0 * k + kk] + p[1 * k + kk]) + (p[2 * k + kk] + p[3 * k + kk])) +
+                           ((p[4 * k + kk] + p[5 * k + kk]) + (p[6 * k + kk] + p[7 * k + kk]));
+        q[kk] = bnd == 0 ? band : q[kk] + band;
+      }
+    }
+  }
+  const int64_t groups = k / 16;
+  for (int64_t row = 0; row < m; ++row) {
+    decode_row(kind, a, sfa, row, k, row_v);
+    float p[32], pa[32];
+    for (int j = 0; j < 32; ++j) {
+      float acc = 0.f, acc_a = 0.f;
+      for (int64_t g = j; g < groups; g += 32) {
+        for (int64_t kk = g * 16; kk < g * 16 + 16; ++kk) {
+          acc = fmaf(row_v[kk], u[kk], acc);
+          acc_a = fmaf(fabsf(row_v[kk]), ua[kk], acc_a);
+        }
+      }
+      p[j] = acc;
+      pa[j] = acc_a;
+    }
+    for (int w = 16; w >= 1; w >>= 1) {
+      float np[32], npa[32];
+      for (int j = 0; j < 32; ++j) {
+        np[j] = p[j] + p[j ^ w];
+        npa[j] = pa[j] + pa[j ^ w];
+      }
+      memcpy(p, np, sizeof(p));
+      memcpy(pa, npa, sizeof(pa));
+    }
+    pred[row] = alpha * p[0];
+    mag[row] = fabsf(alpha) * pa[0];
+  }
+  free(u);
+  free(ua);
+  free(lanes);
+  free(row_v);
+  return 0;
+}

@@ -47,6 +47,10 @@ def lib():
         _lib.oracle_tile_reference_subset.restype = ctypes.c_int
         _lib.oracle_observed_epilogue.argtypes = [f32, i64, i64, f32, ctypes.c_int, f32, i64]
         _lib.oracle_observed_epilogue.restype = ctypes.c_int
+        _lib.oracle_row_observed.argtypes = [f32, i64, i64, f32]
+        _lib.oracle_row_observed.restype = ctypes.c_int
+        _lib.oracle_row_reference.argtypes = [ctypes.c_int, u8, u8, u8, u8, i64, i64, i64, ctypes.c_float, f32, f32]
+        _lib.oracle_row_reference.restype = ctypes.c_int
         u16 = ctypes.POINTER(ctypes.c_uint16)
         _lib.oracle_augment_encode.argtypes = [u16, i64, i64, u16, ctypes.c_int, u16]
         _lib.oracle_augment_encode.restype = ctypes.c_int
@@ -196,3 +200,31 @@ def augment_encode(a_bits, w_bits):
     if rc:
         raise MemoryError("oracle allocation failed")
     return q
+
+
+def row_observed(values):
+    """Row sums per 64-column block, [ceil(n/64), m], of the fp32 values [m, n]
+    the epilogue summed (columns ascending from +0)."""
+    values = np.ascontiguousarray(values, dtype=np.float32)
+    m, n = values.shape
+    out = np.zeros(((n + 63) // 64, m), np.float32)
+    f32 = ctypes.POINTER(ctypes.c_float)
+    lib().oracle_row_observed(values.ctypes.data_as(f32), m, n, out.ctypes.data_as(f32))
+    return out
+
+
+def row_reference(kind, a, sfa, b, sfb, m, n, k, alpha):
+    """(predicted_rows, magnitude_rows) [m] of the row checksums (alpha * A . e^T B
+    and |alpha| * |A| . e^T |B|) in the library's order."""
+    pred = np.zeros(m, np.float32)
+    mag = np.zeros(m, np.float32)
+    pa, ka = _ptr(a)
+    pb, kb = _ptr(b)
+    psa, ksa = _ptr(sfa)
+    psb, ksb = _ptr(sfb)
+    f32 = ctypes.POINTER(ctypes.c_float)
+    rc = lib().oracle_row_reference(KINDS[kind], pa, psa, pb, psb, m, n, k, ctypes.c_float(np.float32(alpha)),
+                                    pred.ctypes.data_as(f32), mag.ctypes.data_as(f32))
+    if rc:
+        raise MemoryError("oracle allocation failed")
+    return pred, mag

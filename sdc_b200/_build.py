@@ -37,6 +37,7 @@ CUDA_SOURCES = [
     "locate.cu",
     "augmented.cu",
     "kslice.cu",
+    "rowsum.cu",
 ]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -48,6 +48,7 @@ class AbftConfig:
     parameters: dict = field(default_factory=dict)
     reference_layout: str = "tile"
     locate: bool = False
+    row_checksums: bool = False
 
     def __post_init__(self):
         if not isinstance(self.parameters, dict):
@@ -77,9 +78,11 @@ class AbftConfig:
             raise ValueError("Invalid ABFT recovery/on_error policy")
         if type(self.reference_block_k) is not int or self.reference_block_k <= 0 or self.reference_block_k % 16:
             raise ValueError("reference_block_k must be a positive multiple of 16")
-        for name in ("diagnostics", "timing", "locate"):
+        for name in ("diagnostics", "timing", "locate", "row_checksums"):
             if type(getattr(self, name)) is not bool:
                 raise ValueError(f"{name} must be boolean")
+        if self.row_checksums and (self.implementation != "native" or self.reference_mode != "input_fused"):
+            raise ValueError("row_checksums needs the native input_fused execution")
         if self.reference_layout not in {"tile", "kslice"}:
             raise ValueError("reference_layout must be tile or kslice")
 

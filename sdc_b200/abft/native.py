@@ -128,7 +128,8 @@ def execute_input_fused(prepared, cfg, fault, context, *, method=None, policy=No
     policy = method.validate_execution(prepared, cfg) if policy is None else policy
     if cfg.reference_mode != "input_fused":
         raise NotImplementedError("native executions on B200 use the input_fused reference")
-    locate = cfg.locate and policy.algorithm == 0
+    rows = cfg.row_checksums
+    locate = (cfg.locate and policy.algorithm == 0) or rows
     statistics = cfg.diagnostics or method.needs_diagnostics or locate
     require_device(prepared.a.device)
     plan = _Plan(prepared, cfg, fault, context, method, policy, _selected(fault, context))
@@ -142,26 +143,47 @@ def execute_input_fused(prepared, cfg, fault, context, *, method=None, policy=No
 
     def gemm(injected):
         nonfinite = torch.empty(1, device=prepared.a.device, dtype=torch.int32)
+        if rows:
+            output, observed, hit, predicted, magnitude, *row_evidence = prepared.collected_rows_native(
+                weights, injected, algorithm=policy.algorithm, nonfinite=nonfinite, layout=cfg.reference_layout)
+            return output, (observed, predicted, magnitude, hit, nonfinite), row_evidence
         output, observed, hit, predicted, magnitude = prepared.collected_reference_native(
             weights, injected, algorithm=policy.algorithm, nonfinite=nonfinite, layout=cfg.reference_layout)
-        return output, (observed, predicted, magnitude, hit, nonfinite)
+        return output, (observed, predicted, magnitude, hit, nonfinite), None
 
     def finalize(evidence, reference):
         return ops.abft_finalize_reference(*evidence, prepared.n, cfg.atol, cfg.rtol, reference, statistics,
                                            policy.algorithm, thresholds)
 
+    def decide(evidence, row_evidence, reference):
+        """Column decisions from the finalize; with row checksums, the row
+        check is merged in and the location is the failing (row, column)
+        pair, if exactly one of each failed."""
+        reference, tensors, (residual, threshold, flags) = _decisions(finalize(evidence, reference), statistics)
+        if row_evidence is not None:
+            location, located, row_flags, row_residual, row_threshold = ops.abft_locate2d(
+                *row_evidence, cfg.atol, cfg.rtol, residual, threshold, flags, policy.algorithm)
+            tensors["detected"] = tensors["detected"] | row_flags[0]
+            tensors["nonfinite"] = tensors["nonfinite"] | row_flags[1]
+            tensors["location"], tensors["located"] = location, located
+            if cfg.diagnostics:
+                tensors.update(row_residual=row_residual, row_threshold=row_threshold)
+        return reference, tensors, (residual, threshold, flags)
+
     with timer.phase("execute"):
-        output, evidence = gemm(injection)
+        output, evidence, row_evidence = gemm(injection)
     with timer.phase("finalize"):
-        first_reference, tensors, (residual, threshold, flags) = _decisions(finalize(evidence, None), statistics)
-    del evidence
-    if locate:
+        first_reference, tensors, (residual, threshold, flags) = decide(evidence, row_evidence, None)
+    del evidence, row_evidence
+    if locate and not rows:
         with timer.phase("locate"):
             tensors["location"], tensors["located"] = ops.abft_locate(residual, threshold, flags, prepared.m)
     plan.state = {**plan.state, "reference": first_reference}
     described = call_context(prepared, cfg, fault, context, plan.selected, output, method)
     described["reference_operand_reuse"] = "mainloop_shared_operands"
     described["threshold_source"] = "method_state" if thresholds is not None else "config_atol_rtol"
+    if rows:
+        described["location_assumption"] = "row_and_column_checksums"
     report = AbftReport(tensors, described, cfg.method, "input_fused_native", timer.events)
 
     def recheck():
@@ -173,8 +195,8 @@ def execute_input_fused(prepared, cfg, fault, context, *, method=None, policy=No
             tensors["recovered"], tensors["recheck_failed"] = fixed, ~fixed
             report.context["recovery_action"] = "located_element_recomputed"
             return None, None
-        replacement, retry_evidence = gemm((-1, -1, -1))
-        _, checked, _ = _decisions(finalize(retry_evidence, first_reference), statistics)
+        replacement, retry_evidence, retry_rows = gemm((-1, -1, -1))
+        _, checked, _ = decide(retry_evidence, retry_rows, first_reference)
         report.context["recovery_action"] = "full_recompute"
         return replacement, checked
 

@@ -130,6 +130,25 @@ class PreparedGemm:
         op = ops.abft_fp8_reference_mm if self.precision == "fp8" else ops.abft_nvfp4_reference_mm
         return op(*self._native_args(), weights, *fault, algorithm, nonfinite, LAYOUTS[layout])
 
+    def collected_rows_native(self, weights, fault=(-1, -1, -1), *, algorithm=0, nonfinite=None, layout="tile"):
+        """``collected_reference_native`` plus the row checksums: observed
+        row sums per 64-column block [ceil(N/64), M], predicted row sums
+        alpha * A (B^T e) [M] and their magnitude [M]."""
+        if self.precision not in INPUT_REFERENCE_PRECISIONS:
+            raise NotImplementedError(f"row checksums are not implemented for {self.precision}")
+        ops = _ops()
+        a, b = self.a, self.b
+        if self.blockwise:
+            if layout != "kslice":
+                raise NotImplementedError("block-scaled FP8 computes its input-fused prediction in the kslice "
+                                          "layout only")
+            args = (2, a.view(torch.float8_e4m3fn), self.sfa, b.view(torch.float8_e4m3fn), self.sfb, self.k, None)
+        elif self.precision == "fp8":
+            args = (0, a.view(torch.float8_e4m3fn), None, b.view(torch.float8_e4m3fn), None, self.k, self.alpha)
+        else:
+            args = (1, a, self.sfa, b, self.sfb, self.k, self.alpha)
+        return ops.abft_reference_rows_mm(*args, weights, *fault, algorithm, nonfinite, LAYOUTS[layout])
+
     def augmented_native(self, weights, fault=(-1, -1, -1), *, algorithm=0):
         """Output, observed, hit, predicted and magnitude partials of the
         augmented BF16 GEMM (the checksum rows are extra M-tiles of the same

@@ -55,6 +55,13 @@ PROTOTYPES = {
     "sdc_abft_fp8_block_reference_gemm": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _size, _vp]),
     "sdc_abft_correct_fp8_block": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
     "sdc_bf16_gemm": (_int, [_vp, _vp, _i64, _i64, _i64, _vp, _vp]),
+    "sdc_abft_reference_gemm_rows": (_int, [_int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _int, _vp, _i64, _i64,
+                                             _i64, _vp, _vp, _vp, _vp, _vp, _vp, _int, _vp, _vp, _size, _vp]),
+    "sdc_abft_row_workspace_bytes": (_size, [_i64]),
+    "sdc_abft_row_reference": (_int, [_int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _size, _vp]),
+    "sdc_abft_locate2d_workspace_bytes": (_size, []),
+    "sdc_abft_locate2d": (_int, [_vp, _i64, _vp, _vp, _i64, ctypes.c_float, ctypes.c_float, _vp, _vp, _int, _i64,
+                                 _vp, _vp, _vp, _vp, _vp, _vp, _vp, _size, _vp]),
     "sdc_abft_augment_encode": (_int, [_vp, _i64, _i64, _int, _vp, _vp, _vp]),
     "sdc_abft_augmented_workspace_bytes": (_size, [_int, _i64, _i64]),
     "sdc_abft_bf16_augmented_gemm": (_int, [_vp, _vp, _i64, _i64, _i64, _int, _vp, _i64, _i64, _i64, _vp, _vp, _vp,

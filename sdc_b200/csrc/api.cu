@@ -288,4 +288,43 @@ int sdc_abft_fp8_block_reference_gemm(const uint8_t* a, const uint8_t* b_rows, c
   return run_input_fused(g, predicted, magnitude, SDC_LAYOUT_KSLICE, workspace, workspace_bytes, stream);
 }
 
+// ---- row checksums (extension) ----
+
+int sdc_abft_reference_gemm_rows(int kind, const uint8_t* a, const void* a_scales, const uint8_t* b_rows,
+                                 const void* b_scales, int64_t m, int64_t n, int64_t k, const float* alpha,
+                                 int algorithm, const float* weights, int64_t row, int64_t col, int64_t bit,
+                                 int32_t* nonfinite, void* d, float* observed, int32_t* hit, float* predicted,
+                                 float* magnitude, int reference_layout, float* row_observed, void* workspace,
+                                 size_t workspace_bytes, sdc_stream_t stream) {
+  using namespace sdc;
+  SDC_REQUIRE(row_observed != nullptr, "row checksums need row_observed [ceil(N/64)][M]");
+  int rc = SDC_OK;
+  GemmProblem g{};
+  int tile = 128;
+  if (kind == SDC_KIND_FP8) {
+    rc = check_fp8(a, b_rows, m, n, k, alpha, d);
+    g = make_problem(Kind::kFp8, a, b_rows, nullptr, nullptr, m, n, k, alpha, false, d);
+    tile = 64;
+  } else if (kind == SDC_KIND_NVFP4) {
+    const uint8_t* sfa = static_cast<const uint8_t*>(a_scales);
+    const uint8_t* sfb = static_cast<const uint8_t*>(b_scales);
+    rc = check_nvfp4(a, b_rows, sfa, sfb, m, n, k, alpha, d);
+    g = make_problem(Kind::kNvf4, a, b_rows, sfa, sfb, m, n, k, alpha, true, d);
+  } else if (kind == SDC_KIND_FP8_BLOCK) {
+    const float* sa = static_cast<const float*>(a_scales);
+    const float* sb = static_cast<const float*>(b_scales);
+    rc = check_fp8_block(a, b_rows, sa, sb, m, n, k, d);
+    g = make_problem(Kind::kFp8Block, a, b_rows, reinterpret_cast<const uint8_t*>(sa),
+                     reinterpret_cast<const uint8_t*>(sb), m, n, k, nullptr, true, d);
+    SDC_REQUIRE(reference_layout == SDC_LAYOUT_KSLICE, "block-scaled FP8 offers the K-slice layout only");
+  } else {
+    return fail(SDC_ERR_INVALID, "row checksums: kind must be SDC_KIND_FP8, SDC_KIND_NVFP4 or SDC_KIND_FP8_BLOCK");
+  }
+  if (rc == SDC_OK) rc = check_abft(algorithm, weights, m, n, row, col, bit, observed, hit);
+  if (rc != SDC_OK) return rc;
+  set_abft(g, algorithm, weights, row, col, bit, nonfinite, observed, hit, tile);
+  g.row_observed = row_observed;
+  return run_input_fused(g, predicted, magnitude, reference_layout, workspace, workspace_bytes, stream);
+}
+
 }  // extern "C"

@@ -181,6 +181,9 @@ struct Params {
   int32_t tiles_m_all;
   int32_t aug_rows;
   int32_t* tile_flags;
+  // Row checksums (extension, nullable): sum over each 64-column block of
+  // every output row's fp32 values (after the fault), [ceil(N/64)][M].
+  float* row_observed;
   int32_t flag_cols;
 };
 
@@ -369,7 +372,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
   // thread owning output row `row`: fault injection, nonfinite check, the
   // observed checksum partials of the warp's 32 rows into `red`, the store.
   auto emit_chunk = [&](float (&v)[32], int q, int row, bool row_ok, int c0, int chunk, const float* w,
-                        uint32_t& nonfinite, uint32_t& faulted) {
+                        uint32_t& nonfinite, uint32_t& faulted, float& row_acc) {
     if (C > 0 && p.fbit >= 0 && row == p.frow && p.fcol >= c0 && p.fcol < c0 + 32) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
@@ -377,6 +380,22 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
       }
       atomicOr(p.hit, 1);
       faulted |= 1u << (chunk >> 2);  // bit per 128-column block of the tile
+    }
+    if constexpr (C > 0) {
+      if (p.row_observed != nullptr) {
+        // Row sums per 64-column block (chunks 2b and 2b + 1): columns in
+        // ascending order from +0, only those < n.
+        float sum = (chunk & 1) ? row_acc : 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (c0 + j < p.n) sum = __fadd_rn(sum, v[j]);
+        }
+        if (chunk & 1) {
+          if (row_ok && c0 - 32 < p.n) p.row_observed[static_cast<int64_t>(c0 >> 6) * p.m + row] = sum;
+        } else {
+          row_acc = sum;
+        }
+      }
     }
     if constexpr (BF16OUT) {
       // The output as stored first: one round-to-nearest conversion per
@@ -805,6 +824,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
         const bool live = !named_barrier_or(1, kAccThreads, !ok || *abort_flag != 0);
         if (live) {
           uint32_t nonfinite = 0, faulted = 0;
+          float row_acc = 0.f;  // row sum of the current 64-column block
 #pragma unroll
           for (int cc = 0; cc < kHalfCols / 32; ++cc) {
             float v[32];
@@ -814,7 +834,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
               v[2 * j + 1] = total[cc * 16 + j].y;
             }
             const int chunk = half * (kHalfCols / 32) + cc;
-            emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite, faulted);
+            emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite, faulted, row_acc);
           }
           if (nonfinite) atomicExch(p.nonfinite, 1);
         }
@@ -867,6 +887,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
         }
       };
       uint32_t nonfinite = 0, faulted = 0;
+      float row_acc = 0.f;  // row sum of the current 64-column block
       if (live) {
         if constexpr (WIDE) {
           uint32_t r[kWarpChunks][32];
@@ -880,7 +901,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(alpha, __uint_as_float(r[cc][j]));
             const int chunk = first_chunk + cc;
-            emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite, faulted);
+            emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite, faulted, row_acc);
           }
         } else {
 #pragma unroll 1
@@ -903,7 +924,7 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
                 }
               }
             } else {
-              emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite, faulted);
+              emit_chunk(v, q, row, row_ok, n0 + chunk * 32, chunk, w, nonfinite, faulted, row_acc);
             }
           }
         }
@@ -1232,6 +1253,7 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   p.tiles_m_all = p.tiles_m + (AUG ? static_cast<int32_t>(ceil_div(g.aug_rows, kBM)) : 0);
   p.aug_rows = AUG ? static_cast<int32_t>(g.aug_rows) : 0;
   p.tile_flags = g.tile_flags;
+  p.row_observed = g.row_observed;
   p.flag_cols = static_cast<int32_t>(g.flag_cols);
   p.tiles_n = static_cast<int32_t>(ceil_div(g.n, tile_n(KIND)));
   p.num_tiles = p.tiles_m_all * p.tiles_n;

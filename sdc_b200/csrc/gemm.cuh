@@ -58,6 +58,9 @@ struct GemmProblem {
   // The caller zeroed hit and tile_flags on this stream already (launch_gemm
   // then issues no memsets for them).
   bool status_zeroed;
+  // Row checksums (nullable): fp32 [ceil(N/64)][M] row sums of the output
+  // per 64-column block, after the fault (FP8 and NVFP4 kinds).
+  float* row_observed;
 };
 
 // Launches the GEMM (and its fused epilogue) on `stream`. Zeroes hit/nonfinite

@@ -281,6 +281,30 @@ int standalone_kind(const ReferenceProblem& r, const KsliceScratch& s, cudaStrea
 
 }  // namespace
 
+int launch_projection_sums(Kind kind, int channels, const ProjectionView& view, float* q_full, cudaStream_t stream) {
+  const int64_t bands = ceil_div(view.m, kBandRows);
+  const dim3 grid(static_cast<unsigned>(view.num_slices));
+  const dim3 block(32 * kProjectWarps);
+  switch (kind) {
+    case Kind::kFp8:
+      if (channels == 2) kslice_project<Kind::kFp8, 2><<<grid, block, 0, stream>>>(view, bands, q_full);
+      else kslice_project<Kind::kFp8, 1><<<grid, block, 0, stream>>>(view, bands, q_full);
+      break;
+    case Kind::kNvf4:
+      if (channels == 2) kslice_project<Kind::kNvf4, 2><<<grid, block, 0, stream>>>(view, bands, q_full);
+      else kslice_project<Kind::kNvf4, 1><<<grid, block, 0, stream>>>(view, bands, q_full);
+      break;
+    case Kind::kFp8Block:
+      if (channels == 2) kslice_project<Kind::kFp8Block, 2><<<grid, block, 0, stream>>>(view, bands, q_full);
+      else kslice_project<Kind::kFp8Block, 1><<<grid, block, 0, stream>>>(view, bands, q_full);
+      break;
+    default:
+      return fail(SDC_ERR_INVALID, "projection sums are defined for the FP8 and NVFP4 kinds");
+  }
+  SDC_CUDA_CHECK(cudaGetLastError());
+  return SDC_OK;
+}
+
 bool kslice_standalone(const ReferenceProblem& r) {
   const int mode = g_kslice_mode.load(std::memory_order_relaxed);
   if (mode == 1) return false;

@@ -18,16 +18,19 @@ namespace sdc {
 constexpr int kSliceK = 64;     // K elements per input-checksum slice
 constexpr int kBandRows = 128;  // rows per projection band
 
-// What one projection item reads and writes.
+// What one projection item reads and writes. The projected operand is A for
+// the column checksums and B (rows [N][K], unit weights) for the row
+// checksums' e^T B.
 struct ProjectionView {
   const uint8_t* a;        // codes: e4m3 [M][K] or packed e2m1 [M][K/2]
-  const float* sa;         // block-scaled FP8: A scales [M][K/128]
-  const uint8_t* sfa;      // NVFP4: A scale atoms
-  const float* weights;    // [C][M]
+  const float* sa;         // block-scaled FP8: scales [ceil(M / 2^scale_shift)][K/128]
+  const uint8_t* sfa;      // NVFP4: scale atoms
+  const float* weights;    // [C][M]; null = every weight 1
   int64_t m, k;
   int64_t k_blocks;        // K / 128 (block-scaled)
   int64_t num_slices;      // ceil(K / 64)
   float* q_part;           // [bands][K_pad][C][2]
+  int scale_shift = 0;     // block-scaled FP8: log2 rows per scale row (0 for A, 7 for B)
 };
 
 // One item = (band, slice `chunk`) for one warp: lane = 4 * l + g covers
@@ -62,7 +65,9 @@ __device__ __forceinline__ void project_item(const ProjectionView& v, int64_t ba
       if constexpr (is_e4m3(KIND)) {
         raw[i] = in ? __ldg(reinterpret_cast<const uint4*>(v.a + row * row_bytes + k0)) : make_uint4(0, 0, 0, 0);
         // Block-scaled: the row's scale of the 128-wide block holding these 16 k.
-        if constexpr (BLK) sfv[i] = in ? __float_as_uint(__ldg(v.sa + row * v.k_blocks + (k0 >> 7))) : 0u;
+        if constexpr (BLK) {
+          sfv[i] = in ? __float_as_uint(__ldg(v.sa + (row >> v.scale_shift) * v.k_blocks + (k0 >> 7))) : 0u;
+        }
       } else {
         const uint2 u = in ? __ldg(reinterpret_cast<const uint2*>(v.a + row * row_bytes + k0 / 2)) : make_uint2(0, 0);
         raw[i] = make_uint4(u.x, u.y, 0, 0);
@@ -71,7 +76,9 @@ __device__ __forceinline__ void project_item(const ProjectionView& v, int64_t ba
         sfv[i] = in ? __ldg(v.sfa + off) : 0u;
       }
 #pragma unroll
-      for (int c = 0; c < C; ++c) w[i][c] = row_in ? __ldg(v.weights + static_cast<int64_t>(c) * v.m + row) : 0.f;
+      for (int c = 0; c < C; ++c) {
+        w[i][c] = !row_in ? 0.f : v.weights != nullptr ? __ldg(v.weights + static_cast<int64_t>(c) * v.m + row) : 1.f;
+      }
     }
 #pragma unroll
     for (int i = 0; i < kBatch; ++i) {
@@ -136,6 +143,10 @@ __device__ __forceinline__ void project_item(const ProjectionView& v, int64_t ba
     }
   }
 }
+
+// q_full [K_pad][C][2] of `view` (bands summed in ascending order) by the
+// standalone projection kernel: one block per slice (kslice.cu).
+int launch_projection_sums(Kind kind, int channels, const ProjectionView& view, float* q_full, cudaStream_t stream);
 
 // The band partial of item (band, chunk) in the [bands][K_pad][C][2] layout.
 template <int C>

@@ -317,6 +317,110 @@ Out5 abft_fp8_block_reference_mm(const Tensor& a, const Tensor& b, const Tensor&
   return {out, observed, hit, predicted, magnitude};
 }
 
+// ---------------------------------------------------- row checksums (ext) ----
+
+using Out8 = std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor>;
+void check_common(int64_t n, double atol, double rtol);  // finalize's checks (below)
+
+// The input-fused GEMM of `kind` with its row checksums: the reference op's
+// five outputs plus row_observed [ceil(N/64), M] and the row prediction and
+// magnitude [M]. Operands as the kind's own op takes them (a_scales/b_scales:
+// NVFP4 scale atoms or block-scaled FP8 fp32 scales; alpha: FP8 and NVFP4).
+Out8 abft_reference_rows_mm(int64_t kind, const Tensor& a, OptTensor a_scales, const Tensor& b, OptTensor b_scales,
+                            int64_t k, OptTensor alpha, const Tensor& weights, int64_t row, int64_t col, int64_t bit,
+                            int64_t algorithm, OptTensor nonfinite, int64_t layout) {
+  const int c = channels_of(algorithm);
+  TORCH_CHECK(kind == SDC_KIND_FP8 || kind == SDC_KIND_NVFP4 || kind == SDC_KIND_FP8_BLOCK,
+              "row checksums: kind must be 0 (FP8), 1 (NVFP4) or 2 (block-scaled FP8)");
+  TORCH_CHECK(layout == SDC_LAYOUT_TILE || layout == SDC_LAYOUT_KSLICE, "ABFT reference layout must be 0 or 1");
+  const void* sa = nullptr;
+  const void* sb = nullptr;
+  const float* al = nullptr;
+  if (kind == SDC_KIND_FP8) {
+    TORCH_CHECK(alpha.has_value(), "FP8 row checksums need alpha");
+    check_fp8_operands(a, b, *alpha);
+    TORCH_CHECK(a.size(1) == k, "K must equal the operands' K");
+    al = alpha->const_data_ptr<float>();
+  } else if (kind == SDC_KIND_NVFP4) {
+    TORCH_CHECK(alpha.has_value() && a_scales.has_value() && b_scales.has_value(),
+                "NVFP4 row checksums need both scale tensors and alpha");
+    check_nvfp4_operands(a, b, *a_scales, *b_scales, k, *alpha);
+    sa = a_scales->const_data_ptr();
+    sb = b_scales->const_data_ptr();
+    al = alpha->const_data_ptr<float>();
+  } else {
+    TORCH_CHECK(a_scales.has_value() && b_scales.has_value(), "block-scaled FP8 row checksums need both scales");
+    check_fp8_block_operands(a, b, *a_scales, *b_scales);
+    TORCH_CHECK(a.size(1) == k, "K must equal the operands' K");
+    sa = a_scales->const_data_ptr();
+    sb = b_scales->const_data_ptr();
+  }
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int64_t m = a.size(0), n = b.size(0);
+  check_projection(a, weights, c, m, n, row, col, bit, nonfinite);
+  const int64_t tm = (m + 127) / 128, np = kind == SDC_KIND_FP8 ? ((n + 63) / 64) * 64 : ((n + 127) / 128) * 128;
+  Tensor out = kind == SDC_KIND_FP8 ? at::empty_strided({m, n}, {1, m}, a.options().dtype(at::kFloat))
+                                    : at::empty({m, n}, a.options().dtype(at::kBFloat16));
+  const auto f32 = a.options().dtype(at::kFloat);
+  auto observed = at::empty({c, tm, np}, f32);
+  auto predicted = at::empty_like(observed);
+  auto magnitude = at::empty_like(observed);
+  auto hit = at::empty({1}, a.options().dtype(at::kInt));
+  auto row_observed = at::empty({(n + 63) / 64, m}, f32);
+  auto row_predicted = at::empty({m}, f32);
+  auto row_magnitude = at::empty({m}, f32);
+  const size_t ws_bytes = sdc_abft_workspace_bytes(static_cast<int>(algorithm), m, n, k, static_cast<int>(layout));
+  auto ws = workspace(a, ws_bytes);
+  check_status(sdc_abft_reference_gemm_rows(
+      static_cast<int>(kind), u8(a), sa, u8(b), sb, m, n, k, al, static_cast<int>(algorithm),
+      weights.const_data_ptr<float>(), row, col, bit, opt_i32(nonfinite), out.data_ptr(), observed.data_ptr<float>(),
+      hit.data_ptr<int32_t>(), predicted.data_ptr<float>(), magnitude.data_ptr<float>(), static_cast<int>(layout),
+      row_observed.data_ptr<float>(), ws.data_ptr(), ws_bytes, stream_of(a)));
+  const size_t row_ws_bytes = sdc_abft_row_workspace_bytes(k);
+  auto row_ws = workspace(a, row_ws_bytes);
+  check_status(sdc_abft_row_reference(static_cast<int>(kind), u8(a), sa, u8(b), sb, m, n, k, al,
+                                      row_predicted.data_ptr<float>(), row_magnitude.data_ptr<float>(),
+                                      row_ws.data_ptr(), row_ws_bytes, stream_of(a)));
+  return {out, observed, hit, predicted, magnitude, row_observed, row_predicted, row_magnitude};
+}
+
+Out5 abft_locate2d(const Tensor& row_observed, const Tensor& row_predicted, const Tensor& row_magnitude, double atol,
+                   double rtol, const Tensor& residual, const Tensor& threshold, const Tensor& flags,
+                   int64_t algorithm) {
+  const int c = channels_of(algorithm);
+  for (const Tensor* t : {&row_observed, &row_predicted, &row_magnitude, &residual, &threshold}) {
+    TORCH_CHECK(t->is_cuda() && t->device() == row_observed.device() && t->is_contiguous() &&
+                    t->scalar_type() == at::kFloat,
+                "locate2d tensors must be contiguous CUDA float32 on one device");
+  }
+  TORCH_CHECK(row_observed.dim() == 2 && row_predicted.dim() == 1 && row_magnitude.sizes() == row_predicted.sizes() &&
+                  row_observed.size(1) == row_predicted.size(0),
+              "locate2d: row_observed [ceil(N/64), M] and row prediction/magnitude [M]");
+  TORCH_CHECK(residual.dim() == 2 && residual.size(0) == c && threshold.sizes() == residual.sizes(),
+              "locate2d: residual and threshold must be finalize's diagnostics [channels, N]");
+  TORCH_CHECK(flags.is_cuda() && flags.scalar_type() == at::kBool && flags.numel() == 5,
+              "locate2d: flags must be finalize's bool[5]");
+  check_common(residual.size(1), atol, rtol);
+  const c10::cuda::CUDAGuard guard(row_observed.device());
+  const int64_t m = row_predicted.size(0), n = residual.size(1);
+  const auto f32 = row_observed.options();
+  auto row_residual = at::empty({m}, f32);
+  auto row_threshold = at::empty({m}, f32);
+  auto location = at::empty({2}, f32.dtype(at::kLong));
+  auto located = at::empty({}, f32.dtype(at::kBool));
+  auto row_flags = at::empty({2}, f32.dtype(at::kBool));
+  const size_t ws_bytes = sdc_abft_locate2d_workspace_bytes();
+  auto ws = workspace(row_observed, ws_bytes);
+  check_status(sdc_abft_locate2d(
+      row_observed.const_data_ptr<float>(), row_observed.size(0), row_predicted.const_data_ptr<float>(),
+      row_magnitude.const_data_ptr<float>(), m, static_cast<float>(atol), static_cast<float>(rtol),
+      residual.const_data_ptr<float>(), threshold.const_data_ptr<float>(), static_cast<int>(algorithm), n,
+      static_cast<const uint8_t*>(flags.const_data_ptr()), row_residual.data_ptr<float>(),
+      row_threshold.data_ptr<float>(), location.data_ptr<int64_t>(), static_cast<uint8_t*>(located.data_ptr()),
+      static_cast<uint8_t*>(row_flags.data_ptr()), ws.data_ptr(), ws_bytes, stream_of(row_observed)));
+  return {location, located, row_flags, row_residual, row_threshold};
+}
+
 // -------------------------------------------------------------- finalize ----
 // Restates the checks of src/cutlass_gemm/csrc/abft/common/finalize.cu:154-319.
 
@@ -749,6 +853,8 @@ TORCH_LIBRARY(sdc_cutlass, lib) {
   lib.def("quantize_nvfp4(Tensor x, float? global_scale=None, Tensor? amax=None) -> (Tensor, Tensor, Tensor, Tensor)");
   lib.def("nvfp4_pack_scales(Tensor scales, int k) -> Tensor");
   lib.def("abft_locate(Tensor residual, Tensor threshold, Tensor flags, int m) -> (Tensor, Tensor)");
+  lib.def("abft_reference_rows_mm(int kind, Tensor a, Tensor? a_scales, Tensor b_rows, Tensor? b_scales, int k, Tensor? alpha, Tensor weights, int row, int col, int bit, int algorithm=0, Tensor(a!)? nonfinite=None, int layout=1) -> (Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor)");
+  lib.def("abft_locate2d(Tensor row_observed, Tensor row_predicted, Tensor row_magnitude, float atol, float rtol, Tensor residual, Tensor threshold, Tensor flags, int algorithm=0) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
   lib.def("abft_fp8_correct(Tensor a, Tensor b_rows, Tensor alpha, Tensor location, Tensor located, Tensor(a!) output) -> Tensor");
   lib.def("abft_nvfp4_correct(Tensor a_packed, Tensor b_packed, Tensor sfa, Tensor sfb, int k, Tensor alpha, Tensor location, Tensor located, Tensor(a!) output) -> Tensor");
 }
@@ -776,6 +882,8 @@ TORCH_LIBRARY_IMPL(sdc_cutlass, CUDA, lib) {
   lib.impl("abft_fp8_block_correct", &abft_fp8_block_correct);
   lib.impl("nvfp4_pack_scales", &nvfp4_pack_scales);
   lib.impl("abft_locate", &abft_locate);
+  lib.impl("abft_reference_rows_mm", &abft_reference_rows_mm);
+  lib.impl("abft_locate2d", &abft_locate2d);
   lib.impl("abft_fp8_correct", &abft_fp8_correct);
   lib.impl("abft_nvfp4_correct", &abft_nvfp4_correct);
 }

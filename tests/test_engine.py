@@ -395,7 +395,9 @@ def test_native_rejects_collector_overrides():
     {"method": "classic", "reference_mode": "augmented"}, {"method": "none", "implementation": "native"},
     {"method": "classic", "unknown": 1}, {"method": "classic", "parameters": {"x": math.nan}},
     {"method": "classic", "parameters": {1: 2}}, {"method": "classic", "reference_layout": "rows"},
-    {"method": "classic", "locate": "yes"}, {"method": ""}])
+    {"method": "classic", "locate": "yes"}, {"method": ""}, {"method": "classic", "row_checksums": 1},
+    {"method": "classic", "row_checksums": True},
+    {"method": "classic", "row_checksums": True, "implementation": "native", "reference_mode": "direct"}])
 def test_invalid_configurations_rejected(value):
     with pytest.raises(ValueError):
         parse_abft_config(value)
@@ -408,3 +410,6 @@ def test_configuration_defaults_and_extensions():
     assert parse_abft_config({"method": "classic", "recovery": "correct", "locate": True,
                               "reference_layout": "kslice"}).recovery == "correct"
     assert AbftConfig().parameters is not AbftConfig().parameters
+    rows = parse_abft_config({"method": "sum", "implementation": "native", "reference_mode": "input_fused",
+                              "row_checksums": True})
+    assert rows.row_checksums and not cfg.row_checksums

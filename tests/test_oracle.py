@@ -337,3 +337,40 @@ def test_c_oracle_block_scaled_matches_float64():
     assert np.all(np.abs(pred.sum(axis=1)[:, :n] - exact) <= 1e-5 * exact_mag + 1e-6)
     assert np.allclose(mag.sum(axis=1)[:, :n], exact_mag, rtol=1e-5)
     assert not pred[:, :, n:].any()
+
+
+# --- row checksums (extension) ----------------------------------------------
+
+@pytest.mark.parametrize("kind", ["fp8", "nvfp4", "fp8_block"])
+def test_c_oracle_row_checksums_match_float64(kind):
+    rng = np.random.default_rng(13)
+    m, n, k = 150, 200, 256
+    if kind == "fp8":
+        a = formats.e4m3_encode(rng.normal(size=(m, k)).astype(np.float32) * 8)
+        b = formats.e4m3_encode(rng.normal(size=(n, k)).astype(np.float32) * 8)
+        sfa = sfb = None
+        da, db = formats.e4m3_decode(a), formats.e4m3_decode(b)
+    elif kind == "nvfp4":
+        a, sa, _ = quant.quantize_nvfp4(rng.normal(size=(m, k)).astype(np.float32))
+        b, sb, _ = quant.quantize_nvfp4(rng.normal(size=(n, k)).astype(np.float32))
+        sfa, sfb = quant.pack_scales(sa, k), quant.pack_scales(sb, k)
+        da, db = quant.dequantize_nvfp4(a, sa, 1.0), quant.dequantize_nvfp4(b, sb, 1.0)
+    else:
+        a, sfa = quant.quantize_fp8_block(rng.normal(size=(m, k)).astype(np.float32), 1)
+        b, sfb = quant.quantize_fp8_block(rng.normal(size=(n, k)).astype(np.float32), 128)
+        da, db = quant.dequantize_fp8_block(a, sfa, 1), quant.dequantize_fp8_block(b, sfb, 128)
+    alpha = 1.0 if kind == "fp8_block" else 0.25
+    pred, mag = native.row_reference(kind, a, sfa, b, sfb, m, n, k, alpha)
+    exact = da.astype(np.float64) @ db.astype(np.float64).sum(axis=0) * alpha
+    exact_mag = np.abs(da).astype(np.float64) @ np.abs(db).astype(np.float64).sum(axis=0) * alpha
+    assert np.all(np.abs(pred - exact) <= 1e-5 * exact_mag + 1e-6)
+    assert np.allclose(mag, exact_mag, rtol=1e-5)
+    # Observed row sums: per 64-column block, the columns added in ascending order from +0.
+    values = rng.normal(size=(m, n)).astype(np.float32)
+    blocks = native.row_observed(values)
+    assert blocks.shape == (4, m)
+    for j in range(4):
+        acc = np.zeros(m, np.float32)
+        for c in range(64 * j, min(n, 64 * j + 64)):
+            acc = acc + values[:, c]
+        assert np.array_equal(blocks[j], acc)
