@@ -330,8 +330,9 @@ int sdc_abft_reference_gemm_rows(
     float* row_observed, void* workspace, size_t workspace_bytes,
     sdc_stream_t stream);
 
-/* Workspace of sdc_abft_row_reference (u, u_abs for K rounded up to 64). */
-size_t sdc_abft_row_workspace_bytes(int64_t k);
+/* Workspace of sdc_abft_row_reference: u, u_abs for K rounded up to 64,
+ * and the projection's partials of each 128-row band of B. */
+size_t sdc_abft_row_workspace_bytes(int64_t n, int64_t k);
 /* predicted_rows / magnitude_rows fp32 [M] of `kind`; alpha null for
  * SDC_KIND_FP8_BLOCK. */
 int sdc_abft_row_reference(int kind, const uint8_t* a, const void* a_scales,

@@ -57,7 +57,7 @@ PROTOTYPES = {
     "sdc_bf16_gemm": (_int, [_vp, _vp, _i64, _i64, _i64, _vp, _vp]),
     "sdc_abft_reference_gemm_rows": (_int, [_int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _int, _vp, _i64, _i64,
                                              _i64, _vp, _vp, _vp, _vp, _vp, _vp, _int, _vp, _vp, _size, _vp]),
-    "sdc_abft_row_workspace_bytes": (_size, [_i64]),
+    "sdc_abft_row_workspace_bytes": (_size, [_i64, _i64]),
     "sdc_abft_row_reference": (_int, [_int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _size, _vp]),
     "sdc_abft_locate2d_workspace_bytes": (_size, []),
     "sdc_abft_locate2d": (_int, [_vp, _i64, _vp, _vp, _i64, ctypes.c_float, ctypes.c_float, _vp, _vp, _int, _i64,

@@ -98,7 +98,7 @@ int launch_tile_propagate(const ReferenceProblem& p, cudaStream_t stream);
 struct KsliceScratch {
   uint32_t* grid_sync;  // 256 bytes, zeroed by launch_gemm
   float* q_full;        // [K_pad][C][2]
-  float* q_part;        // [ceil(M / 512)][K_pad][C][2]
+  float* q_part;        // [ceil(M / 128)][K_pad][C][2]
 };
 KsliceScratch kslice_scratch(const ReferenceProblem& p);
 // NVFP4 with a short M (rows <= kStandaloneMaxRows) and N >= 16 M: the

@@ -7,9 +7,11 @@
 // GEMM. This path spreads the same arithmetic over the whole GPU instead
 // (chosen by kslice_standalone):
 //
-//   kslice_project  one block per slice, its warps over the 128-row bands:
-//                   project_item, the same device function the fused path
-//                   runs, then the bands added in ascending order into q_full;
+//   kslice_project  one warp per (128-row band, slice) item: project_item,
+//                   the same device function the fused path runs, into the
+//                   band partials;
+//   kslice_fold     one thread per entry: the bands added in ascending order
+//                   into q_full (the fused path's phase 2);
 //   kslice_predict  one thread per (slot t, column n): each slice's q staged
 //                   in shared memory, the column's fma chains over the slices
 //                   s % Tm == t (ascending), k ascending, exactly as the fused
@@ -25,40 +27,46 @@
 namespace sdc {
 namespace {
 
-constexpr int kMaxBands = 32;  // bands staged in shared memory at a time
 constexpr int kProjectWarps = 8;
+constexpr int kItemBatch = 4;     // rows of a row lane loaded ahead of their fma chains
+constexpr int kFoldThreads = 64;  // small blocks: the entries spread over every SM
+constexpr int kFoldBatch = 32;    // band partials loaded ahead of their adds
 constexpr int kPredictThreads = 128;
 
 // Test hook: 0 = choose by size, 1 = always fused, 2 = always standalone.
 std::atomic<int> g_kslice_mode{0};
 
-// One block per slice; its warps take the 128-row bands in turn, kMaxBands
-// at a time: each band's partial (project_item, as in the fused path) goes to
-// shared memory, then the first kEntries threads add the bands to their
-// entry's running sum in ascending order (the fused path's phase 2), and
-// q_full of the slice is that sum.
+// One warp per item (band, slice), items in band-major order so that a
+// block's warps read neighbouring slices of the same rows: the band's partial
+// of the slice (project_item, as in the fused path) into q_part.
 template <Kind KIND, int C>
-__global__ void __launch_bounds__(32 * kProjectWarps) kslice_project(ProjectionView v, int64_t bands, float* q_full) {
-  constexpr int kEntries = kSliceK * C * 2;
-  static_assert(kEntries <= 32 * kProjectWarps, "one entry per summing thread");
-  __shared__ __align__(16) float part[kMaxBands][kEntries];
-  const int64_t chunk = blockIdx.x;
-  const int e = threadIdx.x;
+__global__ void __launch_bounds__(32 * kProjectWarps, 2) kslice_project(ProjectionView v, int64_t items) {
   griddep_launch_dependents();
-  float q = 0.f;
-  for (int64_t band0 = 0; band0 < bands; band0 += kMaxBands) {
-    const int64_t count = min(static_cast<int64_t>(kMaxBands), bands - band0);
-    for (int64_t b = threadIdx.x >> 5; b < count; b += kProjectWarps) {
-      // All 16 rows of each row lane in flight at once (a band is 128 rows).
-      project_item<KIND, C, kBandRows / 8>(v, band0 + b, chunk, static_cast<int>(threadIdx.x & 31), part[b]);
-    }
-    __syncthreads();
-    if (e < kEntries) {
-      for (int64_t b = 0; b < count; ++b) q = (band0 + b == 0) ? part[0][e] : __fadd_rn(q, part[b][e]);
-    }
-    __syncthreads();  // part is rewritten by the next group of bands
+  const int64_t item = static_cast<int64_t>(blockIdx.x) * kProjectWarps + (threadIdx.x >> 5);
+  if (item >= items) return;
+  const int64_t band = item / v.num_slices, chunk = item % v.num_slices;
+  project_item<KIND, C, kItemBatch>(v, band, chunk, static_cast<int>(threadIdx.x & 31),
+                                    band_partial<C>(v, band, chunk));
+}
+
+// q_full[e] = the bands' partials of entry e added in ascending band order
+// (the fused path's phase 2), the loads batched ahead of the adds.
+__global__ void __launch_bounds__(kFoldThreads) kslice_fold(const float* q_part, int64_t entries, int64_t bands,
+                                                           float* q_full) {
+  griddep_launch_dependents();
+  const int64_t e = static_cast<int64_t>(blockIdx.x) * kFoldThreads + threadIdx.x;
+  if (e >= entries) return;
+  float q = __ldg(q_part + e);
+  int64_t b = 1;
+  for (; b + kFoldBatch <= bands; b += kFoldBatch) {
+    float x[kFoldBatch];
+#pragma unroll
+    for (int i = 0; i < kFoldBatch; ++i) x[i] = __ldg(q_part + (b + i) * entries + e);
+#pragma unroll
+    for (int i = 0; i < kFoldBatch; ++i) q = __fadd_rn(q, x[i]);
   }
-  if (e < kEntries) q_full[chunk * kEntries + e] = q;
+  for (; b < bands; ++b) q = __fadd_rn(q, __ldg(q_part + b * entries + e));
+  q_full[e] = q;
 }
 
 // Packed decodes for the prediction's inner loop. Every e2m1 code times its
@@ -243,10 +251,10 @@ int standalone_impl(const ReferenceProblem& r, const KsliceScratch& s, cudaStrea
                             r.k,
                             r.k / 128,
                             num_slices,
-                            nullptr};
-  kslice_project<KIND, C><<<static_cast<unsigned>(num_slices), 32 * kProjectWarps, 0, stream>>>(view, bands,
-                                                                                                 s.q_full);
-  SDC_CUDA_CHECK(cudaGetLastError());
+                            s.q_part};
+  (void)bands;
+  const int rc = launch_projection_sums(KIND, C, view, s.q_full, stream);
+  if (rc != SDC_OK) return rc;
   PredictArgs pa{};
   pa.b = r.b;
   pa.sfb = KIND == Kind::kNvf4 ? r.sfb : nullptr;
@@ -282,26 +290,38 @@ int standalone_kind(const ReferenceProblem& r, const KsliceScratch& s, cudaStrea
 }  // namespace
 
 int launch_projection_sums(Kind kind, int channels, const ProjectionView& view, float* q_full, cudaStream_t stream) {
+  if (channels != 1 && channels != 2) return fail(SDC_ERR_INVALID, "projection sums need 1 or 2 channels");
   const int64_t bands = ceil_div(view.m, kBandRows);
-  const dim3 grid(static_cast<unsigned>(view.num_slices));
+  ProjectionView v = view;
+  // One band: its partial is the sum, written straight into q_full.
+  if (bands == 1) v.q_part = q_full;
+  if (v.q_part == nullptr) return fail(SDC_ERR_WORKSPACE, "projection sums need band scratch");
+  const int64_t items = bands * v.num_slices;
+  const dim3 grid(static_cast<unsigned>(ceil_div(items, kProjectWarps)));
   const dim3 block(32 * kProjectWarps);
   switch (kind) {
     case Kind::kFp8:
-      if (channels == 2) kslice_project<Kind::kFp8, 2><<<grid, block, 0, stream>>>(view, bands, q_full);
-      else kslice_project<Kind::kFp8, 1><<<grid, block, 0, stream>>>(view, bands, q_full);
+      if (channels == 2) kslice_project<Kind::kFp8, 2><<<grid, block, 0, stream>>>(v, items);
+      else kslice_project<Kind::kFp8, 1><<<grid, block, 0, stream>>>(v, items);
       break;
     case Kind::kNvf4:
-      if (channels == 2) kslice_project<Kind::kNvf4, 2><<<grid, block, 0, stream>>>(view, bands, q_full);
-      else kslice_project<Kind::kNvf4, 1><<<grid, block, 0, stream>>>(view, bands, q_full);
+      if (channels == 2) kslice_project<Kind::kNvf4, 2><<<grid, block, 0, stream>>>(v, items);
+      else kslice_project<Kind::kNvf4, 1><<<grid, block, 0, stream>>>(v, items);
       break;
     case Kind::kFp8Block:
-      if (channels == 2) kslice_project<Kind::kFp8Block, 2><<<grid, block, 0, stream>>>(view, bands, q_full);
-      else kslice_project<Kind::kFp8Block, 1><<<grid, block, 0, stream>>>(view, bands, q_full);
+      if (channels == 2) kslice_project<Kind::kFp8Block, 2><<<grid, block, 0, stream>>>(v, items);
+      else kslice_project<Kind::kFp8Block, 1><<<grid, block, 0, stream>>>(v, items);
       break;
     default:
       return fail(SDC_ERR_INVALID, "projection sums are defined for the FP8 and NVFP4 kinds");
   }
   SDC_CUDA_CHECK(cudaGetLastError());
+  if (bands > 1) {
+    const int64_t entries = v.num_slices * kSliceK * channels * 2;
+    kslice_fold<<<static_cast<unsigned>(ceil_div(entries, kFoldThreads)), kFoldThreads, 0, stream>>>(
+        v.q_part, entries, bands, q_full);
+    SDC_CUDA_CHECK(cudaGetLastError());
+  }
   return SDC_OK;
 }
 

@@ -145,7 +145,9 @@ __device__ __forceinline__ void project_item(const ProjectionView& v, int64_t ba
 }
 
 // q_full [K_pad][C][2] of `view` (bands summed in ascending order) by the
-// standalone projection kernel: one block per slice (kslice.cu).
+// standalone projection kernels (kslice.cu): the band partials go to
+// view.q_part ([bands][K_pad][C][2]; unused when there is one band), then
+// they are added in ascending band order.
 int launch_projection_sums(Kind kind, int channels, const ProjectionView& view, float* q_full, cudaStream_t stream);
 
 // The band partial of item (band, chunk) in the [bands][K_pad][C][2] layout.

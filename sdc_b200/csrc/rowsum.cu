@@ -38,8 +38,8 @@ constexpr int kPanelGroups = 32;   // 16-element groups per staged panel of u (5
 constexpr int kPanelStride = 33;   // float2 per panel row e (32 groups + 1 pad)
 constexpr int kPanelFloat2 = 16 * kPanelStride;
 constexpr int kMaxStagedPanels = 48;  // 48 * 528 * 8 B = 198 KiB of shared memory
-constexpr int kLocate2dThreads = 256;
-constexpr int kLocate2dBlocks = 148;
+constexpr int kLocate2dThreads = 64;  // small blocks: the rows spread over every SM
+constexpr int kLocate2dBlocks = 4 * 148;
 constexpr int kLocateBatch = 32;  // row blocks loaded ahead of their adds
 constexpr int kBlockState = 5;    // per block: failing rows, first row, status bits, failing columns, first column
 constexpr unsigned kRowFailed = 1u;
@@ -110,7 +110,7 @@ __device__ __forceinline__ void decode_half(const GroupRaw& raw, int h, float (&
 // chains carry across chunks, in the same order. The next panel's bytes are
 // loaded while the current panel is summed.
 template <Kind KIND>
-__global__ void __launch_bounds__(32 * kRowWarps, 3)
+__global__ void __launch_bounds__(32 * kRowWarps, KIND == Kind::kNvf4 ? 2 : 3)
     row_predict(const uint8_t* a, const float* sa, const uint8_t* sfa, int64_t m, int64_t k, const float* u,
                 const float* alpha, float* predicted, float* magnitude, int chunk_panels) {
   extern __shared__ float2 staged_u[];
@@ -398,9 +398,11 @@ Kind row_kind(int kind) {
 
 extern "C" {
 
-size_t sdc_abft_row_workspace_bytes(int64_t k) {
-  if (k <= 0) return 0;
-  return static_cast<size_t>(sdc::ceil_div(k, 64) * 64 * 2) * sizeof(float);
+size_t sdc_abft_row_workspace_bytes(int64_t n, int64_t k) {
+  if (n <= 0 || k <= 0) return 0;
+  // u [K_pad][2], then the projection's band partials [ceil(N/128)][K_pad][2].
+  const int64_t floats = sdc::ceil_div(k, 64) * 64 * 2;
+  return static_cast<size_t>(floats * (1 + sdc::ceil_div(n, sdc::kBandRows))) * sizeof(float);
 }
 
 int sdc_abft_row_reference(int kind, const uint8_t* a, const void* a_scales, const uint8_t* b_rows,
@@ -418,7 +420,7 @@ int sdc_abft_row_reference(int kind, const uint8_t* a, const void* a_scales, con
   SDC_REQUIRE(kind == SDC_KIND_FP8_BLOCK || alpha != nullptr, "row checksums need alpha (FP8, NVFP4)");
   SDC_REQUIRE(k % (kind == SDC_KIND_FP8_BLOCK ? 128 : kind == SDC_KIND_NVFP4 ? 32 : 16) == 0,
               "row checksums: K must be a multiple of 16 (FP8), 32 (NVFP4) or 128 (block-scaled FP8)");
-  if (workspace == nullptr || workspace_bytes < sdc_abft_row_workspace_bytes(k) ||
+  if (workspace == nullptr || workspace_bytes < sdc_abft_row_workspace_bytes(n, k) ||
       reinterpret_cast<uintptr_t>(workspace) % 16 != 0) {
     return fail(SDC_ERR_WORKSPACE, "row checksum workspace too small or not 16-byte aligned");
   }
@@ -435,7 +437,7 @@ int sdc_abft_row_reference(int kind, const uint8_t* a, const void* a_scales, con
                       k,
                       k / 128,
                       ceil_div(k, 64),
-                      nullptr};
+                      u + ceil_div(k, 64) * 64 * 2};
   view.scale_shift = 7;  // B's block scales cover 128 rows
   rc = launch_projection_sums(kd, 1, view, u, stream);
   if (rc != SDC_OK) return rc;

@@ -376,7 +376,7 @@ Out8 abft_reference_rows_mm(int64_t kind, const Tensor& a, OptTensor a_scales, c
       weights.const_data_ptr<float>(), row, col, bit, opt_i32(nonfinite), out.data_ptr(), observed.data_ptr<float>(),
       hit.data_ptr<int32_t>(), predicted.data_ptr<float>(), magnitude.data_ptr<float>(), static_cast<int>(layout),
       row_observed.data_ptr<float>(), ws.data_ptr(), ws_bytes, stream_of(a)));
-  const size_t row_ws_bytes = sdc_abft_row_workspace_bytes(k);
+  const size_t row_ws_bytes = sdc_abft_row_workspace_bytes(n, k);
   auto row_ws = workspace(a, row_ws_bytes);
   check_status(sdc_abft_row_reference(static_cast<int>(kind), u8(a), sa, u8(b), sb, m, n, k, al,
                                       row_predicted.data_ptr<float>(), row_magnitude.data_ptr<float>(),
