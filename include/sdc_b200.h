@@ -87,10 +87,10 @@ int sdc_read_device_error(sdc_stream_t stream, int32_t* code);
  * without hanging or faulting the GPU. */
 int sdc_test_set_watchdog(uint64_t wait_limit_ns, int32_t pace_extra);
 /* Test hook (no counterpart in the reference): how later K-slice launches
- * compute their prediction. 0 (default) chooses by shape: NVFP4 with
- * M <= 4096 rows and N >= 16 M runs the projection and the prediction as two
- * kernels before an observed-only GEMM, everything else inside the GEMM;
- * 1 forces the in-GEMM path, 2 the two kernels. Both give bit-identical
+ * compute their prediction. 0 (default) chooses by shape; 1 forces the
+ * in-GEMM path (projection and prediction inside the GEMM), 2 the standalone
+ * kernels before an observed-only GEMM, 3 the projection by the standalone
+ * kernels and the prediction inside the GEMM. All give bit-identical
  * partials; the hook lets a test check it. */
 int sdc_test_set_kslice_path(int mode);
 

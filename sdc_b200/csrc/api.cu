@@ -151,6 +151,14 @@ int run_input_fused(GemmProblem g, float* predicted, float* magnitude, int layou
     g.grid_sync = scratch.grid_sync;
     g.predicted = predicted;
     g.magnitude = magnitude;
+    if (kslice_preproject(r)) {
+      rc = check_current_device();
+      if (rc != SDC_OK) return rc;
+      rc = launch_kslice_projection(r, scratch, stream);
+      if (rc != SDC_OK) return rc;
+      g.q_ready = true;
+      g.grid_sync = nullptr;  // no grid barriers in the launch
+    }
     return launch_gemm(g, stream);
   }
   int rc = launch_projection(r, stream);

@@ -102,8 +102,12 @@ __host__ __device__ constexpr int num_stages(Kind k, bool pair) {
 __host__ __device__ constexpr int pred_slice_bytes(Kind k, bool chk) {
   return (chk && is_e4m3(k)) ? tile_n(k) * 64 : 0;
 }
+// Checked launches stage each K slice's q (64 k x 2 channels x value and
+// magnitude, fp32) for the prediction warps: one batch of loads per slice.
+__host__ __device__ constexpr int pred_q_bytes(bool chk) { return chk ? 64 * 2 * 2 * 4 : 0; }
 __host__ __device__ constexpr int smem_bytes(Kind k, bool pair = false, bool chk = false) {
-  return 1024 + num_stages(k, pair) * stage_bytes(k, pair) + red_floats(k) * 4 + pred_slice_bytes(k, chk) + 512;
+  return 1024 + num_stages(k, pair) * stage_bytes(k, pair) + red_floats(k) * 4 + pred_slice_bytes(k, chk) +
+         pred_q_bytes(chk) + 512;
 }
 __host__ __device__ constexpr int num_acc(Kind k) { return k == Kind::kNvf4 ? 1 : 2; }
 // Warp roles. Tensorwise FP8: 0 TMA, 1 MMA, 2-5 epilogue, 6-9 prediction
@@ -166,6 +170,7 @@ struct Params {
   float* q_part;        // [bands][K_pad][C][2]: per-band partials
   uint32_t* grid_sync;  // arrival counter of the prediction warpgroups (zeroed per launch)
   int32_t q_bands;
+  int32_t q_ready;      // q_full computed before the launch: no projection phases
   const uint8_t* a;     // A operand rows (projection) and B rows (prediction),
   const uint8_t* sfa;   // read directly by the prediction warps
   const uint8_t* b;
@@ -254,9 +259,9 @@ __device__ __forceinline__ bool prediction_grid_barrier(uint32_t* counter, uint3
         *abort_flag = kWaitGrid;
         break;
       }
-      // Sparse polling: every CTA polls the same word, and the wait is off the
-      // tensor cores' critical path.
-      __nanosleep(4000);
+      // Every CTA polls the same word; at a short M the wait is on the
+      // launch's critical path, so the poll is frequent.
+      __nanosleep(256);
     }
     __threadfence();
   }
@@ -297,7 +302,8 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
   float* red = reinterpret_cast<float*>(smem + kS * kStageBytes);
   // 1024-byte aligned: the stages and the reduction area are multiples of 1 KiB.
   uint8_t* pred_slice = reinterpret_cast<uint8_t*>(red + red_floats(KIND));
-  uint64_t* full = reinterpret_cast<uint64_t*>(pred_slice + pred_slice_bytes(KIND, CHK));
+  float* pred_q = reinterpret_cast<float*>(pred_slice + pred_slice_bytes(KIND, CHK));
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(pred_q) + pred_q_bytes(CHK));
   uint64_t* empty = full + kS;
   uint64_t* acc_full = empty + kS;
   uint64_t* acc_empty = acc_full + 2;
@@ -972,35 +978,49 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
         }
         return true;
       };
-      // ---- phase 1: per-band projection partials (project_item, kslice.cuh),
-      // spread over the first half of the CTA's tiles.
-      {
-        const ProjectionView view{p.a, p.sa, p.sfa, p.weights, p.m, p.k, p.k_blocks, num_slices, p.q_part};
-        const int64_t items = static_cast<int64_t>(num_slices) * p.q_bands;
-        const int64_t first_item = static_cast<int64_t>(blockIdx.x) * 4 + prediction_index<WIDE>(warp);
-        const int64_t item_step = static_cast<int64_t>(gridDim.x) * 4;
-        const int64_t my_items = first_item < items ? (items - 1 - first_item) / item_step + 1 : 0;
-        int64_t j = 0;
-        for (int64_t item = first_item; item < items && !*abort_flag; item += item_step, ++j) {
-          // A few items (a short M) run at once: pacing only matters when
-          // the projection is large enough to take L2 bandwidth from the
-          // mainloop's loads.
-          if (my_items > kPacedItems && !pace(static_cast<uint32_t>(j * half / my_items))) break;
-          const int64_t band = item / num_slices, chunk = item % num_slices;
-          project_item<KIND, C>(view, band, chunk, lane, band_partial<C>(view, band, chunk));
+      if (!p.q_ready) {
+        // ---- phase 1: per-band projection partials (project_item, kslice.cuh),
+        // spread over the first half of the CTA's tiles.
+        {
+          const ProjectionView view{p.a, p.sa, p.sfa, p.weights, p.m, p.k, p.k_blocks, num_slices, p.q_part};
+          const int64_t items = static_cast<int64_t>(num_slices) * p.q_bands;
+          const int64_t first_item = static_cast<int64_t>(blockIdx.x) * 4 + prediction_index<WIDE>(warp);
+          const int64_t item_step = static_cast<int64_t>(gridDim.x) * 4;
+          const int64_t my_items = first_item < items ? (items - 1 - first_item) / item_step + 1 : 0;
+          int64_t j = 0;
+          for (int64_t item = first_item; item < items && !*abort_flag; item += item_step, ++j) {
+            // A few items (a short M) run at once: pacing only matters when
+            // the projection is large enough to take L2 bandwidth from the
+            // mainloop's loads.
+            if (my_items > kPacedItems && !pace(static_cast<uint32_t>(j * half / my_items))) break;
+            const int64_t band = item / num_slices, chunk = item % num_slices;
+            project_item<KIND, C>(view, band, chunk, lane, band_partial<C>(view, band, chunk));
+          }
         }
-      }
-      // ---- phase 2: q_full = sum over bands (ascending) ----
-      if (prediction_grid_barrier(p.grid_sync, gridDim.x, ct, abort_flag, p.watchdog, p.wait_limit_ns)) {
-        const int64_t entries = k_pad * C * 2;
-        for (int64_t e = static_cast<int64_t>(blockIdx.x) * 128 + ct; e < entries;
-             e += static_cast<int64_t>(gridDim.x) * 128) {
-          float acc = __ldcg(p.q_part + e);
-          for (int b = 1; b < p.q_bands; ++b) acc += __ldcg(p.q_part + b * entries + e);
-          p.q_full[e] = acc;
+        // ---- phase 2: q_full = sum over bands (ascending) ----
+        if (prediction_grid_barrier(p.grid_sync, gridDim.x, ct, abort_flag, p.watchdog, p.wait_limit_ns)) {
+          const int64_t entries = k_pad * C * 2;
+          for (int64_t e = static_cast<int64_t>(blockIdx.x) * 128 + ct; e < entries;
+               e += static_cast<int64_t>(gridDim.x) * 128) {
+            // Bands in ascending order; their loads batched ahead of the adds.
+            float acc = __ldcg(p.q_part + e);
+            int b = 1;
+            for (; b + 8 <= p.q_bands; b += 8) {
+              float x[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) x[i] = __ldcg(p.q_part + (b + i) * entries + e);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) acc = __fadd_rn(acc, x[i]);
+            }
+            for (; b < p.q_bands; ++b) acc = __fadd_rn(acc, __ldcg(p.q_part + b * entries + e));
+            p.q_full[e] = acc;
+          }
         }
+        prediction_grid_barrier(p.grid_sync, 2 * gridDim.x, ct, abort_flag, p.watchdog, p.wait_limit_ns);
+      } else {
+        // q_full was written by the kernels before this launch.
+        griddep_wait();
       }
-      prediction_grid_barrier(p.grid_sync, 2 * gridDim.x, ct, abort_flag, p.watchdog, p.wait_limit_ns);
       // ---- phase 3: predictions of this CTA's tiles ----
       const uint32_t last = my_tiles > 0 ? my_tiles - 1 : 0u;
       const uint32_t start = min(static_cast<uint32_t>(*tiles_done), last);
@@ -1079,20 +1099,27 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
               break;
             }
           }
-          // q_full is zero-padded to a multiple of 64 K, so loads need no guard;
-          // 8 elements of q are loaded ahead of their fma chains.
+          // The slice's q in shared memory: one batch of L2 loads (q_full was
+          // written by other CTAs during this launch, so they bypass L1)
+          // instead of a round trip per 8 k. q_full is zero-padded to a
+          // multiple of 64 K, so the loads need no guard.
+          named_barrier(2, 128);  // the previous slice's reads of pred_q are done
+          if (ct < kSliceK * C * 2 / 4) {
+            reinterpret_cast<float4*>(pred_q)[ct] =
+                __ldcg(reinterpret_cast<const float4*>(p.q_full + static_cast<int64_t>(k0) * C * 2) + ct);
+          }
+          named_barrier(2, 128);
 #pragma unroll
           for (int e0 = 0; e0 < kSliceK; e0 += 8) {
             float qv[8][C][2];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              const float* qk = p.q_full + static_cast<int64_t>(k0 + e0 + e) * C * 2;
-              // q_full was written by other CTAs during this launch: read through L2.
+              const float* qk = pred_q + (e0 + e) * C * 2;
               if constexpr (C == 2) {
-                const float4 f = __ldcg(reinterpret_cast<const float4*>(qk));
+                const float4 f = *reinterpret_cast<const float4*>(qk);
                 qv[e][0][0] = f.x; qv[e][0][1] = f.y; qv[e][1][0] = f.z; qv[e][1][1] = f.w;
               } else {
-                const float2 f = __ldcg(reinterpret_cast<const float2*>(qk));
+                const float2 f = *reinterpret_cast<const float2*>(qk);
                 qv[e][0][0] = f.x; qv[e][0][1] = f.y;
               }
             }
@@ -1277,6 +1304,7 @@ int launch_impl(const GemmProblem& g, cudaStream_t stream) {
   p.q_part = g.q_part;
   p.grid_sync = g.grid_sync;
   p.q_bands = static_cast<int32_t>(ceil_div(g.m, kBandRows));
+  p.q_ready = g.q_ready ? 1 : 0;
   p.a = g.a;
   p.sfa = g.sfa;
   p.b = g.b;

@@ -61,6 +61,10 @@ struct GemmProblem {
   // Row checksums (nullable): fp32 [ceil(N/64)][M] row sums of the output
   // per 64-column block, after the fault (FP8 and NVFP4 kinds).
   float* row_observed;
+  // q_full already holds the projection of A (computed by the standalone
+  // projection kernels before this launch): the prediction warps go straight
+  // to the per-tile prediction.
+  bool q_ready;
 };
 
 // Launches the GEMM (and its fused epilogue) on `stream`. Zeroes hit/nonfinite
@@ -101,12 +105,19 @@ struct KsliceScratch {
   float* q_part;        // [ceil(M / 128)][K_pad][C][2]
 };
 KsliceScratch kslice_scratch(const ReferenceProblem& p);
-// NVFP4 with a short M (rows <= kStandaloneMaxRows) and N >= 16 M: the
-// projection and the K-slice prediction run as two kernels spread over the
-// whole GPU before an observed-only GEMM, with bit-identical partials
-// (kslice.cu); otherwise they stay inside the GEMM, behind its tiles.
+// NVFP4 with a short M (rows <= kStandaloneMaxRows) and N >= 16 M, unless
+// kslice_preproject takes it: the projection and the K-slice prediction run
+// as two kernels spread over the whole GPU before an observed-only GEMM, with
+// bit-identical partials (kslice.cu); otherwise they stay inside the GEMM,
+// behind its tiles.
 constexpr int64_t kStandaloneMaxRows = 4096;
 bool kslice_standalone(const ReferenceProblem& p);
 int launch_kslice_standalone(const ReferenceProblem& p, const KsliceScratch& s, cudaStream_t stream);
+// The projection of A alone, by the standalone kernels, into s.q_full (the
+// partials bit-identical to the in-GEMM projection's). Chosen by
+// kslice_preproject when the GEMM has too few tiles per CTA to hide the
+// in-GEMM projection behind its mainloop.
+bool kslice_preproject(const ReferenceProblem& p);
+int launch_kslice_projection(const ReferenceProblem& p, const KsliceScratch& s, cudaStream_t stream);
 
 }  // namespace sdc

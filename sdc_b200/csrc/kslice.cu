@@ -33,7 +33,9 @@ constexpr int kFoldThreads = 64;  // small blocks: the entries spread over every
 constexpr int kFoldBatch = 32;    // band partials loaded ahead of their adds
 constexpr int kPredictThreads = 128;
 
-// Test hook: 0 = choose by size, 1 = always fused, 2 = always standalone.
+// Test hook: 0 = choose by size, 1 = always fused (projection inside the
+// GEMM), 2 = always standalone, 3 = always fused with the projection
+// computed before the GEMM.
 std::atomic<int> g_kslice_mode{0};
 
 // One warp per item (band, slice), items in band-major order so that a
@@ -325,15 +327,53 @@ int launch_projection_sums(Kind kind, int channels, const ProjectionView& view, 
   return SDC_OK;
 }
 
+// Measured on B200 over the Qwen2.5-7B linear shapes at M = 2048 / 4096 /
+// 8192 (protected step over the unprotected GEMM): the projection computed
+// before the GEMM wins only at M <= 2048 when the in-GEMM projection has many
+// items per prediction warp next to few tiles per CTA, i.e. a long K
+// (down, K = 18944: NVFP4 57 vs 70 %, FP8 36 vs 53 %), and for NVFP4 with
+// N >= 16 M (gate/up: 57 vs 61 % standalone, 68 % in-GEMM). It loses for
+// block-scaled FP8 (whose 128-wide tiles give the in-GEMM projection twice
+// the tiles to hide behind) and at M >= 4096 everywhere.
+static bool kslice_preproject_auto(const ReferenceProblem& r) {
+  if (r.kind == Kind::kFp8Block || r.m > 2048) return false;
+  return r.k >= 4 * r.n || (r.kind == Kind::kNvf4 && r.n >= 16 * r.m);
+}
+
 bool kslice_standalone(const ReferenceProblem& r) {
   const int mode = g_kslice_mode.load(std::memory_order_relaxed);
-  if (mode == 1) return false;
+  if (mode == 1 || mode == 3) return false;
   if (mode == 2) return true;
   // Measured on B200 over the Qwen2.5-7B linear shapes at M = 2048 / 4096 /
   // 8192: the in-GEMM path wins except for NVFP4 (whose in-GEMM prediction
-  // reads B with plain loads) when N dwarfs a short M (gate/up at M = 2048:
-  // 270 vs 302 us, the GEMM alone 175 us).
-  return r.kind == Kind::kNvf4 && r.m <= kStandaloneMaxRows && r.n >= 16 * r.m;
+  // reads B with plain loads) when N dwarfs a short M; up to M = 2048 the
+  // projection computed before the GEMM does better still.
+  return r.kind == Kind::kNvf4 && r.m <= kStandaloneMaxRows && r.n >= 16 * r.m && !kslice_preproject_auto(r);
+}
+
+bool kslice_preproject(const ReferenceProblem& r) {
+  const int mode = g_kslice_mode.load(std::memory_order_relaxed);
+  if (mode == 1 || mode == 2) return false;
+  if (mode == 3) return true;
+  return kslice_preproject_auto(r);
+}
+
+int launch_kslice_projection(const ReferenceProblem& r, const KsliceScratch& s, cudaStream_t stream) {
+  const Kind kind = r.kind;
+  if (kind != Kind::kFp8 && kind != Kind::kNvf4 && kind != Kind::kFp8Block) {
+    return fail(SDC_ERR_INVALID, "K-slice prediction is defined for the FP8 and NVFP4 kinds");
+  }
+  const bool blk = kind == Kind::kFp8Block;
+  const ProjectionView view{r.a,
+                            blk ? reinterpret_cast<const float*>(r.sfa) : nullptr,
+                            kind == Kind::kNvf4 ? r.sfa : nullptr,
+                            r.weights,
+                            r.m,
+                            r.k,
+                            r.k / 128,
+                            ceil_div(r.k, kSliceK),
+                            s.q_part};
+  return launch_projection_sums(kind, r.channels, view, s.q_full, stream);
 }
 
 int launch_kslice_standalone(const ReferenceProblem& r, const KsliceScratch& s, cudaStream_t stream) {
@@ -352,7 +392,7 @@ int launch_kslice_standalone(const ReferenceProblem& r, const KsliceScratch& s, 
 }  // namespace sdc
 
 extern "C" int sdc_test_set_kslice_path(int mode) {
-  if (mode < 0 || mode > 2) return sdc::fail(SDC_ERR_INVALID, "kslice path mode must be 0 (auto), 1 or 2");
+  if (mode < 0 || mode > 3) return sdc::fail(SDC_ERR_INVALID, "kslice path mode must be 0 (auto), 1, 2 or 3");
   sdc::g_kslice_mode.store(mode, std::memory_order_relaxed);
   return SDC_OK;
 }

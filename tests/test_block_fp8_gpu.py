@@ -104,10 +104,11 @@ def test_random_output_within_accumulation_bound(shape):
 
 @pytest.mark.parametrize("shape", [(136, 144, 128), (300, 200, 384), (2048, 2048, 512), (2560, 4352, 2048),
                                    (640, 33024, 1024), (5000, 640, 512)])
-@pytest.mark.parametrize("path", [1, 2])
+@pytest.mark.parametrize("path", [1, 2, 3])
 def test_kslice_prediction_bit_exact_vs_oracle(shape, path):
     # path 1: the prediction inside the GEMM; path 2: the two standalone
-    # kernels before an observed-only GEMM (the default for M <= 4096).
+    # kernels before an observed-only GEMM; path 3: the projection by the
+    # standalone kernels, the prediction inside the GEMM.
     from sdc_b200 import capi
 
     m, n, k = shape

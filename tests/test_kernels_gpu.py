@@ -444,8 +444,9 @@ def test_persistent_multi_tile_per_cta_bit_exact(precision, shape, layout):
 @pytest.mark.parametrize("shape", [(136, 144, 288), (300, 200, 96), (2560, 4352, 2048), (640, 33024, 1024),
                                    (5000, 640, 512)])
 def test_kslice_standalone_and_fused_paths_are_bit_identical(precision, shape):
-    # The K-slice prediction runs inside the GEMM (long M) or as two kernels
-    # before an observed-only GEMM (short M); both must give the oracle's
+    # The K-slice prediction runs inside the GEMM (path 1), as two kernels
+    # before an observed-only GEMM (path 2), or inside the GEMM from a
+    # projection computed before it (path 3); all must give the oracle's
     # partials bit for bit, and the same output and observation.
     from sdc_b200 import capi
 
@@ -457,15 +458,16 @@ def test_kslice_standalone_and_fused_paths_are_bit_identical(precision, shape):
     lib = capi.lib()
     results = []
     try:
-        for mode in (1, 2):
+        for mode in (1, 2, 3):
             capi.check(lib.sdc_test_set_kslice_path(mode))
             results.append([x.clone() for x in reference(*args, weights, -1, -1, -1, 0, None, 1)])
             torch.cuda.synchronize()
     finally:
         capi.check(lib.sdc_test_set_kslice_path(0))
-    (out1, obs1, hit1, pred1, mag1), (out2, obs2, hit2, pred2, mag2) = results
-    assert torch.equal(out1, out2) and torch.equal(obs1, obs2) and hit1.item() == hit2.item() == 0
-    assert torch.equal(pred1, pred2) and torch.equal(mag1, mag2)
+    (out1, obs1, hit1, pred1, mag1) = results[0]
+    for out2, obs2, hit2, pred2, mag2 in results[1:]:
+        assert torch.equal(out1, out2) and torch.equal(obs1, obs2) and hit1.item() == hit2.item() == 0
+        assert torch.equal(pred1, pred2) and torch.equal(mag1, mag2)
     a, sfa, b, sfb = _oracle_inputs(precision, qa, qb)
     epred, emag = native.input_reference(precision, a, sfa, b, sfb, m, n, k, _np(weights), _np(alpha),
                                          pred1.shape[-1], "kslice")
