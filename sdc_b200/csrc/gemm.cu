@@ -1038,11 +1038,13 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
         int mt, nt;
         work_coords<PAIR>(t, p, rank, mt, nt);
         if (mt >= p.tiles_m) continue;
-        float acc[kRowsPerThread][C][2];
+        // Per row and channel: the value chain (.x) and the magnitude chain
+        // (.y), advanced together by one f32x2 fma (two independent fmas).
+        float2 acc[kRowsPerThread][C];
 #pragma unroll
         for (int h = 0; h < kRowsPerThread; ++h)
 #pragma unroll
-          for (int c = 0; c < C; ++c) acc[h][c][0] = acc[h][c][1] = 0.f;
+          for (int c = 0; c < C; ++c) acc[h][c] = make_float2(0.f, 0.f);
         for (int sl = mt; sl < num_slices; sl += p.tiles_m) {
           const int k0 = sl * kSliceK;
           constexpr int kChunksPerSlice = is_e4m3(KIND) ? 4 : 2;  // 16-byte chunks per row
@@ -1109,18 +1111,30 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
                 __ldcg(reinterpret_cast<const float4*>(p.q_full + static_cast<int64_t>(k0) * C * 2) + ct);
           }
           named_barrier(2, 128);
+          // NVFP4: each row's four block scales of the slice as fp16 pairs (s, s).
+          uint32_t scale_h2[kRowsPerThread][4];
+          if constexpr (KIND == Kind::kNvf4) {
+#pragma unroll
+            for (int h = 0; h < kRowsPerThread; ++h) {
+              const uint32_t lo = e4m3x2_to_h2(sfw[h] & 0xFFFFu), hi = e4m3x2_to_h2(sfw[h] >> 16);
+              scale_h2[h][0] = __byte_perm(lo, 0, 0x1010);
+              scale_h2[h][1] = __byte_perm(lo, 0, 0x3232);
+              scale_h2[h][2] = __byte_perm(hi, 0, 0x1010);
+              scale_h2[h][3] = __byte_perm(hi, 0, 0x3232);
+            }
+          }
 #pragma unroll
           for (int e0 = 0; e0 < kSliceK; e0 += 8) {
-            float qv[8][C][2];
+            float2 qv[8][C];  // (q, q magnitude) per element and channel
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               const float* qk = pred_q + (e0 + e) * C * 2;
               if constexpr (C == 2) {
                 const float4 f = *reinterpret_cast<const float4*>(qk);
-                qv[e][0][0] = f.x; qv[e][0][1] = f.y; qv[e][1][0] = f.z; qv[e][1][1] = f.w;
+                qv[e][0] = make_float2(f.x, f.y);
+                qv[e][1] = make_float2(f.z, f.w);
               } else {
-                const float2 f = *reinterpret_cast<const float2*>(qk);
-                qv[e][0][0] = f.x; qv[e][0][1] = f.y;
+                qv[e][0] = *reinterpret_cast<const float2*>(qk);
               }
             }
 #pragma unroll
@@ -1143,19 +1157,21 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
                 const uint4 chunk = raw[h][e0 >> 5];
                 const int wi = (e0 >> 3) & 3;
                 const uint32_t word = wi == 0 ? chunk.x : wi == 1 ? chunk.y : wi == 2 ? chunk.z : chunk.w;
-                e2m1x8_to_float(word, value);
-                const float scale = decode_e4m3((sfw[h] >> (8 * (e0 >> 4))) & 0xFFu);
+                // code x block scale, two at a time in fp16: exact (at most
+                // 6 significant bits), so the same values as in fp32.
+                const uint32_t sh2 = scale_h2[h][e0 >> 4];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) value[e] *= scale;
+                for (int i = 0; i < 4; ++i) {
+                  const float2 v = h2_to_float2(hmul2_rn(e2m1x2_to_h2((word >> (8 * i)) & 0xFFu), sh2));
+                  value[2 * i] = v.x;
+                  value[2 * i + 1] = v.y;
+                }
               }
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
-                const float av = fabsf(value[e]);
+                const float2 vv = make_float2(value[e], fabsf(value[e]));
 #pragma unroll
-                for (int c = 0; c < C; ++c) {
-                  acc[h][c][0] = fmaf(qv[e][c][0], value[e], acc[h][c][0]);
-                  acc[h][c][1] = fmaf(qv[e][c][1], av, acc[h][c][1]);
-                }
+                for (int c = 0; c < C; ++c) acc[h][c] = fma2(qv[e][c], vv, acc[h][c]);
               }
             }
           }
@@ -1169,8 +1185,8 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
 #pragma unroll
             for (int c = 0; c < C; ++c) {
               const int64_t off = (static_cast<int64_t>(c) * p.tiles_m + mt) * p.padded_n + col;
-              p.predicted[off] = alpha * (in ? acc[h][c][0] : 0.f);
-              p.magnitude[off] = fabsf(alpha) * (in ? acc[h][c][1] : 0.f);
+              p.predicted[off] = alpha * (in ? acc[h][c].x : 0.f);
+              p.magnitude[off] = fabsf(alpha) * (in ? acc[h][c].y : 0.f);
             }
           }
         }

@@ -71,37 +71,6 @@ __global__ void __launch_bounds__(kFoldThreads) kslice_fold(const float* q_part,
   q_full[e] = q;
 }
 
-// Packed decodes for the prediction's inner loop. Every e2m1 code times its
-// ue4m3 block scale is exact in fp16 (at most 6 significant bits, magnitudes
-// 2^-10 .. 2688), so the product is formed two at a time in fp16 and widened:
-// the same fp32 values as code * scale computed in fp32.
-__device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t two_bytes) {
-  uint32_t h2;
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(static_cast<uint16_t>(two_bytes)));
-  return h2;
-}
-
-__device__ __forceinline__ uint32_t e2m1x2_to_h2(uint32_t byte) {
-  uint32_t h2;
-  asm("{\n\t.reg .b8 b;\n\tcvt.u8.u32 b, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b;\n\t}" : "=r"(h2) : "r"(byte));
-  return h2;
-}
-
-__device__ __forceinline__ uint32_t hmul2_rn(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
-__device__ __forceinline__ float2 h2_to_float2(uint32_t h2) {
-  float2 out;
-  asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-      "cvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
-      : "=f"(out.x), "=f"(out.y)
-      : "r"(h2));
-  return out;
-}
-
 struct PredictArgs {
   const uint8_t* b;        // B rows [N][K] (e4m3) or [N][K/2] (packed e2m1)
   const uint8_t* sfb;      // NVFP4: B scale atoms

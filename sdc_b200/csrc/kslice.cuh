@@ -144,6 +144,37 @@ __device__ __forceinline__ void project_item(const ProjectionView& v, int64_t ba
   }
 }
 
+// Packed decodes for the prediction's inner loop. Every e2m1 code times its
+// ue4m3 block scale is exact in fp16 (at most 6 significant bits, magnitudes
+// 2^-10 .. 2688), so the product is formed two at a time in fp16 and widened:
+// the same fp32 values as code * scale computed in fp32.
+__device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t two_bytes) {
+  uint32_t h2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(static_cast<uint16_t>(two_bytes)));
+  return h2;
+}
+
+__device__ __forceinline__ uint32_t e2m1x2_to_h2(uint32_t byte) {
+  uint32_t h2;
+  asm("{\n\t.reg .b8 b;\n\tcvt.u8.u32 b, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b;\n\t}" : "=r"(h2) : "r"(byte));
+  return h2;
+}
+
+__device__ __forceinline__ uint32_t hmul2_rn(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ float2 h2_to_float2(uint32_t h2) {
+  float2 out;
+  asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "cvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
+      : "=f"(out.x), "=f"(out.y)
+      : "r"(h2));
+  return out;
+}
+
 // q_full [K_pad][C][2] of `view` (bands summed in ascending order) by the
 // standalone projection kernels (kslice.cu): the band partials go to
 // view.q_part ([bands][K_pad][C][2]; unused when there is one band), then
