@@ -782,6 +782,8 @@ def run_ours(args):
             continue
         size = args.size or SIZES[precision]
         m = n = k = size
+        if args.shape:
+            m, n, k = (int(x) for x in args.shape.split(","))
         prot = Protected(precision, m, n, k, device, SEEDS[precision] + 1000 * rank, rtol=args.rtol)
         flops = 2.0 * m * n * k
         ring = torch.zeros(EXCHANGE_EVERY, 4, dtype=torch.float32, device=device)
@@ -1245,6 +1247,9 @@ def main():
                         help="train workload: no detection threshold, report the clean residual / magnitude")
     parser.add_argument("--size", type=int, default=0,
                         help="override M=N=K of the workloads (profiling captures and CPU tests; not a bench line)")
+    parser.add_argument("--shape", default="",
+                        help="M,N,K of the GEMM step (profiling captures at one layer's shard shape; not a bench line; "
+                             "the end-to-end leg needs --no-e2e)")
     args = parser.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
