@@ -1045,6 +1045,21 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
         for (int h = 0; h < kRowsPerThread; ++h)
 #pragma unroll
           for (int c = 0; c < C; ++c) acc[h][c] = make_float2(0.f, 0.f);
+        // e4m3: one thread copies each slice of the tile's B rows into
+        // shared memory (rows past N and K past the row read as zeros); the
+        // next slice's copy is issued as soon as every prediction thread holds
+        // the current one in registers, so it lands while that one is summed.
+        auto copy_slice = [&](int sl_copy) {
+          if (ct == 0) {
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(pred_full, static_cast<uint32_t>(pred_slice_bytes(KIND, CHK)));
+            tma_load_2d(pred_slice, &tm_sfb, pred_full, sl_copy * kSliceK, nt * kTN);
+            copy_in_flight = true;
+          }
+        };
+        if constexpr (is_e4m3(KIND)) {
+          if (mt < num_slices) copy_slice(mt);
+        }
         for (int sl = mt; sl < num_slices; sl += p.tiles_m) {
           const int k0 = sl * kSliceK;
           constexpr int kChunksPerSlice = is_e4m3(KIND) ? 4 : 2;  // 16-byte chunks per row
@@ -1052,15 +1067,6 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
           uint32_t sfw[kRowsPerThread];
           bool landed = true;
           if constexpr (is_e4m3(KIND)) {
-            // One thread copies the slice (rows past N and K past the row
-            // read as zeros); every prediction thread waits for it. The
-            // previous slice's reads ended at the barrier below.
-            if (ct == 0) {
-              fence_proxy_async_smem();
-              mbar_arrive_expect_tx(pred_full, static_cast<uint32_t>(pred_slice_bytes(KIND, CHK)));
-              tma_load_2d(pred_slice, &tm_sfb, pred_full, k0, nt * kTN);
-              copy_in_flight = true;
-            }
             landed = mbar_wait(pred_full, slices_staged & 1u, kWaitProjection, abort_flag, p.watchdog, p.wait_limit_ns);
             if (ct == 0 && landed) copy_in_flight = false;
             ++slices_staged;
@@ -1100,6 +1106,8 @@ __global__ void __launch_bounds__(num_threads(CHK, is_wide(KIND)), 1)
               stopped = true;
               break;
             }
+            // No thread reads this slice's buffer any more: it takes the next.
+            if (sl + p.tiles_m < num_slices) copy_slice(sl + p.tiles_m);
           }
           // The slice's q in shared memory: one batch of L2 loads (q_full was
           // written by other CTAs during this launch, so they bypass L1)
