@@ -413,3 +413,37 @@ def test_configuration_defaults_and_extensions():
     rows = parse_abft_config({"method": "sum", "implementation": "native", "reference_mode": "input_fused",
                               "row_checksums": True})
     assert rows.row_checksums and not cfg.row_checksums
+
+
+def test_profile_summary_per_stage():
+    """summarize_profile: stage statistics from CPU scope events, the GEMM
+    kernels' share (own and child scopes), and a loud error when a stage the
+    path must run is missing a sample."""
+    from types import SimpleNamespace
+
+    from sdc_b200.abft import profiling
+
+    cpu = SimpleNamespace(name="CPU")
+
+    def scope(name, device_us, cpu_us, kernels=(), children=()):
+        return SimpleNamespace(name=name, device_type=cpu, device_time_total=device_us, cpu_time_total=cpu_us,
+                               kernels=[SimpleNamespace(name=k, duration=d) for k, d in kernels],
+                               cpu_children=list(children))
+
+    events = []
+    for i in range(2):
+        launch = scope("sdc_cutlass::abft_fp8_reference_mm", 50.0, 5.0, kernels=[("sdc::gemm_kernel<0,2>", 45.0)])
+        events += [scope("baseline.gemm", 40.0 + i, 6.0, kernels=[("sdc::gemm_kernel<0,0>", 40.0 + i)]),
+                   scope("abft.reference", 0.0, 2.0), scope("abft.execute", 55.0, 20.0, children=[launch]),
+                   scope("abft.finalize", 9.0, 15.0), scope("abft.total", 64.0, 40.0),
+                   SimpleNamespace(name="abft.total", device_type=SimpleNamespace(name="CUDA"))]
+    result = profiling.summarize_profile(events, 2, input_fused=True, native=True)
+    rows = {row["stage"]: row for row in result["stages"]}
+    assert set(rows) == {"baseline.gemm", "abft.reference", "abft.execute", "abft.finalize", "abft.total"}
+    assert rows["baseline.gemm"]["gpu_active_ms"]["samples"] == [0.040, 0.041]
+    assert rows["abft.execute"]["gemm_kernel_ms"]["median"] == 0.045
+    assert abs(rows["abft.execute"]["other_gpu_activity_ms"]["median"] - 0.010) < 1e-12
+    assert rows["abft.finalize"]["cpu_scope_ms"]["median"] == 0.015
+    with pytest.raises(RuntimeError, match="Incomplete profile: abft.finalize"):
+        profiling.summarize_profile([e for e in events if e.name != "abft.finalize"], 2, input_fused=True,
+                                    native=True)

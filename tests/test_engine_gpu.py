@@ -141,3 +141,21 @@ def test_timing_events_are_reported():
     assert {"reference", "execute", "finalize", "locate"} <= set(timing)
     assert all(value >= 0 for value in timing.values())
     assert sdc_b200.LIB_PATH.exists()
+
+
+def test_stage_profile_of_a_native_call():
+    """profile_prepared: every native stage appears with one sample per
+    repeat, the GEMM kernels account for most of abft.execute, and the clean
+    protected output equals the unprotected GEMM's."""
+    from sdc_b200.abft.profiling import profile_prepared
+
+    a, b = _operands(512, 512, 512, seed=12)
+    prepared = PreparedGemm.prepare(a, b, "fp8", "tensorwise")
+    result = profile_prepared(prepared, _cfg(reference_layout="kslice"), warmup=2, repeats=4)
+    rows = {row["stage"]: row for row in result["stages"]}
+    for stage in ("baseline.gemm", "abft.reference", "abft.execute", "abft.finalize", "abft.total"):
+        assert stage in rows and len(rows[stage]["gpu_active_ms"]["samples"]) == 4 * rows[stage]["calls_per_repeat"]
+    assert rows["abft.execute"]["gemm_kernel_ms"]["median"] > 0
+    assert rows["baseline.gemm"]["gemm_kernel_ms"]["median"] > 0
+    assert result["last_output_comparison"]["bit_identical"]
+    assert result["last_report"]["detected"] in (False, [False])
