@@ -56,10 +56,12 @@ enum sdc_reference_layout {
    * mainloop) instead of ~C/32 of the GEMM on CUDA cores; that launch
    * synchronises its CTAs twice, so two such launches must not run
    * concurrently on one GPU (different streams): one of them would wait until
-   * its watchdog gives up and reports the call as detected. NVFP4 launches
-   * with M <= 4096 and N >= 16 M run them as two kernels before an
-   * observed-only GEMM instead (no such restriction), with bit-identical
-   * results. */
+   * its watchdog gives up and reports the call as detected. Short-M shapes
+   * take the projection out of the GEMM instead (no such restriction), with
+   * bit-identical results: at M <= 2048 with K >= 4 N (FP8, NVFP4) or NVFP4
+   * with N >= 16 M, two kernels compute it before the GEMM; NVFP4 with
+   * 2048 < M <= 4096 and N >= 16 M runs the projection and the prediction as
+   * kernels before an observed-only GEMM. */
   SDC_LAYOUT_KSLICE = 1
 };
 
